@@ -1,0 +1,171 @@
+/*
+ * hier_b200.h - C ABI of libhier_b200.so, the B200 (sm_100a) implementation of
+ * Multics' hierarchical group attention.
+ *
+ * Every entry point takes plain device pointers, element counts/strides and a
+ * CUDA stream (as void*), returns a status code (HIER_OK on success) and
+ * never allocates device memory itself: callers pass output buffers and, where
+ * a kernel needs scratch space, a workspace whose size is given by the
+ * matching *_workspace_size call.  On failure the message of the last error
+ * of the calling thread is available from hier_last_error().
+ *
+ * Reference interfaces (TencentARC/Multics, paths relative to the checkout)
+ * that each entry point replaces are cited beside it.
+ */
+#ifndef HIER_B200_H
+#define HIER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The Python host layer maps them onto the exception types the
+ * reference raises: VALUE -> ValueError, NOTIMPL -> NotImplementedError,
+ * RUNTIME/CUDA -> RuntimeError, ASSERT -> AssertionError. */
+#define HIER_OK 0
+#define HIER_EVALUE 1
+#define HIER_ENOTIMPL 2
+#define HIER_ERUNTIME 3
+#define HIER_EASSERT 4
+#define HIER_ECUDA 5
+
+/* Last error message / code of the calling thread ("" / HIER_OK if none). */
+const char* hier_last_error(void);
+int hier_last_error_code(void);
+/* ABI version, bumped on any signature change. */
+int hier_abi_version(void);
+
+/*
+ * Grouping description shared by the mask and metadata builders.  Mirrors the
+ * tensors normalised by _prepare_hier_group_tensors /
+ * _prepare_hier_membership_tensors (multics/models/hier_masks.py:22-71,
+ * 127-193).  All pointers are device pointers; the host layer has already
+ * validated shapes and ranges with the reference's messages.
+ *   labels      int64 [T,P]   (membership_mode == 0)
+ *   membership  uint8 [T,N,P] (membership_mode == 1)
+ *   global_only uint8 [T,P]   (membership_mode == 1)
+ *   active      uint8 [T,N]   (both modes; labels mode: scatter of labels or
+ *                              the caller's active_group)
+ */
+typedef struct hier_grouping {
+  int32_t P, T, L, N, KL, KG;
+  int32_t n_block;    /* num_frame_per_block */
+  int32_t local_attn; /* local_attn_size, -1 = unlimited */
+  int32_t direct;     /* direct_player */
+  int32_t no_local;   /* hier_no_local_hub */
+  int32_t membership_mode;
+  const int64_t* labels;
+  const uint8_t* membership;
+  const uint8_t* global_only;
+  const uint8_t* active;
+} hier_grouping;
+
+/* ---------------------------------------------------------------------------
+ * Masks
+ * ------------------------------------------------------------------------- */
+
+/* Dense bool mask rows [row0, row0+nrows) of the [S,S] hierarchical mask into
+ * out (uint8 [nrows, S]).  Replaces build_stage2_hier_self_attn_mask
+ * (multics/models/hier_masks.py:364-507) and its membership variant
+ * (hier_masks.py:510-641).  Bit-exact. */
+int hier_dense_mask(const hier_grouping* g, int64_t row0, int64_t nrows, uint8_t* out,
+                    void* stream);
+
+/* Workspace bytes for hier_block_mask_build / hier_block_plan_build. */
+int hier_block_workspace_size(const hier_grouping* g, size_t* bytes);
+
+/* 128x128 block classification of the mask padded to S_pad = ceil(S/128)*128,
+ * with the same partial / full block lists as the Flex BlockMask built by
+ * build_stage2_hier_flex_block_mask (hier_masks.py:722-934, membership
+ * variant :937-1149): per query block the number of partial blocks and of
+ * full blocks, and the CSR-concatenated ascending block indices (offsets are
+ * exclusive scans of the counts).  Outputs (device int32):
+ *   kv_num [nb], kv_off [nb+1], kv_idx [nb*nb capacity]
+ *   full_num [nb], full_off [nb+1], full_idx [nb*nb capacity]
+ * totals (device int32 [2]) receives (#partial, #full). */
+int hier_block_mask_build(const hier_grouping* g, void* workspace, int32_t* kv_num,
+                          int32_t* kv_off, int32_t* kv_idx, int32_t* full_num,
+                          int32_t* full_off, int32_t* full_idx, int32_t* totals,
+                          void* stream);
+
+/* Attention work plan for the full-sequence hierarchical layout, built from
+ * the block classification of hier_block_mask_build (same workspace, after
+ * it).  Writes, for every 128-row query tile qb:
+ *   q_tiles [nb][4]   = (q_start, q_rows, kv_begin, kv_end)
+ *   kv_tiles [n_partial + n_full][4] = (k_row0, k_row1, mask_idx, ncols),
+ *       ascending key block order per query tile; k_row0/k_row1 are the pool
+ *       rows of the two 64-key halves (page_table != NULL maps logical 64-key
+ *       pages to physical pages: page p holds keys [64p, 64p+64)); mask_idx
+ *       -1 marks a full block, otherwise it indexes row_masks.
+ *   row_masks [n_partial][128][4] uint32 = per-row key bitmask of each partial
+ *       block (bit c of word c/32 set <=> key c of the block is visible).
+ *   order [nb] = query tiles sorted by descending number of key tiles.
+ * The full-sequence layout is the reference's dense/Flex mask semantics
+ * (hier_masks.py:364-1149), so inactive local-hub rows keep their self edge. */
+int hier_block_plan_build(const hier_grouping* g, const void* workspace, const int32_t* kv_off,
+                          const int32_t* kv_idx, const int32_t* full_off,
+                          const int32_t* full_idx, const int32_t* page_table,
+                          int32_t* q_tiles, int32_t* kv_tiles, uint32_t* row_masks,
+                          int32_t* order, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused Q/K prologue
+ * ------------------------------------------------------------------------- */
+
+/* q = RoPE(RMSNorm(qx + cam @ wcq^T) * nqw), k likewise, for S tokens of
+ * dimension dim = H * D (bf16 in, bf16 out), computed in fp32.  Replaces the
+ * post-projection part of SelfAttention._project_self_attn_qkv
+ * (multics/models/attention.py:355-365): camera adapter add
+ * (_apply_camera_qk, attention.py:307-320, bias-free, cam_dim inputs),
+ * RMSNorm over the full dim (attention.py:231-242, eps) and rope_apply
+ * (multics/models/rope.py:248-254).  cam may be NULL (no camera tokens).
+ * freqs: float32 [S, D/2, 2] (cos, sin) per token, shared by all heads.
+ * Row strides are in elements. */
+int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, const void* cam,
+                 int32_t cam_dim, const void* wcq, const void* wck, const void* nqw,
+                 const void* nkw, const float* freqs, int64_t S, int32_t H, int32_t D,
+                 float eps, void* q_out, void* k_out, int64_t out_stride, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Attention
+ * ------------------------------------------------------------------------- */
+
+/* Block-sparse flash attention forward on sm_100a (tcgen05 MMA with TMEM
+ * accumulators, TMA-staged tiles, online softmax), bf16 in/out, D = 128.
+ *   q   bf16 [q_rows_total, H*D] (row stride q_stride elements)
+ *   k,v bf16 [kv_rows_total, H*D] key/value pool (row stride kv_stride)
+ *   out bf16 [q_rows_total, H*D] (row stride out_stride); only rows covered
+ *       by q_tiles are written; rows whose key set is empty are written as 0
+ *       (the cached backends' contract, hier_segmented_attention.py:104-109).
+ *   q_tiles/kv_tiles/row_masks/order as produced by the plan builders.
+ *   dev_err: device int32, set non-zero if a pipeline wait timed out.
+ * Replaces the attention kernels of the reference backends: masked SDPA
+ * (attention.py:39-54), FlexAttention (attention.py:322-353), the Triton
+ * segmented / tiled128 kernels (kernels/hier_segmented_attention.py:27-114,
+ * kernels/hier_tiled_attention.py:52-146), aten FA2 varlen
+ * (kernels/hier_packed_attention.py:230-242) and FlashInfer paged prefill
+ * (kernels/hier_paged_attention.py:238-266). */
+int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stride, const void* k,
+                  const void* v, int64_t kv_rows_total, int64_t kv_stride, void* out,
+                  int64_t out_stride, int32_t H, int32_t D, const int32_t* q_tiles,
+                  int32_t n_q_tiles, const int32_t* kv_tiles, const uint32_t* row_masks,
+                  const int32_t* order, float softmax_scale, int32_t* dev_err, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Self-test of the tensor-core operand encodings (no reference counterpart):
+ * with A, B bf16 [128,128] row-major,
+ *   c_ss = A @ B^T   (both operands K-major in shared memory)
+ *   c_mn = A @ B     (B MN-major in shared memory)
+ *   c_ts = A @ B     (A read from tensor memory, B MN-major)
+ * as fp32 [128,128]. */
+int hier_selftest_umma(const void* a, const void* b, float* c_ss, float* c_mn, float* c_ts,
+                       int32_t* dev_err, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HIER_B200_H */

@@ -1,0 +1,92 @@
+"""ctypes binding of libhier_b200.so (the C ABI declared in include/hier_b200.h).
+
+The library is required: there is no CPU or PyTorch fallback for any entry
+point.  Loading fails loudly with the build command if the in-tree library is
+missing.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from ctypes import c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libhier_b200.so"
+HEADER = PKG.parent / "include" / "hier_b200.h"
+
+HIER_OK = 0
+_EXC = {1: ValueError, 2: NotImplementedError, 3: RuntimeError, 4: AssertionError, 5: RuntimeError}
+
+
+class HierGrouping(ctypes.Structure):
+    """Mirror of ``struct hier_grouping`` in include/hier_b200.h."""
+
+    _fields_ = [
+        ("P", c_int32), ("T", c_int32), ("L", c_int32), ("N", c_int32), ("KL", c_int32),
+        ("KG", c_int32), ("n_block", c_int32), ("local_attn", c_int32), ("direct", c_int32),
+        ("no_local", c_int32), ("membership_mode", c_int32), ("labels", c_void_p),
+        ("membership", c_void_p), ("global_only", c_void_p), ("active", c_void_p),
+    ]
+
+
+_P = c_void_p
+_SIGS = {
+    "hier_last_error": (c_char_p, []),
+    "hier_last_error_code": (c_int, []),
+    "hier_abi_version": (c_int, []),
+    "hier_dense_mask": (c_int, [ctypes.POINTER(HierGrouping), c_int64, c_int64, _P, _P]),
+    "hier_block_workspace_size": (c_int, [ctypes.POINTER(HierGrouping), ctypes.POINTER(c_size_t)]),
+    "hier_block_mask_build": (c_int, [ctypes.POINTER(HierGrouping), _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "hier_block_plan_build": (c_int, [ctypes.POINTER(HierGrouping), _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                      _P, _P]),
+    "hier_prep_qk": (c_int, [_P, _P, c_int64, _P, c_int32, _P, _P, _P, _P, _P, c_int64, c_int32,
+                             c_int32, c_float, _P, _P, c_int64, _P]),
+    "hier_attn_fwd": (c_int, [_P, c_int64, c_int64, _P, _P, c_int64, c_int64, _P, c_int64, c_int32,
+                              c_int32, _P, c_int32, _P, _P, _P, c_float, _P, _P]),
+    "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),
+}
+
+_LIB = None
+
+
+def lib():
+    """Load the in-tree library (once) and declare the C signatures."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH.name} is not built; run `python -m multics_b200.build` "
+                "(the hierarchical attention path has no fallback implementation)")
+        h = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(h, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = h
+    return _LIB
+
+
+def declared_symbols():
+    """Function names declared in include/hier_b200.h."""
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(hier_\w+)\s*\(", text, re.M)))
+
+
+def check(rc: int):
+    """Raise the reference's exception type for a non-zero status code."""
+    if rc != HIER_OK:
+        msg = lib().hier_last_error().decode(errors="replace")
+        raise _EXC.get(rc, RuntimeError)(msg)
+
+
+def ptr(t):
+    """Device pointer of a tensor (None -> NULL)."""
+    return None if t is None else c_void_p(t.data_ptr())
+
+
+def stream_ptr(device=None):
+    import torch
+
+    return c_void_p(torch.cuda.current_stream(device).cuda_stream)

@@ -1,0 +1,520 @@
+// Integer metadata kernels for the full-sequence hierarchical layout:
+// dense mask rows, 128x128 block classification (Flex BlockMask lists), and
+// the attention work plan (query tiles, key tiles, per-row key bitmasks).
+//
+// The mask predicate follows build_stage2_hier_self_attn_mask
+// (multics/models/hier_masks.py:364-507) and its membership variant
+// (hier_masks.py:510-641).  Inside a "unit" (one player frame of L tokens,
+// one local-hub slot of K_L tokens, one global frame of K_G tokens) the mask
+// is uniform, except for the token-level self edge of inactive local-hub
+// rows (hier_masks.py:484-486), so blocks are classified on the unit-level
+// matrix and only partial blocks are expanded to token bitmasks.
+
+#include <stdio.h>
+
+#include "common.cuh"
+
+namespace hier {
+
+struct Dims {
+  int P, T, L, N, KL, KG, nblk, win, direct, no_local, mem;
+  int64_t A, LS, S;
+  int U;
+  const int64_t* labels;
+  const uint8_t* membership;
+  const uint8_t* go;
+  const uint8_t* active;
+};
+
+static Dims make_dims(const hier_grouping* g) {
+  Dims d;
+  d.P = g->P;
+  d.T = g->T;
+  d.L = g->L;
+  d.N = g->N;
+  d.KL = g->KL;
+  d.KG = g->KG;
+  d.nblk = g->n_block;
+  d.win = g->local_attn;
+  d.direct = g->direct;
+  d.no_local = g->no_local;
+  d.mem = g->membership_mode;
+  d.A = (int64_t)g->P * g->T * g->L;
+  d.LS = (int64_t)g->T * g->N * g->KL;
+  d.S = d.A + d.LS + (int64_t)g->T * g->KG;
+  d.U = g->P * g->T + g->T * g->N + g->T;
+  d.labels = g->labels;
+  d.membership = g->membership;
+  d.go = g->global_only;
+  d.active = g->active;
+  return d;
+}
+
+struct Unit {
+  int kind;  // 0 player, 1 local hub, 2 global hub, 3 padding
+  int t, p, g, u;
+  int64_t start, end;  // token range of the unit
+};
+
+__device__ __forceinline__ Unit unit_of_token(const Dims& d, int64_t i) {
+  Unit r;
+  r.p = 0;
+  r.g = 0;
+  r.t = 0;
+  if (i < d.A) {
+    const int64_t tl = (int64_t)d.T * d.L;
+    r.kind = 0;
+    r.p = (int)(i / tl);
+    r.t = (int)((i % tl) / d.L);
+    r.u = r.p * d.T + r.t;
+    r.start = (int64_t)r.u * d.L;
+    r.end = r.start + d.L;
+  } else if (i < d.A + d.LS) {
+    const int64_t loc = i - d.A;
+    r.kind = 1;
+    r.t = (int)(loc / ((int64_t)d.N * d.KL));
+    r.g = (int)((loc % ((int64_t)d.N * d.KL)) / d.KL);
+    r.u = d.P * d.T + r.t * d.N + r.g;
+    r.start = d.A + ((int64_t)r.t * d.N + r.g) * d.KL;
+    r.end = r.start + d.KL;
+  } else if (i < d.S) {
+    const int64_t glob = i - d.A - d.LS;
+    r.kind = 2;
+    r.t = (int)(glob / d.KG);
+    r.u = d.P * d.T + d.T * d.N + r.t;
+    r.start = d.A + d.LS + (int64_t)r.t * d.KG;
+    r.end = r.start + d.KG;
+  } else {
+    r.kind = 3;
+    r.u = -1;
+    r.start = i;
+    r.end = i + 1;
+  }
+  return r;
+}
+
+__device__ __forceinline__ Unit unit_of_index(const Dims& d, int u) {
+  Unit r;
+  r.u = u;
+  r.p = 0;
+  r.g = 0;
+  if (u < d.P * d.T) {
+    r.kind = 0;
+    r.p = u / d.T;
+    r.t = u % d.T;
+  } else if (u < d.P * d.T + d.T * d.N) {
+    const int x = u - d.P * d.T;
+    r.kind = 1;
+    r.t = x / d.N;
+    r.g = x % d.N;
+  } else {
+    r.kind = 2;
+    r.t = u - d.P * d.T - d.T * d.N;
+  }
+  r.start = r.end = 0;
+  return r;
+}
+
+__device__ __forceinline__ bool act(const Dims& d, int t, int g) {
+  return d.active[(int64_t)t * d.N + g] != 0;
+}
+
+// player p (at frame t) belongs to group g
+__device__ __forceinline__ bool in_group(const Dims& d, int t, int p, int g) {
+  if (d.mem) return d.membership[((int64_t)t * d.N + g) * d.P + p] != 0;
+  return d.labels[(int64_t)t * d.P + p] == (int64_t)g;
+}
+
+__device__ __forceinline__ bool share_group(const Dims& d, int t, int p, int o) {
+  if (d.mem) {
+    for (int g = 0; g < d.N; ++g)
+      if (d.membership[((int64_t)t * d.N + g) * d.P + p] &&
+          d.membership[((int64_t)t * d.N + g) * d.P + o])
+        return true;
+    return false;
+  }
+  return d.labels[(int64_t)t * d.P + p] == d.labels[(int64_t)t * d.P + o];
+}
+
+__device__ __forceinline__ bool global_only_at(const Dims& d, int t, int p) {
+  return d.go[(int64_t)t * d.P + p] != 0;
+}
+
+// Unit-level edge predicate: the eleven edge sets of the dense mask
+// (hier_masks.py:463-507 labels, :599-641 membership) minus the token-level
+// inactive-local self edge.
+__device__ bool unit_edge(const Dims& d, const Unit& q, const Unit& k) {
+  if (q.kind == 3 || k.kind == 3) return false;
+  const int qb = q.t / d.nblk, kb = k.t / d.nblk;
+  const bool win = (kb <= qb) && (d.win == -1 || q.t - k.t < d.win);
+  if (q.kind == 0) {
+    if (k.kind == 0) {
+      if (q.p == k.p) return win;
+      if (!d.direct) return false;
+      return (qb == kb) && share_group(d, q.t, q.p, k.p);
+    }
+    if (k.kind == 1) return win && act(d, k.t, k.g) && in_group(d, q.t, q.p, k.g);
+    return win && (d.no_local || (d.mem && global_only_at(d, q.t, q.p)));
+  }
+  if (q.kind == 1) {
+    if (!act(d, q.t, q.g)) return false;
+    if (k.kind == 0) return win && in_group(d, q.t, k.p, q.g);
+    if (k.kind == 1) return win && q.g == k.g && act(d, k.t, k.g);
+    return win;
+  }
+  // global query
+  if (k.kind == 1) return win && act(d, k.t, k.g);
+  if (k.kind == 2) return win;
+  return win && (d.no_local || (d.mem && global_only_at(d, k.t, k.p)));
+}
+
+__device__ __forceinline__ bool inactive_local(const Dims& d, const Unit& q) {
+  return q.kind == 1 && !act(d, q.t, q.g);
+}
+
+// ---------------------------------------------------------------------------
+// kernels
+// ---------------------------------------------------------------------------
+
+__global__ void dense_mask_kernel(Dims d, int64_t row0, int64_t nrows, uint8_t* out) {
+  const int64_t total = nrows * d.S;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t qi = row0 + e / d.S;
+    const int64_t ki = e % d.S;
+    const Unit q = unit_of_token(d, qi);
+    const Unit k = unit_of_token(d, ki);
+    bool m = unit_edge(d, q, k);
+    if (!m && qi == ki && inactive_local(d, q)) m = true;
+    out[e] = m ? 1 : 0;
+  }
+}
+
+__global__ void unit_matrix_kernel(Dims d, uint8_t* M) {
+  const int64_t total = (int64_t)d.U * d.U;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const Unit q = unit_of_index(d, (int)(e / d.U));
+    const Unit k = unit_of_index(d, (int)(e % d.U));
+    M[e] = unit_edge(d, q, k) ? 1 : 0;
+  }
+}
+
+// class: 0 empty, 1 partial, 2 full (Flex semantics: padded rows/cols masked)
+__global__ void block_classify_kernel(Dims d, const uint8_t* M, int nb, uint8_t* cls) {
+  const int64_t total = (int64_t)nb * nb;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int qb = (int)(e / nb), kb = (int)(e % nb);
+    const int64_t r0 = (int64_t)qb * 128, c0 = (int64_t)kb * 128;
+    uint8_t c = 0;
+    if (r0 < d.S && c0 < d.S) {
+      const int64_t r1 = min(r0 + 128, d.S), c1 = min(c0 + 128, d.S);
+      bool any = false, all = (r1 - r0 == 128) && (c1 - c0 == 128);
+      for (int64_t i = r0; i < r1;) {
+        const Unit q = unit_of_token(d, i);
+        const int64_t qe = min(q.end, r1);
+        for (int64_t j = c0; j < c1;) {
+          const Unit k = unit_of_token(d, j);
+          const bool m = M[(int64_t)q.u * d.U + k.u] != 0;
+          any |= m;
+          all &= m;
+          j = min(k.end, c1);
+        }
+        if (inactive_local(d, q) && max(i, c0) < min(qe, c1)) any = true;
+        i = qe;
+      }
+      c = any ? (all ? 2 : 1) : 0;
+    }
+    cls[e] = c;
+  }
+}
+
+// one warp per query block: counts of partial / full blocks
+__global__ void block_count_kernel(const uint8_t* cls, int nb, int32_t* kv_num,
+                                   int32_t* full_num) {
+  const int qb = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (qb >= nb) return;
+  int np = 0, nf = 0;
+  for (int kb0 = 0; kb0 < nb; kb0 += 32) {
+    const int kb = kb0 + lane;
+    const uint8_t c = kb < nb ? cls[(int64_t)qb * nb + kb] : 0;
+    np += __popc(__ballot_sync(0xffffffffu, c == 1));
+    nf += __popc(__ballot_sync(0xffffffffu, c == 2));
+  }
+  if (lane == 0) {
+    kv_num[qb] = np;
+    full_num[qb] = nf;
+  }
+}
+
+// Exclusive scan of up to ~1e6 int32 counts by one block (used once per plan).
+__global__ void scan_kernel(const int32_t* in, int n, int32_t* out, int32_t* total) {
+  __shared__ int32_t warp_sums[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < n; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const int32_t x = i < n ? in[i] : 0;
+    int32_t v = x;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
+    }
+    if (lane == 31) warp_sums[w] = v;
+    __syncthreads();
+    if (w == 0) {
+      const int nw = blockDim.x / 32;
+      int32_t s = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t y = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += y;
+      }
+      if (lane < nw) warp_sums[lane] = s;
+    }
+    __syncthreads();
+    const int32_t prefix = carry + (w > 0 ? warp_sums[w - 1] : 0) + v - x;
+    if (i < n) out[i] = prefix;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = prefix + x;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    out[n] = carry;
+    if (total) *total = carry;
+  }
+}
+
+// one warp per query block: ascending partial / full block lists
+__global__ void block_fill_kernel(const uint8_t* cls, int nb, const int32_t* kv_off,
+                                  int32_t* kv_idx, const int32_t* full_off,
+                                  int32_t* full_idx) {
+  const int qb = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (qb >= nb) return;
+  int np = kv_off[qb], nf = full_off[qb];
+  for (int kb0 = 0; kb0 < nb; kb0 += 32) {
+    const int kb = kb0 + lane;
+    const uint8_t c = kb < nb ? cls[(int64_t)qb * nb + kb] : 0;
+    const unsigned bp = __ballot_sync(0xffffffffu, c == 1);
+    const unsigned bf = __ballot_sync(0xffffffffu, c == 2);
+    const unsigned lower = (1u << lane) - 1u;
+    if (c == 1) kv_idx[np + __popc(bp & lower)] = kb;
+    if (c == 2) full_idx[nf + __popc(bf & lower)] = kb;
+    np += __popc(bp);
+    nf += __popc(bf);
+  }
+}
+
+// one warp per query block: merged ascending key-tile list of the plan
+__global__ void plan_fill_kernel(Dims d, const uint8_t* cls, int nb, const int32_t* kv_off,
+                                 const int32_t* full_off, const int32_t* page_table,
+                                 int32_t* q_tiles, int32_t* kv_tiles) {
+  const int qb = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (qb >= nb) return;
+  const int32_t begin = kv_off[qb] + full_off[qb];
+  const int32_t n_tot = (kv_off[qb + 1] - kv_off[qb]) + (full_off[qb + 1] - full_off[qb]);
+  if (lane == 0) {
+    q_tiles[qb * 4 + 0] = qb * 128;
+    q_tiles[qb * 4 + 1] = (int32_t)min((int64_t)128, d.S - (int64_t)qb * 128);
+    q_tiles[qb * 4 + 2] = begin;
+    q_tiles[qb * 4 + 3] = begin + n_tot;
+  }
+  int pos = begin, pidx = kv_off[qb];
+  for (int kb0 = 0; kb0 < nb; kb0 += 32) {
+    const int kb = kb0 + lane;
+    const uint8_t c = kb < nb ? cls[(int64_t)qb * nb + kb] : 0;
+    const unsigned ba = __ballot_sync(0xffffffffu, c != 0);
+    const unsigned bp = __ballot_sync(0xffffffffu, c == 1);
+    const unsigned lower = (1u << lane) - 1u;
+    if (c != 0) {
+      int32_t* e = kv_tiles + (int64_t)(pos + __popc(ba & lower)) * 4;
+      int32_t r0, r1;
+      if (page_table) {
+        r0 = page_table[2 * kb] * 64;
+        r1 = page_table[2 * kb + 1] * 64;
+      } else {
+        r0 = kb * 128;
+        r1 = kb * 128 + 64;
+      }
+      e[0] = r0;
+      e[1] = r1;
+      e[2] = c == 1 ? pidx + __popc(bp & lower) : -1;
+      e[3] = (int32_t)min((int64_t)128, d.S - (int64_t)kb * 128);
+    }
+    pos += __popc(ba);
+    pidx += __popc(bp);
+  }
+}
+
+__device__ __forceinline__ void set_bits(uint32_t (&w)[4], int a, int b) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int lo = max(a, 32 * i), hi = min(b, 32 * i + 32);
+    if (lo < hi) {
+      const int n = hi - lo;
+      const uint32_t m = n == 32 ? 0xffffffffu : (((1u << n) - 1u) << (lo - 32 * i));
+      w[i] |= m;
+    }
+  }
+}
+
+// One block (128 threads) per query block; thread = query row of the block.
+// Mask index pi of a partial block equals its position in the Flex partial
+// list (kv_idx), which is also the order plan_fill_kernel assigns.
+__global__ void rowmask_kernel(Dims d, const uint8_t* M, const int32_t* kv_off,
+                               const int32_t* kv_idx, uint4* row_masks) {
+  const int qb = blockIdx.x;
+  const int r = threadIdx.x;
+  const int64_t qi = (int64_t)qb * 128 + r;
+  const Unit q = unit_of_token(d, qi);
+  const bool self = q.kind != 3 && inactive_local(d, q);
+  for (int32_t pi = kv_off[qb]; pi < kv_off[qb + 1]; ++pi) {
+    const int kb = kv_idx[pi];
+    const int64_t c0 = (int64_t)kb * 128, c1 = min(c0 + 128, d.S);
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (q.kind != 3) {
+      for (int64_t j = c0; j < c1;) {
+        const Unit k = unit_of_token(d, j);
+        const int64_t je = min(k.end, c1);
+        if (M[(int64_t)q.u * d.U + k.u]) set_bits(w, (int)(j - c0), (int)(je - c0));
+        j = je;
+      }
+      if (self && qi >= c0 && qi < c1) set_bits(w, (int)(qi - c0), (int)(qi - c0 + 1));
+    }
+    row_masks[(int64_t)pi * 128 + r] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// order[rank] = query tile, by descending key-tile count (ties: lower index first)
+__global__ void order_kernel(const int32_t* q_tiles, int n, int32_t* order) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int ci = q_tiles[i * 4 + 3] - q_tiles[i * 4 + 2];
+    int rank = 0;
+    for (int j = 0; j < n; ++j) {
+      const int cj = q_tiles[j * 4 + 3] - q_tiles[j * 4 + 2];
+      rank += (cj > ci) || (cj == ci && j < i);
+    }
+    order[rank] = i;
+  }
+}
+
+static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static int check_grouping(const hier_grouping* g) {
+  if (!g) {
+    set_error(HIER_EVALUE, "hier_grouping is NULL");
+    return HIER_EVALUE;
+  }
+  if (g->P <= 0 || g->T <= 0 || g->L <= 0 || g->N <= 0 || g->KL < 0 || g->KG < 0 ||
+      g->n_block <= 0) {
+    set_error(HIER_EVALUE, "invalid hierarchical dims P=%d T=%d L=%d N=%d K_L=%d K_G=%d n=%d",
+              g->P, g->T, g->L, g->N, g->KL, g->KG, g->n_block);
+    return HIER_EVALUE;
+  }
+  if (g->membership_mode ? (!g->membership || !g->global_only) : !g->labels) {
+    set_error(HIER_EVALUE, "grouping tensors missing for %s mode",
+              g->membership_mode ? "membership" : "labels");
+    return HIER_EVALUE;
+  }
+  if (!g->active) {
+    set_error(HIER_EVALUE, "active_group tensor missing");
+    return HIER_EVALUE;
+  }
+  const int64_t S = (int64_t)g->P * g->T * g->L + (int64_t)g->T * (g->N * g->KL + g->KG);
+  if (S > (int64_t)INT32_MAX / 2) {
+    set_error(HIER_EVALUE, "sequence too long for int32 plans: S=%lld", (long long)S);
+    return HIER_EVALUE;
+  }
+  return HIER_OK;
+}
+
+static int grid_for(int64_t n, int threads) {
+  int64_t b = (n + threads - 1) / threads;
+  if (b > 148 * 64) b = 148 * 64;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+}  // namespace hier
+
+using namespace hier;
+
+extern "C" int hier_dense_mask(const hier_grouping* g, int64_t row0, int64_t nrows, uint8_t* out,
+                               void* stream) {
+  clear_error();
+  int rc = check_grouping(g);
+  if (rc) return rc;
+  Dims d = make_dims(g);
+  if (row0 < 0 || nrows < 0 || row0 + nrows > d.S) {
+    set_error(HIER_EVALUE, "dense mask rows [%lld,%lld) outside [0,%lld)", (long long)row0,
+              (long long)(row0 + nrows), (long long)d.S);
+    return HIER_EVALUE;
+  }
+  if (nrows == 0) return HIER_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  dense_mask_kernel<<<grid_for(nrows * d.S, 256), 256, 0, s>>>(d, row0, nrows, out);
+  HIER_CHECK_CUDA(cudaGetLastError(), "dense_mask_kernel launch");
+  return HIER_OK;
+}
+
+extern "C" int hier_block_workspace_size(const hier_grouping* g, size_t* bytes) {
+  clear_error();
+  int rc = check_grouping(g);
+  if (rc) return rc;
+  Dims d = make_dims(g);
+  const int64_t nb = (d.S + 127) / 128;
+  *bytes = align256((size_t)d.U * d.U) + align256((size_t)(nb * nb));
+  return HIER_OK;
+}
+
+extern "C" int hier_block_mask_build(const hier_grouping* g, void* workspace, int32_t* kv_num,
+                                     int32_t* kv_off, int32_t* kv_idx, int32_t* full_num,
+                                     int32_t* full_off, int32_t* full_idx, int32_t* totals,
+                                     void* stream) {
+  clear_error();
+  int rc = check_grouping(g);
+  if (rc) return rc;
+  Dims d = make_dims(g);
+  const int nb = (int)((d.S + 127) / 128);
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* M = (uint8_t*)workspace;
+  uint8_t* cls = M + align256((size_t)d.U * d.U);
+  unit_matrix_kernel<<<grid_for((int64_t)d.U * d.U, 256), 256, 0, s>>>(d, M);
+  block_classify_kernel<<<grid_for((int64_t)nb * nb, 128), 128, 0, s>>>(d, M, nb, cls);
+  block_count_kernel<<<(nb + 7) / 8, 256, 0, s>>>(cls, nb, kv_num, full_num);
+  scan_kernel<<<1, 1024, 0, s>>>(kv_num, nb, kv_off, totals);
+  scan_kernel<<<1, 1024, 0, s>>>(full_num, nb, full_off, totals ? totals + 1 : nullptr);
+  block_fill_kernel<<<(nb + 7) / 8, 256, 0, s>>>(cls, nb, kv_off, kv_idx, full_off, full_idx);
+  HIER_CHECK_CUDA(cudaGetLastError(), "block mask kernels launch");
+  return HIER_OK;
+}
+
+extern "C" int hier_block_plan_build(const hier_grouping* g, const void* workspace,
+                                     const int32_t* kv_off, const int32_t* kv_idx,
+                                     const int32_t* full_off, const int32_t* full_idx,
+                                     const int32_t* page_table, int32_t* q_tiles,
+                                     int32_t* kv_tiles, uint32_t* row_masks, int32_t* order,
+                                     void* stream) {
+  clear_error();
+  int rc = check_grouping(g);
+  if (rc) return rc;
+  (void)full_idx;
+  Dims d = make_dims(g);
+  const int nb = (int)((d.S + 127) / 128);
+  cudaStream_t s = (cudaStream_t)stream;
+  const uint8_t* M = (const uint8_t*)workspace;
+  const uint8_t* cls = M + align256((size_t)d.U * d.U);
+  plan_fill_kernel<<<(nb + 7) / 8, 256, 0, s>>>(d, cls, nb, kv_off, full_off, page_table,
+                                                q_tiles, kv_tiles);
+  if (row_masks) rowmask_kernel<<<nb, 128, 0, s>>>(d, M, kv_off, kv_idx, (uint4*)row_masks);
+  if (order) order_kernel<<<grid_for(nb, 128), 128, 0, s>>>(q_tiles, nb, order);
+  HIER_CHECK_CUDA(cudaGetLastError(), "block plan kernels launch");
+  return HIER_OK;
+}
