@@ -1,0 +1,394 @@
+"""Benchmark of the B200 hierarchical group-attention layer.
+
+One step = one hierarchical attention layer forward over one batch of
+synthetic input (configuration 2 by default: 4 players x 42 latent frames x
+220 tokens, 24 heads x 128, frame-segmented causal masking): the fused
+camera + RMSNorm + RoPE prologue for Q and K, then the tcgen05 block-sparse
+attention.  The block plan is built once per grouping (the reference caches
+its block mask per grouping value as well) and reported separately.
+
+Prints one JSON line (rank 0).  Metric: useful TFLOP/s = 4*H*D*(unmasked
+query/key pairs) / time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "hier-attn useful TFLOP/s"
+UNIT = "TFLOP/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="cfg2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), \
+            float(d["hbm_gbs"]), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        loaded = [x for x in sm if mx is None or x > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def useful_pairs(bm):
+    import torch
+
+    rm = bm.row_masks[: bm.n_partial].view(torch.int32)
+    bits = 0
+    if bm.n_partial:
+        # popcount of the partial blocks' row masks
+        x = rm.view(-1).to(torch.int64) & 0xFFFFFFFF
+        for s in range(32):
+            bits += int(((x >> s) & 1).sum())
+    return bits + bm.n_full * 128 * 128
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from multics_b200.attention import attention_from_plan, device_error, freqs_table, hier_prep_qk
+    from multics_b200.hier_masks import build_stage2_hier_flex_block_mask
+    from multics_b200.synth import CONFIGS, make_inputs
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = CONFIGS[args.config]
+    inp = make_inputs(cfg, device=dev)
+    ft = freqs_table(inp.freqs)
+    stream = torch.cuda.current_stream(dev)
+
+    # block plan (once per grouping), timed separately
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    bm, S, _ = build_stage2_hier_flex_block_mask(cfg.P, cfg.T, cfg.L, cfg.N, cfg.KL, cfg.KG,
+                                                 cfg.n_block, cfg.local_attn, inp.labels, None,
+                                                 cfg.direct, dev)
+    t1.record()
+    torch.cuda.synchronize()
+    meta_ms = t0.elapsed_time(t1)
+    pairs = useful_pairs(bm)
+    useful_flops = 4.0 * cfg.H * cfg.D * pairs
+    tile_flops = bm.tile_flops(cfg.D, cfg.H)
+
+    q_buf = torch.empty(S, cfg.dim, dtype=torch.bfloat16, device=dev)
+    k_buf = torch.empty_like(q_buf)
+    o_buf = torch.empty_like(q_buf)
+
+    def step():
+        hier_prep_qk(inp.qx, inp.kx, ft, cfg.H, norm_q_weight=inp.nqw, norm_k_weight=inp.nkw,
+                     cam_tokens=inp.cam, cam_q_weight=inp.wcq, cam_k_weight=inp.wck,
+                     out=(q_buf, k_buf))
+        ev_mid.record(stream)
+        attention_from_plan(q_buf, k_buf, inp.v, bm, cfg.H, out=o_buf)
+
+    ev_mid = torch.cuda.Event(enable_timing=True)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clk:
+        time.sleep(0.3)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            ev_mid = mids[i]
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    total_ms = starts[0].elapsed_time(ends[-1])
+    attn_ms = [mids[i].elapsed_time(ends[i]) for i in range(args.steps)]
+    prep_ms = [starts[i].elapsed_time(mids[i]) for i in range(args.steps)]
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        dist.barrier()
+    err = device_error(dev)
+    ms_per_step = total_ms / args.steps
+    value = useful_flops * world / (ms_per_step * 1e-3) / 1e12
+    attn_avg = statistics.mean(attn_ms)
+
+    # end-to-end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, cfg, inp, bm, ft, dev, useful_flops, world)
+
+    peak_b, peak_s, hbm, peak_kind = load_peaks()
+    achieved = useful_flops / (attn_avg * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; shapes of the reference configs)",
+        "config": {"workload": f"{cfg.name}: hierarchical attention layer forward "
+                               f"(prologue + attention), P={cfg.P} players x T={cfg.T} frames x "
+                               f"L={cfg.L} tokens, N={cfg.N} groups, K_L={cfg.KL}, K_G={cfg.KG}, "
+                               f"H={cfg.H}x{cfg.D}, n_block={cfg.n_block}, "
+                               f"local_attn={cfg.local_attn}, direct={cfg.direct}",
+                   "S": S, "useful_pairs": pairs, "useful_gflop_per_step": useful_flops / 1e9,
+                   "tile_gflop_per_step": tile_flops / 1e9,
+                   "parallelism": f"players sharded x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (q/k/v 3 x %.0f MB)" % (S * cfg.dim * 2 / 1e6)},
+        "breakdown_ms": {"prologue": round(statistics.mean(prep_ms), 4),
+                         "attention": round(attn_avg, 4), "block_plan_once": round(meta_ms, 3)},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_b,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak_b, 4),
+                     "peak_kind": f"{peak_kind} bf16 burst", "frac_vs_sustained":
+                         round(achieved / peak_s, 4), "traffic": None,
+                     "kernel": "hier_attn_kernel",
+                     "algorithmic": "useful FLOPs = 4*H*D*unmasked pairs per launch"},
+        "gpu_launches": 2 * args.steps,
+        "device_error": err,
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    clocks = clk.summary()
+    if clocks:
+        line["clocks"] = clocks
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, sample_seconds=15.0)
+    return line
+
+
+def run_e2e(args, cfg, inp, bm, ft, dev, useful_flops, world):
+    """Same metric through the public layer API with pinned host buffers:
+    every step copies q/k/v projections + camera tokens host->device and the
+    attention output device->host inside the timed region."""
+    import torch
+
+    from multics_b200.attention import hier_attention_layer
+
+    hq = inp.qx.cpu().pin_memory()
+    hk = inp.kx.cpu().pin_memory()
+    hv = inp.v.cpu().pin_memory()
+    hc = inp.cam.cpu().pin_memory()
+    ho = torch.empty_like(hq).pin_memory()
+    dq, dk, dv, dc = (torch.empty_like(t, device=dev) for t in (hq, hk, hv, hc))
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        dc.copy_(hc, non_blocking=True)
+        o = hier_attention_layer(dq, dk, dv, ft, bm, cfg.H, norm_q_weight=inp.nqw,
+                                 norm_k_weight=inp.nkw, cam_tokens=dc, cam_q_weight=inp.wcq,
+                                 cam_k_weight=inp.wck)
+        ho.copy_(o, non_blocking=True)
+
+    steps = max(3, min(args.steps, 10))
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    bi = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hc))
+    return {"value": round(useful_flops * world / (ms * 1e-3) / 1e12, 2), "unit": UNIT,
+            "ms_per_step": round(ms, 3), "h2d_bytes_per_step": bi,
+            "d2h_bytes_per_step": ho.numel() * ho.element_size(), "steps": steps}
+
+
+class CPUPath:
+    """The reference's CPU attention path, restated by the oracle port: dense
+    hierarchical mask rows + fp32 masked-softmax attention, on prologue
+    outputs (fp32 camera add, RMSNorm over the full row, float64 RoPE) for
+    head 0.  Inputs are prepared once; :meth:`sample` times a bounded number
+    of query-row chunks, walking backwards from the last frames of player 0
+    (the rows with the most keys)."""
+
+    def __init__(self, cfg):
+        import numpy as np
+
+        from oracle import hier_oracle as O
+        from multics_b200.synth import make_inputs
+
+        self.O = O
+        self.cfg = cfg
+        inp = make_inputs(cfg, device="cpu")
+        self.labels = inp.labels.numpy()
+        f32 = lambda t: t.float().numpy()  # noqa: E731
+        freqs = np.ascontiguousarray(np.stack([inp.freqs[:, 0].real.numpy(),
+                                               inp.freqs[:, 0].imag.numpy()], -1))
+        cam = f32(inp.cam)
+        self.q = O.prologue_head(f32(inp.qx), cam, f32(inp.wcq), f32(inp.nqw), freqs, cfg.H, 0)
+        self.k = O.prologue_head(f32(inp.kx), cam, f32(inp.wck), f32(inp.nkw), freqs, cfg.H, 0)
+        self.v = np.ascontiguousarray(f32(inp.v)[:, : cfg.D])
+        self.cursor = cfg.T * cfg.L
+
+    def sample(self, seconds, rows_per_chunk=512):
+        cfg, O = self.cfg, self.O
+        pairs, elapsed = 0, 0.0
+        while elapsed < seconds:
+            if self.cursor <= 0:
+                self.cursor = cfg.T * cfg.L
+            a, r = max(0, self.cursor - rows_per_chunk), self.cursor
+            t = time.perf_counter()
+            m = O.dense_mask(cfg.P, cfg.T, cfg.L, cfg.N, cfg.KL, cfg.KG, cfg.n_block,
+                             cfg.local_attn, labels=self.labels, direct=cfg.direct,
+                             rows=slice(a, r))
+            O.masked_attention(self.q[a:r], self.k, self.v, 1, lambda x, y: m[x:y],
+                               row_chunk=rows_per_chunk)
+            elapsed += time.perf_counter() - t
+            pairs += int(m.sum())
+            self.cursor = a
+        return pairs, elapsed
+
+    def value(self, seconds):
+        pairs, elapsed = self.sample(seconds)
+        return 4.0 * self.cfg.D * pairs / elapsed / 1e12, pairs, elapsed
+
+
+def cpu_baseline(cfg, sample_seconds=15.0):
+    """cpu_baseline object of the JSON line (rank 0, N=1)."""
+    path = CPUPath(cfg)
+    v, pairs, el = path.value(sample_seconds)
+    return {"value": round(v, 6), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"oracle port (dense mask + fp32 masked attention, head 0) over {pairs} "
+                      f"unmasked pairs of the last frames of player 0 in {el:.1f} s; useful "
+                      f"FLOP/s = 4*D*pairs/time"}
+
+
+def run_reference(args, rank, world):
+    """Reference arm: the reference's CPU path (oracle port; the reference is
+    pure Python and cannot be installed on the GPU box) on host cores."""
+    from multics_b200.synth import CONFIGS
+
+    cfg = CONFIGS[args.config]
+    if rank != 0:
+        return None
+    path = CPUPath(cfg)
+    per_step = min(10.0, max(1.0, 90.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        path.value(per_step / 2)
+    t = time.perf_counter()
+    vals = [path.value(per_step)[0] for _ in range(args.steps)]
+    wall = time.perf_counter() - t
+    v = statistics.mean(vals)
+    return {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(wall * 1e3 / args.steps, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded)", "impl": "reference",
+            "config": {"workload": f"{cfg.name} (bounded CPU sample)"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{per_step:.0f} s of dense-mask fp32 attention rows per step"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    line = run_ours(args, rank, world, local_rank)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

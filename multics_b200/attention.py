@@ -157,6 +157,19 @@ def hier_block_attention(q, k, v, block_mask: HierBlockMask, num_heads, *, out=N
     return o.unsqueeze(0)
 
 
+def hier_attention_layer(qx, kx, v, freqs, block_mask: HierBlockMask, num_heads, *,
+                         norm_q_weight, norm_k_weight, cam_tokens=None, cam_q_weight=None,
+                         cam_k_weight=None, eps=1e-6, out=None):
+    """One hierarchical attention layer after the q/k/v projections: fused
+    camera + RMSNorm + RoPE prologue, then block-sparse attention.  Equivalent
+    to the reference's ``_project_self_attn_qkv`` tail + ``flash_attention(mask)``
+    (``attention.py:355-365,39-54``); returns ``[S, H*D]`` bf16."""
+    q, k = hier_prep_qk(qx, kx, freqs, num_heads, norm_q_weight=norm_q_weight,
+                        norm_k_weight=norm_k_weight, cam_tokens=cam_tokens,
+                        cam_q_weight=cam_q_weight, cam_k_weight=cam_k_weight, eps=eps)
+    return attention_from_plan(q, k, v, block_mask, num_heads, out=out)
+
+
 class RMSNorm(nn.Module):
     """``attention.py:231-242``: fp32 ``x*rsqrt(mean(x^2)+eps)`` then ``*weight``."""
 

@@ -623,6 +623,22 @@ def prologue(qx, kx, cam, wcq, wck, nqw, nkw, freqs, H, eps=1e-6):
     return one(qx, wcq, nqw), one(kx, wck, nkw)
 
 
+def prologue_head(x, cam, w_cam, w_norm, freqs, H, head, eps=1e-6):
+    """Same math as :func:`prologue` for one tensor, returning only the
+    columns of ``head`` (the RMSNorm statistic still covers the full row)."""
+    x = x.astype(np.float32)
+    if cam is not None:
+        x = x + cam.astype(np.float32) @ w_cam.astype(np.float32).T
+    r = 1.0 / np.sqrt((x * x).mean(-1, keepdims=True) + np.float32(eps))
+    S, dim = x.shape
+    D = dim // H
+    sl = slice(head * D, (head + 1) * D)
+    y = (x[:, sl] * r * w_norm[sl].astype(np.float32)).astype(np.float64).reshape(S, D // 2, 2)
+    fr, fi = freqs[..., 0], freqs[..., 1]
+    o = np.stack([y[..., 0] * fr - y[..., 1] * fi, y[..., 0] * fi + y[..., 1] * fr], -1)
+    return o.reshape(S, D).astype(np.float32)
+
+
 def masked_attention(q, k, v, H, mask_rows_fn, row_chunk=1024, heads=None):
     """fp32 ``softmax(q k^T / sqrt(D) + mask) v`` per head, as SDPA with a bool
     mask (``attention.py:47-54``).  ``mask_rows_fn(r0, r1)`` returns the bool
