@@ -91,6 +91,31 @@ int hier_block_mask_build(const hier_grouping* g, void* workspace, int32_t* kv_n
                           int32_t* full_off, int32_t* full_idx, int32_t* totals,
                           void* stream);
 
+/* Size of the fixed device scratch buffer used by
+ * hier_block_mask_build_static (bytes). */
+#define HIER_STATIC_SCRATCH_BYTES (4u << 20)
+
+/* Allocation-free variant of hier_block_mask_build.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory on the
+ * call path, such as a serving loop whose device memory is entirely
+ * pre-reserved by its own allocator, or a foreign-language binding with no
+ * device allocator from which to pass a workspace.  Same inputs and outputs
+ * as hier_block_mask_build, minus the workspace: the scratch (unit matrix and
+ * block classes, align256(U*U) + align256(nb*nb) bytes with U = P*T + T*N + T
+ * and nb = ceil(S/128)) lives in a file-scope device array of
+ * HIER_STATIC_SCRATCH_BYTES that every GPU loading the library holds until
+ * the process exits.  Larger problems are rejected with HIER_EVALUE.  Call it
+ * with the stream's device current.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) and should come before any
+ * stream capture.  Every call uses the same array: calls that overlap on the
+ * GPU (different streams, or different host threads on one device) race on
+ * it.  The kernels overwrite every scratch byte they read, so stale contents
+ * of an earlier call never reach the results.  Never allocates or frees
+ * device memory. */
+int hier_block_mask_build_static(const hier_grouping* g, int32_t* kv_num, int32_t* kv_off,
+                                 int32_t* kv_idx, int32_t* full_num, int32_t* full_off,
+                                 int32_t* full_idx, int32_t* totals, void* stream);
+
 /* Attention work plan for the full-sequence hierarchical layout, built from
  * the block classification of hier_block_mask_build (same workspace, after
  * it).  Writes, for every 128-row query tile qb:

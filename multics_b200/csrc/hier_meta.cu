@@ -518,3 +518,74 @@ extern "C" int hier_block_plan_build(const hier_grouping* g, const void* workspa
   HIER_CHECK_CUDA(cudaGetLastError(), "block plan kernels launch");
   return HIER_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free block classification: the scratch of hier_block_mask_build
+// (unit matrix + block classes) lives in a fixed file-scope device array.
+// Host code never dereferences or passes the array's name to a kernel: its
+// device address is looked up once per device with cudaGetSymbolAddress.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace hier {
+
+static __device__ __align__(256) uint8_t g_static_scratch[HIER_STATIC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+static std::mutex g_static_mu;
+static void* g_static_ptr[kMaxDevices] = {};
+
+static int static_scratch(void** out) {
+  int dev = 0;
+  HIER_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error(HIER_ERUNTIME, "device ordinal %d beyond the %d supported by the static scratch",
+              dev, kMaxDevices);
+    return HIER_ERUNTIME;
+  }
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    HIER_CHECK_CUDA(cudaGetSymbolAddress(&p, g_static_scratch),
+                    "cudaGetSymbolAddress(static scratch)");
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return HIER_OK;
+}
+
+}  // namespace hier
+
+extern "C" int hier_block_mask_build_static(const hier_grouping* g, int32_t* kv_num,
+                                            int32_t* kv_off, int32_t* kv_idx, int32_t* full_num,
+                                            int32_t* full_off, int32_t* full_idx, int32_t* totals,
+                                            void* stream) {
+  clear_error();
+  int rc = check_grouping(g);
+  if (rc) return rc;
+  Dims d = make_dims(g);
+  const int nb = (int)((d.S + 127) / 128);
+  const size_t m_bytes = align256((size_t)d.U * d.U);
+  const size_t need = m_bytes + align256((size_t)nb * nb);
+  if (need > (size_t)HIER_STATIC_SCRATCH_BYTES) {
+    set_error(HIER_EVALUE,
+              "hier_block_mask_build_static needs %zu bytes of scratch (U=%d units, %d blocks), "
+              "more than its fixed %u-byte buffer; use hier_block_mask_build with a workspace",
+              need, d.U, nb, (unsigned)HIER_STATIC_SCRATCH_BYTES);
+    return HIER_EVALUE;
+  }
+  void* scratch = nullptr;
+  rc = static_scratch(&scratch);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* M = (uint8_t*)scratch;
+  uint8_t* cls = M + m_bytes;
+  unit_matrix_kernel<<<grid_for((int64_t)d.U * d.U, 256), 256, 0, s>>>(d, M);
+  block_classify_kernel<<<grid_for((int64_t)nb * nb, 128), 128, 0, s>>>(d, M, nb, cls);
+  block_count_kernel<<<(nb + 7) / 8, 256, 0, s>>>(cls, nb, kv_num, full_num);
+  scan_kernel<<<1, 1024, 0, s>>>(kv_num, nb, kv_off, totals);
+  scan_kernel<<<1, 1024, 0, s>>>(full_num, nb, full_off, totals ? totals + 1 : nullptr);
+  block_fill_kernel<<<(nb + 7) / 8, 256, 0, s>>>(cls, nb, kv_off, kv_idx, full_off, full_idx);
+  HIER_CHECK_CUDA(cudaGetLastError(), "static block mask kernels launch");
+  return HIER_OK;
+}
