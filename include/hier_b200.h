@@ -118,23 +118,28 @@ int hier_block_mask_build_static(const hier_grouping* g, int32_t* kv_num, int32_
 
 /* Attention work plan for the full-sequence hierarchical layout, built from
  * the block classification of hier_block_mask_build (same workspace, after
- * it).  Writes, for every 128-row query tile qb:
- *   q_tiles [nb][4]   = (q_start, q_rows, kv_begin, kv_end)
- *   kv_tiles [n_partial + n_full][4] = (k_row0, k_row1, mask_idx, ncols),
- *       ascending key block order per query tile; k_row0/k_row1 are the pool
- *       rows of the two 64-key halves (page_table != NULL maps logical 64-key
- *       pages to physical pages: page p holds keys [64p, 64p+64)); mask_idx
- *       -1 marks a full block, otherwise it indexes row_masks.
+ * it).  Query blocks are paired: pair p = query blocks 2p and 2p+1 (the two
+ * halves the attention kernel computes together).  Writes
+ *   q_pairs [np][8]  = (q_start0, q_rows0, q_start1, q_rows1, kv_begin, kv_end,
+ *       0, 0), np = ceil(nb/2); a missing second block has q_rows1 = 0;
+ *   kv_tiles [<= n_partial + n_full][4] = (k_row0, k_row1, mask0, mask1):
+ *       ascending key blocks used by either half; k_row0/k_row1 are the pool
+ *       rows of the two 64-key halves of the block (page_table != NULL maps
+ *       logical 64-key pages to physical pages: page p holds keys
+ *       [64p, 64p+64)); mask_h = -1 full block for half h, -2 block not used
+ *       by half h, otherwise an index into row_masks;
  *   row_masks [n_partial][128][4] uint32 = per-row key bitmask of each partial
- *       block (bit c of word c/32 set <=> key c of the block is visible).
- *   order [nb] = query tiles sorted by descending number of key tiles.
+ *       block, in the order of the Flex partial list (bit c of word c/32 set
+ *       <=> key c of the block is visible);
+ *   order [np] = pairs sorted by descending number of key tiles;
+ *   n_kv_tiles (device int32) = number of kv_tiles entries written.
  * The full-sequence layout is the reference's dense/Flex mask semantics
  * (hier_masks.py:364-1149), so inactive local-hub rows keep their self edge. */
-int hier_block_plan_build(const hier_grouping* g, const void* workspace, const int32_t* kv_off,
+int hier_block_plan_build(const hier_grouping* g, void* workspace, const int32_t* kv_off,
                           const int32_t* kv_idx, const int32_t* full_off,
                           const int32_t* full_idx, const int32_t* page_table,
-                          int32_t* q_tiles, int32_t* kv_tiles, uint32_t* row_masks,
-                          int32_t* order, void* stream);
+                          int32_t* q_pairs, int32_t* kv_tiles, uint32_t* row_masks,
+                          int32_t* order, int32_t* n_kv_tiles, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Fused Q/K prologue
@@ -163,9 +168,11 @@ int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, const void* c
  *   q   bf16 [q_rows_total, H*D] (row stride q_stride elements)
  *   k,v bf16 [kv_rows_total, H*D] key/value pool (row stride kv_stride)
  *   out bf16 [q_rows_total, H*D] (row stride out_stride); only rows covered
- *       by q_tiles are written; rows whose key set is empty are written as 0
+ *       by q_pairs are written; rows whose key set is empty are written as 0
  *       (the cached backends' contract, hier_segmented_attention.py:104-109).
- *   q_tiles/kv_tiles/row_masks/order as produced by the plan builders.
+ *   q_pairs [n_pairs][8], kv_tiles [][4], row_masks, order [n_pairs] (or
+ *       NULL) in the format of hier_block_plan_build: each CTA computes the
+ *       two 128-row query tiles of a pair for one head.
  *   dev_err: device int32, set non-zero if a pipeline wait timed out.
  * Replaces the attention kernels of the reference backends: masked SDPA
  * (attention.py:39-54), FlexAttention (attention.py:322-353), the Triton
@@ -175,8 +182,8 @@ int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, const void* c
  * (kernels/hier_paged_attention.py:238-266). */
 int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stride, const void* k,
                   const void* v, int64_t kv_rows_total, int64_t kv_stride, void* out,
-                  int64_t out_stride, int32_t H, int32_t D, const int32_t* q_tiles,
-                  int32_t n_q_tiles, const int32_t* kv_tiles, const uint32_t* row_masks,
+                  int64_t out_stride, int32_t H, int32_t D, const int32_t* q_pairs,
+                  int32_t n_pairs, const int32_t* kv_tiles, const uint32_t* row_masks,
                   const int32_t* order, float softmax_scale, int32_t* dev_err, void* stream);
 
 /* ---------------------------------------------------------------------------
@@ -188,6 +195,11 @@ int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stride, const v
  * as fp32 [128,128]. */
 int hier_selftest_umma(const void* a, const void* b, float* c_ss, float* c_mn, float* c_ts,
                        int32_t* dev_err, void* stream);
+
+/* Self-test of the FMA-pipe exp2 used for part of the softmax exponentials
+ * (no reference counterpart): y[i] = 2^x[i] for n fp32 values, 0 for
+ * x <= -127. */
+int hier_selftest_exp2(const float* x, float* y, int64_t n, void* stream);
 
 #ifdef __cplusplus
 }

@@ -40,7 +40,7 @@ _SIGS = {
     "hier_block_workspace_size": (c_int, [ctypes.POINTER(HierGrouping), ctypes.POINTER(c_size_t)]),
     "hier_block_mask_build": (c_int, [ctypes.POINTER(HierGrouping), _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "hier_block_plan_build": (c_int, [ctypes.POINTER(HierGrouping), _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                      _P, _P]),
+                                      _P, _P, _P]),
     "hier_block_mask_build_static": (c_int, [ctypes.POINTER(HierGrouping), _P, _P, _P, _P, _P, _P, _P,
                                              _P]),
     "hier_prep_qk": (c_int, [_P, _P, c_int64, _P, c_int32, _P, _P, _P, _P, _P, c_int64, c_int32,
@@ -48,6 +48,7 @@ _SIGS = {
     "hier_attn_fwd": (c_int, [_P, c_int64, c_int64, _P, _P, c_int64, c_int64, _P, c_int64, c_int32,
                               c_int32, _P, c_int32, _P, _P, _P, c_float, _P, _P]),
     "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),
+    "hier_selftest_exp2": (c_int, [_P, _P, c_int64, _P]),
 }
 
 _LIB = None

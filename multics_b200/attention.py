@@ -112,14 +112,15 @@ def hier_prep_qk(qx, kx, freqs, num_heads, *, norm_q_weight, norm_k_weight, cam_
 
 
 class AttentionPlan:
-    """Generic attention work plan: query tiles, key tiles, row bitmasks.
+    """Generic attention work plan: query pairs, key tiles, row bitmasks.
 
-    ``q_tiles`` int32 ``[n,4]`` = (q_start, q_rows, kv_begin, kv_end);
-    ``kv_tiles`` int32 ``[m,4]`` = (k_row0, k_row1, mask_idx, ncols);
+    ``q_pairs`` int32 ``[n,8]`` = (q_start0, q_rows0, q_start1, q_rows1,
+    kv_begin, kv_end, 0, 0); ``kv_tiles`` int32 ``[m,4]`` = (k_row0, k_row1,
+    mask0, mask1) with mask -1 full, -2 skip, else a row-mask index;
     ``row_masks`` int32 ``[k,128,4]``; ``order`` int32 ``[n]`` (or None)."""
 
-    def __init__(self, q_tiles, kv_tiles, row_masks, order=None):
-        self.q_tiles = q_tiles
+    def __init__(self, q_pairs, kv_tiles, row_masks, order=None):
+        self.q_pairs = q_pairs
         self.kv_tiles = kv_tiles
         self.row_masks = row_masks
         self.order = order
@@ -141,11 +142,11 @@ def attention_from_plan(q, k, v, plan, num_heads, *, out=None, softmax_scale=Non
     if out is None:
         out = torch.empty(S, dim, dtype=torch.bfloat16, device=q2.device)
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
-    n_qt = plan.q_tiles.shape[0]
+    n_pairs = plan.q_pairs.shape[0]
     check(_lib.lib().hier_attn_fwd(
         ptr(q2), S if q_rows_total is None else q_rows_total, q2.stride(0), ptr(k2), ptr(v2),
-        k2.shape[0], k2.stride(0), ptr(out), out.stride(0), num_heads, D, ptr(plan.q_tiles),
-        n_qt, ptr(plan.kv_tiles), ptr(plan.row_masks), ptr(plan.order), scale,
+        k2.shape[0], k2.stride(0), ptr(out), out.stride(0), num_heads, D, ptr(plan.q_pairs),
+        n_pairs, ptr(plan.kv_tiles), ptr(plan.row_masks), ptr(plan.order), scale,
         ptr(_dev_err(q2.device)), stream_ptr(q2.device)))
     return out
 

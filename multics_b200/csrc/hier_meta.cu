@@ -311,45 +311,72 @@ __global__ void block_fill_kernel(const uint8_t* cls, int nb, const int32_t* kv_
   }
 }
 
-// one warp per query block: merged ascending key-tile list of the plan
-__global__ void plan_fill_kernel(Dims d, const uint8_t* cls, int nb, const int32_t* kv_off,
-                                 const int32_t* full_off, const int32_t* page_table,
-                                 int32_t* q_tiles, int32_t* kv_tiles) {
-  const int qb = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+// Query pairs: pair p holds query blocks 2p and 2p+1 (the attention kernel's
+// two halves).  A key block is listed for the pair when either half sees it.
+__device__ __forceinline__ uint8_t cls_at(const uint8_t* cls, int nb, int qb, int kb) {
+  return (qb < nb && kb < nb) ? cls[(int64_t)qb * nb + kb] : 0;
+}
+
+// one warp per query pair: number of key blocks used by either half
+__global__ void pair_count_kernel(const uint8_t* cls, int nb, int np, int32_t* cnt) {
+  const int p = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  if (qb >= nb) return;
-  const int32_t begin = kv_off[qb] + full_off[qb];
-  const int32_t n_tot = (kv_off[qb + 1] - kv_off[qb]) + (full_off[qb + 1] - full_off[qb]);
-  if (lane == 0) {
-    q_tiles[qb * 4 + 0] = qb * 128;
-    q_tiles[qb * 4 + 1] = (int32_t)min((int64_t)128, d.S - (int64_t)qb * 128);
-    q_tiles[qb * 4 + 2] = begin;
-    q_tiles[qb * 4 + 3] = begin + n_tot;
-  }
-  int pos = begin, pidx = kv_off[qb];
+  if (p >= np) return;
+  int n = 0;
   for (int kb0 = 0; kb0 < nb; kb0 += 32) {
     const int kb = kb0 + lane;
-    const uint8_t c = kb < nb ? cls[(int64_t)qb * nb + kb] : 0;
-    const unsigned ba = __ballot_sync(0xffffffffu, c != 0);
-    const unsigned bp = __ballot_sync(0xffffffffu, c == 1);
+    const bool any = (cls_at(cls, nb, 2 * p, kb) | cls_at(cls, nb, 2 * p + 1, kb)) != 0;
+    n += __popc(__ballot_sync(0xffffffffu, any));
+  }
+  if (lane == 0) cnt[p] = n;
+}
+
+// one warp per query pair: the pair record and its ascending key-tile list
+// (pool rows of the two 64-key halves, per-half mask selector: -1 full,
+// -2 skip, otherwise the Flex partial-list index of that half's block)
+__global__ void pair_plan_fill_kernel(Dims d, const uint8_t* cls, int nb, int np,
+                                      const int32_t* kv_off, const int32_t* pair_off,
+                                      const int32_t* page_table, int32_t* pairs,
+                                      int32_t* kv_tiles) {
+  const int p = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (p >= np) return;
+  const int qb0 = 2 * p, qb1 = 2 * p + 1;
+  if (lane == 0) {
+    int32_t* rec = pairs + (int64_t)p * 8;
+    rec[0] = qb0 * 128;
+    rec[1] = (int32_t)min((int64_t)128, d.S - (int64_t)qb0 * 128);
+    rec[2] = qb1 < nb ? qb1 * 128 : qb0 * 128;
+    rec[3] = qb1 < nb ? (int32_t)min((int64_t)128, d.S - (int64_t)qb1 * 128) : 0;
+    rec[4] = pair_off[p];
+    rec[5] = pair_off[p + 1];
+    rec[6] = 0;
+    rec[7] = 0;
+  }
+  int pos = pair_off[p];
+  int p0 = kv_off[qb0], p1 = qb1 < nb ? kv_off[qb1] : 0;
+  for (int kb0 = 0; kb0 < nb; kb0 += 32) {
+    const int kb = kb0 + lane;
+    const uint8_t c0 = cls_at(cls, nb, qb0, kb), c1 = cls_at(cls, nb, qb1, kb);
+    const unsigned ba = __ballot_sync(0xffffffffu, (c0 | c1) != 0);
+    const unsigned b0 = __ballot_sync(0xffffffffu, c0 == 1);
+    const unsigned b1 = __ballot_sync(0xffffffffu, c1 == 1);
     const unsigned lower = (1u << lane) - 1u;
-    if (c != 0) {
+    if ((c0 | c1) != 0) {
       int32_t* e = kv_tiles + (int64_t)(pos + __popc(ba & lower)) * 4;
-      int32_t r0, r1;
       if (page_table) {
-        r0 = page_table[2 * kb] * 64;
-        r1 = page_table[2 * kb + 1] * 64;
+        e[0] = page_table[2 * kb] * 64;
+        e[1] = page_table[2 * kb + 1] * 64;
       } else {
-        r0 = kb * 128;
-        r1 = kb * 128 + 64;
+        e[0] = kb * 128;
+        e[1] = kb * 128 + 64;
       }
-      e[0] = r0;
-      e[1] = r1;
-      e[2] = c == 1 ? pidx + __popc(bp & lower) : -1;
-      e[3] = (int32_t)min((int64_t)128, d.S - (int64_t)kb * 128);
+      e[2] = c0 == 2 ? -1 : (c0 == 1 ? p0 + __popc(b0 & lower) : -2);
+      e[3] = c1 == 2 ? -1 : (c1 == 1 ? p1 + __popc(b1 & lower) : -2);
     }
     pos += __popc(ba);
-    pidx += __popc(bp);
+    p0 += __popc(b0);
+    p1 += __popc(b1);
   }
 }
 
@@ -392,13 +419,14 @@ __global__ void rowmask_kernel(Dims d, const uint8_t* M, const int32_t* kv_off,
   }
 }
 
-// order[rank] = query tile, by descending key-tile count (ties: lower index first)
-__global__ void order_kernel(const int32_t* q_tiles, int n, int32_t* order) {
+// order[rank] = work item, by descending key-tile count (ties: lower index
+// first); item i's count is rec[i*stride + 5] - rec[i*stride + 4].
+__global__ void order_kernel(const int32_t* rec, int stride, int n, int32_t* order) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int ci = q_tiles[i * 4 + 3] - q_tiles[i * 4 + 2];
+    const int ci = rec[i * stride + 5] - rec[i * stride + 4];
     int rank = 0;
     for (int j = 0; j < n; ++j) {
-      const int cj = q_tiles[j * 4 + 3] - q_tiles[j * 4 + 2];
+      const int cj = rec[j * stride + 5] - rec[j * stride + 4];
       rank += (cj > ci) || (cj == ci && j < i);
     }
     order[rank] = i;
@@ -470,7 +498,9 @@ extern "C" int hier_block_workspace_size(const hier_grouping* g, size_t* bytes) 
   if (rc) return rc;
   Dims d = make_dims(g);
   const int64_t nb = (d.S + 127) / 128;
-  *bytes = align256((size_t)d.U * d.U) + align256((size_t)(nb * nb));
+  const int64_t np = (nb + 1) / 2;
+  *bytes = align256((size_t)d.U * d.U) + align256((size_t)(nb * nb)) +
+           2 * align256((size_t)(np + 1) * sizeof(int32_t));
   return HIER_OK;
 }
 
@@ -496,25 +526,31 @@ extern "C" int hier_block_mask_build(const hier_grouping* g, void* workspace, in
   return HIER_OK;
 }
 
-extern "C" int hier_block_plan_build(const hier_grouping* g, const void* workspace,
+extern "C" int hier_block_plan_build(const hier_grouping* g, void* workspace,
                                      const int32_t* kv_off, const int32_t* kv_idx,
                                      const int32_t* full_off, const int32_t* full_idx,
-                                     const int32_t* page_table, int32_t* q_tiles,
+                                     const int32_t* page_table, int32_t* q_pairs,
                                      int32_t* kv_tiles, uint32_t* row_masks, int32_t* order,
-                                     void* stream) {
+                                     int32_t* n_kv_tiles, void* stream) {
   clear_error();
   int rc = check_grouping(g);
   if (rc) return rc;
+  (void)full_off;
   (void)full_idx;
   Dims d = make_dims(g);
   const int nb = (int)((d.S + 127) / 128);
+  const int np = (nb + 1) / 2;
   cudaStream_t s = (cudaStream_t)stream;
-  const uint8_t* M = (const uint8_t*)workspace;
-  const uint8_t* cls = M + align256((size_t)d.U * d.U);
-  plan_fill_kernel<<<(nb + 7) / 8, 256, 0, s>>>(d, cls, nb, kv_off, full_off, page_table,
-                                                q_tiles, kv_tiles);
+  uint8_t* M = (uint8_t*)workspace;
+  uint8_t* cls = M + align256((size_t)d.U * d.U);
+  int32_t* pair_cnt = (int32_t*)(cls + align256((size_t)nb * nb));
+  int32_t* pair_off = (int32_t*)((uint8_t*)pair_cnt + align256((size_t)(np + 1) * sizeof(int32_t)));
+  pair_count_kernel<<<(np + 7) / 8, 256, 0, s>>>(cls, nb, np, pair_cnt);
+  scan_kernel<<<1, 1024, 0, s>>>(pair_cnt, np, pair_off, n_kv_tiles);
+  pair_plan_fill_kernel<<<(np + 7) / 8, 256, 0, s>>>(d, cls, nb, np, kv_off, pair_off, page_table,
+                                                     q_pairs, kv_tiles);
   if (row_masks) rowmask_kernel<<<nb, 128, 0, s>>>(d, M, kv_off, kv_idx, (uint4*)row_masks);
-  if (order) order_kernel<<<grid_for(nb, 128), 128, 0, s>>>(q_tiles, nb, order);
+  if (order) order_kernel<<<grid_for(np, 128), 128, 0, s>>>(q_pairs, 8, np, order);
   HIER_CHECK_CUDA(cudaGetLastError(), "block plan kernels launch");
   return HIER_OK;
 }

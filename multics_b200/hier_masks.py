@@ -293,7 +293,7 @@ class HierBlockMask:
 
     ``kv_num_blocks / kv_indices / full_kv_num_blocks / full_kv_indices`` have
     the shapes of the Flex BlockMask fields (``[1,1,nb]`` / ``[1,1,nb,nb]``)
-    with the same values in each row's valid prefix.  ``q_tiles``,
+    with the same values in each row's valid prefix.  ``q_pairs``,
     ``kv_tiles``, ``row_masks`` and ``order`` are the attention work plan
     (see include/hier_b200.h, hier_block_plan_build)."""
 
@@ -307,12 +307,13 @@ class HierBlockMask:
     full_offsets: torch.Tensor
     kv_flat: torch.Tensor
     full_flat: torch.Tensor
-    q_tiles: torch.Tensor
+    q_pairs: torch.Tensor
     kv_tiles: torch.Tensor
     row_masks: torch.Tensor
     order: torch.Tensor
     n_partial: int
     n_full: int
+    n_kv_tiles: torch.Tensor
     spec: HierGroupingSpec
 
     @property
@@ -320,8 +321,8 @@ class HierBlockMask:
         return (1, 1, self.S_pad, self.S_pad)
 
     @property
-    def num_q_tiles(self) -> int:
-        return self.q_tiles.shape[0]
+    def num_pairs(self) -> int:
+        return self.q_pairs.shape[0]
 
     def tile_flops(self, head_dim: int, heads: int) -> float:
         """FLOPs of all computed 128x128 tiles (full + partial), 4*128*128*D each."""
@@ -353,10 +354,12 @@ def build_block_plan(spec: HierGroupingSpec, page_table: Optional[torch.Tensor] 
     check(L.hier_block_mask_build(ctypes.byref(g), ptr(ws), ptr(kv_num), ptr(kv_off), ptr(kv_flat),
                                   ptr(full_num), ptr(full_off), ptr(full_flat), ptr(totals), s))
     n_partial, n_full = (int(x) for x in totals.tolist())
-    q_tiles = torch.empty(nb, 4, **i32)
+    n_pairs = (nb + 1) // 2
+    q_pairs = torch.empty(n_pairs, 8, **i32)
     kv_tiles = torch.empty(max(n_partial + n_full, 1), 4, **i32)
     row_masks = torch.empty(max(n_partial, 1), 128, 4, **i32)
-    order = torch.empty(nb, **i32)
+    order = torch.empty(n_pairs, **i32)
+    n_kv_tiles = torch.zeros(1, **i32)
     if page_table is not None:
         pt = page_table.to(device=dev, dtype=torch.int32).contiguous()
         need = 2 * nb
@@ -365,8 +368,8 @@ def build_block_plan(spec: HierGroupingSpec, page_table: Optional[torch.Tensor] 
     else:
         pt = None
     check(L.hier_block_plan_build(ctypes.byref(g), ptr(ws), ptr(kv_off), ptr(kv_flat),
-                                  ptr(full_off), ptr(full_flat), ptr(pt), ptr(q_tiles),
-                                  ptr(kv_tiles), ptr(row_masks), ptr(order), s))
+                                  ptr(full_off), ptr(full_flat), ptr(pt), ptr(q_pairs),
+                                  ptr(kv_tiles), ptr(row_masks), ptr(order), ptr(n_kv_tiles), s))
     kv_flat = kv_flat[:n_partial]
     full_flat = full_flat[:n_full]
 
@@ -383,9 +386,9 @@ def build_block_plan(spec: HierGroupingSpec, page_table: Optional[torch.Tensor] 
         S=S, S_pad=nb * 128, kv_num_blocks=kv_num.view(1, 1, nb),
         kv_indices=padded(kv_flat, kv_off, kv_num), full_kv_num_blocks=full_num.view(1, 1, nb),
         full_kv_indices=padded(full_flat, full_off, full_num), kv_offsets=kv_off,
-        full_offsets=full_off, kv_flat=kv_flat, full_flat=full_flat, q_tiles=q_tiles,
+        full_offsets=full_off, kv_flat=kv_flat, full_flat=full_flat, q_pairs=q_pairs,
         kv_tiles=kv_tiles, row_masks=row_masks, order=order, n_partial=n_partial,
-        n_full=n_full, spec=spec)
+        n_full=n_full, n_kv_tiles=n_kv_tiles, spec=spec)
 
 
 def _cache_size():

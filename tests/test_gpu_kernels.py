@@ -62,6 +62,28 @@ def test_umma_operand_selftest(dev):
     torch.testing.assert_close(outs[2], af @ bf, atol=1e-2, rtol=1e-3)
 
 
+def test_poly_exp2_matches_exp2f(dev):
+    """The FMA-pipe exp2 used for part of the softmax vs CUDA exp2f (torch.exp2)
+    and a float64 reference: relative error < 1e-4, exactly 0 at and below -127
+    (masked keys)."""
+    from multics_b200 import _lib
+    from multics_b200._lib import ptr, stream_ptr
+
+    x = torch.cat([torch.linspace(-126.0, 12.0, 1 << 20), torch.rand(1 << 16) * 2 - 1,
+                   torch.tensor([-127.0, -130.0, -1e30, float("-inf"), 0.0, 1.0, -0.5, 0.5])])
+    x = x.to(dev)
+    y = torch.empty_like(x)
+    _lib.check(_lib.lib().hier_selftest_exp2(ptr(x), ptr(y), x.numel(), stream_ptr()))
+    torch.cuda.synchronize()
+    fin = x > -126.5
+    ref64 = torch.exp2(x.double())
+    rel = ((y.double() - ref64) / ref64)[fin].abs().max().item()
+    assert rel < 1e-4, rel
+    rel_f = ((y - torch.exp2(x)) / torch.exp2(x))[fin].abs().max().item()
+    assert rel_f < 1e-4, rel_f
+    assert torch.all(y[x <= -127.0] == 0)
+
+
 @pytest.mark.parametrize("name", case_names("mask"))
 def test_dense_mask_bit_exact(dev, name):
     from multics_b200.hier_masks import build_stage2_hier_self_attn_mask
@@ -86,22 +108,26 @@ def test_block_mask_lists_bit_exact(dev, name):
 
 
 def expand_plan(bm):
-    """Dense [S,S] mask implied by an attention plan (q tiles, key tiles, bitmasks)."""
+    """Dense [S,S] mask implied by an attention plan (query pairs, key tiles,
+    per-half mask selectors, row bitmasks)."""
     S = bm.S
-    qt = bm.q_tiles.cpu().numpy()
+    qp = bm.q_pairs.cpu().numpy()
     kv = bm.kv_tiles.cpu().numpy()
     rm = bm.row_masks.cpu().numpy().view(np.uint32)
     dense = np.zeros((S, S + 256), bool)
-    for q0, qn, b, e in qt:
+    for q0, qn0, q1, qn1, b, e, _, _ in qp:
         for j in range(b, e):
-            k0, _, mi, nc = kv[j]
-            if mi < 0:
-                bits = np.ones((128, 128), bool)
-            else:
-                w = rm[mi]
-                bits = ((w[:, np.arange(128) // 32] >> (np.arange(128) % 32)) & 1).astype(bool)
-            bits[:, nc:] = False
-            dense[q0:q0 + qn, k0:k0 + 128] |= bits[:qn]
+            k0, k1, m0, m1 = kv[j]
+            for qs, qn, mi in ((q0, qn0, m0), (q1, qn1, m1)):
+                if mi == -2 or qn == 0:
+                    continue
+                if mi == -1:
+                    bits = np.ones((128, 128), bool)
+                else:
+                    w = rm[mi]
+                    bits = ((w[:, np.arange(128) // 32] >> (np.arange(128) % 32)) & 1).astype(bool)
+                dense[qs:qs + qn, k0:k0 + 64] |= bits[:qn, :64]
+                dense[qs:qs + qn, k1:k1 + 64] |= bits[:qn, 64:]
     return dense[:, :S]
 
 
@@ -114,7 +140,8 @@ def test_plan_row_masks_reproduce_dense_mask(dev, name):
     bm, _, _ = build_stage2_hier_flex_block_mask(*_dims(c), **_mask_args(c, dev))
     assert np.array_equal(expand_plan(bm), c["dense"])
     order = bm.order.cpu().numpy()
-    assert sorted(order.tolist()) == list(range(bm.num_q_tiles))
+    assert sorted(order.tolist()) == list(range(bm.num_pairs))
+    assert int(bm.n_kv_tiles.item()) == int(bm.q_pairs[:, 5].max().item())
 
 
 def _cos(a, b):
