@@ -186,6 +186,113 @@ int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stride, const v
                   int32_t n_pairs, const int32_t* kv_tiles, const uint32_t* row_masks,
                   const int32_t* order, float softmax_scale, int32_t* dev_err, void* stream);
 
+/* Maximum number of key/value tensors (streams) one attention launch reads. */
+#define HIER_MAX_KV_STREAMS 32
+
+/* hier_attn_fwd over keys/values held in several tensors ("streams", e.g. one
+ * rolling cache per player, per local-hub group and the global hub), read in
+ * place: no pool concatenation (the reference copies every cache into one
+ * pool per call, hier_segmented_attention.py:484-495,
+ * hier_paged_attention.py:182-191).  Stream s is k[s], v[s]: bf16
+ * [stream_rows[s], H*D] with row stride kv_stride[s] elements (device
+ * pointers in a host array).  A key-box row of kv_tiles is
+ * (s << 24) | row-within-stream.  tile_masks holds mask_rows entries of four
+ * uint32 per partial tile: 128 (one key bitmask per query row, the format of
+ * hier_block_plan_build) or 1 (one key bitmask shared by every query row, the
+ * format of hier_cached_build).  Other arguments as hier_attn_fwd. */
+int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_t q_stride,
+                          int32_t n_streams, const void* const* k, const void* const* v,
+                          const int64_t* stream_rows, const int64_t* kv_stride, void* out,
+                          int64_t out_stride, int32_t H, int32_t D, const int32_t* q_pairs,
+                          int32_t n_pairs, const int32_t* kv_tiles, const uint32_t* tile_masks,
+                          int32_t mask_rows, const int32_t* order, float softmax_scale,
+                          int32_t* dev_err, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Cached (rolling key/value cache) step
+ * ------------------------------------------------------------------------- */
+
+/* One cached step: the query block of n_frames new frames (player rows,
+ * then local-hub rows, then global-hub rows, as causal_forward_hier_hub
+ * orders them, multics/models/attention.py:456-1005) against the retained
+ * frames of every cache.  Mirrors the arguments of _build_metadata
+ * (multics/models/kernels/hier_segmented_attention.py:156-395) with the
+ * per-token tensors of the cached-backend plugin signature
+ * (hier_paged_attention.py:79-106) instead of host tuples.  Device pointers:
+ *   agent_frames[p]  int64 [fa*L]   frame id of every cached token of player p
+ *   local_frames[g]  int64 [fl*KL]  (no_local: unused, fl = 0, K_L = 0)
+ *   local_active[g]  uint8 [fl*KL]  token activity of local-hub caches
+ *   global_frames    int64 [fg*KG]
+ *   labels           int64 [n_frames, P]   (membership_mode == 0)
+ *   q_active         uint8 [n_frames, N]
+ *   membership       uint8 [T_mem, N, P]   (membership_mode == 1), indexed by
+ *   global_only      uint8 [T_mem, P]       absolute frame id */
+typedef struct hier_cached_grouping {
+  int32_t P, N, L, KL, KG;
+  int32_t n_frames, n_block, local_attn, direct, no_local, membership_mode;
+  int32_t fa, fl, fg; /* retained frames per agent / local / global cache */
+  int32_t T_mem;
+  const int64_t* agent_frames[HIER_MAX_KV_STREAMS];
+  const int64_t* local_frames[HIER_MAX_KV_STREAMS];
+  const uint8_t* local_active[HIER_MAX_KV_STREAMS];
+  const int64_t* global_frames;
+  const int64_t* labels;
+  const uint8_t* q_active;
+  const uint8_t* membership;
+  const uint8_t* global_only;
+} hier_cached_grouping;
+
+typedef struct hier_cached_sizes_t {
+  int32_t n_seg;         /* segments: P*n + N*n (unless no_local) + n */
+  int32_t n_prog;        /* block_m programs */
+  int32_t n_pairs;       /* attention query pairs */
+  int32_t n_streams;     /* key/value streams: P agents, N local (unless no_local), global */
+  int32_t n_cand;        /* candidate runs per segment */
+  int32_t tile_capacity; /* upper bound of attention key tiles */
+  int64_t q_rows;        /* query rows of the step */
+  int64_t pool_rows;     /* rows of the reference's concatenated pool */
+} hier_cached_sizes_t;
+
+/* Host-only sizes of a cached step (validates the grouping with the
+ * reference's messages). */
+int hier_cached_sizes(const hier_cached_grouping* g, int32_t block_m, hier_cached_sizes_t* out);
+
+/* Per segment: number of keys (kv_count, as _build_metadata) and of 64-row
+ * key boxes of the attention plan.  status (device int32, may be NULL) gets
+ * bit 0 set if a membership / global_only frame is out of range. */
+int hier_cached_count(const hier_cached_grouping* g, int32_t* kv_count, int32_t* n_boxes,
+                      int32_t* status, void* stream);
+
+/* Fill the outputs of a cached step; any group may be NULL to skip it.
+ *   prog_qbase/prog_nq/prog_seg [n_prog]: block_m programs (bit-exact);
+ *   kv_index [n_seg, kv_width] int32, zero padded (bit-exact for
+ *       kv_width = ceil64(max kv_count), as _build_metadata);
+ *   q_pairs [n_pairs][8], kv_tiles [tile_capacity][4], tile_masks
+ *       [tile_capacity][4] (mask_rows = 1), order [n_pairs]: the attention
+ *       plan for hier_attn_fwd_streams, needs n_boxes from hier_cached_count.
+ * status bit 1 is set if the plan exceeds tile_capacity.  No host sync. */
+int hier_cached_build(const hier_cached_grouping* g, int32_t block_m, const int32_t* n_boxes,
+                      int32_t* prog_qbase, int32_t* prog_nq, int32_t* prog_seg,
+                      int32_t* kv_index, int32_t kv_width, int32_t* q_pairs, int32_t* kv_tiles,
+                      uint32_t* tile_masks, int32_t tile_capacity, int32_t* order,
+                      int32_t* status, void* stream);
+
+/* Workspace bytes for hier_varlen_plan_build. */
+int hier_varlen_workspace_size(int32_t n_seg, size_t* bytes);
+
+/* Packed varlen plan of _get_varlen_plan (hier_packed_attention.py:32-102)
+ * from one-program-per-segment metadata: over the segments with rows and
+ * keys, q_index (int64 [sum q]) = their query rows, k_index (int64 [sum k]) =
+ * their kv_index rows, cu_q / cu_k (int32 [active+1]); page_indices (int32
+ * [sum k], may be NULL) = k_index as the page table of page size 1
+ * (hier_paged_attention.py:232-249); scalars (int64 [5]) = max_q, max_k,
+ * min_k_index, max_k_index, number of active segments. */
+int hier_varlen_plan_build(const int32_t* prog_qbase, const int32_t* prog_nq,
+                           const int32_t* kv_index, int32_t kv_width, const int32_t* kv_count,
+                           int32_t n_seg, void* workspace, int64_t* q_index, int64_t* k_index,
+                           int32_t* cu_q, int32_t* cu_k, int32_t* page_indices, int64_t* scalars,
+                           void* stream);
+
 /* ---------------------------------------------------------------------------
  * Self-test of the tensor-core operand encodings (no reference counterpart):
  * with A, B bf16 [128,128] row-major,

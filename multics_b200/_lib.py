@@ -31,6 +31,35 @@ class HierGrouping(ctypes.Structure):
     ]
 
 
+MAX_KV_STREAMS = 32
+
+
+class HierCachedGrouping(ctypes.Structure):
+    """Mirror of ``struct hier_cached_grouping`` in include/hier_b200.h."""
+
+    _fields_ = [
+        ("P", c_int32), ("N", c_int32), ("L", c_int32), ("KL", c_int32), ("KG", c_int32),
+        ("n_frames", c_int32), ("n_block", c_int32), ("local_attn", c_int32),
+        ("direct", c_int32), ("no_local", c_int32), ("membership_mode", c_int32),
+        ("fa", c_int32), ("fl", c_int32), ("fg", c_int32), ("T_mem", c_int32),
+        ("agent_frames", c_void_p * MAX_KV_STREAMS),
+        ("local_frames", c_void_p * MAX_KV_STREAMS),
+        ("local_active", c_void_p * MAX_KV_STREAMS),
+        ("global_frames", c_void_p), ("labels", c_void_p), ("q_active", c_void_p),
+        ("membership", c_void_p), ("global_only", c_void_p),
+    ]
+
+
+class HierCachedSizes(ctypes.Structure):
+    """Mirror of ``hier_cached_sizes_t``."""
+
+    _fields_ = [
+        ("n_seg", c_int32), ("n_prog", c_int32), ("n_pairs", c_int32), ("n_streams", c_int32),
+        ("n_cand", c_int32), ("tile_capacity", c_int32), ("q_rows", c_int64),
+        ("pool_rows", c_int64),
+    ]
+
+
 _P = c_void_p
 _SIGS = {
     "hier_last_error": (c_char_p, []),
@@ -47,6 +76,17 @@ _SIGS = {
                              c_int32, c_float, _P, _P, c_int64, _P]),
     "hier_attn_fwd": (c_int, [_P, c_int64, c_int64, _P, _P, c_int64, c_int64, _P, c_int64, c_int32,
                               c_int32, _P, c_int32, _P, _P, _P, c_float, _P, _P]),
+    "hier_attn_fwd_streams": (c_int, [_P, c_int64, c_int64, c_int32, _P, _P, _P, _P, _P, c_int64,
+                                      c_int32, c_int32, _P, c_int32, _P, _P, c_int32, _P,
+                                      c_float, _P, _P]),
+    "hier_cached_sizes": (c_int, [ctypes.POINTER(HierCachedGrouping), c_int32,
+                                  ctypes.POINTER(HierCachedSizes)]),
+    "hier_cached_count": (c_int, [ctypes.POINTER(HierCachedGrouping), _P, _P, _P, _P]),
+    "hier_cached_build": (c_int, [ctypes.POINTER(HierCachedGrouping), c_int32, _P, _P, _P, _P, _P,
+                                  c_int32, _P, _P, _P, c_int32, _P, _P, _P]),
+    "hier_varlen_workspace_size": (c_int, [c_int32, ctypes.POINTER(c_size_t)]),
+    "hier_varlen_plan_build": (c_int, [_P, _P, _P, c_int32, _P, c_int32, _P, _P, _P, _P, _P, _P,
+                                       _P, _P]),
     "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "hier_selftest_exp2": (c_int, [_P, _P, c_int64, _P]),
 }

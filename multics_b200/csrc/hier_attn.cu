@@ -43,6 +43,7 @@
 
 #include <math.h>
 #include <stdio.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "tmap.h"
@@ -66,6 +67,9 @@ constexpr int kSmemBytes = kSmemBar + 256 + 1024;  // + slack for 1024-byte alig
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;
 constexpr int kSkip = -2;  // mask selector: this half does not use the key tile
+// A key-box row carries the index of its key/value tensor map in the top bits.
+constexpr int kMapShift = 24;
+constexpr int kRowMask = (1 << kMapShift) - 1;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr uint32_t kRegsControl = 40;
 constexpr uint32_t kRegsSoftmax = 224;
@@ -80,9 +84,24 @@ struct AttnArgs {
   __nv_bfloat16* out;
   int64_t out_stride;
   int n_pairs;
+  int mask_stride;    // entries per partial-tile mask: 128 (per row) or 1 (per key only)
+  int mask_row_and;   // 127 or 0
   float scale_log2;
   int* err;
 };
+
+// Key and value tensor maps, one per KV stream (a contiguous pool uses one).
+template <int kMaps>
+struct KVMaps {
+  CUtensorMap k[kMaps];
+  CUtensorMap v[kMaps];
+};
+
+// Mask selector of half h for a key tile; a half without query rows skips
+// every tile.
+__device__ __forceinline__ int half_sel(const int4& e, int h, int use) {
+  return ((use >> h) & 1) ? (h ? e.w : e.z) : kSkip;
+}
 
 struct Bars {
   uint64_t* q_full;
@@ -129,14 +148,29 @@ __device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint3
             (accumulate || k > 0) ? 1u : 0u);
 }
 
+template <int kMaps>
+__device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* maps, uint64_t* bar,
+                                             int col, int r0, int r1) {
+  const CUtensorMap* m0 = maps + (kMaps == 1 ? 0 : (r0 >> kMapShift));
+  const CUtensorMap* m1 = maps + (kMaps == 1 ? 0 : (r1 >> kMapShift));
+  r0 &= kRowMask;
+  r1 &= kRowMask;
+  mbar_arrive_expect_tx(bar, kTile);
+  tma_load_2d(dst, m0, bar, col, r0);
+  tma_load_2d(dst + kBoxBytes, m1, bar, col, r1);
+  tma_load_2d(dst + kHalf, m0, bar, col + 64, r0);
+  tma_load_2d(dst + kHalf + kBoxBytes, m1, bar, col + 64, r1);
+}
+
+template <int kMaps>
 __device__ __forceinline__ void control_role(const AttnArgs& a, int4 pq, int kv_begin, int n_kv,
                                              uint32_t tbase, int warp, int lane, uint8_t* smem,
-                                             const CUtensorMap* tmq, const CUtensorMap* tmk,
-                                             const CUtensorMap* tmv, const Bars& B, int col) {
+                                             const CUtensorMap* tmq, const KVMaps<kMaps>& kv,
+                                             const Bars& B, int col, int use) {
   if (n_kv > 0 && warp == 0 && lane == 0) {
     // -------------------------------------------------------- Q + K producer
     prefetch_tmap(tmq);
-    prefetch_tmap(tmk);
+    if (kMaps == 1) prefetch_tmap(&kv.k[0]);
     mbar_arrive_expect_tx(B.q_full, 2 * kTile);
     tma_load_2d(smem + kSmemQ, tmq, B.q_full, col, pq.x);
     tma_load_2d(smem + kSmemQ + kHalf, tmq, B.q_full, col + 64, pq.x);
@@ -146,26 +180,16 @@ __device__ __forceinline__ void control_role(const AttnArgs& a, int4 pq, int kv_
       const int st = j % kKStages;
       if (j >= kKStages && !mbar_wait(B.k_empty + st, ((j / kKStages) - 1) & 1, a.err, 1)) break;
       const int4 e = a.kv_tiles[kv_begin + j];
-      uint8_t* kd = smem + kSmemK + st * kTile;
-      mbar_arrive_expect_tx(B.k_full + st, kTile);
-      tma_load_2d(kd, tmk, B.k_full + st, col, e.x);
-      tma_load_2d(kd + kBoxBytes, tmk, B.k_full + st, col, e.y);
-      tma_load_2d(kd + kHalf, tmk, B.k_full + st, col + 64, e.x);
-      tma_load_2d(kd + kHalf + kBoxBytes, tmk, B.k_full + st, col + 64, e.y);
+      load_kv_tile<kMaps>(smem + kSmemK + st * kTile, kv.k, B.k_full + st, col, e.x, e.y);
     }
   } else if (n_kv > 0 && warp == 2 && lane == 0) {
     // ------------------------------------------------------------ V producer
-    prefetch_tmap(tmv);
+    if (kMaps == 1) prefetch_tmap(&kv.v[0]);
     for (int j = 0; j < n_kv; ++j) {
       const int st = j % kVStages;
       if (j >= kVStages && !mbar_wait(B.v_empty + st, ((j / kVStages) - 1) & 1, a.err, 2)) break;
       const int4 e = a.kv_tiles[kv_begin + j];
-      uint8_t* vd = smem + kSmemV + st * kTile;
-      mbar_arrive_expect_tx(B.v_full + st, kTile);
-      tma_load_2d(vd, tmv, B.v_full + st, col, e.x);
-      tma_load_2d(vd + kBoxBytes, tmv, B.v_full + st, col, e.y);
-      tma_load_2d(vd + kHalf, tmv, B.v_full + st, col + 64, e.x);
-      tma_load_2d(vd + kHalf + kBoxBytes, tmv, B.v_full + st, col + 64, e.y);
+      load_kv_tile<kMaps>(smem + kSmemV + st * kTile, kv.v, B.v_full + st, col, e.x, e.y);
     }
   } else if (n_kv > 0 && warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
@@ -182,7 +206,7 @@ __device__ __forceinline__ void control_role(const AttnArgs& a, int4 pq, int kv_
     tc_fence_after();
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      if ((h ? e_cur.w : e_cur.z) == kSkip) continue;
+      if (half_sel(e_cur, h, use) == kSkip) continue;
       issue_s(tbase + h * kBN, q_lo[h], k_lo0);
       umma_commit(B.s_full + h);
     }
@@ -196,7 +220,7 @@ __device__ __forceinline__ void control_role(const AttnArgs& a, int4 pq, int kv_
       // PV_h(j) issued just before it reads first (in-order execution).
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        if ((h ? e_cur.w : e_cur.z) != kSkip) {
+        if (half_sel(e_cur, h, use) != kSkip) {
           if (!mbar_wait(B.p_full + h, cp[h] & 1, a.err, 6 + h)) return;
           tc_fence_after();
           issue_pv(tbase + kColO + h * kBN, tbase + h * kBN, v_lo0 + ((stv * kTile) >> 4),
@@ -205,7 +229,7 @@ __device__ __forceinline__ void control_role(const AttnArgs& a, int4 pq, int kv_
         }
         if (!more) continue;
         if (h == 0 && !mbar_wait(B.k_full + stk, ((j + 1) / kKStages) & 1, a.err, 4)) return;
-        if ((h ? e_next.w : e_next.z) != kSkip) {
+        if (half_sel(e_next, h, use) != kSkip) {
           tc_fence_after();
           issue_s(tbase + h * kBN, q_lo[h], k_lo0 + ((stk * kTile) >> 4));
           umma_commit(B.s_full + h);
@@ -222,7 +246,8 @@ __device__ __forceinline__ void control_role(const AttnArgs& a, int4 pq, int kv_
 }
 
 __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_begin, int n_kv,
-                                             uint32_t tbase, int warp, const Bars& B, int col) {
+                                             uint32_t tbase, int warp, const Bars& B, int col,
+                                             int use) {
   const int h = (warp >> 2) - 1;  // 0 for warps 4-7, 1 for warps 8-11
   const int row = threadIdx.x - 128 * (h + 1);
   const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
@@ -241,11 +266,11 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
   for (int j = 0; j < n_kv; ++j) {
     const int4 e = e_next;
     if (j + 1 < n_kv) e_next = a.kv_tiles[kv_begin + j + 1];
-    const int mi = h ? e.w : e.z;
+    const int mi = half_sel(e, h, use);
     if (mi == kSkip) continue;
     const bool partial = mi >= 0;  // uniform across the CTA
     uint4 mk = make_uint4(~0u, ~0u, ~0u, ~0u);
-    if (partial) mk = a.row_masks[(int64_t)mi * kBM + row];
+    if (partial) mk = a.row_masks[(int64_t)mi * a.mask_stride + (row & a.mask_row_and)];
     // S_h(c) is committed after PV_h(c-1), so once it is visible O holds
     // every earlier P V product and can be rescaled without another wait.
     if (!mbar_wait(B.s_full + h, c & 1, a.err, 11)) return;
@@ -343,10 +368,10 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
   }
 }
 
+template <int kMaps>
 __global__ void __launch_bounds__(384, 1)
     hier_attn_kernel(const __grid_constant__ CUtensorMap tmq,
-                     const __grid_constant__ CUtensorMap tmk,
-                     const __grid_constant__ CUtensorMap tmv, AttnArgs a) {
+                     const __grid_constant__ KVMaps<kMaps> kv, AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -371,6 +396,7 @@ __global__ void __launch_bounds__(384, 1)
   const int4 pk = a.pairs[2 * pr + 1];
   const int kv_begin = pk.x;
   const int n_kv = pk.y - pk.x;
+  const int use = (pq.y > 0 ? 1 : 0) | (pq.w > 0 ? 2 : 0);  // halves with query rows
 
   if (threadIdx.x == 0) {
     mbar_init(B.q_full, 1);
@@ -398,10 +424,10 @@ __global__ void __launch_bounds__(384, 1)
   const int col = head * kHD;
   if (warp >= 4) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-    softmax_role(a, pq, kv_begin, n_kv, tbase, warp, B, col);
+    softmax_role(a, pq, kv_begin, n_kv, tbase, warp, B, col, use);
   } else {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
-    control_role(a, pq, kv_begin, n_kv, tbase, warp, lane, smem, &tmq, &tmk, &tmv, B, col);
+    control_role<kMaps>(a, pq, kv_begin, n_kv, tbase, warp, lane, smem, &tmq, kv, B, col, use);
   }
 
   tc_fence_before();
@@ -416,13 +442,10 @@ __global__ void __launch_bounds__(384, 1)
 
 using namespace hier;
 
-extern "C" int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stride, const void* k,
-                             const void* v, int64_t kv_rows_total, int64_t kv_stride, void* out,
-                             int64_t out_stride, int32_t H, int32_t D, const int32_t* q_pairs,
-                             int32_t n_pairs, const int32_t* kv_tiles, const uint32_t* row_masks,
-                             const int32_t* order, float softmax_scale, int32_t* dev_err,
-                             void* stream) {
-  clear_error();
+namespace {
+
+int attn_setup(const void* q, int64_t q_rows_total, int64_t q_stride, int32_t H, int32_t D,
+               int32_t n_pairs, CUtensorMap* tmq) {
   if (D != kHD) {
     set_error(HIER_ENOTIMPL, "hier_attn_fwd supports head_dim=128 only; got head_dim=%d", D);
     return HIER_ENOTIMPL;
@@ -431,19 +454,22 @@ extern "C" int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stri
     set_error(HIER_EVALUE, "invalid heads=%d or query pairs=%d", H, n_pairs);
     return HIER_EVALUE;
   }
-  if (n_pairs == 0) return HIER_OK;
   if ((int64_t)n_pairs * H > INT32_MAX) {
     set_error(HIER_EVALUE, "too many work items");
     return HIER_EVALUE;
   }
-  CUtensorMap tmq, tmk, tmv;
-  int rc = make_tmap_bf16_2d(&tmq, q, (uint64_t)H * D, (uint64_t)q_rows_total, q_stride, 64, 128);
-  if (!rc) rc = make_tmap_bf16_2d(&tmk, k, (uint64_t)H * D, (uint64_t)kv_rows_total, kv_stride, 64, 64);
-  if (!rc) rc = make_tmap_bf16_2d(&tmv, v, (uint64_t)H * D, (uint64_t)kv_rows_total, kv_stride, 64, 64);
-  if (rc) return rc;
+  if (n_pairs == 0) return HIER_OK;
+  return make_tmap_bf16_2d(tmq, q, (uint64_t)H * D, (uint64_t)q_rows_total, q_stride, 64, 128);
+}
+
+template <int kMaps>
+int attn_launch(const CUtensorMap& tmq, const KVMaps<kMaps>& kv, void* out, int64_t out_stride,
+                int32_t H, const int32_t* q_pairs, int32_t n_pairs, const int32_t* kv_tiles,
+                const uint32_t* row_masks, int mask_rows, const int32_t* order,
+                float softmax_scale, int32_t* dev_err, void* stream) {
   static bool attr_set = false;
   if (!attr_set) {
-    HIER_CHECK_CUDA(cudaFuncSetAttribute(hier_attn_kernel,
+    HIER_CHECK_CUDA(cudaFuncSetAttribute(hier_attn_kernel<kMaps>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
                     "cudaFuncSetAttribute(hier_attn_kernel)");
     attr_set = true;
@@ -456,9 +482,90 @@ extern "C" int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stri
   args.out = reinterpret_cast<__nv_bfloat16*>(out);
   args.out_stride = out_stride;
   args.n_pairs = n_pairs;
+  args.mask_stride = mask_rows;
+  args.mask_row_and = mask_rows - 1;
   args.scale_log2 = softmax_scale * 1.4426950408889634f;
   args.err = dev_err;
-  hier_attn_kernel<<<n_pairs * H, 384, kSmemBytes, (cudaStream_t)stream>>>(tmq, tmk, tmv, args);
+  hier_attn_kernel<kMaps><<<n_pairs * H, 384, kSmemBytes, (cudaStream_t)stream>>>(tmq, kv, args);
   HIER_CHECK_CUDA(cudaGetLastError(), "hier_attn_kernel launch");
   return HIER_OK;
+}
+
+}  // namespace
+
+extern "C" int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stride, const void* k,
+                             const void* v, int64_t kv_rows_total, int64_t kv_stride, void* out,
+                             int64_t out_stride, int32_t H, int32_t D, const int32_t* q_pairs,
+                             int32_t n_pairs, const int32_t* kv_tiles, const uint32_t* row_masks,
+                             const int32_t* order, float softmax_scale, int32_t* dev_err,
+                             void* stream) {
+  clear_error();
+  CUtensorMap tmq;
+  int rc = attn_setup(q, q_rows_total, q_stride, H, D, n_pairs, &tmq);
+  if (rc || n_pairs == 0) return rc;
+  if (kv_rows_total > kRowMask) {
+    set_error(HIER_EVALUE, "key/value pool of %lld rows exceeds %d", (long long)kv_rows_total,
+              kRowMask);
+    return HIER_EVALUE;
+  }
+  KVMaps<1> kv;
+  rc = make_tmap_bf16_2d(&kv.k[0], k, (uint64_t)H * D, (uint64_t)kv_rows_total, kv_stride, 64, 64);
+  if (!rc) rc = make_tmap_bf16_2d(&kv.v[0], v, (uint64_t)H * D, (uint64_t)kv_rows_total, kv_stride, 64, 64);
+  if (rc) return rc;
+  return attn_launch<1>(tmq, kv, out, out_stride, H, q_pairs, n_pairs, kv_tiles, row_masks, kBM,
+                        order, softmax_scale, dev_err, stream);
+}
+
+extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_t q_stride,
+                                     int32_t n_streams, const void* const* k, const void* const* v,
+                                     const int64_t* stream_rows, const int64_t* kv_stride,
+                                     void* out, int64_t out_stride, int32_t H, int32_t D,
+                                     const int32_t* q_pairs, int32_t n_pairs,
+                                     const int32_t* kv_tiles, const uint32_t* tile_masks,
+                                     int32_t mask_rows, const int32_t* order,
+                                     float softmax_scale, int32_t* dev_err, void* stream) {
+  clear_error();
+  if (mask_rows != 1 && mask_rows != kBM) {
+    set_error(HIER_EVALUE, "mask_rows must be 1 or %d; got %d", kBM, mask_rows);
+    return HIER_EVALUE;
+  }
+  if (n_streams <= 0 || n_streams > HIER_MAX_KV_STREAMS || !k || !v || !stream_rows || !kv_stride) {
+    set_error(HIER_EVALUE, "need 1..%d key/value streams; got %d", HIER_MAX_KV_STREAMS, n_streams);
+    return HIER_EVALUE;
+  }
+  CUtensorMap tmq;
+  int rc = attn_setup(q, q_rows_total, q_stride, H, D, n_pairs, &tmq);
+  if (rc || n_pairs == 0) return rc;
+  // Streams without rows are never addressed by a plan; their slots (and the
+  // unused ones) repeat the first non-empty stream's maps.
+  int first = -1;
+  for (int s = 0; s < n_streams; ++s) {
+    if (stream_rows[s] < 0 || stream_rows[s] > kRowMask) {
+      set_error(HIER_EVALUE, "key/value stream %d has %lld rows; allowed 0..%d", s,
+                (long long)stream_rows[s], kRowMask);
+      return HIER_EVALUE;
+    }
+    if (first < 0 && stream_rows[s] > 0) first = s;
+  }
+  KVMaps<HIER_MAX_KV_STREAMS> kv;
+  memset(&kv, 0, sizeof(kv));
+  if (first >= 0) {
+    for (int s = 0; s < n_streams; ++s) {
+      if (stream_rows[s] == 0) continue;
+      rc = make_tmap_bf16_2d(&kv.k[s], k[s], (uint64_t)H * D, (uint64_t)stream_rows[s],
+                             kv_stride[s], 64, 64);
+      if (!rc)
+        rc = make_tmap_bf16_2d(&kv.v[s], v[s], (uint64_t)H * D, (uint64_t)stream_rows[s],
+                               kv_stride[s], 64, 64);
+      if (rc) return rc;
+    }
+    for (int s = 0; s < HIER_MAX_KV_STREAMS; ++s) {
+      if (s < n_streams && stream_rows[s] > 0) continue;
+      kv.k[s] = kv.k[first];
+      kv.v[s] = kv.v[first];
+    }
+  }
+  return attn_launch<HIER_MAX_KV_STREAMS>(tmq, kv, out, out_stride, H, q_pairs, n_pairs, kv_tiles,
+                                          tile_masks, mask_rows, order, softmax_scale, dev_err,
+                                          stream);
 }

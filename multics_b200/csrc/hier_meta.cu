@@ -419,20 +419,6 @@ __global__ void rowmask_kernel(Dims d, const uint8_t* M, const int32_t* kv_off,
   }
 }
 
-// order[rank] = work item, by descending key-tile count (ties: lower index
-// first); item i's count is rec[i*stride + 5] - rec[i*stride + 4].
-__global__ void order_kernel(const int32_t* rec, int stride, int n, int32_t* order) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int ci = rec[i * stride + 5] - rec[i * stride + 4];
-    int rank = 0;
-    for (int j = 0; j < n; ++j) {
-      const int cj = rec[j * stride + 5] - rec[j * stride + 4];
-      rank += (cj > ci) || (cj == ci && j < i);
-    }
-    order[rank] = i;
-  }
-}
-
 static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 static int check_grouping(const hier_grouping* g) {
@@ -550,7 +536,7 @@ extern "C" int hier_block_plan_build(const hier_grouping* g, void* workspace,
   pair_plan_fill_kernel<<<(np + 7) / 8, 256, 0, s>>>(d, cls, nb, np, kv_off, pair_off, page_table,
                                                      q_pairs, kv_tiles);
   if (row_masks) rowmask_kernel<<<nb, 128, 0, s>>>(d, M, kv_off, kv_idx, (uint4*)row_masks);
-  if (order) order_kernel<<<grid_for(np, 128), 128, 0, s>>>(q_pairs, 8, np, order);
+  if (order) order_by_work_kernel<8><<<grid_for(np, 128), 128, 0, s>>>(q_pairs, np, order);
   HIER_CHECK_CUDA(cudaGetLastError(), "block plan kernels launch");
   return HIER_OK;
 }
