@@ -294,6 +294,65 @@ int hier_varlen_plan_build(const int32_t* prog_qbase, const int32_t* prog_nq,
                            void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Tiled128 block layouts
+ * ------------------------------------------------------------------------- */
+
+#define HIER_TILED_FULL 0   /* build_hier_tiled_full_sequence_layouts */
+#define HIER_TILED_CACHED 1 /* build_hier_tiled_cached_layout */
+
+/* Inputs of the Tiled128 layout builders
+ * (multics/models/kernels/hier_tiled_attention.py:244-429, 474-655).  Device
+ * pointers.  Full sequence (mode 0): T frames, labels int64 [T, P], active
+ * uint8 [T, N] (labels constant inside each block of n_block frames, checked
+ * by the host layer).  Cached (mode 1): n_frames query frames, labels int64
+ * [n_frames, P], active = q_active uint8 [n_frames, N], and the per-token
+ * cache tensors as in hier_cached_grouping (fa / fl / fg retained frames). */
+typedef struct hier_tiled_grouping {
+  int32_t mode;
+  int32_t P, N, L, KL, KG, n_block, local_attn, direct;
+  int32_t T;
+  int32_t n_frames, fa, fl, fg;
+  const int64_t* labels;
+  const uint8_t* active;
+  const int64_t* agent_frames[HIER_MAX_KV_STREAMS];
+  const int64_t* local_frames[HIER_MAX_KV_STREAMS];
+  const uint8_t* local_active[HIER_MAX_KV_STREAMS];
+  const int64_t* global_frames;
+} hier_tiled_grouping;
+
+typedef struct hier_tiled_sizes_t {
+  int32_t n_layouts;     /* T / n_block (full) or 1 (cached) */
+  int32_t n_seg;         /* segments per layout */
+  int32_t n_prog;        /* BLOCK_M=16 programs per layout */
+  int32_t n_pairs;       /* attention query pairs per layout */
+  int32_t tile_capacity; /* upper bound of attention key tiles, all layouts */
+  int32_t reserved;
+  int64_t q_rows;        /* query rows */
+} hier_tiled_sizes_t;
+
+int hier_tiled_sizes(const hier_tiled_grouping* g, hier_tiled_sizes_t* out);
+
+/* Per (layout, segment), layout-major: kv_count (kept 128-slot chunks x 128,
+ * as the reference), attention key boxes, and slots [2] int64 = (logical =
+ * valid slots, dense slots).  status bit 2: a query frame is missing from an
+ * agent cache (the reference's KeyError). */
+int hier_tiled_count(const hier_tiled_grouping* g, int32_t* kv_count, int32_t* n_boxes,
+                     int64_t* slots, int32_t* status, void* stream);
+
+/* Fill the layouts (NULL groups skipped): programs [n_layouts*n_prog];
+ * kv_index (int32) / kv_valid (uint8) of layout b at element offset
+ * kv_off[b] with row width kv_width[b] (device arrays; bit-exact for
+ * kv_width = ceil128(max kv_count of the layout)); and one attention plan
+ * over all layouts (q_pairs [n_layouts*n_pairs][8], kv_tiles / tile_masks
+ * [tile_capacity][4], order) for hier_attn_fwd_streams with mask_rows = 1 on
+ * the full-sequence (or concatenated cached) key/value pool. */
+int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_boxes, const int64_t* kv_off,
+                     const int32_t* kv_width, int32_t* prog_qbase, int32_t* prog_nq,
+                     int32_t* prog_seg, int32_t* kv_index, uint8_t* kv_valid, int32_t* q_pairs,
+                     int32_t* kv_tiles, uint32_t* tile_masks, int32_t tile_capacity,
+                     int32_t* order, int32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Self-test of the tensor-core operand encodings (no reference counterpart):
  * with A, B bf16 [128,128] row-major,
  *   c_ss = A @ B^T   (both operands K-major in shared memory)

@@ -60,6 +60,30 @@ class HierCachedSizes(ctypes.Structure):
     ]
 
 
+class HierTiledGrouping(ctypes.Structure):
+    """Mirror of ``struct hier_tiled_grouping``."""
+
+    _fields_ = [
+        ("mode", c_int32), ("P", c_int32), ("N", c_int32), ("L", c_int32), ("KL", c_int32),
+        ("KG", c_int32), ("n_block", c_int32), ("local_attn", c_int32), ("direct", c_int32),
+        ("T", c_int32), ("n_frames", c_int32), ("fa", c_int32), ("fl", c_int32), ("fg", c_int32),
+        ("labels", c_void_p), ("active", c_void_p),
+        ("agent_frames", c_void_p * MAX_KV_STREAMS),
+        ("local_frames", c_void_p * MAX_KV_STREAMS),
+        ("local_active", c_void_p * MAX_KV_STREAMS),
+        ("global_frames", c_void_p),
+    ]
+
+
+class HierTiledSizes(ctypes.Structure):
+    """Mirror of ``hier_tiled_sizes_t``."""
+
+    _fields_ = [
+        ("n_layouts", c_int32), ("n_seg", c_int32), ("n_prog", c_int32), ("n_pairs", c_int32),
+        ("tile_capacity", c_int32), ("reserved", c_int32), ("q_rows", c_int64),
+    ]
+
+
 _P = c_void_p
 _SIGS = {
     "hier_last_error": (c_char_p, []),
@@ -87,6 +111,10 @@ _SIGS = {
     "hier_varlen_workspace_size": (c_int, [c_int32, ctypes.POINTER(c_size_t)]),
     "hier_varlen_plan_build": (c_int, [_P, _P, _P, c_int32, _P, c_int32, _P, _P, _P, _P, _P, _P,
                                        _P, _P]),
+    "hier_tiled_sizes": (c_int, [ctypes.POINTER(HierTiledGrouping), ctypes.POINTER(HierTiledSizes)]),
+    "hier_tiled_count": (c_int, [ctypes.POINTER(HierTiledGrouping), _P, _P, _P, _P, _P]),
+    "hier_tiled_build": (c_int, [ctypes.POINTER(HierTiledGrouping), _P, _P, _P, _P, _P, _P, _P, _P,
+                                 _P, _P, _P, c_int32, _P, _P, _P]),
     "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "hier_selftest_exp2": (c_int, [_P, _P, c_int64, _P]),
 }

@@ -23,14 +23,18 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "seg_plan.cuh"
 
 namespace hier {
 namespace {
 
-constexpr int kThreads = 256;
+using segplan::kBoxRows;
+using segplan::kStreamShift;
+using segplan::kThreads;
+using segplan::SegSmem;
+using segplan::block_scan;
+
 constexpr int kMaxCand = 2048;  // frames of all streams together
-constexpr int kBoxRows = 64;
-constexpr int kStreamShift = 24;
 
 // status bits written by the builders
 constexpr int kStatusBadFrame = 1;     // membership / global_only frame out of range
@@ -229,68 +233,12 @@ __device__ int candidate(const hier_cached_grouping& g, const CDims& d, const Se
   return sel ? d.KG : 0;
 }
 
-// Block-wide inclusive scan (sum or max) of one value per thread.
-template <bool kMax>
-__device__ int block_scan(int v, int* warp_tmp) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int t = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v = kMax ? max(v, t) : v + t;
-  }
-  if (lane == 31) warp_tmp[w] = v;
-  __syncthreads();
-  if (w == 0) {
-    int x = lane < kThreads / 32 ? warp_tmp[lane] : (kMax ? INT_MIN : 0);
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x = kMax ? max(x, t) : x + t;
-    }
-    if (lane < kThreads / 32) warp_tmp[lane] = x;
-  }
-  __syncthreads();
-  if (w > 0) v = kMax ? max(v, warp_tmp[w - 1]) : v + warp_tmp[w - 1];
-  __syncthreads();
-  return v;
-}
+size_t seg_smem_bytes(int C) { return segplan::seg_smem_ints(C) * sizeof(int); }
 
-// Shared-memory layout of one segment's run analysis.
-struct SegSmem {
-  int* w;     // [C] selected width (0 = not attended)
-  int* key;   // [C] stream-packed first row
-  int* pool;  // [C] first pool index
-  int* off;   // [C] exclusive key offset
-  int* rf;    // [C+1] key offset of each merged run (rf[n_runs] = total)
-  int* rk;    // [C] stream-packed first row of each merged run
-  int* rb;    // [C+1] exclusive box offset of each merged run
-  int* misc;  // [0] total keys, [1] runs, [2] boxes, [3] bad frame, [8..] scan scratch
-};
-
-constexpr int kMiscInts = 32 + kThreads;
-
-__device__ SegSmem seg_smem(int* base, int C) {
-  SegSmem m;
-  m.w = base;
-  m.key = m.w + C;
-  m.pool = m.key + C;
-  m.off = m.pool + C;
-  m.rf = m.off + C;
-  m.rk = m.rf + C + 1;
-  m.rb = m.rk + C;
-  m.misc = m.rb + C + 1;
-  return m;
-}
-
-size_t seg_smem_bytes(int C) { return (size_t)(7 * C + 2 + kMiscInts) * sizeof(int); }
-
-// Enumerate the segment's candidates and derive key offsets, merged runs and
-// 64-row key boxes.
+// Evaluate the segment's candidate runs into m.w / m.key / m.pool, then
+// derive its key offsets, merged runs and boxes.
 __device__ void analyse_segment(const hier_cached_grouping& g, const CDims& d, const Seg& sg,
                                 const SegSmem& m) {
-  int* wtmp = m.misc + 8;       // block_scan scratch
-  int* carry = m.misc + 16;     // values carried from one chunk to the next
-  int* incl_max = m.misc + 32;  // [kThreads] inclusive max-scan of one chunk
   if (threadIdx.x == 0) m.misc[3] = 0;
   __syncthreads();
   const int64_t qf = query_frame(g, d, sg.qrel);
@@ -303,64 +251,14 @@ __device__ void analyse_segment(const hier_cached_grouping& g, const CDims& d, c
   }
   if (bad) atomicOr(&m.misc[3], 1);
   __syncthreads();
-  // Key offsets and merged runs: a selected run continues the previous
-  // selected one when it holds the next rows of the same stream.
-  int carry_sum = 0, carry_prev = -1, carry_runs = 0;
-  for (int base = 0; base < d.C; base += kThreads) {
-    const int c = base + threadIdx.x;
-    const int wc = c < d.C ? m.w[c] : 0;
-    const int incl = block_scan<false>(wc, wtmp) + carry_sum;
-    const int pm = max(block_scan<true>(wc > 0 ? c : -1, wtmp), carry_prev);
-    incl_max[threadIdx.x] = pm;
-    __syncthreads();
-    const int prev = threadIdx.x == 0 ? carry_prev : incl_max[threadIdx.x - 1];
-    const bool start = wc > 0 && (prev < 0 || m.key[prev] + m.w[prev] != m.key[c]);
-    if (wc > 0) m.off[c] = incl - wc;
-    const int rid = block_scan<false>(start ? 1 : 0, wtmp) + carry_runs - 1;
-    if (start) {
-      m.rf[rid] = incl - wc;
-      m.rk[rid] = m.key[c];
-    }
-    if (threadIdx.x == kThreads - 1) {
-      carry[0] = incl;
-      carry[1] = pm;
-      carry[2] = rid + 1;
-    }
-    __syncthreads();
-    carry_sum = carry[0];
-    carry_prev = carry[1];
-    carry_runs = carry[2];
-    __syncthreads();
-  }
-  const int total = carry_sum, n_runs = carry_runs;
-  if (threadIdx.x == 0) m.rf[n_runs] = total;
-  __syncthreads();
-  // boxes per merged run
-  int carry_box = 0;
-  for (int base = 0; base < n_runs; base += kThreads) {
-    const int r = base + threadIdx.x;
-    const int nbx = r < n_runs ? (m.rf[r + 1] - m.rf[r] + kBoxRows - 1) / kBoxRows : 0;
-    const int incl = block_scan<false>(nbx, wtmp) + carry_box;
-    if (r < n_runs) m.rb[r] = incl - nbx;
-    if (threadIdx.x == kThreads - 1) carry[0] = incl;
-    __syncthreads();
-    carry_box = carry[0];
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    m.rb[n_runs] = carry_box;
-    m.misc[0] = total;
-    m.misc[1] = n_runs;
-    m.misc[2] = carry_box;
-  }
-  __syncthreads();
+  segplan::analyse_runs(m, d.C);
 }
 
 __global__ void __launch_bounds__(kThreads)
     cached_count_kernel(const hier_cached_grouping g, const CDims d, int32_t* kv_count,
                         int32_t* n_boxes, int32_t* status) {
   extern __shared__ int smem_i[];
-  const SegSmem m = seg_smem(smem_i, d.C);
+  const SegSmem m = segplan::seg_smem(smem_i, d.C);
   const int s = blockIdx.x;
   const Seg sg = seg_of(d, s);
   analyse_segment(g, d, sg, m);
@@ -385,14 +283,10 @@ struct BuildOut {
   int32_t* status;
 };
 
-__device__ __forceinline__ uint32_t low_bits(int n) {  // n in [0, 32]
-  return n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
-}
-
 __global__ void __launch_bounds__(kThreads)
     cached_build_kernel(const hier_cached_grouping g, const CDims d, const BuildOut o) {
   extern __shared__ int smem_i[];
-  const SegSmem m = seg_smem(smem_i, d.C);
+  const SegSmem m = segplan::seg_smem(smem_i, d.C);
   const int s = blockIdx.x;
   const Seg sg = seg_of(d, s);
   // programs (block_m rows each)
@@ -408,7 +302,7 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   analyse_segment(g, d, sg, m);
-  const int total = m.misc[0], n_runs = m.misc[1], n_box = m.misc[2];
+  const int total = m.misc[0], n_box = m.misc[2];
   if (threadIdx.x == 0 && m.misc[3] && o.status) atomicOr(o.status, kStatusBadFrame);
   // kv_index row (zero padded), one warp per candidate run
   if (o.kv_index) {
@@ -423,75 +317,18 @@ __global__ void __launch_bounds__(kThreads)
     for (int i = total + threadIdx.x; i < o.kv_width; i += kThreads) row[i] = 0;
   }
   if (!o.q_pairs) return;
-  // tile base: tiles of the segments before this one
-  int tb = 0;
-  for (int i = threadIdx.x; i < s; i += kThreads) tb += (o.n_boxes[i] + 1) >> 1;
-  tb = block_scan<false>(tb, m.misc + 8);  // inclusive: the last thread holds the sum
-  __shared__ int tile_base_s;
-  if (threadIdx.x == kThreads - 1) tile_base_s = tb;
-  __syncthreads();
-  const int tile_base = tile_base_s;
+  const int tile_base = segplan::tile_base_of(o.n_boxes, s, m.misc + 8);
   const int n_tiles = (n_box + 1) >> 1;
   if (tile_base + n_tiles > o.tile_capacity) {
     if (threadIdx.x == 0 && o.status) atomicOr(o.status, kStatusTileOverflow);
     return;
   }
-  // boxes: box b of merged run r starts at row rk[r] + 64 (b - rb[r])
-  for (int b = threadIdx.x; b < 2 * n_tiles; b += kThreads) {
-    const int t = tile_base + (b >> 1), slot = b & 1;
-    int key, valid;
-    if (b < n_box) {
-      int lo = 0, hi = n_runs - 1;  // last run with rb[r] <= b
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (m.rb[mid] <= b) lo = mid;
-        else hi = mid - 1;
-      }
-      const int k = b - m.rb[lo];
-      key = m.rk[lo] + kBoxRows * k;
-      valid = min(kBoxRows, m.rf[lo + 1] - m.rf[lo] - kBoxRows * k);
-    } else {  // odd box count: empty second box (same rows, no valid keys)
-      int lo = 0, hi = n_runs - 1;
-      const int bb = b - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (m.rb[mid] <= bb) lo = mid;
-        else hi = mid - 1;
-      }
-      key = m.rk[lo] + kBoxRows * (bb - m.rb[lo]);
-      valid = 0;
-    }
-    o.kv_tiles[(int64_t)t * 4 + slot] = key;
-    o.tile_masks[(int64_t)t * 4 + 2 * slot] = low_bits(valid);
-    o.tile_masks[(int64_t)t * 4 + 2 * slot + 1] = low_bits(max(valid - 32, 0));
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < n_tiles; i += kThreads) {
-    const int t = tile_base + i;
-    const uint32_t* mk = o.tile_masks + (int64_t)t * 4;
-    const bool full = (mk[0] & mk[1] & mk[2] & mk[3]) == 0xffffffffu;
-    const int sel = full ? -1 : t;
-    o.kv_tiles[(int64_t)t * 4 + 2] = sel;
-    o.kv_tiles[(int64_t)t * 4 + 3] = sel;
-  }
-  // query pairs: two 128-row tiles of the segment's rows per pair
+  segplan::emit_plan(m, tile_base, o.kv_tiles, o.tile_masks);
   if (sg.ql > 0) {
-    const int per = sg.type == 0 ? d.npA : (sg.type == 1 ? d.npL : d.npG);
     const int base = sg.type == 0   ? s * d.npA
                      : sg.type == 1 ? d.nA * d.npA + (s - d.nA) * d.npL
                                     : d.nA * d.npA + d.nLs * d.npL + (s - d.nA - d.nLs) * d.npG;
-    for (int i = threadIdx.x; i < per; i += kThreads) {
-      int32_t* r = o.q_pairs + (int64_t)(base + i) * 8;
-      const int r0 = 256 * i;
-      r[0] = sg.q0 + r0;
-      r[1] = min(128, sg.ql - r0);
-      r[2] = sg.q0 + r0 + 128;
-      r[3] = max(0, min(128, sg.ql - r0 - 128));
-      r[4] = tile_base;
-      r[5] = tile_base + n_tiles;
-      r[6] = 0;
-      r[7] = 0;
-    }
+    segplan::emit_pairs(sg.q0, sg.ql, base, tile_base, n_tiles, o.q_pairs);
   }
 }
 
