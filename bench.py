@@ -37,7 +37,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="cfg2")
+    ap.add_argument("--config", default=None,
+                    help="cfg2 (default at 1 GPU) or cfg4/cfg5 (default cfg4 when sharded)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -117,6 +118,187 @@ def useful_pairs(bm):
         for s in range(32):
             bits += int(((x >> s) & 1).sum())
     return bits + bm.n_full * 128 * 128
+
+
+def run_sharded(args, rank, world, local_rank):
+    """Players sharded over the ranks (strong scaling of one layer): each rank
+    runs the prologue of its rows (its players, then the replicated hub
+    rows), the mate-frame exchange, the attention launch and the hub merge."""
+    import torch
+    import torch.distributed as dist
+
+    from multics_b200.attention import device_error, freqs_table, hier_prep_qk
+    from multics_b200.hier_masks import build_stage2_hier_flex_block_mask
+    from multics_b200.sharded import ShardedHierAttention, ShardTopology
+    from multics_b200.synth import CONFIGS, make_inputs
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = CONFIGS[args.config]
+    inp = make_inputs(cfg, device=dev)
+    ft_all = freqs_table(inp.freqs)
+    stream = torch.cuda.current_stream(dev)
+    labels = inp.labels.cpu().numpy()
+    topo = ShardTopology(P=cfg.P, T=cfg.T, L=cfg.L, N=cfg.N, KL=cfg.KL, KG=cfg.KG,
+                         n_block=cfg.n_block, local_attn=cfg.local_attn, direct=cfg.direct,
+                         labels=labels, world=world, rank=rank)
+    loc = torch.from_numpy(topo.local_rows()).to(dev)
+    qx, kx, v = (t.index_select(0, loc).contiguous() for t in (inp.qx, inp.kx, inp.v))
+    cam = inp.cam.index_select(0, loc).contiguous()
+    ft = ft_all.index_select(0, loc).contiguous()
+    # global useful pairs (the same count as one GPU running the whole layer)
+    bm, S, _ = build_stage2_hier_flex_block_mask(cfg.P, cfg.T, cfg.L, cfg.N, cfg.KL, cfg.KG,
+                                                 cfg.n_block, cfg.local_attn, inp.labels, None,
+                                                 cfg.direct, dev)
+    pairs = useful_pairs(bm)
+    useful_flops = 4.0 * cfg.H * cfg.D * pairs
+    w = {k: getattr(inp, k) for k in ("wcq", "wck", "nqw", "nkw")}
+    del bm, inp
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    sh = ShardedHierAttention(topo, cfg.H, dev)
+    torch.cuda.synchronize()
+    plan_ms = (time.perf_counter() - t0) * 1e3
+    sh.check_status()
+    q_buf = torch.empty_like(qx)
+    k_buf = torch.empty_like(qx)
+    o_buf = torch.empty_like(qx)
+    marks = {}
+
+    def step(i=None):
+        hier_prep_qk(qx, kx, ft, cfg.H, norm_q_weight=w["nqw"], norm_k_weight=w["nkw"],
+                     cam_tokens=cam, cam_q_weight=w["wcq"], cam_k_weight=w["wck"],
+                     out=(q_buf, k_buf))
+        if i is not None:
+            marks["a"][i].record(stream)
+        sh.exchange(k_buf, v)
+        if i is not None:
+            marks["b"][i].record(stream)
+        sh.attend(q_buf, k_buf, v, o_buf)
+        if i is not None:
+            marks["c"][i].record(stream)
+        from multics_b200.sharded import merge_hub_partials
+        merge_hub_partials(o_buf[topo.own_rows:], sh.lse[topo.own_rows:], cfg.H, cfg.D,
+                           world=world)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    K = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    marks = {k: [torch.cuda.Event(enable_timing=True) for _ in range(K)] for k in "abc"}
+    with ClockSampler(local_rank) as clk:
+        time.sleep(0.3)
+        for i in range(K):
+            starts[i].record(stream)
+            step(i)
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    total_ms = starts[0].elapsed_time(ends[-1])
+    parts = {
+        "prologue": statistics.mean(starts[i].elapsed_time(marks["a"][i]) for i in range(K)),
+        "exchange": statistics.mean(marks["a"][i].elapsed_time(marks["b"][i]) for i in range(K)),
+        "attention": statistics.mean(marks["b"][i].elapsed_time(marks["c"][i]) for i in range(K)),
+        "hub_merge": statistics.mean(marks["c"][i].elapsed_time(ends[i]) for i in range(K)),
+    }
+    t = torch.tensor([total_ms, parts["attention"]], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    total_ms, attn_max = float(t[0]), float(t[1])
+    ms_per_step = total_ms / K
+    value = useful_flops / (ms_per_step * 1e-3) / 1e12
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e_sharded(args, cfg, topo, sh, qx, kx, v, cam, ft, w, dev, useful_flops,
+                              world)
+    peak_b, peak_s, hbm, peak_kind = load_peaks()
+    # kernel roofline: this rank's share of the useful FLOPs over its slowest
+    # attention launch (the players split evenly or nearly so)
+    share = topo.n_own / cfg.P
+    achieved = useful_flops * share / (attn_max * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; shapes of the reference configs)",
+        "config": {"workload": f"{cfg.name}: hierarchical attention layer forward, players "
+                               f"sharded over {world} GPUs (prologue + mate-frame all_to_all + "
+                               f"attention + hub merge), P={cfg.P} x T={cfg.T} x L={cfg.L}, "
+                               f"N={cfg.N} groups (regroup every {cfg.regroup_every} frames), "
+                               f"K_L={cfg.KL}, K_G={cfg.KG}, H={cfg.H}x{cfg.D}",
+                   "S": S, "useful_pairs": pairs, "useful_gflop_per_step": useful_flops / 1e9,
+                   "parallelism": f"players sharded x{world} (ranks own {topo.bounds})",
+                   "remote_units_rank0": len(topo.needs[0]),
+                   "l2": "inputs larger than L2"},
+        "breakdown_ms": {k: round(v_, 4) for k, v_ in parts.items()},
+        "plan_once_ms": round(plan_ms, 3),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_b,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak_b, 4),
+                     "peak_kind": f"{peak_kind} bf16 burst", "traffic": None,
+                     "kernel": "hier_attn_kernel (rank with the most players)"},
+        "gpu_launches": 4 * K,
+        "device_error": device_error(dev),
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    clocks = clk.summary()
+    if clocks:
+        line["clocks"] = clocks
+    return line
+
+
+def run_e2e_sharded(args, cfg, topo, sh, qx, kx, v, cam, ft, w, dev, useful_flops, world):
+    """The sharded layer through its public API with pinned host buffers: each
+    rank copies its rows' projections and camera tokens in and its output
+    rows out every step."""
+    import torch
+    import torch.distributed as dist
+
+    from multics_b200.attention import hier_prep_qk
+    from multics_b200.sharded import merge_hub_partials
+
+    hq, hk, hv, hc = (t.cpu().pin_memory() for t in (qx, kx, v, cam))
+    ho = torch.empty_like(hq).pin_memory()
+    dq, dk, dv, dc = (torch.empty_like(t, device=dev) for t in (hq, hk, hv, hc))
+    qb, kb = torch.empty_like(dq), torch.empty_like(dq)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for d_, h_ in ((dq, hq), (dk, hk), (dv, hv), (dc, hc)):
+            d_.copy_(h_, non_blocking=True)
+        hier_prep_qk(dq, dk, ft, cfg.H, norm_q_weight=w["nqw"], norm_k_weight=w["nkw"],
+                     cam_tokens=dc, cam_q_weight=w["wcq"], cam_k_weight=w["wck"], out=(qb, kb))
+        o = sh.forward(qb, kb, dv)
+        ho.copy_(o, non_blocking=True)
+
+    steps = max(3, min(args.steps, 10))
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / steps], device=dev)
+    bi = torch.tensor([sum(x.numel() * x.element_size() for x in (hq, hk, hv, hc)),
+                       ho.numel() * ho.element_size()], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(bi)
+    ms = float(t.item())
+    return {"value": round(useful_flops / (ms * 1e-3) / 1e12, 2), "unit": UNIT,
+            "ms_per_step": round(ms, 3), "h2d_bytes_per_step": int(bi[0]),
+            "d2h_bytes_per_step": int(bi[1]), "steps": steps}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -355,8 +537,8 @@ def run_reference(args, rank, world):
     v = statistics.mean(vals)
     return {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(wall * 1e3 / args.steps, 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic (seeded)", "impl": "reference",
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)", "impl": "reference",
             "config": {"workload": f"{cfg.name} (bounded CPU sample)"},
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                              "sample": f"{per_step:.0f} s of dense-mask fp32 attention rows per step"},
@@ -368,6 +550,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.config is None:
+        args.config = "cfg2" if world == 1 else "cfg4"
     if args.impl == "reference":
         line = run_reference(args, rank, world)
         if line is not None:
@@ -381,7 +565,10 @@ def main():
 
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-    line = run_ours(args, rank, world, local_rank)
+    if world == 1 and args.config == "cfg2":
+        line = run_ours(args, rank, world, local_rank)
+    else:
+        line = run_sharded(args, rank, world, local_rank)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -199,14 +199,19 @@ int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stride, const v
  * (s << 24) | row-within-stream.  tile_masks holds mask_rows entries of four
  * uint32 per partial tile: 128 (one key bitmask per query row, the format of
  * hier_block_plan_build) or 1 (one key bitmask shared by every query row, the
- * format of hier_cached_build).  Other arguments as hier_attn_fwd. */
+ * format of hier_cached_build).  lse (float [q_rows_total][H], may be NULL)
+ * receives per written row and head log2(sum_j 2^(s_j)) of the scaled scores
+ * s_j = q.k_j * softmax_scale * log2(e) (-inf for rows without keys), so that
+ * partial results over disjoint key sets merge as
+ * O = sum_r 2^(lse_r - M) O_r / sum_r 2^(lse_r - M).  Other arguments as
+ * hier_attn_fwd. */
 int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_t q_stride,
                           int32_t n_streams, const void* const* k, const void* const* v,
                           const int64_t* stream_rows, const int64_t* kv_stride, void* out,
                           int64_t out_stride, int32_t H, int32_t D, const int32_t* q_pairs,
                           int32_t n_pairs, const int32_t* kv_tiles, const uint32_t* tile_masks,
                           int32_t mask_rows, const int32_t* order, float softmax_scale,
-                          int32_t* dev_err, void* stream);
+                          float* lse, int32_t* dev_err, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Cached (rolling key/value cache) step
@@ -351,6 +356,50 @@ int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_boxes, const
                      int32_t* prog_seg, int32_t* kv_index, uint8_t* kv_valid, int32_t* q_pairs,
                      int32_t* kv_tiles, uint32_t* tile_masks, int32_t tile_capacity,
                      int32_t* order, int32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Player-sharded execution (one rank per GPU)
+ * ------------------------------------------------------------------------- */
+
+/* One rank's share of a full-sequence layer (labels mode, active hubs): the
+ * rank owns players [p0, p1); its query rows are its players' rows (in
+ * sequence order) followed by every hub row (T*N*K_L local, then T*K_G
+ * global); its key/value streams for hier_attn_fwd_streams are
+ *   0 = its players' rows, 1 = the hub rows, 2 = remote group-mate frames
+ *   (unit (o, f) = the L rows of player o at frame f, at slot
+ *   remote_slot[o*T + f] of the remote buffer, -1 if absent).
+ * Player rows get their full key sets; hub rows get the keys this rank holds
+ * (its players' rows, plus the hub rows if hub_keys) and are merged across
+ * ranks with hier_lse_prepare / hier_lse_finish.  No reference counterpart
+ * in code: the reference runs every player on one device; this realises the
+ * player sharding of the multi-GPU configurations. */
+typedef struct hier_shard_desc {
+  int32_t P, N, L, KL, KG, T, n_block, local_attn, direct;
+  int32_t p0, p1;
+  int32_t hub_keys;
+  int32_t hub_group_major; /* stream 1 holds the local hubs group-major: (g, f, slot) at row
+                              (g*T + f)*K_L + slot, then the global hubs frame-major */
+  const int64_t* labels;      /* [T, P] */
+  const uint8_t* active;      /* [T, N] */
+  const int32_t* remote_slot; /* [P*T] */
+} hier_shard_desc;
+
+/* n_layouts, n_seg, n_pairs (per layout), tile_capacity, q_rows of a shard. */
+int hier_shard_sizes(const hier_shard_desc* g, hier_tiled_sizes_t* out);
+
+/* Attention plan of a shard (n_boxes: int32 [n_layouts*n_seg] scratch);
+ * status bit 3: a remote unit the plan needs has no slot.  No host sync. */
+int hier_shard_plan(const hier_shard_desc* g, int32_t* n_boxes, int32_t* q_pairs,
+                    int32_t* kv_tiles, uint32_t* tile_masks, int32_t tile_capacity,
+                    int32_t* order, int32_t* status, void* stream);
+
+/* Partial-row merge: x = 2^(lse - lse_max) * o (fp32 [rows, H*D]),
+ * w = 2^(lse - lse_max) (fp32 [rows, H]); after summing x and w over the
+ * ranks, out = x / w in bf16 (0 where w = 0). */
+int hier_lse_prepare(const void* o, int64_t o_stride, const float* lse, const float* lse_max,
+                     int64_t rows, int32_t H, int32_t D, float* x, float* w, void* stream);
+int hier_lse_finish(const float* x, const float* w, int64_t rows, int32_t H, int32_t D, void* out,
+                    int64_t out_stride, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Self-test of the tensor-core operand encodings (no reference counterpart):

@@ -84,6 +84,17 @@ class HierTiledSizes(ctypes.Structure):
     ]
 
 
+class HierShardDesc(ctypes.Structure):
+    """Mirror of ``struct hier_shard_desc``."""
+
+    _fields_ = [
+        ("P", c_int32), ("N", c_int32), ("L", c_int32), ("KL", c_int32), ("KG", c_int32),
+        ("T", c_int32), ("n_block", c_int32), ("local_attn", c_int32), ("direct", c_int32),
+        ("p0", c_int32), ("p1", c_int32), ("hub_keys", c_int32), ("hub_group_major", c_int32),
+        ("labels", c_void_p), ("active", c_void_p), ("remote_slot", c_void_p),
+    ]
+
+
 _P = c_void_p
 _SIGS = {
     "hier_last_error": (c_char_p, []),
@@ -102,7 +113,7 @@ _SIGS = {
                               c_int32, _P, c_int32, _P, _P, _P, c_float, _P, _P]),
     "hier_attn_fwd_streams": (c_int, [_P, c_int64, c_int64, c_int32, _P, _P, _P, _P, _P, c_int64,
                                       c_int32, c_int32, _P, c_int32, _P, _P, c_int32, _P,
-                                      c_float, _P, _P]),
+                                      c_float, _P, _P, _P]),
     "hier_cached_sizes": (c_int, [ctypes.POINTER(HierCachedGrouping), c_int32,
                                   ctypes.POINTER(HierCachedSizes)]),
     "hier_cached_count": (c_int, [ctypes.POINTER(HierCachedGrouping), _P, _P, _P, _P]),
@@ -115,6 +126,11 @@ _SIGS = {
     "hier_tiled_count": (c_int, [ctypes.POINTER(HierTiledGrouping), _P, _P, _P, _P, _P]),
     "hier_tiled_build": (c_int, [ctypes.POINTER(HierTiledGrouping), _P, _P, _P, _P, _P, _P, _P, _P,
                                  _P, _P, _P, c_int32, _P, _P, _P]),
+    "hier_shard_sizes": (c_int, [ctypes.POINTER(HierShardDesc), ctypes.POINTER(HierTiledSizes)]),
+    "hier_shard_plan": (c_int, [ctypes.POINTER(HierShardDesc), _P, _P, _P, _P, c_int32, _P, _P,
+                                _P]),
+    "hier_lse_prepare": (c_int, [_P, c_int64, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P]),
+    "hier_lse_finish": (c_int, [_P, _P, c_int64, c_int32, c_int32, _P, c_int64, _P]),
     "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "hier_selftest_exp2": (c_int, [_P, _P, c_int64, _P]),
 }

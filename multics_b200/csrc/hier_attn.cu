@@ -87,6 +87,8 @@ struct AttnArgs {
   int mask_stride;    // entries per partial-tile mask: 128 (per row) or 1 (per key only)
   int mask_row_and;   // 127 or 0
   float scale_log2;
+  float* lse;  // optional [q_rows_total][H]: log2-sum-exp of the scaled scores per row
+  int n_heads;
   int* err;
 };
 
@@ -342,12 +344,16 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
       const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int q = 0; q < kHD / 8; ++q) reinterpret_cast<uint4*>(orow)[q] = z;
+      if (a.lse) a.lse[(int64_t)(q_start + row) * a.n_heads + col / kHD] = -INFINITY;
     }
     return;
   }
   if (!mbar_wait(B.o_final + h, 0, a.err, 13)) return;
   tc_fence_after();
   const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+  if (a.lse && store_row)  // O = sum_j 2^(s_j - lse) v_j
+    a.lse[(int64_t)(q_start + row) * a.n_heads + col / kHD] =
+        l_run > 0.f ? m_run + __log2f(l_run) : -INFINITY;
   uint32_t r[32];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -466,7 +472,7 @@ template <int kMaps>
 int attn_launch(const CUtensorMap& tmq, const KVMaps<kMaps>& kv, void* out, int64_t out_stride,
                 int32_t H, const int32_t* q_pairs, int32_t n_pairs, const int32_t* kv_tiles,
                 const uint32_t* row_masks, int mask_rows, const int32_t* order,
-                float softmax_scale, int32_t* dev_err, void* stream) {
+                float softmax_scale, float* lse, int32_t* dev_err, void* stream) {
   static bool attr_set = false;
   if (!attr_set) {
     HIER_CHECK_CUDA(cudaFuncSetAttribute(hier_attn_kernel<kMaps>,
@@ -485,6 +491,8 @@ int attn_launch(const CUtensorMap& tmq, const KVMaps<kMaps>& kv, void* out, int6
   args.mask_stride = mask_rows;
   args.mask_row_and = mask_rows - 1;
   args.scale_log2 = softmax_scale * 1.4426950408889634f;
+  args.lse = lse;
+  args.n_heads = H;
   args.err = dev_err;
   hier_attn_kernel<kMaps><<<n_pairs * H, 384, kSmemBytes, (cudaStream_t)stream>>>(tmq, kv, args);
   HIER_CHECK_CUDA(cudaGetLastError(), "hier_attn_kernel launch");
@@ -513,7 +521,7 @@ extern "C" int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stri
   if (!rc) rc = make_tmap_bf16_2d(&kv.v[0], v, (uint64_t)H * D, (uint64_t)kv_rows_total, kv_stride, 64, 64);
   if (rc) return rc;
   return attn_launch<1>(tmq, kv, out, out_stride, H, q_pairs, n_pairs, kv_tiles, row_masks, kBM,
-                        order, softmax_scale, dev_err, stream);
+                        order, softmax_scale, nullptr, dev_err, stream);
 }
 
 extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_t q_stride,
@@ -523,7 +531,8 @@ extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_
                                      const int32_t* q_pairs, int32_t n_pairs,
                                      const int32_t* kv_tiles, const uint32_t* tile_masks,
                                      int32_t mask_rows, const int32_t* order,
-                                     float softmax_scale, int32_t* dev_err, void* stream) {
+                                     float softmax_scale, float* lse, int32_t* dev_err,
+                                     void* stream) {
   clear_error();
   if (mask_rows != 1 && mask_rows != kBM) {
     set_error(HIER_EVALUE, "mask_rows must be 1 or %d; got %d", kBM, mask_rows);
@@ -566,6 +575,103 @@ extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_
     }
   }
   return attn_launch<HIER_MAX_KV_STREAMS>(tmq, kv, out, out_stride, H, q_pairs, n_pairs, kv_tiles,
-                                          tile_masks, mask_rows, order, softmax_scale, dev_err,
-                                          stream);
+                                          tile_masks, mask_rows, order, softmax_scale, lse,
+                                          dev_err, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Merge of partial attention rows computed over disjoint key sets
+// ---------------------------------------------------------------------------
+
+namespace hier {
+namespace {
+
+// x[r, h*D + i] = w * o[r, h*D + i], w[r, h] = 2^(lse - lse_max) (0 if no keys)
+__global__ void lse_prepare_kernel(const __nv_bfloat16* o, int64_t o_stride, const float* lse,
+                                   const float* lse_max, int64_t rows, int H, int D, float* x,
+                                   float* w) {
+  const int per = D / 8;  // threads per (row, head)
+  const int64_t n = rows * H * per;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t rh = t / per;
+    const int part = (int)(t % per);
+    const int64_t r = rh / H;
+    const int h = (int)(rh % H);
+    const float l = lse[rh], m = lse_max[rh];
+    const float wt = (l == -INFINITY || m == -INFINITY) ? 0.f : exp2f(l - m);
+    const uint4 raw = *reinterpret_cast<const uint4*>(o + r * o_stride + h * D + part * 8);
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    float4 a, b;
+    float2 f0 = __bfloat1622float2(p2[0]), f1 = __bfloat1622float2(p2[1]);
+    float2 f2 = __bfloat1622float2(p2[2]), f3 = __bfloat1622float2(p2[3]);
+    a = make_float4(f0.x * wt, f0.y * wt, f1.x * wt, f1.y * wt);
+    b = make_float4(f2.x * wt, f2.y * wt, f3.x * wt, f3.y * wt);
+    float4* dst = reinterpret_cast<float4*>(x + (r * H + h) * D + part * 8);
+    dst[0] = a;
+    dst[1] = b;
+    if (part == 0) w[rh] = wt;
+  }
+}
+
+__global__ void lse_finish_kernel(const float* x, const float* w, int64_t rows, int H, int D,
+                                  __nv_bfloat16* out, int64_t out_stride) {
+  const int per = D / 8;
+  const int64_t n = rows * H * per;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t rh = t / per;
+    const int part = (int)(t % per);
+    const int64_t r = rh / H;
+    const int h = (int)(rh % H);
+    const float ws = w[rh];
+    const float inv = ws > 0.f ? 1.f / ws : 0.f;
+    const float4* src = reinterpret_cast<const float4*>(x + (r * H + h) * D + part * 8);
+    const float4 a = src[0], b = src[1];
+    uint4 v;
+    v.x = pack_bf16x2(a.x * inv, a.y * inv);
+    v.y = pack_bf16x2(a.z * inv, a.w * inv);
+    v.z = pack_bf16x2(b.x * inv, b.y * inv);
+    v.w = pack_bf16x2(b.z * inv, b.w * inv);
+    *reinterpret_cast<uint4*>(out + r * out_stride + h * D + part * 8) = v;
+  }
+}
+
+int merge_grid(int64_t n) {
+  int64_t b = (n + 255) / 256;
+  return (int)(b < 1 ? 1 : (b > 148 * 32 ? 148 * 32 : b));
+}
+
+}  // namespace
+}  // namespace hier
+
+extern "C" int hier_lse_prepare(const void* o, int64_t o_stride, const float* lse,
+                                const float* lse_max, int64_t rows, int32_t H, int32_t D, float* x,
+                                float* w, void* stream) {
+  clear_error();
+  if (rows < 0 || H <= 0 || D <= 0 || D % 8 || o_stride % 8) {
+    set_error(HIER_EVALUE, "invalid merge shape rows=%lld H=%d D=%d", (long long)rows, H, D);
+    return HIER_EVALUE;
+  }
+  if (rows == 0) return HIER_OK;
+  const int64_t n = rows * H * (D / 8);
+  lse_prepare_kernel<<<merge_grid(n), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o), o_stride, lse, lse_max, rows, H, D, x, w);
+  HIER_CHECK_CUDA(cudaGetLastError(), "lse_prepare_kernel launch");
+  return HIER_OK;
+}
+
+extern "C" int hier_lse_finish(const float* x, const float* w, int64_t rows, int32_t H, int32_t D,
+                               void* out, int64_t out_stride, void* stream) {
+  clear_error();
+  if (rows < 0 || H <= 0 || D <= 0 || D % 8 || out_stride % 8) {
+    set_error(HIER_EVALUE, "invalid merge shape rows=%lld H=%d D=%d", (long long)rows, H, D);
+    return HIER_EVALUE;
+  }
+  if (rows == 0) return HIER_OK;
+  const int64_t n = rows * H * (D / 8);
+  lse_finish_kernel<<<merge_grid(n), 256, 0, (cudaStream_t)stream>>>(
+      x, w, rows, H, D, reinterpret_cast<__nv_bfloat16*>(out), out_stride);
+  HIER_CHECK_CUDA(cudaGetLastError(), "lse_finish_kernel launch");
+  return HIER_OK;
 }

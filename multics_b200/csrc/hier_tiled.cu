@@ -125,15 +125,15 @@ __device__ __forceinline__ int n_candidates(const TDims& d, int type, int Rb) {
 
 // Candidate c of a full-sequence segment (hier_tiled_attention.py:300-420):
 // sets its first pool row, width and validity.
-__device__ void full_candidate(const hier_tiled_grouping& g, const TDims& d, const TSeg& sg,
-                               int bs, int ret0, int Rb, int c, int* base, int* width,
-                               bool* valid) {
+__device__ void full_candidate(const int64_t* labels, const uint8_t* active, const TDims& d,
+                               const TSeg& sg, int bs, int ret0, int Rb, int c, int* base,
+                               int* width, bool* valid) {
   const int qf = bs + sg.qrel;
   auto ab = [&](int p, int f) { return (p * d.T + f) * d.L; };
   auto lb = [&](int gi, int f) { return (int)(d.A + (int64_t)(f * d.N + gi) * d.KL); };
   auto gb = [&](int f) { return (int)(d.GS + (int64_t)f * d.KG); };
-  auto lab = [&](int f, int p) { return g.labels[(int64_t)f * d.P + p]; };
-  auto act = [&](int f, int gi) { return g.active[(int64_t)f * d.N + gi] != 0; };
+  auto lab = [&](int f, int p) { return labels[(int64_t)f * d.P + p]; };
+  auto act = [&](int f, int gi) { return active[(int64_t)f * d.N + gi] != 0; };
   if (sg.type == 0) {
     if (c < Rb) {
       const int kf = ret0 + c;
@@ -277,7 +277,7 @@ __device__ void analyse_tiled(const hier_tiled_grouping& g, const TDims& d, int 
   for (int c = threadIdx.x; c < C; c += kThreads) {
     int base = 0, width = 0;
     bool valid = false;
-    if (d.mode == 0) full_candidate(g, d, sg, bs, ret0, Rb, c, &base, &width, &valid);
+    if (d.mode == 0) full_candidate(g.labels, g.active, d, sg, bs, ret0, Rb, c, &base, &width, &valid);
     else cached_candidate(g, d, sg, c, &base, &width, &valid, &missing);
     m.dw[c] = width;
     m.pool[c] = base;
@@ -431,6 +431,153 @@ __global__ void __launch_bounds__(kThreads)
                       : sg.type == 1 ? d.nA * d.npA + (s - d.nA) * d.npL
                                      : d.nA * d.npA + d.nLs * d.npL + (s - d.nA - d.nLs) * d.npG);
     segplan::emit_pairs(sg.q0, sg.ql, base, tile_base, n_tiles, o.q_pairs);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Player-sharded full-sequence plan
+// ---------------------------------------------------------------------------
+// One rank owns players [p0, p1).  Its query rows are its players' rows
+// followed by every hub row (local hubs frame-major, then global hubs); its
+// key streams are 0 = its players' rows, 1 = the hub rows (replicated),
+// 2 = the frames of remote group-mates it attends to (fetched before the
+// launch, unit (o, f) at slot remote_slot[o*T + f]).  Player segments get
+// their complete key sets; hub segments get the part of their key set this
+// rank holds (its players' rows, plus the hub rows when hub_keys is set) and
+// are merged across ranks from their log-sum-exp.
+
+struct SDims {
+  TDims t;
+  int p0, p1, n_own, hub_keys, group_major;
+  int n_seg, n_pairs;  // per layout
+};
+
+constexpr int kStatusMissingRemote = 8;  // a remote unit the plan needs is not in the buffer
+
+__device__ TSeg sseg_of(const SDims& sd, int layout, int s, int* qrel_frame) {
+  const TDims& d = sd.t;
+  TSeg r;
+  r.p = r.g = 0;
+  const int na = sd.n_own * d.n;
+  const int own_rows = sd.n_own * d.T * d.L;
+  if (s < na) {
+    r.type = 0;
+    r.p = sd.p0 + s / d.n;
+    r.qrel = s % d.n;
+    r.ql = d.L;
+  } else if (s < na + d.n * d.N) {
+    const int t = s - na;
+    r.type = 1;
+    r.qrel = t / d.N;
+    r.g = t % d.N;
+    r.ql = d.KL;
+  } else {
+    r.type = 2;
+    r.qrel = s - na - d.n * d.N;
+    r.ql = d.KG;
+  }
+  const int qf = layout * d.n + r.qrel;
+  *qrel_frame = qf;
+  r.q0 = r.type == 0   ? (r.p - sd.p0) * d.T * d.L + qf * d.L
+         : r.type == 1 ? own_rows + (qf * d.N + r.g) * d.KL
+                       : own_rows + d.T * d.N * d.KL + qf * d.KG;
+  return r;
+}
+
+__device__ void analyse_shard(const hier_shard_desc& g, const SDims& sd, int layout,
+                              const TSeg& sg, const SegSmem& m) {
+  const TDims& d = sd.t;
+  const int bs = layout * d.n, be = bs + d.n;
+  const int ret0 = max(0, be - d.R);
+  const int Rb = be - ret0;
+  const int C = n_candidates(d, sg.type, Rb);
+  if (threadIdx.x == 0) m.misc[3] = 0;
+  __syncthreads();
+  int missing = 0;
+  const int unit_rows = d.T * d.L;
+  for (int c = threadIdx.x; c < C; c += kThreads) {
+    int base = 0, width = 0;
+    bool valid = false;
+    full_candidate(g.labels, g.active, d, sg, bs, ret0, Rb, c, &base, &width, &valid);
+    int w = valid ? width : 0, key = 0;
+    if (w > 0) {
+      if (base < d.A) {
+        const int o = base / unit_rows, rem = base % unit_rows;
+        if (o >= sd.p0 && o < sd.p1) {
+          key = (o - sd.p0) * unit_rows + rem;
+        } else if (sg.type == 0) {
+          const int slot = g.remote_slot[o * d.T + rem / d.L];
+          if (slot < 0) {
+            missing = 1;
+            w = 0;
+          } else {
+            key = (2 << segplan::kStreamShift) | (slot * d.L + rem % d.L);
+          }
+        } else {
+          w = 0;  // another rank's keys: its partial covers them
+        }
+      } else if (sg.type == 0 || sd.hub_keys) {
+        int j = base - (int)d.A;  // hub row in sequence order
+        if (sd.group_major && j < d.T * d.N * d.KL) {
+          // local hubs stored group-major: (g, f, slot) at (g*T + f)*K_L + slot
+          const int f = j / (d.N * d.KL), gi = (j / d.KL) % d.N, slot = j % d.KL;
+          j = (gi * d.T + f) * d.KL + slot;
+        }
+        key = (1 << segplan::kStreamShift) | j;
+      } else {
+        w = 0;
+      }
+    }
+    m.w[c] = w;
+    m.key[c] = key;
+    m.pool[c] = base;
+  }
+  if (missing) atomicOr(&m.misc[3], kStatusMissingRemote);
+  __syncthreads();
+  segplan::analyse_runs(m, C);
+}
+
+__global__ void __launch_bounds__(kThreads)
+    shard_count_kernel(const hier_shard_desc g, const SDims sd, int32_t* n_boxes,
+                       int32_t* status) {
+  extern __shared__ int smem_i[];
+  const SegSmem m = segplan::seg_smem(smem_i, kMaxCand);
+  const int layout = blockIdx.y, s = blockIdx.x;
+  int qf;
+  const TSeg sg = sseg_of(sd, layout, s, &qf);
+  analyse_shard(g, sd, layout, sg, m);
+  if (threadIdx.x == 0) {
+    n_boxes[layout * sd.n_seg + s] = m.misc[2];
+    if (m.misc[3] && status) atomicOr(status, m.misc[3]);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    shard_build_kernel(const hier_shard_desc g, const SDims sd, const int32_t* n_boxes,
+                       int32_t* q_pairs, int32_t* kv_tiles, uint32_t* tile_masks,
+                       int32_t tile_capacity, int32_t* status) {
+  extern __shared__ int smem_i[];
+  const SegSmem m = segplan::seg_smem(smem_i, kMaxCand);
+  const TDims& d = sd.t;
+  const int layout = blockIdx.y, s = blockIdx.x;
+  int qf;
+  const TSeg sg = sseg_of(sd, layout, s, &qf);
+  analyse_shard(g, sd, layout, sg, m);
+  const int gs = layout * sd.n_seg + s;
+  const int tile_base = segplan::tile_base_of(n_boxes, gs, m.misc + 8);
+  const int n_tiles = (m.misc[2] + 1) >> 1;
+  if (tile_base + n_tiles > tile_capacity) {
+    if (threadIdx.x == 0 && status) atomicOr(status, kStatusTileOverflow);
+    return;
+  }
+  segplan::emit_plan(m, tile_base, kv_tiles, tile_masks);
+  if (sg.ql > 0) {
+    const int na = sd.n_own * d.n;
+    const int base = layout * sd.n_pairs +
+                     (sg.type == 0   ? s * d.npA
+                      : sg.type == 1 ? na * d.npA + (s - na) * d.npL
+                                     : na * d.npA + d.n * d.N * d.npL + (s - na - d.n * d.N) * d.npG);
+    segplan::emit_pairs(sg.q0, sg.ql, base, tile_base, n_tiles, q_pairs);
   }
 }
 
@@ -635,6 +782,102 @@ extern "C" int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_b
   HIER_CHECK_CUDA(cudaGetLastError(), "tiled_build_kernel launch");
   const int np = d.n_pairs * d.n_layouts;
   if (q_pairs && order && np > 0) {
+    order_by_work_kernel<8><<<(np + 127) / 128, 128, 0, s>>>(q_pairs, np, order);
+    HIER_CHECK_CUDA(cudaGetLastError(), "order_by_work_kernel launch");
+  }
+  return HIER_OK;
+}
+
+namespace {
+
+int make_sdims(const hier_shard_desc* g, SDims* sd, int64_t* tile_cap) {
+  if (!g) {
+    set_error(HIER_EVALUE, "hier_shard_desc is NULL");
+    return HIER_EVALUE;
+  }
+  hier_tiled_grouping tg;
+  memset(&tg, 0, sizeof(tg));
+  tg.mode = 0;
+  tg.P = g->P, tg.N = g->N, tg.L = g->L, tg.KL = g->KL, tg.KG = g->KG;
+  tg.n_block = g->n_block, tg.local_attn = g->local_attn, tg.direct = g->direct, tg.T = g->T;
+  tg.labels = g->labels, tg.active = g->active;
+  int64_t cap_full;
+  int rc = make_tdims(&tg, &sd->t, &cap_full);
+  if (rc) return rc;
+  if (g->p0 < 0 || g->p1 > g->P || g->p0 >= g->p1) {
+    set_error(HIER_EVALUE, "invalid player shard [%d, %d) of %d players", g->p0, g->p1, g->P);
+    return HIER_EVALUE;
+  }
+  if (g->direct && !g->remote_slot) {
+    set_error(HIER_EVALUE, "direct player edges need the remote unit table");
+    return HIER_EVALUE;
+  }
+  const TDims& d = sd->t;
+  sd->p0 = g->p0, sd->p1 = g->p1, sd->n_own = g->p1 - g->p0, sd->hub_keys = g->hub_keys != 0;
+  sd->group_major = g->hub_group_major != 0;
+  sd->n_seg = sd->n_own * d.n + d.n * d.N + d.n;
+  sd->n_pairs = sd->n_own * d.n * d.npA + d.n * d.N * d.npL + d.n * d.npG;
+  // bound: the full-sequence capacity (every player's segments) covers a shard
+  *tile_cap = cap_full;
+  const int64_t rows = (int64_t)sd->n_own * d.T * d.L;
+  if (rows >= (1 << segplan::kStreamShift)) {
+    set_error(HIER_EVALUE, "shard of %lld player rows exceeds %d", (long long)rows,
+              (1 << segplan::kStreamShift) - 1);
+    return HIER_EVALUE;
+  }
+  return HIER_OK;
+}
+
+}  // namespace
+
+extern "C" int hier_shard_sizes(const hier_shard_desc* g, hier_tiled_sizes_t* out) {
+  clear_error();
+  SDims sd;
+  int64_t cap;
+  int rc = make_sdims(g, &sd, &cap);
+  if (rc) return rc;
+  if (!out) {
+    set_error(HIER_EVALUE, "sizes output is NULL");
+    return HIER_EVALUE;
+  }
+  const TDims& d = sd.t;
+  out->n_layouts = d.n_layouts;
+  out->n_seg = sd.n_seg;
+  out->n_prog = 0;
+  out->n_pairs = sd.n_pairs;
+  out->tile_capacity = (int32_t)cap;
+  out->q_rows = (int64_t)sd.n_own * d.T * d.L + (int64_t)d.T * (d.N * d.KL + d.KG);
+  return HIER_OK;
+}
+
+extern "C" int hier_shard_plan(const hier_shard_desc* g, int32_t* n_boxes, int32_t* q_pairs,
+                               int32_t* kv_tiles, uint32_t* tile_masks, int32_t tile_capacity,
+                               int32_t* order, int32_t* status, void* stream) {
+  clear_error();
+  SDims sd;
+  int64_t cap;
+  int rc = make_sdims(g, &sd, &cap);
+  if (rc) return rc;
+  if (!n_boxes || !q_pairs || !kv_tiles || !tile_masks) {
+    set_error(HIER_EVALUE, "shard plan outputs missing");
+    return HIER_EVALUE;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t sm = tiled_smem_bytes(kMaxCand);
+  HIER_CHECK_CUDA(cudaFuncSetAttribute(shard_count_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                  "cudaFuncSetAttribute(shard_count_kernel)");
+  HIER_CHECK_CUDA(cudaFuncSetAttribute(shard_build_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                  "cudaFuncSetAttribute(shard_build_kernel)");
+  const dim3 grid(sd.n_seg, sd.t.n_layouts);
+  shard_count_kernel<<<grid, kThreads, sm, s>>>(*g, sd, n_boxes, status);
+  HIER_CHECK_CUDA(cudaGetLastError(), "shard_count_kernel launch");
+  shard_build_kernel<<<grid, kThreads, sm, s>>>(*g, sd, n_boxes, q_pairs, kv_tiles, tile_masks,
+                                                tile_capacity, status);
+  HIER_CHECK_CUDA(cudaGetLastError(), "shard_build_kernel launch");
+  const int np = sd.n_pairs * sd.t.n_layouts;
+  if (order && np > 0) {
     order_by_work_kernel<8><<<(np + 127) / 128, 128, 0, s>>>(q_pairs, np, order);
     HIER_CHECK_CUDA(cudaGetLastError(), "order_by_work_kernel launch");
   }

@@ -1,0 +1,279 @@
+"""Player-sharded hierarchical attention: one rank per GPU over NCCL.
+
+Each rank owns a contiguous range of whole players (uneven when the count
+does not divide).  Per layer:
+
+1. **exchange** - ranks send each other exactly the group-mate frames that
+   direct player edges need (``all_to_all_single``; with static groups kept
+   on one rank nothing moves);
+2. **attention** - one tcgen05 launch over the rank's query rows (its
+   players' rows, then every hub row) reading three key/value streams in
+   place: its players' rows, the hub rows, the received mate frames;
+3. **hub merge** - hub rows were computed over the keys each rank holds;
+   their partial results merge from the per-row log-sum-exp with an
+   all-reduce of the max and one all-reduce of the scaled partial sums.
+
+Hub tokens are replicated on every rank (``T*(N*K_L+K_G)`` rows, 1.6k at the
+benchmark shapes), so only mate frames and hub partials cross NVLink.
+Multi-rank host logic (topology, exchange order, merge) is exercised with
+``gloo`` ranks on CPU; the CUDA path requires the library.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import HierShardDesc, HierTiledSizes, check, ptr, stream_ptr
+
+__all__ = ["split_players", "ShardTopology", "ShardedHierAttention", "merge_hub_partials",
+           "exchange_mate_frames"]
+
+
+def split_players(P: int, world: int) -> List[Tuple[int, int]]:
+    """Contiguous player ranges per rank, the first ``P % world`` ranks one larger."""
+    if world < 1 or world > P:
+        raise ValueError(f"cannot shard {P} players over {world} ranks")
+    base, extra = divmod(P, world)
+    out, p = [], 0
+    for r in range(world):
+        n = base + (1 if r < extra else 0)
+        out.append((p, p + n))
+        p += n
+    return out
+
+
+class ShardTopology:
+    """Host-side description of one sharded layer (identical on every rank).
+
+    ``labels``: int64 ``[T, P]`` group labels (constant inside each block of
+    ``n_block`` frames).  ``needs[r]`` lists the remote units ``(o, f)`` (L rows
+    of player ``o`` at frame ``f``) rank ``r`` attends to through direct
+    edges, ordered by (owner rank, player, frame): the order of its remote
+    buffer and of the ``all_to_all`` receive splits."""
+
+    def __init__(self, *, P, T, L, N, KL, KG, n_block, local_attn, direct, labels, world, rank):
+        self.P, self.T, self.L, self.N, self.KL, self.KG = P, T, L, N, KL, KG
+        self.n_block, self.local_attn, self.direct = n_block, local_attn, bool(direct)
+        self.world, self.rank = world, rank
+        lab = np.asarray(labels, dtype=np.int64).reshape(T, P)
+        self.labels = lab
+        self.bounds = split_players(P, world)
+        self.owner = np.zeros(P, dtype=np.int64)
+        for r, (a, b) in enumerate(self.bounds):
+            self.owner[a:b] = r
+        self.p0, self.p1 = self.bounds[rank]
+        self.n_own = self.p1 - self.p0
+        self.hub_rows = T * (N * KL + KG)
+        self.own_rows = self.n_own * T * L
+        self.needs = [self._needs(r) for r in range(world)]
+        mine = self.needs[rank]
+        self.remote_slot = np.full(P * T, -1, dtype=np.int32)
+        for i, (o, f) in enumerate(mine):
+            self.remote_slot[o * T + f] = i
+        self.recv_units = [sum(1 for o, _ in mine if self.owner[o] == i) for i in range(world)]
+        self.send_units = [[u for u in self.needs[j] if self.owner[u[0]] == rank]
+                           for j in range(world)]
+        rows = []
+        for j in range(world):
+            for o, f in self.send_units[j]:
+                start = (o - self.p0) * T * L + f * L
+                rows.append(np.arange(start, start + L))
+        self.send_rows = (np.concatenate(rows) if rows else np.zeros(0, np.int64)).astype(np.int64)
+
+    def _needs(self, r):
+        a, b = self.bounds[r]
+        if not self.direct:
+            return []
+        n, T = self.n_block, self.T
+        units = set()
+        for p in range(a, b):
+            for qf in range(T):
+                bs = (qf // n) * n
+                for o in range(self.P):
+                    if o == p or self.labels[qf, o] != self.labels[qf, p]:
+                        continue
+                    if a <= o < b:
+                        continue
+                    for kf in range(bs, min(bs + n, T)):
+                        units.add((o, kf))
+        return sorted(units, key=lambda u: (self.owner[u[0]], u[0], u[1]))
+
+    def local_rows(self) -> np.ndarray:
+        """Sequence rows of this rank's query rows (own players, then hubs)."""
+        A = self.P * self.T * self.L
+        own = np.arange(self.p0 * self.T * self.L, self.p1 * self.T * self.L)
+        hubs = np.arange(A, A + self.hub_rows)
+        return np.concatenate([own, hubs])
+
+
+def _stream_arrays(streams):
+    n = len(streams)
+    kp = (ctypes.c_void_p * n)(*[k.data_ptr() for k, _ in streams])
+    vp = (ctypes.c_void_p * n)(*[v.data_ptr() for _, v in streams])
+    rows = (ctypes.c_int64 * n)(*[k.shape[0] for k, _ in streams])
+    strides = (ctypes.c_int64 * n)(*[k.stride(0) for k, _ in streams])
+    return n, kp, vp, rows, strides
+
+
+def exchange_mate_frames(topo: ShardTopology, k, v, remote, group=None, send_rows=None):
+    """``all_to_all`` of the group-mate frames each rank's direct edges need:
+    rank ``j`` receives, in its ``needs`` order, the ``[K | V]`` rows of the
+    units it needs into ``remote`` (``[>= units*L, 2*dim]``)."""
+    t = topo
+    if t.world == 1 or not t.direct:
+        return remote
+    import torch.distributed as dist
+
+    rows = send_rows if send_rows is not None else torch.from_numpy(t.send_rows).to(k.device)
+    dim = k.shape[1]
+    send = (torch.cat([k.index_select(0, rows), v.index_select(0, rows)], dim=1)
+            if rows.numel() else torch.empty((0, 2 * dim), dtype=k.dtype, device=k.device))
+    n_recv = sum(t.recv_units) * t.L
+    dist.all_to_all_single(remote[:n_recv], send, [n * t.L for n in t.recv_units],
+                           [len(u) * t.L for u in t.send_units], group=group)
+    return remote
+
+
+def merge_hub_partials(o_hub, lse_hub, H, D, group=None, world=1):
+    """Merge hub-row partial results across ranks in place.
+
+    ``o_hub`` bf16 ``[rows, H*D]`` (normalised over this rank's keys),
+    ``lse_hub`` fp32 ``[rows, H]`` (log2 units, -inf without keys)."""
+    if world == 1:
+        return o_hub
+    import torch.distributed as dist
+
+    rows = o_hub.shape[0]
+    lse_max = lse_hub.clone()
+    dist.all_reduce(lse_max, op=dist.ReduceOp.MAX, group=group)
+    buf = torch.empty(rows * H * D + rows * H, dtype=torch.float32, device=o_hub.device)
+    x = buf[: rows * H * D]
+    w = buf[rows * H * D:]
+    lib = _lib.lib()
+    s = stream_ptr(o_hub.device)
+    check(lib.hier_lse_prepare(ptr(o_hub), o_hub.stride(0), ptr(lse_hub), ptr(lse_max), rows, H,
+                               D, ptr(x), ptr(w), s))
+    dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
+    check(lib.hier_lse_finish(ptr(x), ptr(w), rows, H, D, ptr(o_hub), o_hub.stride(0), s))
+    return o_hub
+
+
+class ShardedHierAttention:
+    """One rank's sharded attention layer (inputs already projected and roped).
+
+    ``forward(q, k, v)`` takes this rank's rows in local order (its players'
+    ``n_own*T*L`` rows then all ``T*(N*K_L+K_G)`` hub rows), bf16
+    ``[rows, H*128]``, and returns the attention output for the same rows;
+    hub rows are identical on every rank after the merge."""
+
+    def __init__(self, topo: ShardTopology, num_heads: int, device, group=None):
+        self.topo = topo
+        self.H = num_heads
+        self.D = 128
+        self.dim = num_heads * 128
+        self.device = torch.device(device)
+        self.group = group
+        t = topo
+        dev = self.device
+        self._labels = torch.from_numpy(t.labels).to(dev).contiguous()
+        act = np.zeros((t.T, t.N), dtype=np.uint8)
+        for f in range(t.T):
+            for p in range(t.P):
+                act[f, t.labels[f, p]] = 1
+        self._active = torch.from_numpy(act).to(dev)
+        self._slots = torch.from_numpy(t.remote_slot).to(dev)
+        d = HierShardDesc()
+        d.P, d.N, d.L, d.KL, d.KG, d.T = t.P, t.N, t.L, t.KL, t.KG, t.T
+        d.n_block, d.local_attn, d.direct = t.n_block, t.local_attn, int(t.direct)
+        d.p0, d.p1, d.hub_keys = t.p0, t.p1, int(t.rank == 0)
+        d.hub_group_major = 1
+        d.labels, d.active, d.remote_slot = (self._labels.data_ptr(), self._active.data_ptr(),
+                                             self._slots.data_ptr())
+        self.desc = d
+        sz = HierTiledSizes()
+        lib = _lib.lib()
+        check(lib.hier_shard_sizes(ctypes.byref(d), ctypes.byref(sz)))
+        self.n_pairs = sz.n_layouts * sz.n_pairs
+        cap = max(sz.tile_capacity, 1)
+        self.q_rows = int(sz.q_rows)
+        self.n_boxes = torch.empty(sz.n_layouts * sz.n_seg, dtype=torch.int32, device=dev)
+        self.q_pairs = torch.empty((max(self.n_pairs, 1), 8), dtype=torch.int32, device=dev)
+        self.kv_tiles = torch.empty((cap, 4), dtype=torch.int32, device=dev)
+        self.tile_masks = torch.empty((cap, 4), dtype=torch.int32, device=dev)
+        self.order = torch.empty(max(self.n_pairs, 1), dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        check(lib.hier_shard_plan(ctypes.byref(d), ptr(self.n_boxes), ptr(self.q_pairs),
+                                  ptr(self.kv_tiles), ptr(self.tile_masks), cap, ptr(self.order),
+                                  ptr(self.status), stream_ptr(dev)))
+        self.send_rows = torch.from_numpy(t.send_rows).to(dev)
+        self.n_recv = sum(t.recv_units) * t.L
+        self.remote = torch.zeros((max(self.n_recv, 1), 2 * self.dim), dtype=torch.bfloat16,
+                                  device=dev)
+        self.lse = torch.empty((self.q_rows, self.H), dtype=torch.float32, device=dev)
+        # hub keys/values group-major, so that a group's hub tokens of
+        # consecutive frames are consecutive rows (one key run per group)
+        jl = np.arange(t.T * t.N * t.KL).reshape(t.N, t.T, t.KL)  # [g, f, slot]
+        g_i, f_i, s_i = np.meshgrid(np.arange(t.N), np.arange(t.T), np.arange(t.KL),
+                                    indexing="ij")
+        src = ((f_i * t.N + g_i) * t.KL + s_i).reshape(-1)
+        del jl
+        perm = np.concatenate([src, np.arange(t.T * t.N * t.KL, t.hub_rows)])
+        self.hub_perm = torch.from_numpy(perm.astype(np.int64)).to(dev)
+        self.hub_k = torch.empty((t.hub_rows, self.dim), dtype=torch.bfloat16, device=dev)
+        self.hub_v = torch.empty_like(self.hub_k)
+        from .attention import _dev_err
+        self.err = _dev_err(dev)
+
+    def check_status(self):
+        st = int(self.status.item())
+        if st:
+            raise RuntimeError(f"sharded plan status {st:#x} (8: missing remote unit, "
+                               "2: tile capacity)")
+
+    def exchange(self, k, v):
+        """Fill the remote buffer with the mate frames this rank needs."""
+        exchange_mate_frames(self.topo, k, v, self.remote, self.group, self.send_rows)
+
+    def fill_remote_from(self, k_all, v_all):
+        """Single-process stand-in for :meth:`exchange`: copy the needed mate
+        frames from full-sequence K/V (tests emulating several ranks)."""
+        t = self.topo
+        for i, (o, f) in enumerate(t.needs[t.rank]):
+            src = (o * t.T + f) * t.L
+            self.remote[i * t.L:(i + 1) * t.L, :self.dim] = k_all[src:src + t.L]
+            self.remote[i * t.L:(i + 1) * t.L, self.dim:] = v_all[src:src + t.L]
+
+    def attend(self, q, k, v, out):
+        t = self.topo
+        own, hub = t.own_rows, t.hub_rows
+        torch.index_select(k[own:own + hub], 0, self.hub_perm, out=self.hub_k)
+        torch.index_select(v[own:own + hub], 0, self.hub_perm, out=self.hub_v)
+        streams = [(k[:own], v[:own]), (self.hub_k, self.hub_v),
+                   (self.remote[:, :self.dim], self.remote[:, self.dim:])]
+        if self.n_recv == 0:
+            streams[2] = streams[0]
+        n, kp, vp, rows, strides = _stream_arrays(streams)
+        check(_lib.lib().hier_attn_fwd_streams(
+            ptr(q), q.shape[0], q.stride(0), n, kp, vp, rows, strides, ptr(out), out.stride(0),
+            self.H, self.D, ptr(self.q_pairs), self.n_pairs, ptr(self.kv_tiles),
+            ptr(self.tile_masks), 1, ptr(self.order), 1.0 / math.sqrt(self.D), ptr(self.lse),
+            ptr(self.err), stream_ptr(q.device)))
+
+    def forward(self, q, k, v, out=None):
+        t = self.topo
+        if q.shape != (self.q_rows, self.dim) or k.shape != q.shape or v.shape != q.shape:
+            raise ValueError(f"expected local rows [{self.q_rows}, {self.dim}], got "
+                             f"{tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}")
+        if out is None:
+            out = torch.empty_like(q)
+        self.exchange(k, v)
+        self.attend(q, k, v, out)
+        merge_hub_partials(out[t.own_rows:], self.lse[t.own_rows:], self.H, self.D,
+                           group=self.group, world=t.world)
+        return out

@@ -1,0 +1,101 @@
+"""Player-sharded layer on one GPU: every rank's plan, attention launch and
+the hub merge run in one process (the exchange copies the mate frames, the
+merge sums the partials), and the assembled output is compared with the
+oracle's dense-mask fp32 attention.  The NCCL version runs in
+test_gpu_multi.py when a box has two GPUs."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import hier_oracle as O
+from test_sharded_cpu import _regrouped_labels
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MIN_COS = 0.9995
+
+
+def _case(P, T, L, N, KL, KG, labels, H, seed):
+    S = P * T * L + T * (N * KL + KG)
+    g = torch.Generator().manual_seed(seed)
+    mk = lambda: (torch.randn((S, H * 128), generator=g) * 0.5).to(torch.bfloat16)  # noqa: E731
+    q, k, v = mk(), mk(), mk()
+    act = O.active_from_labels(labels, N)
+    dense = O.dense_mask(P, T, L, N, KL, KG, 1, -1, labels=labels, active=act, direct=True)
+    f = lambda t: t.float().numpy()  # noqa: E731
+    ref = O.masked_attention(f(q), f(k), f(v), H, lambda r0, r1: dense[r0:r1])
+    return q, k, v, ref
+
+
+def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v):
+    from multics_b200 import _lib
+    from multics_b200._lib import ptr, stream_ptr
+    from multics_b200.sharded import ShardedHierAttention, ShardTopology
+
+    S = q.shape[0]
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    out = torch.zeros((S, H * 128), dtype=torch.float32, device="cuda")
+    hub0 = P * T * L
+    hub_rows = S - hub0
+    lses, parts = [], []
+    for rank in range(world):
+        t = ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=1, local_attn=-1,
+                          direct=True, labels=labels, world=world, rank=rank)
+        sh = ShardedHierAttention(t, H, "cuda")
+        loc = torch.from_numpy(t.local_rows()).cuda()
+        ql, kl, vl = qc[loc].contiguous(), kc[loc].contiguous(), vc[loc].contiguous()
+        sh.fill_remote_from(kc, vc)
+        o = torch.empty_like(ql)
+        sh.attend(ql, kl, vl, o)
+        sh.check_status()
+        out[t.p0 * T * L:t.p1 * T * L] = o[:t.own_rows].float()
+        parts.append(o[t.own_rows:].clone())
+        lses.append(sh.lse[t.own_rows:].clone())
+    # hub merge: what the two all-reduces compute
+    lse_max = torch.stack(lses).amax(0)
+    lib = _lib.lib()
+    xs = torch.zeros((hub_rows, H * 128), dtype=torch.float32, device="cuda")
+    ws = torch.zeros((hub_rows, H), dtype=torch.float32, device="cuda")
+    for o_h, l_h in zip(parts, lses):
+        x = torch.empty_like(xs)
+        w = torch.empty_like(ws)
+        _lib.check(lib.hier_lse_prepare(ptr(o_h), o_h.stride(0), ptr(l_h), ptr(lse_max), hub_rows,
+                                        H, 128, ptr(x), ptr(w), stream_ptr()))
+        xs += x
+        ws += w
+    merged = torch.empty((hub_rows, H * 128), dtype=torch.bfloat16, device="cuda")
+    _lib.check(lib.hier_lse_finish(ptr(xs), ptr(ws), hub_rows, H, 128, ptr(merged),
+                                   merged.stride(0), stream_ptr()))
+    out[hub0:] = merged.float()
+    return out.cpu().numpy()
+
+
+def _check(o, ref):
+    assert np.isfinite(o).all()
+    err = np.abs(o - ref).max()
+    cos = (o * ref).sum() / (np.linalg.norm(o) * np.linalg.norm(ref))
+    assert err <= MAX_ABS, err
+    assert cos >= MIN_COS, cos
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_sharded_dynamic_groups_match_oracle(world):
+    """Config-4 shape in miniature: 8 players, 4 groups of 2 regrouped every
+    3 frames (mates move between ranks)."""
+    P, T, L, N, KL, KG, H = 8, 6, 40, 4, 4, 3, 2
+    lab = _regrouped_labels(P, T, 3, seed=3)
+    q, k, v, ref = _case(P, T, L, N, KL, KG, lab, H, seed=1)
+    _check(_run_sharded(P, T, L, N, KL, KG, lab, H, world, q, k, v), ref)
+
+
+@pytest.mark.parametrize("world", [3, 8])
+def test_sharded_uneven_players_match_oracle(world):
+    """Config-5 grouping in miniature: 10 players in groups (3,3,2,2)."""
+    P, T, L, N, KL, KG, H = 10, 4, 24, 4, 3, 2, 2
+    lab = np.array([[0, 0, 0, 1, 1, 1, 2, 2, 3, 3]] * T)
+    q, k, v, ref = _case(P, T, L, N, KL, KG, lab, H, seed=2)
+    _check(_run_sharded(P, T, L, N, KL, KG, lab, H, world, q, k, v), ref)

@@ -1,0 +1,114 @@
+"""Host logic of the player-sharded layer on CPU: player split, the remote
+units each rank's direct edges need (checked against the dense mask), and
+the all_to_all exchange order with two gloo ranks."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import hier_oracle as O
+
+
+def _regrouped_labels(P, T, every, seed, group_size=2):
+    rng = np.random.default_rng(seed)
+    lab = np.zeros((T, P), np.int64)
+    for t0 in range(0, T, every):
+        perm = rng.permutation(P)
+        row = np.empty(P, np.int64)
+        row[perm] = np.arange(P) // group_size
+        lab[t0:t0 + every] = row
+    return lab
+
+
+def test_split_players():
+    from multics_b200.sharded import split_players
+
+    assert split_players(8, 8) == [(i, i + 1) for i in range(8)]
+    assert split_players(10, 8) == [(0, 2), (2, 4), (4, 5), (5, 6), (6, 7), (7, 8), (8, 9), (9, 10)]
+    assert split_players(4, 1) == [(0, 4)]
+    with pytest.raises(ValueError):
+        split_players(2, 3)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("n_block", [1, 3])
+def test_remote_units_match_dense_mask(world, n_block):
+    from multics_b200.sharded import ShardTopology
+
+    P, T, L, N, KL, KG = 8, 6, 2, 4, 2, 2
+    lab = _regrouped_labels(P, T, 3, seed=world)
+    act = O.active_from_labels(lab, N)
+    dense = O.dense_mask(P, T, L, N, KL, KG, n_block, -1, labels=lab, active=act, direct=True)
+    for rank in range(world):
+        t = ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=n_block, local_attn=-1,
+                          direct=True, labels=lab, world=world, rank=rank)
+        rows = np.arange(t.p0 * T * L, t.p1 * T * L)
+        cols = np.nonzero(dense[rows].any(0))[0]
+        want = set()
+        for c in cols:
+            if c < P * T * L:
+                o, f = c // (T * L), (c % (T * L)) // L
+                if not (t.p0 <= o < t.p1):
+                    want.add((o, f))
+        assert set(t.needs[rank]) == want
+        # every slot of the remote table points at its own unit
+        for i, (o, f) in enumerate(t.needs[rank]):
+            assert t.remote_slot[o * T + f] == i
+
+
+def test_static_groups_on_one_rank_exchange_nothing():
+    from multics_b200.sharded import ShardTopology
+
+    lab = np.array([[0, 0, 1, 1]] * 4)
+    t = ShardTopology(P=4, T=4, L=3, N=2, KL=2, KG=1, n_block=1, local_attn=-1, direct=True,
+                      labels=lab, world=2, rank=0)
+    assert t.needs == [[], []] and t.send_rows.size == 0
+
+
+def _exchange_rank(rank, world, port, q):
+    import torch.distributed as dist
+
+    from multics_b200.sharded import ShardTopology, exchange_mate_frames
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        P, T, L, N, KL, KG, dim = 8, 6, 3, 4, 2, 2, 4
+        lab = _regrouped_labels(P, T, 3, seed=7)
+        S = P * T * L + T * (N * KL + KG)
+        k_all = torch.arange(S * dim, dtype=torch.float32).reshape(S, dim)
+        v_all = -k_all
+        t = ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=1, local_attn=-1,
+                          direct=True, labels=lab, world=world, rank=rank)
+        loc = torch.from_numpy(t.local_rows())
+        k, v = k_all[loc], v_all[loc]
+        n = sum(t.recv_units) * L
+        remote = torch.full((max(n, 1), 2 * dim), float("nan"))
+        exchange_mate_frames(t, k, v, remote)
+        ok = True
+        for i, (o, f) in enumerate(t.needs[rank]):
+            src = (o * T + f) * L
+            ok &= torch.equal(remote[i * L:(i + 1) * L, :dim], k_all[src:src + L])
+            ok &= torch.equal(remote[i * L:(i + 1) * L, dim:], v_all[src:src + L])
+        q.put((rank, bool(ok), len(t.needs[rank])))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_exchange_with_two_gloo_ranks():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = 29600 + os.getpid() % 200
+    procs = [ctx.Process(target=_exchange_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    res = sorted(q.get() for _ in range(2))
+    assert all(p.exitcode == 0 for p in procs)
+    assert [r[1] for r in res] == [True, True]
+    assert all(r[2] > 0 for r in res)  # dynamic groups do cross ranks
