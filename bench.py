@@ -41,6 +41,8 @@ def parse():
                     help="cfg2 (default at 1 GPU) or cfg4/cfg5 (default cfg4 when sharded)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--transport", default="peer", choices=["peer", "exchange"],
+                    help="sharded runs: how group-mate frames on other GPUs are read")
     return ap.parse_args()
 
 
@@ -156,13 +158,20 @@ def run_sharded(args, rank, world, local_rank):
     del bm, inp
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    sh = ShardedHierAttention(topo, cfg.H, dev)
+    sh = ShardedHierAttention(topo, cfg.H, dev, transport=args.transport)
     torch.cuda.synchronize()
     plan_ms = (time.perf_counter() - t0) * 1e3
     sh.check_status()
     q_buf = torch.empty_like(qx)
-    k_buf = torch.empty_like(qx)
     o_buf = torch.empty_like(qx)
+    if sh.transport == "peer":
+        # K is produced straight into the rank's symmetric buffer; V (a layer
+        # input) lives there as well
+        k_buf = sh.k_buffer()
+        sh.v_buffer().copy_(v)
+        v = sh.v_buffer()
+    else:
+        k_buf = torch.empty_like(qx)
     marks = {}
 
     def step(i=None):
@@ -232,7 +241,8 @@ def run_sharded(args, rank, world, local_rank):
                                f"N={cfg.N} groups (regroup every {cfg.regroup_every} frames), "
                                f"K_L={cfg.KL}, K_G={cfg.KG}, H={cfg.H}x{cfg.D}",
                    "S": S, "useful_pairs": pairs, "useful_gflop_per_step": useful_flops / 1e9,
-                   "parallelism": f"players sharded x{world} (ranks own {topo.bounds})",
+                   "parallelism": f"players sharded x{world} (ranks own {topo.bounds}); "
+                                  f"mate frames: {sh.transport}",
                    "remote_units_rank0": len(topo.needs[0]),
                    "l2": "inputs larger than L2"},
         "breakdown_ms": {k: round(v_, 4) for k, v_ in parts.items()},
@@ -266,6 +276,8 @@ def run_e2e_sharded(args, cfg, topo, sh, qx, kx, v, cam, ft, w, dev, useful_flop
     ho = torch.empty_like(hq).pin_memory()
     dq, dk, dv, dc = (torch.empty_like(t, device=dev) for t in (hq, hk, hv, hc))
     qb, kb = torch.empty_like(dq), torch.empty_like(dq)
+    if sh.transport == "peer":
+        dv, kb = sh.v_buffer(), sh.k_buffer()
     stream = torch.cuda.current_stream(dev)
 
     def step():
@@ -563,8 +575,22 @@ def main():
         import torch
         import torch.distributed as dist
 
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        # communicator set-up may print a banner on stdout, which carries only
+        # the result line: send it to stderr while the communicator forms
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local_rank))
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     if world == 1 and args.config == "cfg2":
         line = run_ours(args, rank, world, local_rank)
     else:

@@ -365,9 +365,11 @@ int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_boxes, const
  * rank owns players [p0, p1); its query rows are its players' rows (in
  * sequence order) followed by every hub row (T*N*K_L local, then T*K_G
  * global); its key/value streams for hier_attn_fwd_streams are
- *   0 = its players' rows, 1 = the hub rows, 2 = remote group-mate frames
- *   (unit (o, f) = the L rows of player o at frame f, at slot
- *   remote_slot[o*T + f] of the remote buffer, -1 if absent).
+ *   0 = its players' rows, 1 = the hub rows, and for each remote group-mate
+ *   unit (o, f) (the L rows of player o at frame f) the stream-packed first
+ *   row remote_key[o*T + f] = (stream << 24) | row (-1 if absent): a buffer
+ *   of frames fetched before the launch, or the owning rank's buffer mapped
+ *   from its GPU (read in place over NVLink).
  * Player rows get their full key sets; hub rows get the keys this rank holds
  * (its players' rows, plus the hub rows if hub_keys) and are merged across
  * ranks with hier_lse_prepare / hier_lse_finish.  No reference counterpart
@@ -381,7 +383,7 @@ typedef struct hier_shard_desc {
                               (g*T + f)*K_L + slot, then the global hubs frame-major */
   const int64_t* labels;      /* [T, P] */
   const uint8_t* active;      /* [T, N] */
-  const int32_t* remote_slot; /* [P*T] */
+  const int32_t* remote_key;  /* [P*T] */
 } hier_shard_desc;
 
 /* n_layouts, n_seg, n_pairs (per layout), tile_capacity, q_rows of a shard. */

@@ -91,7 +91,7 @@ class HierShardDesc(ctypes.Structure):
         ("P", c_int32), ("N", c_int32), ("L", c_int32), ("KL", c_int32), ("KG", c_int32),
         ("T", c_int32), ("n_block", c_int32), ("local_attn", c_int32), ("direct", c_int32),
         ("p0", c_int32), ("p1", c_int32), ("hub_keys", c_int32), ("hub_group_major", c_int32),
-        ("labels", c_void_p), ("active", c_void_p), ("remote_slot", c_void_p),
+        ("labels", c_void_p), ("active", c_void_p), ("remote_key", c_void_p),
     ]
 
 

@@ -440,8 +440,9 @@ __global__ void __launch_bounds__(kThreads)
 // One rank owns players [p0, p1).  Its query rows are its players' rows
 // followed by every hub row (local hubs frame-major, then global hubs); its
 // key streams are 0 = its players' rows, 1 = the hub rows (replicated),
-// 2 = the frames of remote group-mates it attends to (fetched before the
-// launch, unit (o, f) at slot remote_slot[o*T + f]).  Player segments get
+// and for the frames of remote group-mates the stream-packed row given by
+// remote_key[o*T + f] (a buffer of fetched frames, or the owning rank's own
+// buffer read over NVLink).  Player segments get
 // their complete key sets; hub segments get the part of their key set this
 // rank holds (its players' rows, plus the hub rows when hub_keys is set) and
 // are merged across ranks from their log-sum-exp.
@@ -506,12 +507,12 @@ __device__ void analyse_shard(const hier_shard_desc& g, const SDims& sd, int lay
         if (o >= sd.p0 && o < sd.p1) {
           key = (o - sd.p0) * unit_rows + rem;
         } else if (sg.type == 0) {
-          const int slot = g.remote_slot[o * d.T + rem / d.L];
-          if (slot < 0) {
+          const int unit_key = g.remote_key[o * d.T + rem / d.L];
+          if (unit_key < 0) {
             missing = 1;
             w = 0;
           } else {
-            key = (2 << segplan::kStreamShift) | (slot * d.L + rem % d.L);
+            key = unit_key + rem % d.L;
           }
         } else {
           w = 0;  // another rank's keys: its partial covers them
@@ -808,7 +809,7 @@ int make_sdims(const hier_shard_desc* g, SDims* sd, int64_t* tile_cap) {
     set_error(HIER_EVALUE, "invalid player shard [%d, %d) of %d players", g->p0, g->p1, g->P);
     return HIER_EVALUE;
   }
-  if (g->direct && !g->remote_slot) {
+  if (g->direct && !g->remote_key) {
     set_error(HIER_EVALUE, "direct player edges need the remote unit table");
     return HIER_EVALUE;
   }

@@ -86,6 +86,23 @@ class ShardTopology:
                 rows.append(np.arange(start, start + L))
         self.send_rows = (np.concatenate(rows) if rows else np.zeros(0, np.int64)).astype(np.int64)
 
+    def remote_keys(self, transport: str) -> np.ndarray:
+        """int32 ``[P*T]``: stream-packed first row of every remote unit this
+        rank reads (-1 elsewhere).  ``"exchange"``: slot ``i`` of the received
+        buffer (stream 2); ``"peer"``: the owning rank's own rows, stream
+        ``2 + j`` for the ``j``-th other rank."""
+        keys = np.full(self.P * self.T, -1, dtype=np.int64)
+        others = [r for r in range(self.world) if r != self.rank]
+        for i, (o, f) in enumerate(self.needs[self.rank]):
+            if transport == "exchange":
+                keys[o * self.T + f] = (2 << 24) | (i * self.L)
+            else:
+                owner = int(self.owner[o])
+                p0 = self.bounds[owner][0]
+                keys[o * self.T + f] = ((2 + others.index(owner)) << 24) | \
+                    ((o - p0) * self.T * self.L + f * self.L)
+        return keys.astype(np.int32)
+
     def _needs(self, r):
         a, b = self.bounds[r]
         if not self.direct:
@@ -170,9 +187,19 @@ class ShardedHierAttention:
     ``forward(q, k, v)`` takes this rank's rows in local order (its players'
     ``n_own*T*L`` rows then all ``T*(N*K_L+K_G)`` hub rows), bf16
     ``[rows, H*128]``, and returns the attention output for the same rows;
-    hub rows are identical on every rank after the merge."""
+    hub rows are identical on every rank after the merge.
 
-    def __init__(self, topo: ShardTopology, num_heads: int, device, group=None):
+    ``transport`` selects how group-mate frames on other ranks are read:
+    ``"exchange"`` fetches them with ``all_to_all`` before the launch;
+    ``"peer"`` keeps every rank's K/V in symmetric memory and the attention
+    kernel reads the other ranks' rows in place over NVLink (plain TMA loads
+    of peer memory, no copy).  In peer mode K and V must be written into
+    :meth:`k_buffer` / :meth:`v_buffer` (other tensors are copied there)."""
+
+    def __init__(self, topo: ShardTopology, num_heads: int, device, group=None,
+                 transport: str = "exchange"):
+        if transport not in ("exchange", "peer"):
+            raise ValueError(f"unknown transport {transport!r}")
         self.topo = topo
         self.H = num_heads
         self.D = 128
@@ -181,20 +208,21 @@ class ShardedHierAttention:
         self.group = group
         t = topo
         dev = self.device
+        self.transport = transport if (t.world > 1 and t.direct) else "exchange"
         self._labels = torch.from_numpy(t.labels).to(dev).contiguous()
         act = np.zeros((t.T, t.N), dtype=np.uint8)
         for f in range(t.T):
             for p in range(t.P):
                 act[f, t.labels[f, p]] = 1
         self._active = torch.from_numpy(act).to(dev)
-        self._slots = torch.from_numpy(t.remote_slot).to(dev)
+        self._keys = torch.from_numpy(t.remote_keys(self.transport)).to(dev)
         d = HierShardDesc()
         d.P, d.N, d.L, d.KL, d.KG, d.T = t.P, t.N, t.L, t.KL, t.KG, t.T
         d.n_block, d.local_attn, d.direct = t.n_block, t.local_attn, int(t.direct)
         d.p0, d.p1, d.hub_keys = t.p0, t.p1, int(t.rank == 0)
         d.hub_group_major = 1
-        d.labels, d.active, d.remote_slot = (self._labels.data_ptr(), self._active.data_ptr(),
-                                             self._slots.data_ptr())
+        d.labels, d.active, d.remote_key = (self._labels.data_ptr(), self._active.data_ptr(),
+                                            self._keys.data_ptr())
         self.desc = d
         sz = HierTiledSizes()
         lib = _lib.lib()
@@ -212,23 +240,57 @@ class ShardedHierAttention:
                                   ptr(self.kv_tiles), ptr(self.tile_masks), cap, ptr(self.order),
                                   ptr(self.status), stream_ptr(dev)))
         self.send_rows = torch.from_numpy(t.send_rows).to(dev)
-        self.n_recv = sum(t.recv_units) * t.L
+        self.n_recv = sum(t.recv_units) * t.L if self.transport == "exchange" else 0
         self.remote = torch.zeros((max(self.n_recv, 1), 2 * self.dim), dtype=torch.bfloat16,
                                   device=dev)
         self.lse = torch.empty((self.q_rows, self.H), dtype=torch.float32, device=dev)
         # hub keys/values group-major, so that a group's hub tokens of
         # consecutive frames are consecutive rows (one key run per group)
-        jl = np.arange(t.T * t.N * t.KL).reshape(t.N, t.T, t.KL)  # [g, f, slot]
         g_i, f_i, s_i = np.meshgrid(np.arange(t.N), np.arange(t.T), np.arange(t.KL),
                                     indexing="ij")
         src = ((f_i * t.N + g_i) * t.KL + s_i).reshape(-1)
-        del jl
         perm = np.concatenate([src, np.arange(t.T * t.N * t.KL, t.hub_rows)])
         self.hub_perm = torch.from_numpy(perm.astype(np.int64)).to(dev)
         self.hub_k = torch.empty((t.hub_rows, self.dim), dtype=torch.bfloat16, device=dev)
         self.hub_v = torch.empty_like(self.hub_k)
         from .attention import _dev_err
         self.err = _dev_err(dev)
+        self._sym = None
+        self._peers = []
+        if self.transport == "peer":
+            self._setup_peer()
+
+    def _setup_peer(self):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        t = self.topo
+        group = self.group if self.group is not None else dist.group.WORLD
+        if hasattr(symm, "enable_symm_mem_for_group"):
+            try:
+                symm.enable_symm_mem_for_group(group.group_name)
+            except Exception:  # already enabled / not needed in this torch version
+                pass
+        rows = max(b - a for a, b in t.bounds) * t.T * t.L + t.hub_rows
+        self._sym_rows = rows
+        self._sym = symm.empty((2, rows, self.dim), dtype=torch.bfloat16, device=self.device)
+        self._sym.zero_()
+        self._handle = symm.rendezvous(self._sym, group)
+        for r in range(t.world):
+            if r == t.rank:
+                continue
+            buf = self._handle.get_buffer(r, (2, rows, self.dim), torch.bfloat16)
+            a, b = t.bounds[r]
+            n = (b - a) * t.T * t.L
+            self._peers.append((buf[0, :n], buf[1, :n]))
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+
+    def k_buffer(self):
+        """Where K of this rank's rows should be written (peer transport)."""
+        return self._sym[0, :self.q_rows] if self._sym is not None else None
+
+    def v_buffer(self):
+        return self._sym[1, :self.q_rows] if self._sym is not None else None
 
     def check_status(self):
         st = int(self.status.item())
@@ -237,7 +299,18 @@ class ShardedHierAttention:
                                "2: tile capacity)")
 
     def exchange(self, k, v):
-        """Fill the remote buffer with the mate frames this rank needs."""
+        """Make the other ranks' mate frames readable: fetch them
+        (``exchange``) or order the peer reads after every rank's writes
+        (``peer``: a one-element all-reduce on the stream)."""
+        if self.transport == "peer":
+            import torch.distributed as dist
+
+            if k.data_ptr() != self.k_buffer().data_ptr():
+                self.k_buffer().copy_(k)
+            if v.data_ptr() != self.v_buffer().data_ptr():
+                self.v_buffer().copy_(v)
+            dist.all_reduce(self._flag, group=self.group)
+            return
         exchange_mate_frames(self.topo, k, v, self.remote, self.group, self.send_rows)
 
     def fill_remote_from(self, k_all, v_all):
@@ -252,12 +325,15 @@ class ShardedHierAttention:
     def attend(self, q, k, v, out):
         t = self.topo
         own, hub = t.own_rows, t.hub_rows
+        if self.transport == "peer":
+            k, v = self.k_buffer(), self.v_buffer()
         torch.index_select(k[own:own + hub], 0, self.hub_perm, out=self.hub_k)
         torch.index_select(v[own:own + hub], 0, self.hub_perm, out=self.hub_v)
-        streams = [(k[:own], v[:own]), (self.hub_k, self.hub_v),
-                   (self.remote[:, :self.dim], self.remote[:, self.dim:])]
-        if self.n_recv == 0:
-            streams[2] = streams[0]
+        streams = [(k[:own], v[:own]), (self.hub_k, self.hub_v)]
+        if self.transport == "peer":
+            streams += self._peers
+        else:
+            streams.append((self.remote[:, :self.dim], self.remote[:, self.dim:]))
         n, kp, vp, rows, strides = _stream_arrays(streams)
         check(_lib.lib().hier_attn_fwd_streams(
             ptr(q), q.shape[0], q.stride(0), n, kp, vp, rows, strides, ptr(out), out.stride(0),

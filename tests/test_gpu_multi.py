@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 WORLD = 2
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, q, transport):
     import datetime
 
     import torch.distributed as dist
@@ -39,8 +39,10 @@ def _rank_main(rank, world, port, q):
         loc = torch.from_numpy(t.local_rows())
         dev = torch.device("cuda", rank)
         ql, kl, vl = (x[loc].contiguous().to(dev) for x in (qa, ka, va))
-        sh = ShardedHierAttention(t, H, dev)
+        sh = ShardedHierAttention(t, H, dev, transport=transport)
         out = sh.forward(ql, kl, vl)
+        out2 = sh.forward(ql, kl, vl)  # a second step over the same buffers
+        assert torch.equal(out, out2)
         torch.cuda.synchronize(dev)
         sh.check_status()
         act = O.active_from_labels(lab, N)
@@ -58,13 +60,16 @@ def _rank_main(rank, world, port, q):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD,
                     reason="needs two GPUs")
-def test_sharded_layer_over_nccl():
+@pytest.mark.parametrize("transport", ["exchange", "peer"])
+def test_sharded_layer_over_nccl(transport):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = 29700 + os.getpid() % 200
-    procs = [ctx.Process(target=_rank_main, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    port += 1 if transport == "peer" else 0
+    procs = [ctx.Process(target=_rank_main, args=(r, WORLD, port, q, transport))
+             for r in range(WORLD)]
     for p in procs:
         p.start()
     for p in procs:
