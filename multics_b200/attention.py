@@ -259,3 +259,158 @@ class SelfAttention(nn.Module):
         q, k, v = self.project_qkv(x, freqs, cam_tokens)
         out = attention_from_plan(q, k, v, mask, self.num_heads)
         return self.o(out.unsqueeze(0))
+
+
+_INFER_KERNELS = ("sdpa", "segmented", "tiled128", "packed_varlen", "paged_kv")
+
+
+def _causal_forward_hier_hub(self, x, freqs, kv_cache, current_start=0, num_frames=None,
+                             num_players=None, num_hub_tokens=None, cam_tokens=None,
+                             group_labels=None, active_group=None, direct_player=False,
+                             membership=None, global_only=None):
+    """Cached hierarchical self-attention of one block of ``num_frames`` new
+    frames (``SelfAttention.causal_forward_hier_hub``,
+    ``multics/models/attention.py:456-1005``): projections, the fused
+    camera/RMSNorm/RoPE prologue, rolling-cache appends in the reference's
+    cache format, then the tcgen05 attention over the caches in place and the
+    output projection.  Every ``WAN_HIER_INFER_KERNEL`` value selects the same
+    B200 kernel; the reference's value checks and refusals are kept."""
+    import os
+
+    from .cached import hierarchical_cached_attention
+    from .hier_masks import (_prepare_hier_group_tensors, _prepare_hier_membership_tensors,
+                             _refuse_membership_on_scalar_kernel)
+    from .kv_cache import rolling_bool_cache_append, rolling_cache_append
+
+    b, s = x.shape[:2]
+    H, D = self.num_heads, self.head_dim
+    P = int(num_players if num_players is not None else kv_cache["num_players"])
+    N = int(kv_cache["num_groups"])
+    KL = int(kv_cache["num_local_hub_tokens"])
+    KG = int(kv_cache["num_global_hub_tokens"])
+    no_local = bool(getattr(self, "hier_no_local_hub", False))
+    if bool(kv_cache.get("hier_no_local_hub", False)) != no_local:
+        raise ValueError("hier_no_local_hub mismatch between SelfAttention and KV cache")
+    n_frames = int(num_frames)
+    K_total = int(num_hub_tokens if num_hub_tokens is not None else N * KL + KG)
+    if K_total != N * KL + KG:
+        raise ValueError(f"hier_hub K_total mismatch: {K_total} != {N}*{KL}+{KG}")
+    if no_local and (KL != 0 or KG <= 0):
+        raise ValueError(
+            f"hier_no_local_hub cached attention requires K_L=0 and K_G>0; got K_L={KL}, K_G={KG}")
+    use_membership = membership is not None
+    mem_full = go_full = None
+    if use_membership:
+        mem_full, go_full, active = _prepare_hier_membership_tensors(
+            membership, global_only, active_group, P, n_frames, N, x.device, allow_full_t=True)
+        labels = None
+    else:
+        labels, active = _prepare_hier_group_tensors(group_labels, active_group, P, n_frames, N,
+                                                     x.device)
+        if n_frames > 1 and labels.numel() and not torch.equal(labels,
+                                                               labels[:1].expand_as(labels)):
+            raise ValueError(
+                "hier_hub cached inference requires group_labels constant inside each latent block")
+    hub_len = n_frames * K_total
+    agent_len = s - hub_len
+    if agent_len <= 0 or agent_len % (P * n_frames) != 0:
+        raise ValueError(
+            f"hier_hub causal seq shape invalid: S={s}, hub_len={hub_len}, P={P}, n={n_frames}")
+    L = agent_len // (P * n_frames)
+    n_block = int(self.num_frame_per_block)
+    local_attn = int(self.local_attn_size)
+    dev = x.device
+    if freqs.shape[0] != s:
+        raise ValueError("hier_hub causal_forward expects freqs.shape[0] == seq_len")
+    if b != 1:
+        raise NotImplementedError(f"B200 cached hierarchical inference supports B=1; got B={b}")
+    kernel = os.environ.get("WAN_HIER_INFER_KERNEL", "sdpa").strip().lower()
+    if kernel not in _INFER_KERNELS:
+        raise ValueError(
+            "WAN_HIER_INFER_KERNEL must be 'sdpa', 'segmented', 'tiled128', 'packed_varlen', "
+            f"or 'paged_kv', got {kernel!r}")
+    if kernel in ("segmented", "tiled128"):
+        if no_local:
+            raise NotImplementedError(
+                "hier_no_local_hub cached inference supports sdpa, packed_varlen, or paged_kv; got "
+                + kernel)
+        if use_membership:
+            _refuse_membership_on_scalar_kernel(infer_kernel=kernel)
+
+    q, k, v = self.project_qkv(x, freqs, cam_tokens)  # [s, H*D] rows, roped q/k
+    q4, k4, v4 = (t.view(1, s, H, D) for t in (q, k, v))
+    local_start = agent_len
+    global_start = agent_len + n_frames * N * KL
+    retention = local_attn + n_frames if local_attn != -1 else -1
+    start_frame = current_start // max(P * L, 1)
+    end_frame = start_frame + n_frames - 1
+    if use_membership:
+        T_full = int(mem_full.shape[0])
+        if start_frame < 0 or start_frame + n_frames > T_full:
+            raise ValueError(f"hier_hub membership T={T_full} does not cover cached block "
+                             f"[{start_frame},{start_frame + n_frames})")
+        mem_blk = mem_full[start_frame:start_frame + n_frames]
+        go_blk = go_full[start_frame:start_frame + n_frames]
+        active = active[start_frame:start_frame + n_frames]
+        if n_frames > 1:
+            if not torch.equal(mem_blk, mem_blk[:1].expand_as(mem_blk)):
+                raise ValueError(
+                    "hier_hub cached inference requires membership constant inside each latent block")
+            if not torch.equal(go_blk, go_blk[:1].expand_as(go_blk)):
+                raise ValueError(
+                    "hier_hub cached inference requires global_only constant inside each latent block")
+    # append this block's keys/values to the rolling caches
+    agent_k = k4[:, :agent_len].reshape(1, P, n_frames * L, H, D)
+    agent_v = v4[:, :agent_len].reshape(1, P, n_frames * L, H, D)
+    for p in range(P):
+        rolling_cache_append(kv_cache["agent_caches"][p], agent_k[:, p], agent_v[:, p],
+                             start_frame * L, (start_frame + n_frames) * L, retention, 0, L)
+    if not no_local:
+        loc_k = k4[:, local_start:global_start].reshape(1, n_frames, N, KL, H, D)
+        loc_v = v4[:, local_start:global_start].reshape(1, n_frames, N, KL, H, D)
+        for g in range(N):
+            c = kv_cache["local_hubs"][g]
+            rolling_bool_cache_append(c, "active", active[:, g].repeat_interleave(KL),
+                                      start_frame * KL, (start_frame + n_frames) * KL,
+                                      retention, 0, KL)
+            rolling_cache_append(c, loc_k[:, :, g].reshape(1, n_frames * KL, H, D),
+                                 loc_v[:, :, g].reshape(1, n_frames * KL, H, D),
+                                 start_frame * KL, (start_frame + n_frames) * KL, retention, 0, KL)
+    if KG > 0:
+        rolling_cache_append(kv_cache["global_hub"], k4[:, global_start:], v4[:, global_start:],
+                             start_frame * KG, (start_frame + n_frames) * KG, retention, 0, KG)
+
+    def window(cache, tpf):
+        end = int(cache["local_end_index"].item())
+        held = end // tpf if tpf > 0 else 0
+        frames = (end_frame - held + 1) + torch.arange(end, device=dev) // max(tpf, 1)
+        return frames, cache["k"][:, :end].reshape(1, end, H * D), \
+            cache["v"][:, :end].reshape(1, end, H * D)
+
+    agent = [window(c, L) for c in kv_cache["agent_caches"]]
+    local, local_active = [], []
+    if not no_local:
+        for c in kv_cache["local_hubs"]:
+            f, kk, vv = window(c, KL)
+            local.append((f, kk, vv))
+            act = c.get("active")
+            local_active.append(torch.ones(f.shape[0], device=dev, dtype=torch.bool) if act is None
+                                else act[:f.shape[0]].to(device=dev, dtype=torch.bool))
+    if KG > 0:
+        gf, gk, gv = window(kv_cache["global_hub"], KG)
+    else:
+        gf = torch.empty(0, device=dev, dtype=torch.long)
+        gk = gv = x.new_zeros(1, 0, H * D)
+    out = hierarchical_cached_attention(
+        roped_q=q4, agent_frames=[a[0] for a in agent], agent_keys=[a[1] for a in agent],
+        agent_vals=[a[2] for a in agent], local_frames=[t[0] for t in local],
+        local_keys=[t[1] for t in local], local_vals=[t[2] for t in local],
+        local_active_tokens=local_active, global_frames=gf, global_keys=gk, global_vals=gv,
+        labels=labels, active=active, P=P, N=N, L=L, KL=KL, KG=KG, n_frames=n_frames,
+        n_block=n_block, local_attn=local_attn, direct_player=direct_player,
+        membership=mem_full if use_membership else None,
+        global_only=go_full if use_membership else None, hier_no_local_hub=no_local)
+    return self.o(out.type_as(self.o.weight))
+
+
+SelfAttention.causal_forward_hier_hub = _causal_forward_hier_hub

@@ -22,6 +22,9 @@ Fixtures written (all under ``tests/golden``):
   varlen plans derived from them (``hier_packed_attention.py:32-102``).
 * ``tiled.npz``      ``build_hier_tiled_full_sequence_layouts`` /
   ``build_hier_tiled_cached_layout`` (``hier_tiled_attention.py:244-655``).
+* ``causal.npz``     ``SelfAttention.causal_forward_hier_hub``
+  (``multics/models/attention.py:456-1005``) over consecutive blocks with
+  rolling caches: per-block inputs and outputs, final cache contents.
 * ``numerics.npz``   fp32 outputs of the reference attention path
   (camera Q/K add ``attention.py:307-320``, RMSNorm ``:231-242``, float64
   RoPE ``rope.py:248-254``, masked SDPA ``attention.py:39-54``) on seeded
@@ -548,9 +551,143 @@ def _euler_zyx(ang):
     return R
 
 
+# ---------------------------------------------------------------------------
+# cached (causal) forward of SelfAttention over consecutive blocks
+# ---------------------------------------------------------------------------
+
+
+def _bits(t):
+    import torch
+
+    return t.detach().to(torch.bfloat16).contiguous().view(torch.int16).numpy().astype(np.uint16)
+
+
+def _causal_cases():
+    return [
+        # tests/test_hier_segmented_causal_forward.py:58-127 shape: initial append,
+        # steady state, regrouping between blocks, rolling eviction
+        dict(name="labels_dyn", P=4, N=2, L=16, KL=3, KG=2, n=2, n_block=2, local_attn=4,
+             heads=2, blocks=4, cam=False, membership=False, no_local=False),
+        dict(name="cam_membership", P=4, N=2, L=12, KL=3, KG=2, n=2, n_block=2, local_attn=4,
+             heads=2, blocks=4, cam=True, membership=True, no_local=False),
+        dict(name="no_local", P=3, N=2, L=16, KL=0, KG=3, n=1, n_block=1, local_attn=3,
+             heads=2, blocks=5, cam=False, membership=False, no_local=True),
+    ]
+
+
+def gen_causal(out: dict):
+    """``SelfAttention.causal_forward_hier_hub`` (``multics/models/attention.py:456-1005``)
+    with the SDPA backend, block after block over rolling caches
+    (``_rolling_cache_append`` / ``_rolling_bool_cache_append``, ``:90-228``)."""
+    import torch
+
+    from multics.models.wan_video_dit import SelfAttention
+
+    os.environ["WAN_HIER_INFER_KERNEL"] = "sdpa"
+    names = []
+    for c in _causal_cases():
+        g = torch.Generator().manual_seed(17)
+        P, N, L, KL, KG, n = c["P"], c["N"], c["L"], c["KL"], c["KG"], c["n"]
+        H, D = c["heads"], 128
+        dim = H * D
+        retention = c["local_attn"] + n
+        S = P * n * L + n * (N * KL + KG)
+        torch.manual_seed(5)
+        layer = SelfAttention(dim=dim, num_heads=H)
+        if c["cam"]:
+            layer.enable_camera_pose_qk(12, dropout_p=0.0)
+        layer = layer.to(dtype=torch.bfloat16).eval()
+        layer.num_frame_per_block = c["n_block"]
+        layer.local_attn_size = c["local_attn"]
+        if c["no_local"]:
+            layer.hier_no_local_hub = True
+        with torch.no_grad():
+            for nrm in (layer.norm_q, layer.norm_k):
+                nrm.weight.copy_(1 + 0.02 * torch.randn(dim, generator=g))
+            if c["cam"]:
+                layer.cam_q.weight.copy_(0.02 * torch.randn(dim, 12, generator=g))
+                layer.cam_k.weight.copy_(0.02 * torch.randn(dim, 12, generator=g))
+
+        def stream(cap):
+            return {"k": torch.zeros(1, cap, H, D, dtype=torch.bfloat16),
+                    "v": torch.zeros(1, cap, H, D, dtype=torch.bfloat16),
+                    "global_end_index": torch.zeros(1, dtype=torch.long),
+                    "local_end_index": torch.zeros(1, dtype=torch.long)}
+
+        cache = {"hier_hub": True, "sparse_hub": True, "num_players": P, "num_groups": N,
+                 "num_local_hub_tokens": KL, "num_global_hub_tokens": KG,
+                 "hier_no_local_hub": c["no_local"],
+                 "agent_caches": [stream(retention * L) for _ in range(P)],
+                 "local_hubs": [] if c["no_local"] else [stream(retention * KL) for _ in range(N)],
+                 "global_hub": stream(retention * max(KG, 1))}
+        for lc in cache["local_hubs"]:
+            lc["active"] = torch.zeros(retention * KL, dtype=torch.bool)
+        T_full = c["blocks"] * n
+        mem = go = None
+        if c["membership"]:
+            mem = torch.zeros(T_full, N, P, dtype=torch.bool)
+            mem[:, 0, 0] = mem[:, 0, 1] = True
+            mem[:, 1, 2] = True
+            mem[n:2 * n, 1, 1] = True  # player 1 anchors both groups in block 1
+            go = torch.zeros(T_full, P, dtype=torch.bool)
+            go[:, 3] = True
+            out[f"{c['name']}/membership"] = mem.numpy().astype(np.uint8)
+            out[f"{c['name']}/global_only"] = go.numpy().astype(np.uint8)
+        nm = c["name"]
+        for k_, v_ in layer.state_dict().items():
+            # the q/k/v/o weights are the same seeded set for every case
+            key = f"{nm}/w/{k_}" if (k_.startswith("cam_") or k_.startswith("norm_")) else f"w/{k_}"
+            out[key] = _bits(v_)
+        with torch.inference_mode():
+            for blk in range(c["blocks"]):
+                x = torch.randn(1, S, dim, generator=g).to(torch.bfloat16)
+                phase = torch.rand(S, 1, D // 2, generator=g, dtype=torch.float64) * 2 * math.pi
+                freqs = torch.polar(torch.ones_like(phase), phase)
+                row = (0, 0, 1, 1)[:P] if blk % 2 == 0 else (0, 1, 0, 1, 1)[:P]
+                labels = torch.tensor([row] * n, dtype=torch.long)
+                active = torch.ones(n, N, dtype=torch.bool)
+                cam = None
+                if c["cam"]:
+                    cam = torch.zeros(1, S, 12)
+                    cam[0, : P * n * L] = torch.randn(P * n, 12, generator=g).repeat_interleave(L, 0)
+                    cam = cam.to(torch.bfloat16)
+                kw = dict(current_start=blk * n * P * L, num_frames=n, num_players=P,
+                          num_hub_tokens=N * KL + KG, cam_tokens=cam, direct_player=True)
+                if c["membership"]:
+                    kw.update(membership=mem, global_only=go, active_group=None)
+                else:
+                    kw.update(group_labels=labels, active_group=active)
+                y = layer.causal_forward_hier_hub(x, freqs, cache, **kw)
+                out[f"{nm}/{blk}/x"] = _bits(x[0])
+                out[f"{nm}/{blk}/freqs"] = np.stack([freqs[:, 0].real.numpy(),
+                                                      freqs[:, 0].imag.numpy()],
+                                                     -1).astype(np.float32)
+                out[f"{nm}/{blk}/labels"] = labels.numpy()
+                out[f"{nm}/{blk}/active"] = active.numpy().astype(np.uint8)
+                if cam is not None:
+                    out[f"{nm}/{blk}/cam"] = _bits(cam[0])
+                out[f"{nm}/{blk}/out"] = _bits(y[0])
+        streams = cache["agent_caches"] + cache["local_hubs"] + [cache["global_hub"]]
+        for i, st in enumerate(streams):
+            out[f"{nm}/cache/{i}/k"] = _bits(st["k"][0])
+            out[f"{nm}/cache/{i}/v"] = _bits(st["v"][0])
+            out[f"{nm}/cache/{i}/idx"] = np.array(
+                [int(st["global_end_index"]), int(st["local_end_index"])], np.int64)
+            if "active" in st:
+                out[f"{nm}/cache/{i}/active"] = st["active"].numpy().astype(np.uint8)
+        meta = {k_: v_ for k_, v_ in c.items()}
+        meta["retention"] = retention
+        meta["S"] = S
+        meta["n_streams"] = len(streams)
+        out[f"{nm}/meta"] = np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)
+        names.append(nm)
+    out["causal_case_names"] = np.frombuffer(json.dumps(names).encode(), dtype=np.uint8)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--only", default=None, help="write one fixture file (e.g. causal)")
     args = ap.parse_args()
     attn_mod = _setup(args.reference)
     import torch
@@ -558,7 +695,10 @@ def main():
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     for fname, fn in (("masks", lambda o: gen_masks(args.reference, o)),
                       ("segmented", gen_segmented), ("tiled", gen_tiled),
-                      ("numerics", lambda o: gen_numerics(o, attn_mod))):
+                      ("numerics", lambda o: gen_numerics(o, attn_mod)),
+                      ("causal", gen_causal)):
+        if args.only and fname != args.only:
+            continue
         out: dict = {}
         fn(out)
         path = HERE / f"{fname}.npz"
