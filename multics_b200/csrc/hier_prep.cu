@@ -46,36 +46,25 @@ __device__ __forceinline__ void bf16x8_to_f32(uint4 v, float (&f)[8]) {
 }
 
 // One thread owns 8 consecutive channels of a token row (blockDim = dim/8);
-// blockIdx.y selects Q (0) or K (1).  Each block iteration handles kRows
-// consecutive tokens, so every thread keeps kRows independent 16-byte loads
-// in flight and the block does one reduction round per kRows tokens.  The
-// camera weights are transposed once into shared memory, channel-contiguous,
-// so a thread reads its 8 channels of one camera input with one 16-byte load.
-constexpr int kPrepRows = 4;
+// blockIdx.y selects Q (0) or K (1).  The CTA walks chunks of kPrepRows
+// consecutive tokens; thread 0 streams each chunk's rows and RoPE rows into a
+// kPrepStages-deep shared-memory ring with bulk async copies, so several
+// chunks of loads are in flight per SM while the block computes one.  The
+// camera weights of a thread's 8 channels sit in registers.
+constexpr int kPrepRows = 8;
+constexpr int kPrepStages = 3;
 
-// proj[i] = sum_c cam[c] * W[d0+i][c] with W staged as wsm[c][thread] (8 bf16)
-template <int CAM>
-__device__ __forceinline__ void cam_project(const uint4* wsm, int nthreads, int t,
-                                            const float* cam, float (&proj)[8]) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) proj[i] = 0.f;
-#pragma unroll
-  for (int c = 0; c < CAM; ++c) {
-    float w[8];
-    bf16x8_to_f32(wsm[c * nthreads + t], w);
-    const float cv = cam[c];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) proj[i] = fmaf(cv, w[i], proj[i]);
-  }
-}
+__device__ int g_prep_err;  // pipeline wait timeouts of the prologue kernel
+
+__host__ __device__ constexpr int align16i(int x) { return (x + 15) & ~15; }
 
 template <int CAM>
 __global__ void __launch_bounds__(384, 1) prep_qk_kernel(PrepArgs a) {
   constexpr int R = kPrepRows;
-  extern __shared__ uint4 wsm[];  // [CAM][blockDim] x 8 bf16
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint64_t full[kPrepStages];
   __shared__ float red[R][12];
   __shared__ float camv[R][CAM > 0 ? CAM : 1];
-  __shared__ float4 frs[R][64];  // RoPE (cos, sin) pairs of the chunk's rows, D <= 256
   const bool is_k = blockIdx.y == 1;
   const __nv_bfloat16* x = is_k ? a.kx : a.qx;
   const __nv_bfloat16* wc = is_k ? a.wck : a.wcq;
@@ -85,127 +74,174 @@ __global__ void __launch_bounds__(384, 1) prep_qk_kernel(PrepArgs a) {
   const int d0 = t * 8;
   const int nt = blockDim.x;
   const int nwarps = nt / 32;
+  const int half = a.D / 2;
+  const int row_bytes = a.dim * 2;
+  const int fr_bytes = half * 8;  // (cos, sin) float pairs of one token
+  const int stage_bytes = align16i(R * (row_bytes + fr_bytes));
+  // camera weights W[d0 + i][c] of this thread's channels, bf16 pairs
+  constexpr int kc = CAM > 0 ? CAM : 1;
+  uint32_t wr[kc][4];
   if (CAM > 0) {
     const uint16_t* w16 = reinterpret_cast<const uint16_t*>(wc);
-    for (int c = 0; c < CAM; ++c) {
-      uint32_t p[4];
+#pragma unroll
+    for (int c = 0; c < CAM; ++c)
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        p[i] = (uint32_t)w16[(int64_t)(d0 + 2 * i) * CAM + c] |
-               ((uint32_t)w16[(int64_t)(d0 + 2 * i + 1) * CAM + c] << 16);
-      wsm[c * nt + t] = make_uint4(p[0], p[1], p[2], p[3]);
-    }
+        wr[c][i] = (uint32_t)w16[(int64_t)(d0 + 2 * i) * CAM + c] |
+                   ((uint32_t)w16[(int64_t)(d0 + 2 * i + 1) * CAM + c] << 16);
   }
   float nv[8];
   bf16x8_to_f32(*reinterpret_cast<const uint4*>(nw + d0), nv);
   const int pair0 = (d0 % a.D) / 2;
-  const int half = a.D / 2;
-  const int64_t stride = (int64_t)gridDim.x * R;
-  // Every global load of a chunk (its R rows, camera values and RoPE pairs)
-  // is issued one chunk ahead into registers; camera values and RoPE pairs
-  // are then staged in shared memory for the whole block.
-  constexpr int kc = CAM > 0 ? CAM : 1;
-  const int fq = half / 2;  // float4 (two pairs) per row of the RoPE table
+  const int64_t n_chunks = (a.S + R - 1) / R;
+  if (t == 0) {
+    for (int s = 0; s < kPrepStages; ++s) mbar_init(full + s, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // chunk i of this CTA is chunk blockIdx.x + i * gridDim.x of the sequence
+  auto issue = [&](int64_t i) {
+    const int64_t c = blockIdx.x + i * (int64_t)gridDim.x;
+    if (c >= n_chunks) return;
+    const int64_t r0 = c * R;
+    const int nr = (int)min((int64_t)R, a.S - r0);
+    uint8_t* st = ring + (i % kPrepStages) * stage_bytes;
+    uint64_t* bar = full + (i % kPrepStages);
+    mbar_arrive_expect_tx(bar, nr * (row_bytes + fr_bytes));
+    for (int r = 0; r < nr; ++r)
+      bulk_load(st + r * row_bytes, x + (r0 + r) * a.x_stride, row_bytes, bar);
+    bulk_load(st + R * row_bytes, a.freqs + r0 * half, nr * fr_bytes, bar);
+  };
+  if (t == 0)
+    for (int i = 0; i < kPrepStages - 1; ++i) issue(i);
+  // camera rows are tiny: plain loads, one chunk ahead, through registers
   const int n_cam = CAM > 0 ? R * CAM : 0;
-  const int n_fr = R * fq;
-  uint4 raw[R];
-  float cam_r[2];
-  float4 fr_r[4];
-  auto fetch = [&](int64_t r0, uint4 (&rows)[R], float (&cr)[2], float4 (&fr)[4]) {
+  // R*CAM <= 128 camera values per chunk, >= 32 threads per block
+  constexpr int kCamPer = (R * kMaxCam + 31) / 32;
+  float cam_r[kCamPer];
+  auto fetch_cam = [&](int64_t i) {
+    const int64_t r0 = (blockIdx.x + i * (int64_t)gridDim.x) * R;
 #pragma unroll
-    for (int r = 0; r < R; ++r)
-      rows[r] = r0 + r < a.S ? *reinterpret_cast<const uint4*>(x + (r0 + r) * a.x_stride + d0)
-                             : make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int i = t + k * nt;
-      cr[k] = 0.f;
-      if (i < n_cam && r0 + i / kc < a.S) cr[k] = __bfloat162float(a.cam[(r0 + i / kc) * CAM + i % kc]);
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int i = t + k * nt;
-      fr[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (i < n_fr && r0 + i / fq < a.S)
-        fr[k] = reinterpret_cast<const float4*>(a.freqs + (r0 + i / fq) * half)[i % fq];
+    for (int k = 0; k < kCamPer; ++k) {
+      const int j = t + k * nt;
+      cam_r[k] = 0.f;
+      if (j < n_cam && r0 + j / kc < a.S) cam_r[k] = __bfloat162float(a.cam[(r0 + j / kc) * CAM + j % kc]);
     }
   };
-  fetch((int64_t)blockIdx.x * R, raw, cam_r, fr_r);
-  for (int64_t row0 = (int64_t)blockIdx.x * R; row0 < a.S; row0 += stride) {
+  if (CAM > 0) fetch_cam(0);
+  for (int64_t i = 0;; ++i) {
+    const int64_t row0 = (blockIdx.x + i * (int64_t)gridDim.x) * R;
+    if (row0 >= a.S) break;
+    if (t == 0) issue(i + kPrepStages - 1);  // into the stage freed by iteration i-1
+    if (CAM > 0) {
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int i = t + k * nt;
-      if (i < n_cam) camv[i / kc][i % kc] = cam_r[k];
+      for (int k = 0; k < kCamPer; ++k) {
+        const int j = t + k * nt;
+        if (j < n_cam) camv[j / kc][j % kc] = cam_r[k];
+      }
+      fetch_cam(i + 1);
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int i = t + k * nt;
-      if (i < n_fr) frs[i / fq][i % fq] = fr_r[k];
-    }
-    uint4 nxt[R];
-    float cam_n[2];
-    float4 fr_n[4];
-    fetch(row0 + stride, nxt, cam_n, fr_n);
-    __syncthreads();
-    float xv[R][8];
-    float ss[R];
-    // Camera rows repeat over a player frame's patches, so the chunk usually
-    // shares one row: project it once (exact: same inputs, same result).
+    const uint8_t* st = ring + (i % kPrepStages) * stage_bytes;
+    mbar_wait(full + (i % kPrepStages), (uint32_t)((i / kPrepStages) & 1), &g_prep_err, 1);
+    __syncthreads();  // camv visible
+    const int nr = (int)min((int64_t)R, a.S - row0);
+    // rows of one player frame share their camera row: project it once
     bool shared_cam = true;
     float proj[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) proj[q] = 0.f;
+    auto project = [&](int r) {  // proj = W cam_r for this thread's 8 channels
+#pragma unroll
+      for (int q = 0; q < 8; ++q) proj[q] = 0.f;
+#pragma unroll
+      for (int c = 0; c < CAM; ++c) {
+        float w[8];
+        bf16x8_to_f32(make_uint4(wr[c][0], wr[c][1], wr[c][2], wr[c][3]), w);
+        const float cv = camv[r][c];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) proj[q] = fmaf(cv, w[q], proj[q]);
+      }
+    };
     if (CAM > 0) {
 #pragma unroll
       for (int r = 1; r < R; ++r)
 #pragma unroll
         for (int c = 0; c < CAM; ++c) shared_cam &= camv[r][c] == camv[0][c];
-      if (shared_cam) cam_project<CAM>(wsm, nt, t, camv[0], proj);
+      if (shared_cam) project(0);
     }
+    // pass 1: sums of squares of all rows, reduced together
+    float ss[R];
+    if (CAM == 0 || shared_cam) {
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      bf16x8_to_f32(raw[r], xv[r]);
-      if (CAM > 0) {
-        if (!shared_cam) cam_project<CAM>(wsm, nt, t, camv[r], proj);
+      for (int r = 0; r < R; ++r) {
+        float xv[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(st + r * row_bytes + d0 * 2), xv);
+        float sq = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) xv[r][i] += proj[i];
+        for (int q = 0; q < 8; ++q) {
+          const float v = CAM > 0 ? xv[q] + proj[q] : xv[q];
+          sq = fmaf(v, v, sq);
+        }
+        ss[r] = r < nr ? sq : 0.f;
       }
-      float s = 0.f;
+    } else {  // a chunk across a frame boundary: one projection per row
+#pragma unroll 1
+      for (int r = 0; r < R; ++r) {
+        project(r);
+        float xv[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(st + r * row_bytes + d0 * 2), xv);
+        float sq = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s = fmaf(xv[r][i], xv[r][i], s);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      ss[r] = s;
+        for (int q = 0; q < 8; ++q) sq = fmaf(xv[q] + proj[q], xv[q] + proj[q], sq);
+        ss[r] = r < nr ? sq : 0.f;
+      }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int r = 0; r < R; ++r) ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], o);
     if ((t & 31) == 0) {
 #pragma unroll
       for (int r = 0; r < R; ++r) red[r][t >> 5] = ss[r];
     }
     __syncthreads();
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if (row0 + r >= a.S) break;
+    // pass 2: normalise, rotate, store
+    const float4* fr = reinterpret_cast<const float4*>(st + R * row_bytes);
+    auto finish = [&](int r) {
       float tot = 0.f;
       for (int w = 0; w < nwarps; ++w) tot += red[r][w];
       const float rs = rsqrtf(tot / a.dim + a.eps);
-      const float4 f0 = frs[r][pair0 / 2], f1 = frs[r][pair0 / 2 + 1];
+      float xv[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(st + r * row_bytes + d0 * 2), xv);
+      if (CAM > 0) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) xv[q] += proj[q];
+      }
+      const float4 f0 = fr[r * (half / 2) + pair0 / 2], f1 = fr[r * (half / 2) + pair0 / 2 + 1];
       uint4 o;
       uint32_t* po = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 f2 = i < 2 ? f0 : f1;
-        const float c = (i & 1) ? f2.z : f2.x;
-        const float s = (i & 1) ? f2.w : f2.y;
-        const float a0 = xv[r][2 * i] * rs * nv[2 * i], a1 = xv[r][2 * i + 1] * rs * nv[2 * i + 1];
-        po[i] = pack_bf16x2(a0 * c - a1 * s, a0 * s + a1 * c);
+      for (int q = 0; q < 4; ++q) {
+        const float4 f2 = q < 2 ? f0 : f1;
+        const float c = (q & 1) ? f2.z : f2.x;
+        const float s = (q & 1) ? f2.w : f2.y;
+        const float a0 = xv[2 * q] * rs * nv[2 * q], a1 = xv[2 * q + 1] * rs * nv[2 * q + 1];
+        po[q] = pack_bf16x2(a0 * c - a1 * s, a0 * s + a1 * c);
       }
       *reinterpret_cast<uint4*>(out + (row0 + r) * a.out_stride + d0) = o;
+    };
+    if (CAM == 0 || shared_cam) {  // proj still holds the chunk's shared projection
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        if (r < nr) finish(r);
+    } else {
+#pragma unroll 1
+      for (int r = 0; r < nr; ++r) {
+        project(r);
+        finish(r);
+      }
     }
-#pragma unroll
-    for (int r = 0; r < R; ++r) raw[r] = nxt[r];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) cam_r[k] = cam_n[k];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) fr_r[k] = fr_n[k];
-    __syncthreads();
+    __syncthreads();  // stage and red free for the next chunks
   }
 }
 
@@ -248,6 +284,12 @@ extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, co
   p.k_out = (__nv_bfloat16*)k_out;
   p.out_stride = out_stride;
   const int threads = dim / 8;
+  if (x_stride % 8 || out_stride % 8 || (reinterpret_cast<uintptr_t>(qx) & 15) ||
+      (reinterpret_cast<uintptr_t>(kx) & 15) || (reinterpret_cast<uintptr_t>(freqs) & 15)) {
+    set_error(HIER_EVALUE, "hier_prep_qk needs 16-byte aligned rows (strides %lld, %lld)",
+              (long long)x_stride, (long long)out_stride);
+    return HIER_EVALUE;
+  }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -256,19 +298,22 @@ extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, co
   const int64_t blocks = chunks < (sms + 1) / 2 ? chunks : (sms + 1) / 2;
   const dim3 grid((unsigned)blocks, 2);
   cudaStream_t st = (cudaStream_t)stream;
-  const size_t wbytes = (size_t)(cam ? cam_dim : 0) * threads * sizeof(uint4);
+  const size_t ring = (size_t)kPrepStages * align16i(kPrepRows * (dim * 2 + (D / 2) * 8));
   if (!cam) {
-    prep_qk_kernel<0><<<grid, threads, 0, st>>>(p);
+    HIER_CHECK_CUDA(cudaFuncSetAttribute(prep_qk_kernel<0>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ring),
+                    "cudaFuncSetAttribute(prep_qk_kernel)");
+    prep_qk_kernel<0><<<grid, threads, ring, st>>>(p);
   } else if (cam_dim == 12) {
     HIER_CHECK_CUDA(cudaFuncSetAttribute(prep_qk_kernel<12>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wbytes),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ring),
                     "cudaFuncSetAttribute(prep_qk_kernel)");
-    prep_qk_kernel<12><<<grid, threads, wbytes, st>>>(p);
+    prep_qk_kernel<12><<<grid, threads, ring, st>>>(p);
   } else if (cam_dim == 16) {
     HIER_CHECK_CUDA(cudaFuncSetAttribute(prep_qk_kernel<16>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wbytes),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ring),
                     "cudaFuncSetAttribute(prep_qk_kernel)");
-    prep_qk_kernel<16><<<grid, threads, wbytes, st>>>(p);
+    prep_qk_kernel<16><<<grid, threads, ring, st>>>(p);
   } else {
     set_error(HIER_ENOTIMPL, "hier_prep_qk supports cam_dim 12 or 16; got %d", cam_dim);
     return HIER_ENOTIMPL;
