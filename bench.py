@@ -43,6 +43,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--transport", default="peer", choices=["peer", "exchange"],
                     help="sharded runs: how group-mate frames on other GPUs are read")
+    ap.add_argument("--path", default=None, choices=["segments", "block", "shard"],
+                    help="1 GPU, cfg2: the layer through the sequence plan (default) or the "
+                         "128x128 block plan; shard: the player-sharded layer with one rank")
     return ap.parse_args()
 
 
@@ -122,6 +125,24 @@ def useful_pairs(bm):
     return bits + bm.n_full * 128 * 128
 
 
+def plan_tile_flops(q_pairs, kv_tiles, H, D):
+    """FLOPs of every computed 128x128 tile of a pair plan: per pair, each
+    half with query rows times its key tiles that the half does not skip."""
+    import torch
+
+    qp = q_pairs.long()
+    counts = qp[:, 5] - qp[:, 4]
+    idx = torch.repeat_interleave(torch.arange(qp.shape[0], device=qp.device), counts)
+    if idx.numel() == 0:
+        return 0.0
+    first = torch.cumsum(counts, 0) - counts
+    tiles = qp[idx, 4] + torch.arange(idx.numel(), device=qp.device) - first[idx]
+    sel = kv_tiles[tiles].long()
+    used = ((qp[idx, 1] > 0) & (sel[:, 2] != -2)).long() + \
+        ((qp[idx, 3] > 0) & (sel[:, 3] != -2)).long()
+    return 4.0 * 128 * 128 * D * H * float(used.sum())
+
+
 def run_sharded(args, rank, world, local_rank):
     """Players sharded over the ranks (strong scaling of one layer): each rank
     runs the prologue of its rows (its players, then the replicated hub
@@ -162,6 +183,7 @@ def run_sharded(args, rank, world, local_rank):
     torch.cuda.synchronize()
     plan_ms = (time.perf_counter() - t0) * 1e3
     sh.check_status()
+    tile_flops = plan_tile_flops(sh.q_pairs[:sh.n_pairs], sh.kv_tiles, cfg.H, cfg.D)
     q_buf = torch.empty_like(qx)
     o_buf = torch.empty_like(qx)
     if sh.transport == "peer":
@@ -244,6 +266,7 @@ def run_sharded(args, rank, world, local_rank):
                    "parallelism": f"players sharded x{world} (ranks own {topo.bounds}); "
                                   f"mate frames: {sh.transport}",
                    "remote_units_rank0": len(topo.needs[0]),
+                   "tile_gflop_per_step_rank0": round(tile_flops / 1e9, 1),
                    "l2": "inputs larger than L2"},
         "breakdown_ms": {k: round(v_, 4) for k, v_ in parts.items()},
         "plan_once_ms": round(plan_ms, 3),
@@ -317,7 +340,8 @@ def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
 
-    from multics_b200.attention import attention_from_plan, device_error, freqs_table, hier_prep_qk
+    from multics_b200.attention import (attention_from_plan, device_error, freqs_table,
+                                        hier_prep_qk, sequence_plan)
     from multics_b200.hier_masks import build_stage2_hier_flex_block_mask
     from multics_b200.synth import CONFIGS, make_inputs
 
@@ -341,7 +365,17 @@ def run_ours(args, rank, world, local_rank):
     meta_ms = t0.elapsed_time(t1)
     pairs = useful_pairs(bm)
     useful_flops = 4.0 * cfg.H * cfg.D * pairs
-    tile_flops = bm.tile_flops(cfg.D, cfg.H)
+    # the sequence plan (built once per grouping), unless the block plan was asked for
+    t0.record()
+    sp = sequence_plan(bm, cfg.H)
+    t1.record()
+    torch.cuda.synchronize()
+    if sp is not None:
+        meta_ms += t0.elapsed_time(t1)
+        core = sp.core
+        tile_flops = plan_tile_flops(core.q_pairs[:core.n_pairs], core.kv_tiles, cfg.H, cfg.D)
+    else:
+        tile_flops = bm.tile_flops(cfg.D, cfg.H)
 
     q_buf = torch.empty(S, cfg.dim, dtype=torch.bfloat16, device=dev)
     k_buf = torch.empty_like(q_buf)
@@ -350,9 +384,12 @@ def run_ours(args, rank, world, local_rank):
     def step():
         hier_prep_qk(inp.qx, inp.kx, ft, cfg.H, norm_q_weight=inp.nqw, norm_k_weight=inp.nkw,
                      cam_tokens=inp.cam, cam_q_weight=inp.wcq, cam_k_weight=inp.wck,
-                     out=(q_buf, k_buf))
+                     out=(q_buf, k_buf), out_rows=None if sp is None else sp.seq_to_plan)
         ev_mid.record(stream)
-        attention_from_plan(q_buf, k_buf, inp.v, bm, cfg.H, out=o_buf)
+        if sp is not None:
+            sp.attend(q_buf, k_buf, inp.v, out=o_buf)
+        else:
+            attention_from_plan(q_buf, k_buf, inp.v, bm, cfg.H, out=o_buf)
 
     ev_mid = torch.cuda.Event(enable_timing=True)
     for _ in range(args.warmup):
@@ -405,9 +442,12 @@ def run_ours(args, rank, world, local_rank):
                    "S": S, "useful_pairs": pairs, "useful_gflop_per_step": useful_flops / 1e9,
                    "tile_gflop_per_step": tile_flops / 1e9,
                    "parallelism": f"players sharded x{world}" if world > 1 else "single GPU",
+                   "plan": ("sequence plan: one query pair per player frame, hub queries in "
+                            "128-row group tiles" if sp is not None else
+                            "128x128 block plan of the Flex block mask"),
                    "l2": "inputs larger than L2 (q/k/v 3 x %.0f MB)" % (S * cfg.dim * 2 / 1e6)},
         "breakdown_ms": {"prologue": round(statistics.mean(prep_ms), 4),
-                         "attention": round(attn_avg, 4), "block_plan_once": round(meta_ms, 3)},
+                         "attention": round(attn_avg, 4), "plans_once": round(meta_ms, 3)},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_b,
                      "unit": "TFLOP/s", "frac": round(achieved / peak_b, 4),
                      "peak_kind": f"{peak_kind} bf16 burst", "frac_vs_sustained":
@@ -591,7 +631,11 @@ def main():
             sys.stdout.flush()
             os.dup2(saved, 1)
             os.close(saved)
-    if world == 1 and args.config == "cfg2":
+    if args.path is None:
+        args.path = "segments" if (world == 1 and args.config == "cfg2") else "shard"
+    if args.path == "block":
+        os.environ["MULTICS_B200_FULL_SEQUENCE_PLAN"] = "blocks"
+    if world == 1 and args.path in ("segments", "block"):
         line = run_ours(args, rank, world, local_rank)
     else:
         line = run_sharded(args, rank, world, local_rank)

@@ -153,11 +153,13 @@ int hier_block_plan_build(const hier_grouping* g, void* workspace, const int32_t
  * RMSNorm over the full dim (attention.py:231-242, eps) and rope_apply
  * (multics/models/rope.py:248-254).  cam may be NULL (no camera tokens).
  * freqs: float32 [S, D/2, 2] (cos, sin) per token, shared by all heads.
- * Row strides are in elements. */
+ * Row strides are in elements.  out_rows (int32 [S], may be NULL) writes
+ * token r's q and k to row out_rows[r] of q_out / k_out. */
 int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, const void* cam,
                  int32_t cam_dim, const void* wcq, const void* wck, const void* nqw,
                  const void* nkw, const float* freqs, int64_t S, int32_t H, int32_t D,
-                 float eps, void* q_out, void* k_out, int64_t out_stride, void* stream);
+                 float eps, void* q_out, void* k_out, int64_t out_stride,
+                 const int32_t* out_rows, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Attention
@@ -199,16 +201,22 @@ int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stride, const v
  * (s << 24) | row-within-stream.  tile_masks holds mask_rows entries of four
  * uint32 per partial tile: 128 (one key bitmask per query row, the format of
  * hier_block_plan_build) or 1 (one key bitmask shared by every query row, the
- * format of hier_cached_build).  lse (float [q_rows_total][H], may be NULL)
+ * format of hier_cached_build); a query pair whose q_pairs[6] is 1 uses 128
+ * (its mask index then counts 128-entry masks) whatever mask_rows says.
+ * lse (float [q_rows_total][H], may be NULL)
  * receives per written row and head log2(sum_j 2^(s_j)) of the scaled scores
  * s_j = q.k_j * softmax_scale * log2(e) (-inf for rows without keys), so that
  * partial results over disjoint key sets merge as
- * O = sum_r 2^(lse_r - M) O_r / sum_r 2^(lse_r - M).  Other arguments as
- * hier_attn_fwd. */
+ * O = sum_r 2^(lse_r - M) O_r / sum_r 2^(lse_r - M).  out_rows (int32
+ * [q_rows_total], may be NULL) sends query row r's output and lse to row
+ * out_rows[r] (a query order other than the output order, e.g. hub rows
+ * grouped by group while the output keeps the sequence order).  Other
+ * arguments as hier_attn_fwd. */
 int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_t q_stride,
                           int32_t n_streams, const void* const* k, const void* const* v,
                           const int64_t* stream_rows, const int64_t* kv_stride, void* out,
-                          int64_t out_stride, int32_t H, int32_t D, const int32_t* q_pairs,
+                          int64_t out_stride, const int32_t* out_rows, int32_t H, int32_t D,
+                          const int32_t* q_pairs,
                           int32_t n_pairs, const int32_t* kv_tiles, const uint32_t* tile_masks,
                           int32_t mask_rows, const int32_t* order, float softmax_scale,
                           float* lse, int32_t* dev_err, void* stream);
@@ -361,37 +369,53 @@ int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_boxes, const
  * Player-sharded execution (one rank per GPU)
  * ------------------------------------------------------------------------- */
 
-/* One rank's share of a full-sequence layer (labels mode, active hubs): the
- * rank owns players [p0, p1); its query rows are its players' rows (in
- * sequence order) followed by every hub row (T*N*K_L local, then T*K_G
- * global); its key/value streams for hier_attn_fwd_streams are
- *   0 = its players' rows, 1 = the hub rows, and for each remote group-mate
- *   unit (o, f) (the L rows of player o at frame f) the stream-packed first
- *   row remote_key[o*T + f] = (stream << 24) | row (-1 if absent): a buffer
- *   of frames fetched before the launch, or the owning rank's buffer mapped
- *   from its GPU (read in place over NVLink).
- * Player rows get their full key sets; hub rows get the keys this rank holds
- * (its players' rows, plus the hub rows if hub_keys) and are merged across
- * ranks with hier_lse_prepare / hier_lse_finish.  No reference counterpart
- * in code: the reference runs every player on one device; this realises the
- * player sharding of the multi-GPU configurations. */
+/* One rank's share of a full-sequence layer (labels mode): the rank owns
+ * players [p0, p1); its query rows are its players' rows (player, frame,
+ * patch) followed by every hub row, the hubs group-major: local hub
+ * (g, f, slot) at own_rows + (g*T + f)*K_L + slot, then global hub (f, slot)
+ * at own_rows + T*N*K_L + f*K_G + slot.  Its key/value streams for
+ * hier_attn_fwd_streams are
+ *   0 = its players' rows, 1 = the hub rows (same order), and for each remote
+ *   group-mate unit (o, f) (the L rows of player o at frame f) the
+ *   stream-packed first row remote_key[o*T + f] = (stream << 24) | row (-1 if
+ *   absent): a buffer of frames fetched before the launch, or the owning
+ *   rank's buffer mapped from its GPU (read in place over NVLink).
+ * Player rows get their full key sets (one query pair per player frame, key
+ * tiles with per-key masks: launch with mask_rows 1).  Hub rows are cut into
+ * 128-row tiles of one group's rows (or of the global rows), two per query
+ * pair, whose key tiles carry one 128-row mask per half (q_pairs[6] = 1
+ * selects those for the pair); they get the keys this rank holds (its
+ * players' rows, plus the hub rows if hub_keys) and are merged across ranks
+ * with hier_lse_prepare / hier_lse_finish.  An inactive local hub attends to
+ * itself only.  No reference counterpart in code: the reference runs every
+ * player on one device; this realises the player sharding of the
+ * multi-GPU configurations. */
 typedef struct hier_shard_desc {
   int32_t P, N, L, KL, KG, T, n_block, local_attn, direct;
   int32_t p0, p1;
   int32_t hub_keys;
-  int32_t hub_group_major; /* stream 1 holds the local hubs group-major: (g, f, slot) at row
-                              (g*T + f)*K_L + slot, then the global hubs frame-major */
+  int32_t reserved;
   const int64_t* labels;      /* [T, P] */
   const uint8_t* active;      /* [T, N] */
   const int32_t* remote_key;  /* [P*T] */
 } hier_shard_desc;
 
-/* n_layouts, n_seg, n_pairs (per layout), tile_capacity, q_rows of a shard. */
-int hier_shard_sizes(const hier_shard_desc* g, hier_tiled_sizes_t* out);
+typedef struct hier_shard_sizes_t {
+  int32_t n_pairs;       /* query pairs: players' (per layout, layouts in order), then hubs' */
+  int32_t n_counts;      /* int32 scratch entries of hier_shard_plan */
+  int32_t tile_capacity; /* key tiles */
+  int32_t reserved;
+  int64_t mask_words;    /* uint32 words of tile_masks */
+  int64_t own_rows;      /* the rank's player rows */
+  int64_t q_rows;        /* query rows (player rows, then hub rows) */
+} hier_shard_sizes_t;
 
-/* Attention plan of a shard (n_boxes: int32 [n_layouts*n_seg] scratch);
- * status bit 3: a remote unit the plan needs has no slot.  No host sync. */
-int hier_shard_plan(const hier_shard_desc* g, int32_t* n_boxes, int32_t* q_pairs,
+int hier_shard_sizes(const hier_shard_desc* g, hier_shard_sizes_t* out);
+
+/* Attention plan of a shard (n_counts: int32 [n_counts] scratch); status
+ * bit 3: a remote unit the plan needs has no slot, bit 1: tile overflow.
+ * No host sync. */
+int hier_shard_plan(const hier_shard_desc* g, int32_t* n_counts, int32_t* q_pairs,
                     int32_t* kv_tiles, uint32_t* tile_masks, int32_t tile_capacity,
                     int32_t* order, int32_t* status, void* stream);
 

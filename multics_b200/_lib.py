@@ -90,8 +90,18 @@ class HierShardDesc(ctypes.Structure):
     _fields_ = [
         ("P", c_int32), ("N", c_int32), ("L", c_int32), ("KL", c_int32), ("KG", c_int32),
         ("T", c_int32), ("n_block", c_int32), ("local_attn", c_int32), ("direct", c_int32),
-        ("p0", c_int32), ("p1", c_int32), ("hub_keys", c_int32), ("hub_group_major", c_int32),
+        ("p0", c_int32), ("p1", c_int32), ("hub_keys", c_int32), ("reserved", c_int32),
         ("labels", c_void_p), ("active", c_void_p), ("remote_key", c_void_p),
+    ]
+
+
+class HierShardSizes(ctypes.Structure):
+    """Mirror of ``hier_shard_sizes_t``."""
+
+    _fields_ = [
+        ("n_pairs", c_int32), ("n_counts", c_int32), ("tile_capacity", c_int32),
+        ("reserved", c_int32), ("mask_words", c_int64), ("own_rows", c_int64),
+        ("q_rows", c_int64),
     ]
 
 
@@ -108,11 +118,11 @@ _SIGS = {
     "hier_block_mask_build_static": (c_int, [ctypes.POINTER(HierGrouping), _P, _P, _P, _P, _P, _P, _P,
                                              _P]),
     "hier_prep_qk": (c_int, [_P, _P, c_int64, _P, c_int32, _P, _P, _P, _P, _P, c_int64, c_int32,
-                             c_int32, c_float, _P, _P, c_int64, _P]),
+                             c_int32, c_float, _P, _P, c_int64, _P, _P]),
     "hier_attn_fwd": (c_int, [_P, c_int64, c_int64, _P, _P, c_int64, c_int64, _P, c_int64, c_int32,
                               c_int32, _P, c_int32, _P, _P, _P, c_float, _P, _P]),
     "hier_attn_fwd_streams": (c_int, [_P, c_int64, c_int64, c_int32, _P, _P, _P, _P, _P, c_int64,
-                                      c_int32, c_int32, _P, c_int32, _P, _P, c_int32, _P,
+                                      _P, c_int32, c_int32, _P, c_int32, _P, _P, c_int32, _P,
                                       c_float, _P, _P, _P]),
     "hier_cached_sizes": (c_int, [ctypes.POINTER(HierCachedGrouping), c_int32,
                                   ctypes.POINTER(HierCachedSizes)]),
@@ -126,7 +136,7 @@ _SIGS = {
     "hier_tiled_count": (c_int, [ctypes.POINTER(HierTiledGrouping), _P, _P, _P, _P, _P]),
     "hier_tiled_build": (c_int, [ctypes.POINTER(HierTiledGrouping), _P, _P, _P, _P, _P, _P, _P, _P,
                                  _P, _P, _P, c_int32, _P, _P, _P]),
-    "hier_shard_sizes": (c_int, [ctypes.POINTER(HierShardDesc), ctypes.POINTER(HierTiledSizes)]),
+    "hier_shard_sizes": (c_int, [ctypes.POINTER(HierShardDesc), ctypes.POINTER(HierShardSizes)]),
     "hier_shard_plan": (c_int, [ctypes.POINTER(HierShardDesc), _P, _P, _P, _P, c_int32, _P, _P,
                                 _P]),
     "hier_lse_prepare": (c_int, [_P, c_int64, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P]),

@@ -7,6 +7,9 @@ Drop-in counterparts of the reference's ``multics/models/attention.py``:
 * :func:`hier_block_attention` - attention over a :class:`HierBlockMask`
   (the role of ``flash_attention(mask)`` / FlexAttention,
   ``attention.py:39-54,322-353``);
+* :class:`HierSequencePlan` - the faster work plan the layer entry points
+  use for labels groupings: one query pair per player frame over its exact
+  key runs, hub queries in 128-row tiles of one group;
 * :class:`SelfAttention` - same constructor and ``forward(x, freqs, mask,
   cam_tokens)`` signature as the reference module (``attention.py:255-442``).
 """
@@ -14,8 +17,10 @@ Drop-in counterparts of the reference's ``multics/models/attention.py``:
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
+import numpy as np
 import torch
 import torch.nn as nn
 
@@ -24,7 +29,13 @@ from ._lib import check, ptr, stream_ptr
 from .hier_masks import HierBlockMask
 
 __all__ = ["hier_prep_qk", "hier_block_attention", "freqs_table", "RMSNorm", "SelfAttention",
-           "AttentionPlan", "attention_from_plan"]
+           "AttentionPlan", "attention_from_plan", "HierSequencePlan", "sequence_plan",
+           "hier_attention_layer"]
+
+# Work plan of the full-sequence layer entry points: "segments" (the
+# HierSequencePlan wherever the grouping allows it) or "blocks" (always the
+# 128x128 block plan of the HierBlockMask).
+FULL_SEQUENCE_PLAN_ENV = "MULTICS_B200_FULL_SEQUENCE_PLAN"
 
 _DEV_ERR = {}
 
@@ -69,11 +80,13 @@ def _rows(x):
 
 
 def hier_prep_qk(qx, kx, freqs, num_heads, *, norm_q_weight, norm_k_weight, cam_tokens=None,
-                 cam_q_weight=None, cam_k_weight=None, eps=1e-6, out=None):
+                 cam_q_weight=None, cam_k_weight=None, eps=1e-6, out=None, out_rows=None):
     """``q = rope(rmsnorm(qx + cam @ Wq^T) * wq)`` and the same for k, bf16.
 
     ``freqs``: complex ``[S,1,D/2]`` (as built by the reference's freq
-    builders) or a float32 ``[S,D/2,2]`` table from :func:`freqs_table`."""
+    builders) or a float32 ``[S,D/2,2]`` table from :func:`freqs_table`.
+    ``out_rows`` (int32 ``[S]`` on the device, a permutation) writes token
+    ``r`` to row ``out_rows[r]`` of the outputs."""
     q2, k2 = _rows(qx), _rows(kx)
     S, dim = q2.shape
     if q2.dtype != torch.bfloat16 or k2.dtype != torch.bfloat16:
@@ -104,10 +117,13 @@ def hier_prep_qk(qx, kx, freqs, num_heads, *, norm_q_weight, norm_k_weight, cam_
         cam_k_weight = cam_k_weight.to(torch.bfloat16).contiguous()
     nqw = norm_q_weight.to(torch.bfloat16).contiguous()
     nkw = norm_k_weight.to(torch.bfloat16).contiguous()
+    if out_rows is not None and (out_rows.dtype != torch.int32 or out_rows.numel() != S
+                                 or out_rows.device != q2.device):
+        raise ValueError(f"out_rows must be int32 [{S}] on {q2.device}")
     check(_lib.lib().hier_prep_qk(
         ptr(q2), ptr(k2), q2.stride(0), ptr(cam), cam_dim, ptr(cam_q_weight), ptr(cam_k_weight),
         ptr(nqw), ptr(nkw), ptr(ft), S, num_heads, D, float(eps), ptr(q_out), ptr(k_out),
-        q_out.stride(0), stream_ptr(q2.device)))
+        q_out.stride(0), ptr(out_rows), stream_ptr(q2.device)))
     return q_out, k_out
 
 
@@ -151,6 +167,77 @@ def attention_from_plan(q, k, v, plan, num_heads, *, out=None, softmax_scale=Non
     return out
 
 
+class HierSequencePlan:
+    """Full-sequence attention plan of one labels grouping on one GPU (the
+    player-shard plan with a single shard, ``hier_shard_plan``).
+
+    Each player frame's L query rows form one query pair over the frame's
+    exact key runs (own history, group-mate frames of the block, its group's
+    hub tokens); hub query rows run in 128-row tiles of one group's frames
+    with per-row masks.  The plan's row order is the sequence order with the
+    hub rows group-major (``ShardTopology.hub_rows_order``): the prologue
+    writes q and k in that order (``seq_to_plan``), ``v``'s hub rows are
+    gathered into it, and the kernel writes every output row back to its
+    sequence row (``plan_to_seq``).  Same edges as the block plan, so the same
+    results up to the order of floating-point sums."""
+
+    def __init__(self, spec, num_heads: int):
+        from .sharded import ShardedHierAttention, ShardTopology
+
+        if not HierSequencePlan.supports(spec):
+            raise ValueError("HierSequencePlan needs a labels grouping without the no-local "
+                             "topology, T % n_block == 0 and local_attn -1 or >= n_block")
+        dev = spec.active.device
+        topo = ShardTopology(P=spec.P, T=spec.T, L=spec.L, N=spec.N, KL=spec.KL, KG=spec.KG,
+                             n_block=spec.n_block, local_attn=spec.local_attn,
+                             direct=spec.direct, labels=spec.labels.cpu().numpy(), world=1,
+                             rank=0)
+        self.topo = topo
+        self.num_heads = num_heads
+        self.core = ShardedHierAttention(topo, num_heads, dev, active=spec.active)
+        order = topo.local_rows()  # plan row -> sequence row
+        inv = np.empty_like(order)
+        inv[order] = np.arange(order.size)
+        self.A = topo.own_rows
+        self.S = int(order.size)
+        self.plan_to_seq = torch.from_numpy(order.astype(np.int32)).to(dev)
+        self.seq_to_plan = torch.from_numpy(inv.astype(np.int32)).to(dev)
+        self.hub_src = torch.from_numpy((order[self.A:] - self.A).astype(np.int64)).to(dev)
+        self.core.check_status()
+
+    @staticmethod
+    def supports(spec) -> bool:
+        return (spec.membership is None and spec.labels is not None and not spec.no_local
+                and spec.T % spec.n_block == 0
+                and (spec.local_attn == -1 or spec.local_attn >= spec.n_block))
+
+    def attend(self, q_plan, k_plan, v, out=None):
+        """Attention of roped ``q_plan`` / ``k_plan`` (plan row order) and
+        ``v`` (sequence order), all ``[S, H*D]`` bf16; returns ``out`` in
+        sequence order."""
+        if out is None:
+            out = torch.empty_like(v)
+        v_hub = v[self.A:].index_select(0, self.hub_src)
+        self.core.attend(q_plan, k_plan, v, out, v_hub=v_hub, out_rows=self.plan_to_seq,
+                         lse=False)
+        return out
+
+
+def sequence_plan(block_mask: HierBlockMask, num_heads: int) -> Optional[HierSequencePlan]:
+    """The :class:`HierSequencePlan` of ``block_mask``'s grouping (built once
+    per mask and head count), or None when the grouping needs the block plan
+    or ``MULTICS_B200_FULL_SEQUENCE_PLAN=blocks``."""
+    mode = os.environ.get(FULL_SEQUENCE_PLAN_ENV, "segments")
+    if mode not in ("segments", "blocks"):
+        raise ValueError(f"{FULL_SEQUENCE_PLAN_ENV} must be 'segments' or 'blocks', got {mode!r}")
+    if mode == "blocks" or not HierSequencePlan.supports(block_mask.spec):
+        return None
+    plans = block_mask.__dict__.setdefault("_sequence_plans", {})
+    if num_heads not in plans:
+        plans[num_heads] = HierSequencePlan(block_mask.spec, num_heads)
+    return plans[num_heads]
+
+
 def hier_block_attention(q, k, v, block_mask: HierBlockMask, num_heads, *, out=None):
     """Attention of roped ``q``/``k`` and ``v`` (``[1,S,H*D]`` or ``[S,H*D]``)
     under a :class:`HierBlockMask`; returns ``[1,S,H*D]`` bf16."""
@@ -165,9 +252,13 @@ def hier_attention_layer(qx, kx, v, freqs, block_mask: HierBlockMask, num_heads,
     camera + RMSNorm + RoPE prologue, then block-sparse attention.  Equivalent
     to the reference's ``_project_self_attn_qkv`` tail + ``flash_attention(mask)``
     (``attention.py:355-365,39-54``); returns ``[S, H*D]`` bf16."""
+    sp = sequence_plan(block_mask, num_heads)
     q, k = hier_prep_qk(qx, kx, freqs, num_heads, norm_q_weight=norm_q_weight,
                         norm_k_weight=norm_k_weight, cam_tokens=cam_tokens,
-                        cam_q_weight=cam_q_weight, cam_k_weight=cam_k_weight, eps=eps)
+                        cam_q_weight=cam_q_weight, cam_k_weight=cam_k_weight, eps=eps,
+                        out_rows=None if sp is None else sp.seq_to_plan)
+    if sp is not None:
+        return sp.attend(q, k, _rows(v), out)
     return attention_from_plan(q, k, v, block_mask, num_heads, out=out)
 
 
@@ -233,8 +324,9 @@ class SelfAttention(nn.Module):
         nn.init.zeros_(self.cam_q.weight)
         nn.init.zeros_(self.cam_k.weight)
 
-    def project_qkv(self, x, freqs, cam_tokens=None):
-        """Projected + fused-prologue ``(q, k, v)`` as ``[S, dim]`` bf16 rows."""
+    def project_qkv(self, x, freqs, cam_tokens=None, out_rows=None):
+        """Projected + fused-prologue ``(q, k, v)`` as ``[S, dim]`` bf16 rows
+        (``out_rows``: the row of each token in q and k, see :func:`hier_prep_qk`)."""
         if cam_tokens is not None and (self.cam_q is None or self.cam_k is None):
             raise RuntimeError("camera_pose was provided but enable_camera_pose_qk() was not called")
         if cam_tokens is not None and cam_tokens.shape[:2] != x.shape[:2]:
@@ -249,15 +341,21 @@ class SelfAttention(nn.Module):
             qx, kx, freqs, self.num_heads, norm_q_weight=self.norm_q.weight,
             norm_k_weight=self.norm_k.weight, cam_tokens=cam_tokens,
             cam_q_weight=None if self.cam_q is None else self.cam_q.weight,
-            cam_k_weight=None if self.cam_k is None else self.cam_k.weight, eps=self.norm_q.eps)
+            cam_k_weight=None if self.cam_k is None else self.cam_k.weight, eps=self.norm_q.eps,
+            out_rows=out_rows)
         return q, k, _rows(v)
 
     def forward(self, x, freqs, mask=None, cam_tokens=None):
         if not isinstance(mask, HierBlockMask):
             raise TypeError("multics_b200 SelfAttention.forward requires a HierBlockMask "
                             "(build_stage2_hier_flex_block_mask)")
-        q, k, v = self.project_qkv(x, freqs, cam_tokens)
-        out = attention_from_plan(q, k, v, mask, self.num_heads)
+        sp = sequence_plan(mask, self.num_heads)
+        q, k, v = self.project_qkv(x, freqs, cam_tokens,
+                                   out_rows=None if sp is None else sp.seq_to_plan)
+        if sp is not None:
+            out = sp.attend(q, k, v)
+        else:
+            out = attention_from_plan(q, k, v, mask, self.num_heads)
         return self.o(out.unsqueeze(0))
 
 

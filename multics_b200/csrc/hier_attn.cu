@@ -83,6 +83,7 @@ struct AttnArgs {
   const int* order;
   __nv_bfloat16* out;
   int64_t out_stride;
+  const int32_t* out_rows;  // output (and lse) row of each query row; NULL: the same row
   int n_pairs;
   int mask_stride;    // entries per partial-tile mask: 128 (per row) or 1 (per key only)
   int mask_row_and;   // 127 or 0
@@ -249,7 +250,7 @@ __device__ __forceinline__ void control_role(const AttnArgs& a, int4 pq, int kv_
 
 __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_begin, int n_kv,
                                              uint32_t tbase, int warp, const Bars& B, int col,
-                                             int use) {
+                                             int use, bool row_masks128) {
   const int h = (warp >> 2) - 1;  // 0 for warps 4-7, 1 for warps 8-11
   const int row = threadIdx.x - 128 * (h + 1);
   const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
@@ -258,7 +259,13 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
   const int q_start = h ? pq.z : pq.x;
   const int q_rows = h ? pq.w : pq.y;
   const bool store_row = row < q_rows;
-  __nv_bfloat16* orow = a.out + (int64_t)(q_start + row) * a.out_stride + col;
+  const int64_t dst_row =
+      (a.out_rows && store_row) ? (int64_t)a.out_rows[q_start + row] : (int64_t)(q_start + row);
+  __nv_bfloat16* orow = a.out + dst_row * a.out_stride + col;
+  // a pair flagged in q_pairs[6] carries one mask per query row whatever the
+  // launch's mask format
+  const int mask_stride = row_masks128 ? kBM : a.mask_stride;
+  const int mask_row_and = row_masks128 ? kBM - 1 : a.mask_row_and;
   float m_run = -INFINITY, l_run = 0.f;  // running max in scaled log2 units
   int c = 0;                             // key tiles processed by this half
   const float sc = a.scale_log2;
@@ -272,7 +279,7 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
     if (mi == kSkip) continue;
     const bool partial = mi >= 0;  // uniform across the CTA
     uint4 mk = make_uint4(~0u, ~0u, ~0u, ~0u);
-    if (partial) mk = a.row_masks[(int64_t)mi * a.mask_stride + (row & a.mask_row_and)];
+    if (partial) mk = a.row_masks[(int64_t)mi * mask_stride + (row & mask_row_and)];
     // S_h(c) is committed after PV_h(c-1), so once it is visible O holds
     // every earlier P V product and can be rescaled without another wait.
     if (!mbar_wait(B.s_full + h, c & 1, a.err, 11)) return;
@@ -344,7 +351,7 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
       const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int q = 0; q < kHD / 8; ++q) reinterpret_cast<uint4*>(orow)[q] = z;
-      if (a.lse) a.lse[(int64_t)(q_start + row) * a.n_heads + col / kHD] = -INFINITY;
+      if (a.lse) a.lse[dst_row * a.n_heads + col / kHD] = -INFINITY;
     }
     return;
   }
@@ -352,7 +359,7 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
   tc_fence_after();
   const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
   if (a.lse && store_row)  // O = sum_j 2^(s_j - lse) v_j
-    a.lse[(int64_t)(q_start + row) * a.n_heads + col / kHD] =
+    a.lse[dst_row * a.n_heads + col / kHD] =
         l_run > 0.f ? m_run + __log2f(l_run) : -INFINITY;
   uint32_t r[32];
 #pragma unroll
@@ -430,7 +437,7 @@ __global__ void __launch_bounds__(384, 1)
   const int col = head * kHD;
   if (warp >= 4) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-    softmax_role(a, pq, kv_begin, n_kv, tbase, warp, B, col, use);
+    softmax_role(a, pq, kv_begin, n_kv, tbase, warp, B, col, use, pk.z == 1);
   } else {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
     control_role<kMaps>(a, pq, kv_begin, n_kv, tbase, warp, lane, smem, &tmq, kv, B, col, use);
@@ -470,7 +477,7 @@ int attn_setup(const void* q, int64_t q_rows_total, int64_t q_stride, int32_t H,
 
 template <int kMaps>
 int attn_launch(const CUtensorMap& tmq, const KVMaps<kMaps>& kv, void* out, int64_t out_stride,
-                int32_t H, const int32_t* q_pairs, int32_t n_pairs, const int32_t* kv_tiles,
+                const int32_t* out_rows, int32_t H, const int32_t* q_pairs, int32_t n_pairs, const int32_t* kv_tiles,
                 const uint32_t* row_masks, int mask_rows, const int32_t* order,
                 float softmax_scale, float* lse, int32_t* dev_err, void* stream) {
   static bool attr_set = false;
@@ -487,6 +494,7 @@ int attn_launch(const CUtensorMap& tmq, const KVMaps<kMaps>& kv, void* out, int6
   args.order = order;
   args.out = reinterpret_cast<__nv_bfloat16*>(out);
   args.out_stride = out_stride;
+  args.out_rows = out_rows;
   args.n_pairs = n_pairs;
   args.mask_stride = mask_rows;
   args.mask_row_and = mask_rows - 1;
@@ -520,15 +528,15 @@ extern "C" int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stri
   rc = make_tmap_bf16_2d(&kv.k[0], k, (uint64_t)H * D, (uint64_t)kv_rows_total, kv_stride, 64, 64);
   if (!rc) rc = make_tmap_bf16_2d(&kv.v[0], v, (uint64_t)H * D, (uint64_t)kv_rows_total, kv_stride, 64, 64);
   if (rc) return rc;
-  return attn_launch<1>(tmq, kv, out, out_stride, H, q_pairs, n_pairs, kv_tiles, row_masks, kBM,
+  return attn_launch<1>(tmq, kv, out, out_stride, nullptr, H, q_pairs, n_pairs, kv_tiles, row_masks, kBM,
                         order, softmax_scale, nullptr, dev_err, stream);
 }
 
 extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_t q_stride,
                                      int32_t n_streams, const void* const* k, const void* const* v,
                                      const int64_t* stream_rows, const int64_t* kv_stride,
-                                     void* out, int64_t out_stride, int32_t H, int32_t D,
-                                     const int32_t* q_pairs, int32_t n_pairs,
+                                     void* out, int64_t out_stride, const int32_t* out_rows,
+                                     int32_t H, int32_t D, const int32_t* q_pairs, int32_t n_pairs,
                                      const int32_t* kv_tiles, const uint32_t* tile_masks,
                                      int32_t mask_rows, const int32_t* order,
                                      float softmax_scale, float* lse, int32_t* dev_err,
@@ -574,7 +582,7 @@ extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_
       kv.v[s] = kv.v[first];
     }
   }
-  return attn_launch<HIER_MAX_KV_STREAMS>(tmq, kv, out, out_stride, H, q_pairs, n_pairs, kv_tiles,
+  return attn_launch<HIER_MAX_KV_STREAMS>(tmq, kv, out, out_stride, out_rows, H, q_pairs, n_pairs, kv_tiles,
                                           tile_masks, mask_rows, order, softmax_scale, lse,
                                           dev_err, stream);
 }

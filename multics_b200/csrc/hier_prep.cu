@@ -31,6 +31,7 @@ struct PrepArgs {
   __nv_bfloat16* q_out;
   __nv_bfloat16* k_out;
   int64_t out_stride;
+  const int32_t* out_rows;  // output row of each input row (NULL: the same row)
 };
 
 constexpr int kMaxCam = 16;
@@ -228,7 +229,8 @@ __global__ void __launch_bounds__(384, 1) prep_qk_kernel(PrepArgs a) {
         const float a0 = xv[2 * q] * rs * nv[2 * q], a1 = xv[2 * q + 1] * rs * nv[2 * q + 1];
         po[q] = pack_bf16x2(a0 * c - a1 * s, a0 * s + a1 * c);
       }
-      *reinterpret_cast<uint4*>(out + (row0 + r) * a.out_stride + d0) = o;
+      const int64_t dst = a.out_rows ? (int64_t)a.out_rows[row0 + r] : row0 + r;
+      *reinterpret_cast<uint4*>(out + dst * a.out_stride + d0) = o;
     };
     if (CAM == 0 || shared_cam) {  // proj still holds the chunk's shared projection
 #pragma unroll
@@ -253,7 +255,7 @@ extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, co
                             int32_t cam_dim, const void* wcq, const void* wck, const void* nqw,
                             const void* nkw, const float* freqs, int64_t S, int32_t H, int32_t D,
                             float eps, void* q_out, void* k_out, int64_t out_stride,
-                            void* stream) {
+                            const int32_t* out_rows, void* stream) {
   clear_error();
   const int dim = H * D;
   if (dim % 8 != 0 || dim / 8 > 384 || dim / 8 < 32 || (dim / 8) % 32 != 0 || D % 8 != 0) {
@@ -283,6 +285,7 @@ extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, co
   p.q_out = (__nv_bfloat16*)q_out;
   p.k_out = (__nv_bfloat16*)k_out;
   p.out_stride = out_stride;
+  p.out_rows = out_rows;
   const int threads = dim / 8;
   if (x_stride % 8 || out_stride % 8 || (reinterpret_cast<uintptr_t>(qx) & 15) ||
       (reinterpret_cast<uintptr_t>(kx) & 15) || (reinterpret_cast<uintptr_t>(freqs) & 15)) {

@@ -7,8 +7,10 @@ does not divide).  Per layer:
    direct player edges need (``all_to_all_single``; with static groups kept
    on one rank nothing moves);
 2. **attention** - one tcgen05 launch over the rank's query rows (its
-   players' rows, then every hub row) reading three key/value streams in
-   place: its players' rows, the hub rows, the received mate frames;
+   players' rows, then every hub row, the hubs group-major) reading three
+   key/value streams in place: its players' rows, the hub rows, the received
+   mate frames.  Player rows run one query pair per player frame; hub rows
+   run in 128-row tiles of one group's frames with per-row masks;
 3. **hub merge** - hub rows were computed over the keys each rank holds;
    their partial results merge from the per-row log-sum-exp with an
    all-reduce of the max and one all-reduce of the scaled partial sums.
@@ -29,7 +31,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import HierShardDesc, HierTiledSizes, check, ptr, stream_ptr
+from ._lib import HierShardDesc, HierShardSizes, check, ptr, stream_ptr
 
 __all__ = ["split_players", "ShardTopology", "ShardedHierAttention", "merge_hub_partials",
            "exchange_mate_frames"]
@@ -121,12 +123,23 @@ class ShardTopology:
                         units.add((o, kf))
         return sorted(units, key=lambda u: (self.owner[u[0]], u[0], u[1]))
 
+    def hub_rows_order(self) -> np.ndarray:
+        """Sequence rows of the hub rows in the shard's order: local hubs
+        group-major ``(g, f, slot)``, then the global hubs ``(f, slot)``.  A
+        group's hub tokens of consecutive frames are consecutive rows, so a
+        hub query tile holds one group and a player's hub keys form one run."""
+        T, N, KL, KG = self.T, self.N, self.KL, self.KG
+        A = self.P * T * self.L
+        g_i, f_i, s_i = np.meshgrid(np.arange(N), np.arange(T), np.arange(KL), indexing="ij")
+        local = A + ((f_i * N + g_i) * KL + s_i).reshape(-1)
+        glob = A + T * N * KL + np.arange(T * KG)
+        return np.concatenate([local, glob]).astype(np.int64)
+
     def local_rows(self) -> np.ndarray:
-        """Sequence rows of this rank's query rows (own players, then hubs)."""
-        A = self.P * self.T * self.L
+        """Sequence rows of this rank's query rows: its players' rows, then
+        every hub row in :meth:`hub_rows_order`."""
         own = np.arange(self.p0 * self.T * self.L, self.p1 * self.T * self.L)
-        hubs = np.arange(A, A + self.hub_rows)
-        return np.concatenate([own, hubs])
+        return np.concatenate([own, self.hub_rows_order()])
 
 
 def _stream_arrays(streams):
@@ -197,7 +210,7 @@ class ShardedHierAttention:
     :meth:`k_buffer` / :meth:`v_buffer` (other tensors are copied there)."""
 
     def __init__(self, topo: ShardTopology, num_heads: int, device, group=None,
-                 transport: str = "exchange"):
+                 transport: str = "exchange", active=None):
         if transport not in ("exchange", "peer"):
             raise ValueError(f"unknown transport {transport!r}")
         self.topo = topo
@@ -210,30 +223,36 @@ class ShardedHierAttention:
         dev = self.device
         self.transport = transport if (t.world > 1 and t.direct) else "exchange"
         self._labels = torch.from_numpy(t.labels).to(dev).contiguous()
-        act = np.zeros((t.T, t.N), dtype=np.uint8)
-        for f in range(t.T):
-            for p in range(t.P):
-                act[f, t.labels[f, p]] = 1
-        self._active = torch.from_numpy(act).to(dev)
+        if active is None:
+            act = np.zeros((t.T, t.N), dtype=np.uint8)
+            for f in range(t.T):
+                for p in range(t.P):
+                    act[f, t.labels[f, p]] = 1
+            self._active = torch.from_numpy(act).to(dev)
+        else:  # the caller's active groups ([T, N]), as the reference accepts
+            self._active = torch.as_tensor(active).to(device=dev, dtype=torch.uint8).contiguous()
+            if tuple(self._active.shape) != (t.T, t.N):
+                raise ValueError(f"active must be [T={t.T}, N={t.N}], got "
+                                 f"{tuple(self._active.shape)}")
         self._keys = torch.from_numpy(t.remote_keys(self.transport)).to(dev)
         d = HierShardDesc()
         d.P, d.N, d.L, d.KL, d.KG, d.T = t.P, t.N, t.L, t.KL, t.KG, t.T
         d.n_block, d.local_attn, d.direct = t.n_block, t.local_attn, int(t.direct)
         d.p0, d.p1, d.hub_keys = t.p0, t.p1, int(t.rank == 0)
-        d.hub_group_major = 1
         d.labels, d.active, d.remote_key = (self._labels.data_ptr(), self._active.data_ptr(),
                                             self._keys.data_ptr())
         self.desc = d
-        sz = HierTiledSizes()
+        sz = HierShardSizes()
         lib = _lib.lib()
         check(lib.hier_shard_sizes(ctypes.byref(d), ctypes.byref(sz)))
-        self.n_pairs = sz.n_layouts * sz.n_pairs
+        self.n_pairs = int(sz.n_pairs)
         cap = max(sz.tile_capacity, 1)
         self.q_rows = int(sz.q_rows)
-        self.n_boxes = torch.empty(sz.n_layouts * sz.n_seg, dtype=torch.int32, device=dev)
+        self.n_boxes = torch.empty(max(sz.n_counts, 1), dtype=torch.int32, device=dev)
         self.q_pairs = torch.empty((max(self.n_pairs, 1), 8), dtype=torch.int32, device=dev)
         self.kv_tiles = torch.empty((cap, 4), dtype=torch.int32, device=dev)
-        self.tile_masks = torch.empty((cap, 4), dtype=torch.int32, device=dev)
+        self.tile_masks = torch.empty((max(sz.mask_words // 4, 1), 4), dtype=torch.int32,
+                                      device=dev)
         self.order = torch.empty(max(self.n_pairs, 1), dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         check(lib.hier_shard_plan(ctypes.byref(d), ptr(self.n_boxes), ptr(self.q_pairs),
@@ -244,15 +263,6 @@ class ShardedHierAttention:
         self.remote = torch.zeros((max(self.n_recv, 1), 2 * self.dim), dtype=torch.bfloat16,
                                   device=dev)
         self.lse = torch.empty((self.q_rows, self.H), dtype=torch.float32, device=dev)
-        # hub keys/values group-major, so that a group's hub tokens of
-        # consecutive frames are consecutive rows (one key run per group)
-        g_i, f_i, s_i = np.meshgrid(np.arange(t.N), np.arange(t.T), np.arange(t.KL),
-                                    indexing="ij")
-        src = ((f_i * t.N + g_i) * t.KL + s_i).reshape(-1)
-        perm = np.concatenate([src, np.arange(t.T * t.N * t.KL, t.hub_rows)])
-        self.hub_perm = torch.from_numpy(perm.astype(np.int64)).to(dev)
-        self.hub_k = torch.empty((t.hub_rows, self.dim), dtype=torch.bfloat16, device=dev)
-        self.hub_v = torch.empty_like(self.hub_k)
         from .attention import _dev_err
         self.err = _dev_err(dev)
         self._sym = None
@@ -322,14 +332,18 @@ class ShardedHierAttention:
             self.remote[i * t.L:(i + 1) * t.L, :self.dim] = k_all[src:src + t.L]
             self.remote[i * t.L:(i + 1) * t.L, self.dim:] = v_all[src:src + t.L]
 
-    def attend(self, q, k, v, out):
+    def attend(self, q, k, v, out, *, v_hub=None, out_rows=None, lse=True):
+        """One attention launch over this rank's query rows.  ``v_hub``
+        replaces ``v``'s hub rows (a group-major copy when ``v`` keeps the
+        sequence order); ``out_rows`` (int32 per query row) sends each row's
+        output (and log-sum-exp) to that row of ``out``; ``lse=False`` skips
+        the log-sum-exp (nothing to merge)."""
         t = self.topo
         own, hub = t.own_rows, t.hub_rows
         if self.transport == "peer":
             k, v = self.k_buffer(), self.v_buffer()
-        torch.index_select(k[own:own + hub], 0, self.hub_perm, out=self.hub_k)
-        torch.index_select(v[own:own + hub], 0, self.hub_perm, out=self.hub_v)
-        streams = [(k[:own], v[:own]), (self.hub_k, self.hub_v)]
+        streams = [(k[:own], v[:own]),
+                   (k[own:own + hub], v[own:own + hub] if v_hub is None else v_hub)]
         if self.transport == "peer":
             streams += self._peers
         else:
@@ -337,9 +351,9 @@ class ShardedHierAttention:
         n, kp, vp, rows, strides = _stream_arrays(streams)
         check(_lib.lib().hier_attn_fwd_streams(
             ptr(q), q.shape[0], q.stride(0), n, kp, vp, rows, strides, ptr(out), out.stride(0),
-            self.H, self.D, ptr(self.q_pairs), self.n_pairs, ptr(self.kv_tiles),
-            ptr(self.tile_masks), 1, ptr(self.order), 1.0 / math.sqrt(self.D), ptr(self.lse),
-            ptr(self.err), stream_ptr(q.device)))
+            ptr(out_rows), self.H, self.D, ptr(self.q_pairs), self.n_pairs, ptr(self.kv_tiles),
+            ptr(self.tile_masks), 1, ptr(self.order), 1.0 / math.sqrt(self.D),
+            ptr(self.lse) if lse else None, ptr(self.err), stream_ptr(q.device)))
 
     def forward(self, q, k, v, out=None):
         t = self.topo

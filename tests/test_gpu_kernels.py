@@ -252,6 +252,76 @@ def test_attention_random_configs_vs_torch_fp32(dev, case):
     assert _cos(out.float(), ref) >= MIN_COS
 
 
+SEQUENCE_CASES = [c for c in RANDOM_CASES if c[-1] == "labels"] + [
+    (3, 4, 70, 3, 5, 6, 2, -1, "labels"),   # a group idle in some frames
+    (2, 12, 40, 2, 16, 6, 1, -1, "labels"),  # several 128-row hub tiles per group
+]
+
+
+@pytest.mark.parametrize("case", SEQUENCE_CASES)
+def test_sequence_plan_random_configs_vs_torch_fp32(dev, case):
+    """The sequence plan (player-frame pairs, group tiles of hub queries) on
+    roped q/k permuted into its row order; output rows return to the
+    sequence order."""
+    from multics_b200.attention import sequence_plan
+    from multics_b200.hier_masks import build_stage2_hier_flex_block_mask
+
+    P, T, L, N, KL, KG, n, win, _ = case
+    H = 2
+    g = torch.Generator().manual_seed(hash(case) & 0xFFFF)
+    S = P * T * L + T * (N * KL + KG)
+    q, k, v = (torch.randn(S, H * 128, generator=g).mul(0.5).to(torch.bfloat16).to(dev)
+               for _ in range(3))
+    labels = torch.randint(0, N, (T, P), generator=g)
+    for t0 in range(0, T, n):
+        labels[t0:t0 + n] = labels[t0]
+    bm, _, _ = build_stage2_hier_flex_block_mask(P, T, L, N, KL, KG, n, win, labels.to(dev), None,
+                                                 True, dev)
+    sp = sequence_plan(bm, H)
+    assert sp is not None
+    src = sp.plan_to_seq.long()
+    out = sp.attend(q[src].contiguous(), k[src].contiguous(), v)
+    mask = torch.from_numpy(O.dense_mask(P, T, L, N, KL, KG, n, win, labels=labels.numpy(),
+                                         direct=True)).to(dev)
+    ref = torch_masked_attention(q, k, v, mask, H)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    assert float((out.float() - ref).abs().max()) <= MAX_ABS
+    assert _cos(out.float(), ref) >= MIN_COS
+
+
+@pytest.mark.parametrize("plan", ["segments", "blocks"])
+@pytest.mark.parametrize("name", [n for n in case_names("num") if "d128" in n])
+def test_layer_entry_matches_reference_fp32(dev, name, plan, monkeypatch):
+    """hier_attention_layer (prologue + attention through the plan the entry
+    point picks) vs the reference fp32 output, with either work plan."""
+    from multics_b200.attention import FULL_SEQUENCE_PLAN_ENV, hier_attention_layer
+    from multics_b200.hier_masks import build_stage2_hier_flex_block_mask
+
+    monkeypatch.setenv(FULL_SEQUENCE_PLAN_ENV, plan)
+    d = num_case(name)
+    m = d["meta"]
+    bf = lambda k: torch.from_numpy(d[k + "_bits"].view(np.int16)).view(torch.bfloat16).to(dev)  # noqa: E731
+    if m["membership"]:
+        kw = dict(group_labels=None, active_group=None,
+                  membership=torch.from_numpy(d["membership"]).to(dev),
+                  global_only=torch.from_numpy(d["global_only"]).to(dev))
+    else:
+        kw = dict(group_labels=torch.from_numpy(d["labels"]).to(dev), active_group=None)
+    bm, S, _ = build_stage2_hier_flex_block_mask(m["P"], m["T"], m["L"], m["N"], m["KL"], m["KG"],
+                                                 m["n"], m["win"], direct_player=True, device=dev,
+                                                 **kw)
+    out = hier_attention_layer(bf("qx"), bf("kx"), bf("v"), torch.from_numpy(d["freqs"]).to(dev),
+                               bm, m["H"], norm_q_weight=bf("nqw"), norm_k_weight=bf("nkw"),
+                               cam_tokens=bf("cam"), cam_q_weight=bf("wcq"),
+                               cam_k_weight=bf("wck"))
+    torch.cuda.synchronize()
+    ref = torch.from_numpy(d["out"]).to(dev)
+    assert torch.isfinite(out).all()
+    assert float((out.float() - ref).abs().max()) <= MAX_ABS
+    assert _cos(out.float(), ref) >= MIN_COS
+
+
 def test_paged_pool_matches_contiguous(dev):
     """Keys/values scattered over shuffled 64-token pages give identical output."""
     from multics_b200.attention import attention_from_plan

@@ -19,19 +19,20 @@ MAX_ABS = 2e-2
 MIN_COS = 0.9995
 
 
-def _case(P, T, L, N, KL, KG, labels, H, seed):
+def _case(P, T, L, N, KL, KG, labels, H, seed, n_block=1, win=-1):
     S = P * T * L + T * (N * KL + KG)
     g = torch.Generator().manual_seed(seed)
     mk = lambda: (torch.randn((S, H * 128), generator=g) * 0.5).to(torch.bfloat16)  # noqa: E731
     q, k, v = mk(), mk(), mk()
     act = O.active_from_labels(labels, N)
-    dense = O.dense_mask(P, T, L, N, KL, KG, 1, -1, labels=labels, active=act, direct=True)
+    dense = O.dense_mask(P, T, L, N, KL, KG, n_block, win, labels=labels, active=act,
+                         direct=True)
     f = lambda t: t.float().numpy()  # noqa: E731
     ref = O.masked_attention(f(q), f(k), f(v), H, lambda r0, r1: dense[r0:r1])
     return q, k, v, ref
 
 
-def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v):
+def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v, n_block=1, win=-1):
     from multics_b200 import _lib
     from multics_b200._lib import ptr, stream_ptr
     from multics_b200.sharded import ShardedHierAttention, ShardTopology
@@ -39,11 +40,10 @@ def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v):
     S = q.shape[0]
     qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
     out = torch.zeros((S, H * 128), dtype=torch.float32, device="cuda")
-    hub0 = P * T * L
-    hub_rows = S - hub0
+    hub_rows = S - P * T * L
     lses, parts = [], []
     for rank in range(world):
-        t = ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=1, local_attn=-1,
+        t = ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=n_block, local_attn=win,
                           direct=True, labels=labels, world=world, rank=rank)
         sh = ShardedHierAttention(t, H, "cuda")
         loc = torch.from_numpy(t.local_rows()).cuda()
@@ -70,7 +70,7 @@ def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v):
     merged = torch.empty((hub_rows, H * 128), dtype=torch.bfloat16, device="cuda")
     _lib.check(lib.hier_lse_finish(ptr(xs), ptr(ws), hub_rows, H, 128, ptr(merged),
                                    merged.stride(0), stream_ptr()))
-    out[hub0:] = merged.float()
+    out[torch.from_numpy(t.hub_rows_order()).cuda()] = merged.float()
     return out.cpu().numpy()
 
 
@@ -99,3 +99,24 @@ def test_sharded_uneven_players_match_oracle(world):
     lab = np.array([[0, 0, 0, 1, 1, 1, 2, 2, 3, 3]] * T)
     q, k, v, ref = _case(P, T, L, N, KL, KG, lab, H, seed=2)
     _check(_run_sharded(P, T, L, N, KL, KG, lab, H, world, q, k, v), ref)
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_sharded_inactive_groups_match_oracle(world):
+    """Frames where a group has no member: its hub rows attend to themselves
+    only (the mask's inactive-local self edge), and no player reaches them."""
+    P, T, L, N, KL, KG, H = 4, 6, 36, 3, 5, 2, 2
+    lab = np.array([[0, 0, 1, 1]] * 3 + [[0, 2, 2, 0]] * 3)  # group 2 idle, then group 1
+    q, k, v, ref = _case(P, T, L, N, KL, KG, lab, H, seed=4)
+    _check(_run_sharded(P, T, L, N, KL, KG, lab, H, world, q, k, v), ref)
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_sharded_blocks_and_window_match_oracle(world):
+    """Temporal blocks of 3 frames with a 3-frame window, groups reassigned
+    per block; 20 frames of local hubs (more than one 128-row hub tile per
+    group)."""
+    P, T, L, N, KL, KG, H = 4, 12, 24, 2, 16, 6, 2
+    lab = _regrouped_labels(P, T, 3, seed=5)
+    q, k, v, ref = _case(P, T, L, N, KL, KG, lab, H, seed=5, n_block=3, win=3)
+    _check(_run_sharded(P, T, L, N, KL, KG, lab, H, world, q, k, v, n_block=3, win=3), ref)

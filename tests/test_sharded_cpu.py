@@ -112,3 +112,22 @@ def test_exchange_with_two_gloo_ranks():
     assert all(p.exitcode == 0 for p in procs)
     assert [r[1] for r in res] == [True, True]
     assert all(r[2] > 0 for r in res)  # dynamic groups do cross ranks
+
+
+def test_local_rows_hubs_group_major():
+    from multics_b200.sharded import ShardTopology
+
+    P, T, L, N, KL, KG = 4, 3, 5, 2, 2, 1
+    lab = np.array([[0, 0, 1, 1]] * T)
+    t = ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=1, local_attn=-1, direct=True,
+                      labels=lab, world=2, rank=1)
+    rows = t.local_rows()
+    A = P * T * L
+    assert list(rows[:t.own_rows]) == list(range(2 * T * L, 4 * T * L))
+    hub = rows[t.own_rows:] - A
+    assert sorted(hub) == list(range(T * (N * KL + KG)))
+    # group 0 frames 0..2, then group 1 frames 0..2 (slots inside), then globals
+    f_major = lambda f, g, s: (f * N + g) * KL + s  # noqa: E731
+    expect = [f_major(f, g, s) for g in range(N) for f in range(T) for s in range(KL)]
+    expect += list(range(T * N * KL, T * (N * KL + KG)))
+    assert list(hub) == expect
