@@ -442,8 +442,8 @@ def run_ours(args, rank, world, local_rank):
                    "S": S, "useful_pairs": pairs, "useful_gflop_per_step": useful_flops / 1e9,
                    "tile_gflop_per_step": tile_flops / 1e9,
                    "parallelism": f"players sharded x{world}" if world > 1 else "single GPU",
-                   "plan": ("sequence plan: one query pair per player frame, hub queries in "
-                            "128-row group tiles" if sp is not None else
+                   "plan": ("sequence plan: 256-row player strips and 128-row group tiles of "
+                            "hub queries over exact key units" if sp is not None else
                             "128x128 block plan of the Flex block mask"),
                    "l2": "inputs larger than L2 (q/k/v 3 x %.0f MB)" % (S * cfg.dim * 2 / 1e6)},
         "breakdown_ms": {"prologue": round(statistics.mean(prep_ms), 4),

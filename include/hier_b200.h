@@ -369,7 +369,8 @@ int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_boxes, const
  * Player-sharded execution (one rank per GPU)
  * ------------------------------------------------------------------------- */
 
-/* One rank's share of a full-sequence layer (labels mode): the rank owns
+/* One rank's share of a full-sequence layer (labels mode), or with one
+ * shard (p0 = 0, p1 = P, hub_keys = 1) the whole layer: the rank owns
  * players [p0, p1); its query rows are its players' rows (player, frame,
  * patch) followed by every hub row, the hubs group-major: local hub
  * (g, f, slot) at own_rows + (g*T + f)*K_L + slot, then global hub (f, slot)
@@ -380,16 +381,16 @@ int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_boxes, const
  *   stream-packed first row remote_key[o*T + f] = (stream << 24) | row (-1 if
  *   absent): a buffer of frames fetched before the launch, or the owning
  *   rank's buffer mapped from its GPU (read in place over NVLink).
- * Player rows get their full key sets (one query pair per player frame, key
- * tiles with per-key masks: launch with mask_rows 1).  Hub rows are cut into
- * 128-row tiles of one group's rows (or of the global rows), two per query
- * pair, whose key tiles carry one 128-row mask per half (q_pairs[6] = 1
- * selects those for the pair); they get the keys this rank holds (its
- * players' rows, plus the hub rows if hub_keys) and are merged across ranks
- * with hier_lse_prepare / hier_lse_finish.  An inactive local hub attends to
- * itself only.  No reference counterpart in code: the reference runs every
- * player on one device; this realises the player sharding of the
- * multi-GPU configurations. */
+ * Query pairs are two 128-row tiles of 256-row strips of one player's rows,
+ * of one group's local-hub rows or of the global-hub rows; their key tiles
+ * cover exactly the key units some row attends to and carry one 128-row
+ * mask per half where a half sees part of a tile (q_pairs[6] = 1; launch
+ * with mask_rows 128).  Hub rows get the keys this rank holds (its players'
+ * rows, plus the hub rows if hub_keys) and are merged across ranks with
+ * hier_lse_prepare / hier_lse_finish.  An inactive local hub attends to
+ * itself only.  The edges are those of the dense mask
+ * (multics/models/hier_masks.py:364-507); no reference counterpart exists
+ * for the sharding itself: the reference runs every player on one device. */
 typedef struct hier_shard_desc {
   int32_t P, N, L, KL, KG, T, n_block, local_attn, direct;
   int32_t p0, p1;
@@ -401,23 +402,27 @@ typedef struct hier_shard_desc {
 } hier_shard_desc;
 
 typedef struct hier_shard_sizes_t {
-  int32_t n_pairs;       /* query pairs: players' (per layout, layouts in order), then hubs' */
-  int32_t n_counts;      /* int32 scratch entries of hier_shard_plan */
-  int32_t tile_capacity; /* key tiles */
-  int32_t reserved;
-  int64_t mask_words;    /* uint32 words of tile_masks */
-  int64_t own_rows;      /* the rank's player rows */
-  int64_t q_rows;        /* query rows (player rows, then hub rows) */
+  int32_t n_pairs;  /* query pairs: players' strips, then local-hub pairs, then global */
+  int32_t n_counts; /* int32 entries of the per-pair counts */
+  int64_t own_rows; /* the rank's player rows */
+  int64_t q_rows;   /* query rows (player rows, then hub rows) */
 } hier_shard_sizes_t;
 
 int hier_shard_sizes(const hier_shard_desc* g, hier_shard_sizes_t* out);
 
-/* Attention plan of a shard (n_counts: int32 [n_counts] scratch); status
- * bit 3: a remote unit the plan needs has no slot, bit 1: tile overflow.
- * No host sync. */
-int hier_shard_plan(const hier_shard_desc* g, int32_t* n_counts, int32_t* q_pairs,
-                    int32_t* kv_tiles, uint32_t* tile_masks, int32_t tile_capacity,
-                    int32_t* order, int32_t* status, void* stream);
+/* First pass: per pair its key tiles and 128-row masks (counts, int32
+ * [n_counts]) and their totals (int32 [2] on the device: key tiles, masks),
+ * from which the caller sizes kv_tiles ([tiles][4] int32) and tile_masks
+ * ([masks][128][4] uint32).  Status bit 3: a remote unit the plan needs has
+ * no slot.  No host sync. */
+int hier_shard_count(const hier_shard_desc* g, int32_t* counts, int32_t* totals,
+                     int32_t* status, void* stream);
+
+/* Second pass: the plan (q_pairs [n_pairs][8], kv_tiles, tile_masks, order
+ * [n_pairs] or NULL); status bit 1: tile capacity, bit 4: mask capacity. */
+int hier_shard_build(const hier_shard_desc* g, const int32_t* counts, int32_t* q_pairs,
+                     int32_t* kv_tiles, int32_t tile_capacity, uint32_t* tile_masks,
+                     int64_t mask_capacity, int32_t* order, int32_t* status, void* stream);
 
 /* Partial-row merge: x = 2^(lse - lse_max) * o (fp32 [rows, H*D]),
  * w = 2^(lse - lse_max) (fp32 [rows, H]); after summing x and w over the

@@ -99,9 +99,7 @@ class HierShardSizes(ctypes.Structure):
     """Mirror of ``hier_shard_sizes_t``."""
 
     _fields_ = [
-        ("n_pairs", c_int32), ("n_counts", c_int32), ("tile_capacity", c_int32),
-        ("reserved", c_int32), ("mask_words", c_int64), ("own_rows", c_int64),
-        ("q_rows", c_int64),
+        ("n_pairs", c_int32), ("n_counts", c_int32), ("own_rows", c_int64), ("q_rows", c_int64),
     ]
 
 
@@ -137,8 +135,9 @@ _SIGS = {
     "hier_tiled_build": (c_int, [ctypes.POINTER(HierTiledGrouping), _P, _P, _P, _P, _P, _P, _P, _P,
                                  _P, _P, _P, c_int32, _P, _P, _P]),
     "hier_shard_sizes": (c_int, [ctypes.POINTER(HierShardDesc), ctypes.POINTER(HierShardSizes)]),
-    "hier_shard_plan": (c_int, [ctypes.POINTER(HierShardDesc), _P, _P, _P, _P, c_int32, _P, _P,
-                                _P]),
+    "hier_shard_count": (c_int, [ctypes.POINTER(HierShardDesc), _P, _P, _P, _P]),
+    "hier_shard_build": (c_int, [ctypes.POINTER(HierShardDesc), _P, _P, _P, c_int32, _P, c_int64,
+                                 _P, _P, _P]),
     "hier_lse_prepare": (c_int, [_P, c_int64, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P]),
     "hier_lse_finish": (c_int, [_P, _P, c_int64, c_int32, c_int32, _P, c_int64, _P]),
     "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),

@@ -169,12 +169,13 @@ def attention_from_plan(q, k, v, plan, num_heads, *, out=None, softmax_scale=Non
 
 class HierSequencePlan:
     """Full-sequence attention plan of one labels grouping on one GPU (the
-    player-shard plan with a single shard, ``hier_shard_plan``).
+    player-shard plan with a single shard, ``hier_shard_count`` / ``hier_shard_build``).
 
-    Each player frame's L query rows form one query pair over the frame's
-    exact key runs (own history, group-mate frames of the block, its group's
-    hub tokens); hub query rows run in 128-row tiles of one group's frames
-    with per-row masks.  The plan's row order is the sequence order with the
+    Each player's rows run as 256-row strips (two 128-row query tiles) over
+    exactly the key units their rows attend to (own history, group-mate
+    frames of the blocks, the group's hub tokens); hub query rows run in
+    128-row tiles of one group's frames.  Tiles that some rows see only in
+    part carry per-row masks.  The plan's row order is the sequence order with the
     hub rows group-major (``ShardTopology.hub_rows_order``): the prologue
     writes q and k in that order (``seq_to_plan``), ``v``'s hub rows are
     gathered into it, and the kernel writes every output row back to its

@@ -67,6 +67,7 @@ constexpr int kSmemBytes = kSmemBar + 256 + 1024;  // + slack for 1024-byte alig
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;
 constexpr int kSkip = -2;  // mask selector: this half does not use the key tile
+
 // A key-box row carries the index of its key/value tensor map in the top bits.
 constexpr int kMapShift = 24;
 constexpr int kRowMask = (1 << kMapShift) - 1;
@@ -324,23 +325,30 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
     }
     if (grow) m_run = mx;
     const float nref = m_run == -INFINITY ? 0.f : -m_run;
-    float r8[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) r8[i] = 0.f;
+    // exponent arguments and row sums two lanes at a time (fp32x2 FMA / add)
+    const uint64_t sc2 = f2_pack(sc, sc), nref2 = f2_pack(nref, nref);
+    uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float p0 = ex2_approx(fmaf(sv[64 * half + 2 * i], sc, nref));
-        const float p1 = ex2_approx(fmaf(sv[64 * half + 2 * i + 1], sc, nref));
-        r8[i & 3] += p0;
-        r8[4 + (i & 3)] += p1;
+        const uint64_t arg =
+            f2_fma(f2_pack(sv[64 * half + 2 * i], sv[64 * half + 2 * i + 1]), sc2, nref2);
+        float a0, a1;
+        f2_unpack(arg, a0, a1);
+        const float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
+        acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
         pk[i] = pack_bf16x2(p0, p1);
       }
       tmem_st32(s_col + 32 * half, pk);
     }
-    l_run += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
+    {
+      const uint64_t s2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
+      float s0, s1;
+      f2_unpack(s2, s0, s1);
+      l_run += s0 + s1;
+    }
     tmem_wait_st();
     tc_fence_before();
     mbar_arrive(B.p_full + h);

@@ -34,7 +34,6 @@ constexpr int kMaxCand = 2048;
 constexpr int kMaxChunks = 8192;
 constexpr int kStatusMissingFrame = 4;   // a query frame is missing from an agent cache
 constexpr int kStatusTileOverflow = 2;
-constexpr int kSelSkip = -2;  // key tile selector: the half does not use the tile
 
 struct TDims {
   int mode;  // 0 full sequence, 1 cached
@@ -438,381 +437,6 @@ __global__ void __launch_bounds__(kThreads)
 // ---------------------------------------------------------------------------
 // Player-sharded full-sequence plan
 // ---------------------------------------------------------------------------
-// One rank owns players [p0, p1).  Its query rows are its players' rows
-// (player-major, then frame) followed by every hub row, the hubs stored
-// group-major: local hub (g, f, slot) at own_rows + (g*T + f)*K_L + slot, then
-// global hub (f, slot) at own_rows + T*N*K_L + f*K_G + slot.  Its key streams
-// are 0 = its players' rows, 1 = the hub rows (replicated, same order), and
-// for the frames of remote group-mates the stream-packed row given by
-// remote_key[o*T + f] (a buffer of fetched frames, or the owning rank's own
-// buffer read over NVLink).
-//
-// Player segments (one player frame each, per temporal layout) get their
-// complete key sets as 64-row key boxes with per-key masks.  Hub rows are
-// cut into 128-row tiles of one group's rows (or of the global rows), two
-// consecutive tiles per query pair, and get the part of their key set this
-// rank holds (its players' rows, plus the hub rows when hub_keys is set)
-// with one 128-row mask per half and key tile; the ranks' partial rows are
-// merged from their log-sum-exp.
-
-struct SDims {
-  TDims t;
-  int p0, p1, n_own, hub_keys;
-  int n_seg, n_pairs;     // player segments / pairs per layout
-  int npl, npg, n_hub;    // hub pairs per group, global hub pairs, all hub pairs
-  int hub_tile_base;      // first key tile of the hub pairs
-  int hub_mask_base;      // first hub mask, in 128-row masks
-  int hub_cand;           // key unit candidates of a hub pair
-};
-
-constexpr int kStatusMissingRemote = 8;  // a remote unit the plan needs is not in the buffer
-
-__device__ TSeg sseg_of(const SDims& sd, int layout, int s) {
-  const TDims& d = sd.t;
-  TSeg r;
-  r.type = 0;
-  r.g = 0;
-  r.p = sd.p0 + s / d.n;
-  r.qrel = s % d.n;
-  r.ql = d.L;
-  const int qf = layout * d.n + r.qrel;
-  r.q0 = (r.p - sd.p0) * d.T * d.L + qf * d.L;
-  return r;
-}
-
-// Row of hub sequence index j (local hubs frame-major, then globals) in the
-// group-major hub stream.
-__device__ __forceinline__ int hub_row_group_major(const TDims& d, int j) {
-  if (j >= d.T * d.N * d.KL) return j;
-  const int f = j / (d.N * d.KL), gi = (j / d.KL) % d.N, slot = j % d.KL;
-  return (gi * d.T + f) * d.KL + slot;
-}
-
-__device__ void analyse_shard(const hier_shard_desc& g, const SDims& sd, int layout,
-                              const TSeg& sg, const SegSmem& m) {
-  const TDims& d = sd.t;
-  const int bs = layout * d.n, be = bs + d.n;
-  const int ret0 = max(0, be - d.R);
-  const int Rb = be - ret0;
-  const int C = n_candidates(d, sg.type, Rb);
-  if (threadIdx.x == 0) m.misc[3] = 0;
-  __syncthreads();
-  int missing = 0;
-  const int unit_rows = d.T * d.L;
-  for (int c = threadIdx.x; c < C; c += kThreads) {
-    int base = 0, width = 0;
-    bool valid = false;
-    full_candidate(g.labels, g.active, d, sg, bs, ret0, Rb, c, &base, &width, &valid);
-    int w = valid ? width : 0, key = 0;
-    if (w > 0) {
-      if (base < d.A) {
-        const int o = base / unit_rows, rem = base % unit_rows;
-        if (o >= sd.p0 && o < sd.p1) {
-          key = (o - sd.p0) * unit_rows + rem;
-        } else {
-          const int unit_key = g.remote_key[o * d.T + rem / d.L];
-          if (unit_key < 0) {
-            missing = 1;
-            w = 0;
-          } else {
-            key = unit_key + rem % d.L;
-          }
-        }
-      } else {
-        key = (1 << segplan::kStreamShift) | hub_row_group_major(d, base - (int)d.A);
-      }
-    }
-    m.w[c] = w;
-    m.key[c] = key;
-    m.pool[c] = base;
-  }
-  if (missing) atomicOr(&m.misc[3], kStatusMissingRemote);
-  __syncthreads();
-  segplan::analyse_runs(m, C);
-}
-
-__global__ void __launch_bounds__(kThreads)
-    shard_count_kernel(const hier_shard_desc g, const SDims sd, int32_t* n_boxes,
-                       int32_t* status) {
-  extern __shared__ int smem_i[];
-  const SegSmem m = segplan::seg_smem(smem_i, kMaxCand);
-  const int layout = blockIdx.y, s = blockIdx.x;
-  const TSeg sg = sseg_of(sd, layout, s);
-  analyse_shard(g, sd, layout, sg, m);
-  if (threadIdx.x == 0) {
-    n_boxes[layout * sd.n_seg + s] = m.misc[2];
-    if (m.misc[3] && status) atomicOr(status, m.misc[3]);
-  }
-}
-
-__global__ void __launch_bounds__(kThreads)
-    shard_build_kernel(const hier_shard_desc g, const SDims sd, const int32_t* n_boxes,
-                       int32_t* q_pairs, int32_t* kv_tiles, uint32_t* tile_masks,
-                       int32_t tile_capacity, int32_t* status) {
-  extern __shared__ int smem_i[];
-  const SegSmem m = segplan::seg_smem(smem_i, kMaxCand);
-  const TDims& d = sd.t;
-  const int layout = blockIdx.y, s = blockIdx.x;
-  const TSeg sg = sseg_of(sd, layout, s);
-  analyse_shard(g, sd, layout, sg, m);
-  const int gs = layout * sd.n_seg + s;
-  const int tile_base = segplan::tile_base_of(n_boxes, gs, m.misc + 8);
-  const int n_tiles = (m.misc[2] + 1) >> 1;
-  if (tile_base + n_tiles > sd.hub_tile_base) {
-    if (threadIdx.x == 0 && status) atomicOr(status, kStatusTileOverflow);
-    return;
-  }
-  segplan::emit_plan(m, tile_base, kv_tiles, tile_masks);
-  segplan::emit_pairs(sg.q0, sg.ql, layout * sd.n_pairs + s * d.npA, tile_base, n_tiles, q_pairs);
-}
-
-// ---- hub query pairs -------------------------------------------------------
-
-struct HubPair {
-  int kind;          // 1 local hubs of group g, 2 global hubs
-  int g;
-  int j0;            // first row within the group's (or the global) rows
-  int n0, n1;        // rows of the two halves
-  int q0;            // first local query row
-  int f_lo, f_hi;    // frames of the pair's rows
-};
-
-__device__ HubPair hub_pair_of(const SDims& sd, int hp) {
-  const TDims& d = sd.t;
-  const int own_rows = sd.n_own * d.T * d.L;
-  HubPair r;
-  int rows, unit;
-  if (hp < d.N * sd.npl) {
-    r.kind = 1;
-    r.g = hp / sd.npl;
-    r.j0 = 256 * (hp % sd.npl);
-    rows = d.T * d.KL;
-    unit = d.KL;
-    r.q0 = own_rows + r.g * rows + r.j0;
-  } else {
-    r.kind = 2;
-    r.g = 0;
-    r.j0 = 256 * (hp - d.N * sd.npl);
-    rows = d.T * d.KG;
-    unit = d.KG;
-    r.q0 = own_rows + d.T * d.N * d.KL + r.j0;
-  }
-  r.n0 = min(128, rows - r.j0);
-  r.n1 = max(0, min(128, rows - r.j0 - 128));
-  r.f_lo = r.j0 / unit;
-  r.f_hi = (r.j0 + r.n0 + r.n1 - 1) / unit;
-  return r;
-}
-
-// Key unit of a hub pair: kind 0 = player p (absolute) frame f, 1 = local
-// hub of group g frame f, 2 = global hub of frame f; [start, end) its rows
-// in its stream.
-struct KeyUnit {
-  int kind, id, f, start, end;
-};
-
-__device__ __forceinline__ KeyUnit key_unit(const SDims& sd, int stream, int row) {
-  const TDims& d = sd.t;
-  KeyUnit u;
-  if (stream == 0) {
-    const int pr = row / (d.T * d.L);
-    u.kind = 0;
-    u.id = sd.p0 + pr;
-    u.f = (row % (d.T * d.L)) / d.L;
-    u.start = (pr * d.T + u.f) * d.L;
-    u.end = u.start + d.L;
-  } else if (row < d.T * d.N * d.KL) {
-    u.kind = 1;
-    u.id = row / (d.T * d.KL);
-    u.f = (row % (d.T * d.KL)) / d.KL;
-    u.start = (u.id * d.T + u.f) * d.KL;
-    u.end = u.start + d.KL;
-  } else {
-    const int x = row - d.T * d.N * d.KL;
-    u.kind = 2;
-    u.id = 0;
-    u.f = x / d.KG;
-    u.start = d.T * d.N * d.KL + u.f * d.KG;
-    u.end = u.start + d.KG;
-  }
-  return u;
-}
-
-// Unit-level edge of a hub query of frame t (of group g for local hubs) to
-// a key unit, labels grouping (the hierarchical mask's local->player,
-// local->local, local->global, global->local and global->global edges).  An
-// inactive local hub has only its self edge, handled per token.
-__device__ __forceinline__ bool hub_edge(const hier_shard_desc& g, const TDims& d, int qkind,
-                                         int qg, int t, const KeyUnit& k) {
-  const bool w = temporal(d, t, k.f);
-  if (qkind == 1) {
-    if (g.active[(int64_t)t * d.N + qg] == 0) return false;
-    if (k.kind == 0) return w && g.labels[(int64_t)t * d.P + k.id] == qg;
-    if (k.kind == 1) return w && k.id == qg && g.active[(int64_t)k.f * d.N + qg] != 0;
-    return w;
-  }
-  if (k.kind == 0) return false;
-  if (k.kind == 1) return w && g.active[(int64_t)k.f * d.N + k.id] != 0;
-  return w;
-}
-
-__device__ __forceinline__ bool inactive_local(const hier_shard_desc& g, const TDims& d,
-                                               int qkind, int qg, int t) {
-  return qkind == 1 && g.active[(int64_t)t * d.N + qg] == 0;
-}
-
-__device__ void analyse_hub(const hier_shard_desc& g, const SDims& sd, const HubPair& hq,
-                            const SegSmem& m) {
-  const TDims& d = sd.t;
-  const int C = sd.hub_cand, Cp = sd.n_own * d.T;
-  if (threadIdx.x == 0) m.misc[3] = 0;
-  __syncthreads();
-  for (int c = threadIdx.x; c < C; c += kThreads) {
-    int stream, row;
-    if (c < Cp) {
-      stream = 0;
-      row = c * d.L;  // (p - p0)*T + f = c
-    } else if (c - Cp < d.T * d.N) {
-      stream = 1;
-      row = (c - Cp) * d.KL;  // g*T + f = c - Cp
-    } else {
-      stream = 1;
-      row = d.T * d.N * d.KL + (c - Cp - d.T * d.N) * d.KG;
-    }
-    const KeyUnit u = key_unit(sd, stream, row);
-    bool any = false;
-    for (int t = hq.f_lo; t <= hq.f_hi && !any; ++t) {
-      any = hub_edge(g, d, hq.kind, hq.g, t, u) ||
-            (u.kind == 1 && u.id == hq.g && u.f == t && inactive_local(g, d, hq.kind, hq.g, t));
-    }
-    const int width = u.end - u.start;
-    m.w[c] = any && width > 0 ? width : 0;
-    m.key[c] = (stream << segplan::kStreamShift) | row;
-    m.pool[c] = 0;
-  }
-  __syncthreads();
-  segplan::analyse_runs(m, C);
-}
-
-__global__ void __launch_bounds__(kThreads)
-    hub_count_kernel(const hier_shard_desc g, const SDims sd, int32_t* n_boxes) {
-  extern __shared__ int smem_i[];
-  const SegSmem m = segplan::seg_smem(smem_i, kMaxCand);
-  const HubPair hq = hub_pair_of(sd, blockIdx.x);
-  analyse_hub(g, sd, hq, m);
-  if (threadIdx.x == 0) n_boxes[sd.t.n_layouts * sd.n_seg + blockIdx.x] = m.misc[2];
-}
-
-// 64 mask bits of one query row over one key box (valid keys from row k0 of
-// a stream).
-__device__ uint64_t hub_box_bits(const hier_shard_desc& g, const SDims& sd, const HubPair& hq,
-                                 int t, int qrow, int stream, int k0, int valid) {
-  const TDims& d = sd.t;
-  uint64_t bits = 0;
-  int pos = 0;
-  while (pos < valid) {
-    const KeyUnit u = key_unit(sd, stream, k0 + pos);
-    const int end = min(valid, u.end - k0);
-    if (hub_edge(g, d, hq.kind, hq.g, t, u)) {
-      const uint64_t hi = end >= 64 ? ~0ull : ((1ull << end) - 1ull);
-      bits |= hi & ~((1ull << pos) - 1ull);
-    } else if (stream == 1 && u.kind == 1 && u.id == hq.g && u.f == t &&
-               inactive_local(g, d, hq.kind, hq.g, t)) {
-      const int self = qrow - k0;  // the query's own token
-      if (self >= pos && self < end) bits |= 1ull << self;
-    }
-    pos = end;
-  }
-  return bits;
-}
-
-__global__ void __launch_bounds__(kThreads)
-    hub_build_kernel(const hier_shard_desc g, const SDims sd, const int32_t* n_boxes,
-                     int32_t* q_pairs, int32_t* kv_tiles, uint32_t* tile_masks,
-                     int32_t tile_capacity, int32_t* status) {
-  extern __shared__ int smem_i[];
-  const SegSmem m = segplan::seg_smem(smem_i, kMaxCand);
-  const TDims& d = sd.t;
-  const int hp = blockIdx.x;
-  const HubPair hq = hub_pair_of(sd, hp);
-  analyse_hub(g, sd, hq, m);
-  const int local_base =
-      segplan::tile_base_of(n_boxes + d.n_layouts * sd.n_seg, hp, m.misc + 8);
-  const int tile_base = sd.hub_tile_base + local_base;
-  const int n_box = m.misc[2], n_tiles = (n_box + 1) >> 1;
-  if (tile_base + n_tiles > tile_capacity) {
-    if (threadIdx.x == 0 && status) atomicOr(status, kStatusTileOverflow);
-    return;
-  }
-  const int n_runs = m.misc[1];
-  // each thread: one row of one half
-  const int h = threadIdx.x >> 7, r = threadIdx.x & 127;
-  const int nrow = h ? hq.n1 : hq.n0;
-  const bool row_ok = r < nrow;
-  const int j = hq.j0 + 128 * h + r;  // row within the group's (global) rows
-  const int unit = hq.kind == 1 ? d.KL : d.KG;
-  const int t = row_ok ? j / unit : 0;
-  // the query row's own position in the hub stream (inactive-local self edge)
-  const int qrow = hq.kind == 1 ? hq.g * d.T * d.KL + j : d.T * d.N * d.KL + j;
-  for (int i = 0; i < n_tiles; ++i) {
-    int key[2], valid[2];
-#pragma unroll
-    for (int slot = 0; slot < 2; ++slot) {
-      const int b = 2 * i + slot;
-      const int bb = b < n_box ? b : b - 1;
-      const int ru = segplan::run_of_box(m, n_runs, bb);
-      const int k = bb - m.rb[ru];
-      key[slot] = m.rk[ru] + segplan::kBoxRows * k;
-      valid[slot] = b < n_box ? min(segplan::kBoxRows, m.rf[ru + 1] - m.rf[ru] - segplan::kBoxRows * k)
-                              : 0;
-    }
-    uint64_t bits[2] = {0ull, 0ull};
-    if (row_ok) {
-#pragma unroll
-      for (int slot = 0; slot < 2; ++slot) {
-        const int stream = key[slot] >> segplan::kStreamShift;
-        const int k0 = key[slot] & ((1 << segplan::kStreamShift) - 1);
-        bits[slot] = hub_box_bits(g, sd, hq, t, qrow, stream, k0, valid[slot]);
-      }
-    }
-    const bool all = (bits[0] & bits[1]) == ~0ull;
-    const bool some = (bits[0] | bits[1]) != 0ull;
-    const int full0 = __syncthreads_and(h == 1 || !row_ok || all);
-    const int full1 = __syncthreads_and(h == 0 || !row_ok || all);
-    const int any0 = __syncthreads_or(h == 0 && row_ok && some);
-    const int any1 = __syncthreads_or(h == 1 && row_ok && some);
-    const int ti = tile_base + i;
-    const int mi = sd.hub_mask_base + 2 * (ti - sd.hub_tile_base) + h;
-    const bool full_h = h ? full1 : full0, any_h = h ? any1 : any0;
-    const int sel = !any_h ? kSelSkip : full_h ? -1 : mi;
-    if (r == 0) {
-      if (h == 0) {
-        kv_tiles[(int64_t)ti * 4 + 0] = key[0];
-        kv_tiles[(int64_t)ti * 4 + 1] = key[1];
-      }
-      kv_tiles[(int64_t)ti * 4 + 2 + h] = sel;
-    }
-    if (sel >= 0) {
-      uint32_t* dst = tile_masks + ((int64_t)mi * 128 + r) * 4;
-      dst[0] = (uint32_t)bits[0];
-      dst[1] = (uint32_t)(bits[0] >> 32);
-      dst[2] = (uint32_t)bits[1];
-      dst[3] = (uint32_t)(bits[1] >> 32);
-    }
-  }
-  if (threadIdx.x == 0) {
-    int32_t* rec = q_pairs + (int64_t)(d.n_layouts * sd.n_pairs + hp) * 8;
-    rec[0] = hq.q0;
-    rec[1] = hq.n0;
-    rec[2] = hq.q0 + 128;
-    rec[3] = hq.n1;
-    rec[4] = tile_base;
-    rec[5] = tile_base + n_tiles;
-    rec[6] = 1;  // 128-row masks
-    rec[7] = 0;
-  }
-}
-
 using segplan::ceil_div;
 
 int64_t boxes_of(int64_t runs, int width) {
@@ -1014,132 +638,6 @@ extern "C" int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_b
   HIER_CHECK_CUDA(cudaGetLastError(), "tiled_build_kernel launch");
   const int np = d.n_pairs * d.n_layouts;
   if (q_pairs && order && np > 0) {
-    order_by_work_kernel<8><<<(np + 127) / 128, 128, 0, s>>>(q_pairs, np, order);
-    HIER_CHECK_CUDA(cudaGetLastError(), "order_by_work_kernel launch");
-  }
-  return HIER_OK;
-}
-
-namespace {
-
-int make_sdims(const hier_shard_desc* g, SDims* sd, hier_shard_sizes_t* sz) {
-  if (!g) {
-    set_error(HIER_EVALUE, "hier_shard_desc is NULL");
-    return HIER_EVALUE;
-  }
-  hier_tiled_grouping tg;
-  memset(&tg, 0, sizeof(tg));
-  tg.mode = 0;
-  tg.P = g->P, tg.N = g->N, tg.L = g->L, tg.KL = g->KL, tg.KG = g->KG;
-  tg.n_block = g->n_block, tg.local_attn = g->local_attn, tg.direct = g->direct, tg.T = g->T;
-  tg.labels = g->labels, tg.active = g->active;
-  int64_t cap_full;
-  memset(sd, 0, sizeof(*sd));
-  int rc = make_tdims(&tg, &sd->t, &cap_full);
-  if (rc) return rc;
-  if (g->p0 < 0 || g->p1 > g->P || g->p0 >= g->p1) {
-    set_error(HIER_EVALUE, "invalid player shard [%d, %d) of %d players", g->p0, g->p1, g->P);
-    return HIER_EVALUE;
-  }
-  if (g->direct && !g->remote_key) {
-    set_error(HIER_EVALUE, "direct player edges need the remote unit table");
-    return HIER_EVALUE;
-  }
-  const TDims& d = sd->t;
-  sd->p0 = g->p0, sd->p1 = g->p1, sd->n_own = g->p1 - g->p0, sd->hub_keys = g->hub_keys != 0;
-  sd->n_seg = sd->n_own * d.n;
-  sd->n_pairs = sd->n_own * d.n * d.npA;
-  sd->npl = ceil_div(ceil_div(d.T * d.KL, 128), 2);
-  sd->npg = ceil_div(ceil_div(d.T * d.KG, 128), 2);
-  sd->n_hub = d.N * sd->npl + sd->npg;
-  sd->hub_cand = sd->n_own * d.T + (sd->hub_keys ? d.T * d.N + d.T : 0);
-  if (sd->hub_cand > kMaxCand) {
-    set_error(HIER_EVALUE, "shard of %d players x %d frames too large for the hub plan builder",
-              sd->n_own, d.T);
-    return HIER_EVALUE;
-  }
-  // key boxes of a hub pair: at most one box per 64 rows of each key unit
-  const int64_t hub_boxes = boxes_of((int64_t)sd->n_own * d.T, d.L) +
-                            (sd->hub_keys ? boxes_of((int64_t)d.T * d.N, d.KL) +
-                                                boxes_of(d.T, d.KG)
-                                          : 0);
-  const int64_t hub_tiles = (int64_t)sd->n_hub * ((hub_boxes + 1) / 2);
-  // the full-sequence capacity (every player's segments) bounds the players'
-  // tiles of a shard
-  const int64_t tiles = cap_full + hub_tiles;
-  if (tiles > INT32_MAX / 8) {
-    set_error(HIER_EVALUE, "shard plan too large");
-    return HIER_EVALUE;
-  }
-  sd->hub_tile_base = (int)cap_full;
-  sd->hub_mask_base = (int)ceil_div((int)cap_full, 128);
-  const int64_t rows = (int64_t)sd->n_own * d.T * d.L;
-  if (rows >= (1 << segplan::kStreamShift)) {
-    set_error(HIER_EVALUE, "shard of %lld player rows exceeds %d", (long long)rows,
-              (1 << segplan::kStreamShift) - 1);
-    return HIER_EVALUE;
-  }
-  if (sz) {
-    memset(sz, 0, sizeof(*sz));
-    sz->n_pairs = d.n_layouts * sd->n_pairs + sd->n_hub;
-    sz->n_counts = d.n_layouts * sd->n_seg + sd->n_hub;
-    sz->tile_capacity = (int32_t)tiles;
-    sz->mask_words = ((int64_t)sd->hub_mask_base + 2 * hub_tiles) * 128 * 4;
-    sz->own_rows = rows;
-    sz->q_rows = rows + (int64_t)d.T * (d.N * d.KL + d.KG);
-  }
-  return HIER_OK;
-}
-
-}  // namespace
-
-extern "C" int hier_shard_sizes(const hier_shard_desc* g, hier_shard_sizes_t* out) {
-  clear_error();
-  if (!out) {
-    set_error(HIER_EVALUE, "sizes output is NULL");
-    return HIER_EVALUE;
-  }
-  SDims sd;
-  return make_sdims(g, &sd, out);
-}
-
-extern "C" int hier_shard_plan(const hier_shard_desc* g, int32_t* n_counts, int32_t* q_pairs,
-                               int32_t* kv_tiles, uint32_t* tile_masks, int32_t tile_capacity,
-                               int32_t* order, int32_t* status, void* stream) {
-  clear_error();
-  SDims sd;
-  hier_shard_sizes_t sz;
-  int rc = make_sdims(g, &sd, &sz);
-  if (rc) return rc;
-  if (!n_counts || !q_pairs || !kv_tiles || !tile_masks) {
-    set_error(HIER_EVALUE, "shard plan outputs missing");
-    return HIER_EVALUE;
-  }
-  if (tile_capacity < sz.tile_capacity) {
-    set_error(HIER_EVALUE, "tile capacity %d below the shard's bound %d", tile_capacity,
-              sz.tile_capacity);
-    return HIER_EVALUE;
-  }
-  cudaStream_t s = (cudaStream_t)stream;
-  const size_t sm = tiled_smem_bytes(kMaxCand);
-  const void* kernels[4] = {(const void*)shard_count_kernel, (const void*)shard_build_kernel,
-                            (const void*)hub_count_kernel, (const void*)hub_build_kernel};
-  for (const void* k : kernels)
-    HIER_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
-                    "cudaFuncSetAttribute(shard plan kernels)");
-  const dim3 grid(sd.n_seg, sd.t.n_layouts);
-  shard_count_kernel<<<grid, kThreads, sm, s>>>(*g, sd, n_counts, status);
-  HIER_CHECK_CUDA(cudaGetLastError(), "shard_count_kernel launch");
-  hub_count_kernel<<<sd.n_hub, kThreads, sm, s>>>(*g, sd, n_counts);
-  HIER_CHECK_CUDA(cudaGetLastError(), "hub_count_kernel launch");
-  shard_build_kernel<<<grid, kThreads, sm, s>>>(*g, sd, n_counts, q_pairs, kv_tiles, tile_masks,
-                                                tile_capacity, status);
-  HIER_CHECK_CUDA(cudaGetLastError(), "shard_build_kernel launch");
-  hub_build_kernel<<<sd.n_hub, kThreads, sm, s>>>(*g, sd, n_counts, q_pairs, kv_tiles, tile_masks,
-                                                  tile_capacity, status);
-  HIER_CHECK_CUDA(cudaGetLastError(), "hub_build_kernel launch");
-  const int np = sz.n_pairs;
-  if (order && np > 0) {
     order_by_work_kernel<8><<<(np + 127) / 128, 128, 0, s>>>(q_pairs, np, order);
     HIER_CHECK_CUDA(cudaGetLastError(), "order_by_work_kernel launch");
   }

@@ -9,8 +9,9 @@ does not divide).  Per layer:
 2. **attention** - one tcgen05 launch over the rank's query rows (its
    players' rows, then every hub row, the hubs group-major) reading three
    key/value streams in place: its players' rows, the hub rows, the received
-   mate frames.  Player rows run one query pair per player frame; hub rows
-   run in 128-row tiles of one group's frames with per-row masks;
+   mate frames.  Player rows run in 256-row strips, hub rows in 128-row
+   tiles of one group's frames, over exactly the key units they attend to
+   (per-row masks where a tile is seen in part);
 3. **hub merge** - hub rows were computed over the keys each rank holds;
    their partial results merge from the per-row log-sum-exp with an
    all-reduce of the max and one all-reduce of the scaled partial sums.
@@ -246,18 +247,23 @@ class ShardedHierAttention:
         lib = _lib.lib()
         check(lib.hier_shard_sizes(ctypes.byref(d), ctypes.byref(sz)))
         self.n_pairs = int(sz.n_pairs)
-        cap = max(sz.tile_capacity, 1)
         self.q_rows = int(sz.q_rows)
-        self.n_boxes = torch.empty(max(sz.n_counts, 1), dtype=torch.int32, device=dev)
-        self.q_pairs = torch.empty((max(self.n_pairs, 1), 8), dtype=torch.int32, device=dev)
-        self.kv_tiles = torch.empty((cap, 4), dtype=torch.int32, device=dev)
-        self.tile_masks = torch.empty((max(sz.mask_words // 4, 1), 4), dtype=torch.int32,
-                                      device=dev)
-        self.order = torch.empty(max(self.n_pairs, 1), dtype=torch.int32, device=dev)
+        # plan: count key tiles and masks, size the tables (one host read), build
+        self.counts = torch.empty(max(sz.n_counts, 1), dtype=torch.int32, device=dev)
+        totals = torch.zeros(2, dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
-        check(lib.hier_shard_plan(ctypes.byref(d), ptr(self.n_boxes), ptr(self.q_pairs),
-                                  ptr(self.kv_tiles), ptr(self.tile_masks), cap, ptr(self.order),
-                                  ptr(self.status), stream_ptr(dev)))
+        check(lib.hier_shard_count(ctypes.byref(d), ptr(self.counts), ptr(totals),
+                                   ptr(self.status), stream_ptr(dev)))
+        n_tiles, n_masks = (int(x) for x in totals.cpu())
+        self.n_tiles, self.n_masks = n_tiles, n_masks
+        self.q_pairs = torch.empty((max(self.n_pairs, 1), 8), dtype=torch.int32, device=dev)
+        self.kv_tiles = torch.empty((max(n_tiles, 1), 4), dtype=torch.int32, device=dev)
+        self.tile_masks = torch.empty((max(n_masks, 1), 128, 4), dtype=torch.int32, device=dev)
+        self.order = torch.empty(max(self.n_pairs, 1), dtype=torch.int32, device=dev)
+        check(lib.hier_shard_build(ctypes.byref(d), ptr(self.counts), ptr(self.q_pairs),
+                                   ptr(self.kv_tiles), max(n_tiles, 1), ptr(self.tile_masks),
+                                   max(n_masks, 1), ptr(self.order), ptr(self.status),
+                                   stream_ptr(dev)))
         self.send_rows = torch.from_numpy(t.send_rows).to(dev)
         self.n_recv = sum(t.recv_units) * t.L if self.transport == "exchange" else 0
         self.remote = torch.zeros((max(self.n_recv, 1), 2 * self.dim), dtype=torch.bfloat16,
@@ -306,7 +312,7 @@ class ShardedHierAttention:
         st = int(self.status.item())
         if st:
             raise RuntimeError(f"sharded plan status {st:#x} (8: missing remote unit, "
-                               "2: tile capacity)")
+                               "2: tile capacity, 16: mask capacity)")
 
     def exchange(self, k, v):
         """Make the other ranks' mate frames readable: fetch them
@@ -352,7 +358,7 @@ class ShardedHierAttention:
         check(_lib.lib().hier_attn_fwd_streams(
             ptr(q), q.shape[0], q.stride(0), n, kp, vp, rows, strides, ptr(out), out.stride(0),
             ptr(out_rows), self.H, self.D, ptr(self.q_pairs), self.n_pairs, ptr(self.kv_tiles),
-            ptr(self.tile_masks), 1, ptr(self.order), 1.0 / math.sqrt(self.D),
+            ptr(self.tile_masks), 128, ptr(self.order), 1.0 / math.sqrt(self.D),
             ptr(self.lse) if lse else None, ptr(self.err), stream_ptr(q.device)))
 
     def forward(self, q, k, v, out=None):
