@@ -208,9 +208,7 @@ def run_sharded(args, rank, world, local_rank):
         sh.attend(q_buf, k_buf, v, o_buf)
         if i is not None:
             marks["c"][i].record(stream)
-        from multics_b200.sharded import merge_hub_partials
-        merge_hub_partials(o_buf[topo.own_rows:], sh.lse[topo.own_rows:], cfg.H, cfg.D,
-                           world=world)
+        sh.merge(o_buf[topo.own_rows:])
 
     for _ in range(args.warmup):
         step()
@@ -293,7 +291,6 @@ def run_e2e_sharded(args, cfg, topo, sh, qx, kx, v, cam, ft, w, dev, useful_flop
     import torch.distributed as dist
 
     from multics_b200.attention import hier_prep_qk
-    from multics_b200.sharded import merge_hub_partials
 
     hq, hk, hv, hc = (t.cpu().pin_memory() for t in (qx, kx, v, cam))
     ho = torch.empty_like(hq).pin_memory()

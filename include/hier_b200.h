@@ -210,8 +210,23 @@ int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stride, const v
  * O = sum_r 2^(lse_r - M) O_r / sum_r 2^(lse_r - M).  out_rows (int32
  * [q_rows_total], may be NULL) sends query row r's output and lse to row
  * out_rows[r] (a query order other than the output order, e.g. hub rows
- * grouped by group while the output keeps the sequence order).  Other
- * arguments as hier_attn_fwd. */
+ * grouped by group while the output keeps the sequence order).  part (may
+ * be NULL): a second query tensor and the destination of partial rows (see
+ * hier_partial_out).  Other arguments as hier_attn_fwd. */
+/* Rows of a query-pair plan beyond the main query tensor: query rows from
+ * q2_row0 on are read from q2 (row r at q2 row r - q2_row0); the outputs of
+ * pairs flagged in q_pairs[7] (bit 0) are partial rows, written to o at row
+ * r - row0 with their log2-sum-exp in lse ([rows][H]) for a later merge
+ * (hier_lse_gather_*). */
+typedef struct hier_partial_out {
+  const void* q2;
+  int64_t q2_rows, q2_stride, q2_row0;
+  void* o;
+  int64_t o_stride;
+  float* lse;
+  int64_t row0;
+} hier_partial_out;
+
 int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_t q_stride,
                           int32_t n_streams, const void* const* k, const void* const* v,
                           const int64_t* stream_rows, const int64_t* kv_stride, void* out,
@@ -219,7 +234,8 @@ int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_t q_stride,
                           const int32_t* q_pairs,
                           int32_t n_pairs, const int32_t* kv_tiles, const uint32_t* tile_masks,
                           int32_t mask_rows, const int32_t* order, float softmax_scale,
-                          float* lse, int32_t* dev_err, void* stream);
+                          float* lse, const hier_partial_out* part, int32_t* dev_err,
+                          void* stream);
 
 /* ---------------------------------------------------------------------------
  * Cached (rolling key/value cache) step
@@ -370,25 +386,34 @@ int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_boxes, const
  * ------------------------------------------------------------------------- */
 
 /* One rank's share of a full-sequence layer (labels mode), or with one
- * shard (p0 = 0, p1 = P, hub_keys = 1) the whole layer: the rank owns
- * players [p0, p1); its query rows are its players' rows (player, frame,
- * patch) followed by every hub row, the hubs group-major: local hub
- * (g, f, slot) at own_rows + (g*T + f)*K_L + slot, then global hub (f, slot)
- * at own_rows + T*N*K_L + f*K_G + slot.  Its key/value streams for
- * hier_attn_fwd_streams are
- *   0 = its players' rows, 1 = the hub rows (same order), and for each remote
- *   group-mate unit (o, f) (the L rows of player o at frame f) the
- *   stream-packed first row remote_key[o*T + f] = (stream << 24) | row (-1 if
- *   absent): a buffer of frames fetched before the launch, or the owning
- *   rank's buffer mapped from its GPU (read in place over NVLink).
- * Query pairs are two 128-row tiles of 256-row strips of one player's rows,
- * of one group's local-hub rows or of the global-hub rows; their key tiles
- * cover exactly the key units some row attends to and carry one 128-row
- * mask per half where a half sees part of a tile (q_pairs[6] = 1; launch
- * with mask_rows 128).  Hub rows get the keys this rank holds (its players'
- * rows, plus the hub rows if hub_keys) and are merged across ranks with
- * hier_lse_prepare / hier_lse_finish.  An inactive local hub attends to
- * itself only.  The edges are those of the dense mask
+ * shard (p0 = 0, p1 = P, hub_keys = 1) the whole layer.  The rank owns
+ * players [p0, p1).  Its query rows:
+ *   [0, own_rows)           its players' rows (player, frame, patch);
+ *   [own_rows, V)           every hub row, group-major: local hub (g, f, slot)
+ *                           at own_rows + (g*T + f)*K_L + slot, then global hub
+ *                           (f, slot) at own_rows + T*N*K_L + f*K_G + slot
+ *                           (V = own_rows + hub_rows);
+ *   [V, V + hub_partial_rows) per own player p and frame t the K_L rows of the
+ *                           local hub of p's group at t, row
+ *                           V + ((p - p0)*T + t)*K_L + slot (a second query
+ *                           tensor: hier_partial_out.q2 with q2_row0 = V).
+ * Key/value streams for hier_attn_fwd_streams: 0 = its players' rows, 1 =
+ * the hub rows (same order), and for each remote group-mate unit (o, f) (the
+ * L rows of player o at frame f) the stream-packed first row
+ * remote_key[o*T + f] = (stream << 24) | row (-1 if absent): a buffer of
+ * frames fetched before the launch, or the owning rank's buffer mapped from
+ * its GPU (read in place over NVLink).
+ * Player rows get their full key sets.  A hub row is split into partial rows
+ * over disjoint key sets: per member player (third block, on the member's
+ * rank) and over the hub tokens (second block, on the hub_keys rank only);
+ * hub pairs are flagged in q_pairs[7] and written as partial rows
+ * (hier_partial_out.row0 = own_rows: hub-key partials at [0, hub_rows),
+ * player partials after), then merged with hier_lse_gather_* /
+ * hier_lse_finish.  Query pairs are two 128-row tiles of 256-row strips of
+ * one block; their key tiles cover exactly the key units some row attends
+ * to and carry a 128-row mask per half where a half sees part of a tile
+ * (q_pairs[6] = 1; launch with mask_rows 128).  An inactive local hub
+ * attends to itself only.  The edges are those of the dense mask
  * (multics/models/hier_masks.py:364-507); no reference counterpart exists
  * for the sharding itself: the reference runs every player on one device. */
 typedef struct hier_shard_desc {
@@ -402,10 +427,11 @@ typedef struct hier_shard_desc {
 } hier_shard_desc;
 
 typedef struct hier_shard_sizes_t {
-  int32_t n_pairs;  /* query pairs: players' strips, then local-hub pairs, then global */
-  int32_t n_counts; /* int32 entries of the per-pair counts */
-  int64_t own_rows; /* the rank's player rows */
-  int64_t q_rows;   /* query rows (player rows, then hub rows) */
+  int32_t n_pairs;          /* player strips, hub-partial strips, hub-key pairs */
+  int32_t n_counts;         /* int32 entries of the per-pair counts */
+  int64_t own_rows;         /* the rank's player rows */
+  int64_t hub_rows;         /* T*(N*K_L + K_G) */
+  int64_t hub_partial_rows; /* (p1 - p0)*T*K_L */
 } hier_shard_sizes_t;
 
 int hier_shard_sizes(const hier_shard_desc* g, hier_shard_sizes_t* out);
@@ -424,13 +450,27 @@ int hier_shard_build(const hier_shard_desc* g, const int32_t* counts, int32_t* q
                      int32_t* kv_tiles, int32_t tile_capacity, uint32_t* tile_masks,
                      int64_t mask_capacity, int32_t* order, int32_t* status, void* stream);
 
-/* Partial-row merge: x = 2^(lse - lse_max) * o (fp32 [rows, H*D]),
- * w = 2^(lse - lse_max) (fp32 [rows, H]); after summing x and w over the
- * ranks, out = x / w in bf16 (0 where w = 0). */
-int hier_lse_prepare(const void* o, int64_t o_stride, const float* lse, const float* lse_max,
-                     int64_t rows, int32_t H, int32_t D, float* x, float* w, void* stream);
+/* Merge of partial rows over disjoint key sets.  Target t has the partial
+ * rows rows[off[t] .. off[t+1]) of o (bf16 [.., H*D], row stride o_stride)
+ * with log2-sum-exp lse ([..][H]); merged row = sum_i 2^(lse_i - M) o_i /
+ * sum_i 2^(lse_i - M), 0 without keys.
+ *   hier_lse_gather_max:     lse_max[t][h] = max_i lse_i (-inf if none);
+ *   hier_lse_gather_prepare: x = sum_i 2^(lse_i - lse_max) o_i (fp32
+ *                            [n_targets, H*D]), w = sum_i 2^(lse_i - lse_max);
+ *   hier_lse_finish:         out[out_rows ? out_rows[t] : t] = x / w (bf16);
+ * over ranks: max all-reduce of lse_max, sum all-reduce of x and w between
+ * the steps.  hier_lse_gather_merge does the three in one process. */
+int hier_lse_gather_max(const float* lse, int32_t H, const int32_t* off, const int32_t* rows,
+                        int64_t n_targets, float* lse_max, void* stream);
+int hier_lse_gather_prepare(const void* o, int64_t o_stride, const float* lse,
+                            const float* lse_max, int32_t H, int32_t D, const int32_t* off,
+                            const int32_t* rows, int64_t n_targets, float* x, float* w,
+                            void* stream);
 int hier_lse_finish(const float* x, const float* w, int64_t rows, int32_t H, int32_t D, void* out,
-                    int64_t out_stride, void* stream);
+                    int64_t out_stride, const int32_t* out_rows, void* stream);
+int hier_lse_gather_merge(const void* o, int64_t o_stride, const float* lse, int32_t H, int32_t D,
+                          const int32_t* off, const int32_t* rows, int64_t n_targets, void* out,
+                          int64_t out_stride, const int32_t* out_rows, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Self-test of the tensor-core operand encodings (no reference counterpart):

@@ -99,7 +99,17 @@ class HierShardSizes(ctypes.Structure):
     """Mirror of ``hier_shard_sizes_t``."""
 
     _fields_ = [
-        ("n_pairs", c_int32), ("n_counts", c_int32), ("own_rows", c_int64), ("q_rows", c_int64),
+        ("n_pairs", c_int32), ("n_counts", c_int32), ("own_rows", c_int64), ("hub_rows", c_int64),
+        ("hub_partial_rows", c_int64),
+    ]
+
+
+class HierPartialOut(ctypes.Structure):
+    """Mirror of ``hier_partial_out``."""
+
+    _fields_ = [
+        ("q2", c_void_p), ("q2_rows", c_int64), ("q2_stride", c_int64), ("q2_row0", c_int64),
+        ("o", c_void_p), ("o_stride", c_int64), ("lse", c_void_p), ("row0", c_int64),
     ]
 
 
@@ -121,7 +131,7 @@ _SIGS = {
                               c_int32, _P, c_int32, _P, _P, _P, c_float, _P, _P]),
     "hier_attn_fwd_streams": (c_int, [_P, c_int64, c_int64, c_int32, _P, _P, _P, _P, _P, c_int64,
                                       _P, c_int32, c_int32, _P, c_int32, _P, _P, c_int32, _P,
-                                      c_float, _P, _P, _P]),
+                                      c_float, _P, ctypes.POINTER(HierPartialOut), _P, _P]),
     "hier_cached_sizes": (c_int, [ctypes.POINTER(HierCachedGrouping), c_int32,
                                   ctypes.POINTER(HierCachedSizes)]),
     "hier_cached_count": (c_int, [ctypes.POINTER(HierCachedGrouping), _P, _P, _P, _P]),
@@ -138,8 +148,12 @@ _SIGS = {
     "hier_shard_count": (c_int, [ctypes.POINTER(HierShardDesc), _P, _P, _P, _P]),
     "hier_shard_build": (c_int, [ctypes.POINTER(HierShardDesc), _P, _P, _P, c_int32, _P, c_int64,
                                  _P, _P, _P]),
-    "hier_lse_prepare": (c_int, [_P, c_int64, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P]),
-    "hier_lse_finish": (c_int, [_P, _P, c_int64, c_int32, c_int32, _P, c_int64, _P]),
+    "hier_lse_gather_max": (c_int, [_P, c_int32, _P, _P, c_int64, _P, _P]),
+    "hier_lse_gather_prepare": (c_int, [_P, c_int64, _P, _P, c_int32, c_int32, _P, _P, c_int64,
+                                        _P, _P, _P]),
+    "hier_lse_finish": (c_int, [_P, _P, c_int64, c_int32, c_int32, _P, c_int64, _P, _P]),
+    "hier_lse_gather_merge": (c_int, [_P, c_int64, _P, c_int32, c_int32, _P, _P, c_int64, _P,
+                                      c_int64, _P, _P]),
     "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "hier_selftest_exp2": (c_int, [_P, _P, c_int64, _P]),
 }

@@ -178,8 +178,10 @@ class HierSequencePlan:
     part carry per-row masks.  The plan's row order is the sequence order with the
     hub rows group-major (``ShardTopology.hub_rows_order``): the prologue
     writes q and k in that order (``seq_to_plan``), ``v``'s hub rows are
-    gathered into it, and the kernel writes every output row back to its
-    sequence row (``plan_to_seq``).  Same edges as the block plan, so the same
+    gathered into it, and the kernel writes every player output row back to
+    its sequence row (``plan_to_seq``).  Hub rows are computed as partial rows
+    (per member player, and over the hub tokens) and merged into their
+    sequence rows from their log-sum-exp.  Same edges as the block plan, so the same
     results up to the order of floating-point sums."""
 
     def __init__(self, spec, num_heads: int):
@@ -204,6 +206,7 @@ class HierSequencePlan:
         self.plan_to_seq = torch.from_numpy(order.astype(np.int32)).to(dev)
         self.seq_to_plan = torch.from_numpy(inv.astype(np.int32)).to(dev)
         self.hub_src = torch.from_numpy((order[self.A:] - self.A).astype(np.int64)).to(dev)
+        self.hub_dst = self.plan_to_seq[self.A:].contiguous()
         self.core.check_status()
 
     @staticmethod
@@ -219,8 +222,8 @@ class HierSequencePlan:
         if out is None:
             out = torch.empty_like(v)
         v_hub = v[self.A:].index_select(0, self.hub_src)
-        self.core.attend(q_plan, k_plan, v, out, v_hub=v_hub, out_rows=self.plan_to_seq,
-                         lse=False)
+        self.core.attend(q_plan, k_plan, v, out, v_hub=v_hub, out_rows=self.plan_to_seq)
+        self.core.merge(out, out_rows=self.hub_dst)
         return out
 
 

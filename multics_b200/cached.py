@@ -428,7 +428,7 @@ def hierarchical_cached_attention(*, roped_q, agent_frames, agent_keys, agent_va
         check(_lib.lib().hier_attn_fwd_streams(
             ptr(q), s, q.stride(0), n, kp, vp, rows, strides, ptr(out), out.stride(0), None, heads,
             head_dim, ptr(plan.q_pairs), plan.n_pairs, ptr(plan.kv_tiles), ptr(plan.tile_masks),
-            1, ptr(plan.order), 1.0 / math.sqrt(head_dim), None, ptr(err), stream_ptr(dev)))
+            1, ptr(plan.order), 1.0 / math.sqrt(head_dim), None, None, ptr(err), stream_ptr(dev)))
     if SYNC_CHECKS if sync_checks is None else sync_checks:
         st = int(plan.status.item())
         if st & 1:

@@ -85,6 +85,13 @@ struct AttnArgs {
   __nv_bfloat16* out;
   int64_t out_stride;
   const int32_t* out_rows;  // output (and lse) row of each query row; NULL: the same row
+  // pairs flagged in q_pairs[7] write partial rows: row r to part_out row
+  // r - part_row0 and its log-sum-exp to part_lse
+  __nv_bfloat16* part_out;
+  int64_t part_stride;
+  float* part_lse;
+  int part_row0;
+  int q2_row0;  // query rows from q2_row0 on are read from the second query map
   int n_pairs;
   int mask_stride;    // entries per partial-tile mask: 128 (per row) or 1 (per key only)
   int mask_row_and;   // 127 or 0
@@ -92,6 +99,11 @@ struct AttnArgs {
   float* lse;  // optional [q_rows_total][H]: log2-sum-exp of the scaled scores per row
   int n_heads;
   int* err;
+};
+
+// Query tensor maps: rows below q2_row0 from q[0], the others from q[1].
+struct QMaps {
+  CUtensorMap q[2];
 };
 
 // Key and value tensor maps, one per KV stream (a contiguous pool uses one).
@@ -169,17 +181,21 @@ __device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* ma
 template <int kMaps>
 __device__ __forceinline__ void control_role(const AttnArgs& a, int4 pq, int kv_begin, int n_kv,
                                              uint32_t tbase, int warp, int lane, uint8_t* smem,
-                                             const CUtensorMap* tmq, const KVMaps<kMaps>& kv,
+                                             const QMaps& qm, const KVMaps<kMaps>& kv,
                                              const Bars& B, int col, int use) {
   if (n_kv > 0 && warp == 0 && lane == 0) {
     // -------------------------------------------------------- Q + K producer
-    prefetch_tmap(tmq);
+    const bool q2a = pq.x >= a.q2_row0, q2b = pq.z >= a.q2_row0;
+    const CUtensorMap* qa = &qm.q[q2a ? 1 : 0];
+    const CUtensorMap* qb = &qm.q[q2b ? 1 : 0];
+    const int ra = pq.x - (q2a ? a.q2_row0 : 0), rb = pq.z - (q2b ? a.q2_row0 : 0);
+    prefetch_tmap(qa);
     if (kMaps == 1) prefetch_tmap(&kv.k[0]);
     mbar_arrive_expect_tx(B.q_full, 2 * kTile);
-    tma_load_2d(smem + kSmemQ, tmq, B.q_full, col, pq.x);
-    tma_load_2d(smem + kSmemQ + kHalf, tmq, B.q_full, col + 64, pq.x);
-    tma_load_2d(smem + kSmemQ + kTile, tmq, B.q_full, col, pq.z);
-    tma_load_2d(smem + kSmemQ + kTile + kHalf, tmq, B.q_full, col + 64, pq.z);
+    tma_load_2d(smem + kSmemQ, qa, B.q_full, col, ra);
+    tma_load_2d(smem + kSmemQ + kHalf, qa, B.q_full, col + 64, ra);
+    tma_load_2d(smem + kSmemQ + kTile, qb, B.q_full, col, rb);
+    tma_load_2d(smem + kSmemQ + kTile + kHalf, qb, B.q_full, col + 64, rb);
     for (int j = 0; j < n_kv; ++j) {
       const int st = j % kKStages;
       if (j >= kKStages && !mbar_wait(B.k_empty + st, ((j / kKStages) - 1) & 1, a.err, 1)) break;
@@ -251,7 +267,7 @@ __device__ __forceinline__ void control_role(const AttnArgs& a, int4 pq, int kv_
 
 __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_begin, int n_kv,
                                              uint32_t tbase, int warp, const Bars& B, int col,
-                                             int use, bool row_masks128) {
+                                             int use, bool row_masks128, bool partial_rows) {
   const int h = (warp >> 2) - 1;  // 0 for warps 4-7, 1 for warps 8-11
   const int row = threadIdx.x - 128 * (h + 1);
   const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
@@ -260,9 +276,19 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
   const int q_start = h ? pq.z : pq.x;
   const int q_rows = h ? pq.w : pq.y;
   const bool store_row = row < q_rows;
-  const int64_t dst_row =
-      (a.out_rows && store_row) ? (int64_t)a.out_rows[q_start + row] : (int64_t)(q_start + row);
-  __nv_bfloat16* orow = a.out + dst_row * a.out_stride + col;
+  int64_t dst_row;
+  __nv_bfloat16* orow;
+  float* lse_out;
+  if (partial_rows) {
+    dst_row = (int64_t)(q_start + row) - a.part_row0;
+    orow = a.part_out + dst_row * a.part_stride + col;
+    lse_out = a.part_lse;
+  } else {
+    dst_row = (a.out_rows && store_row) ? (int64_t)a.out_rows[q_start + row]
+                                        : (int64_t)(q_start + row);
+    orow = a.out + dst_row * a.out_stride + col;
+    lse_out = a.lse;
+  }
   // a pair flagged in q_pairs[6] carries one mask per query row whatever the
   // launch's mask format
   const int mask_stride = row_masks128 ? kBM : a.mask_stride;
@@ -359,15 +385,15 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
       const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int q = 0; q < kHD / 8; ++q) reinterpret_cast<uint4*>(orow)[q] = z;
-      if (a.lse) a.lse[dst_row * a.n_heads + col / kHD] = -INFINITY;
+      if (lse_out) lse_out[dst_row * a.n_heads + col / kHD] = -INFINITY;
     }
     return;
   }
   if (!mbar_wait(B.o_final + h, 0, a.err, 13)) return;
   tc_fence_after();
   const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-  if (a.lse && store_row)  // O = sum_j 2^(s_j - lse) v_j
-    a.lse[dst_row * a.n_heads + col / kHD] =
+  if (lse_out && store_row)  // O = sum_j 2^(s_j - lse) v_j
+    lse_out[dst_row * a.n_heads + col / kHD] =
         l_run > 0.f ? m_run + __log2f(l_run) : -INFINITY;
   uint32_t r[32];
 #pragma unroll
@@ -391,7 +417,7 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
 
 template <int kMaps>
 __global__ void __launch_bounds__(384, 1)
-    hier_attn_kernel(const __grid_constant__ CUtensorMap tmq,
+    hier_attn_kernel(const __grid_constant__ QMaps qm,
                      const __grid_constant__ KVMaps<kMaps> kv, AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -445,10 +471,10 @@ __global__ void __launch_bounds__(384, 1)
   const int col = head * kHD;
   if (warp >= 4) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-    softmax_role(a, pq, kv_begin, n_kv, tbase, warp, B, col, use, pk.z == 1);
+    softmax_role(a, pq, kv_begin, n_kv, tbase, warp, B, col, use, pk.z == 1, (pk.w & 1) != 0);
   } else {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
-    control_role<kMaps>(a, pq, kv_begin, n_kv, tbase, warp, lane, smem, &tmq, kv, B, col, use);
+    control_role<kMaps>(a, pq, kv_begin, n_kv, tbase, warp, lane, smem, qm, kv, B, col, use);
   }
 
   tc_fence_before();
@@ -484,10 +510,11 @@ int attn_setup(const void* q, int64_t q_rows_total, int64_t q_stride, int32_t H,
 }
 
 template <int kMaps>
-int attn_launch(const CUtensorMap& tmq, const KVMaps<kMaps>& kv, void* out, int64_t out_stride,
-                const int32_t* out_rows, int32_t H, const int32_t* q_pairs, int32_t n_pairs, const int32_t* kv_tiles,
-                const uint32_t* row_masks, int mask_rows, const int32_t* order,
-                float softmax_scale, float* lse, int32_t* dev_err, void* stream) {
+int attn_launch(const QMaps& qm, int q2_row0, const KVMaps<kMaps>& kv, void* out,
+                int64_t out_stride, const int32_t* out_rows, int32_t H, const int32_t* q_pairs,
+                int32_t n_pairs, const int32_t* kv_tiles, const uint32_t* row_masks,
+                int mask_rows, const int32_t* order, float softmax_scale, float* lse,
+                const hier_partial_out* part, int32_t* dev_err, void* stream) {
   static bool attr_set = false;
   if (!attr_set) {
     HIER_CHECK_CUDA(cudaFuncSetAttribute(hier_attn_kernel<kMaps>,
@@ -503,6 +530,11 @@ int attn_launch(const CUtensorMap& tmq, const KVMaps<kMaps>& kv, void* out, int6
   args.out = reinterpret_cast<__nv_bfloat16*>(out);
   args.out_stride = out_stride;
   args.out_rows = out_rows;
+  args.part_out = part ? reinterpret_cast<__nv_bfloat16*>(part->o) : nullptr;
+  args.part_stride = part ? part->o_stride : 0;
+  args.part_lse = part ? part->lse : nullptr;
+  args.part_row0 = part ? (int)part->row0 : 0;
+  args.q2_row0 = q2_row0;
   args.n_pairs = n_pairs;
   args.mask_stride = mask_rows;
   args.mask_row_and = mask_rows - 1;
@@ -510,7 +542,7 @@ int attn_launch(const CUtensorMap& tmq, const KVMaps<kMaps>& kv, void* out, int6
   args.lse = lse;
   args.n_heads = H;
   args.err = dev_err;
-  hier_attn_kernel<kMaps><<<n_pairs * H, 384, kSmemBytes, (cudaStream_t)stream>>>(tmq, kv, args);
+  hier_attn_kernel<kMaps><<<n_pairs * H, 384, kSmemBytes, (cudaStream_t)stream>>>(qm, kv, args);
   HIER_CHECK_CUDA(cudaGetLastError(), "hier_attn_kernel launch");
   return HIER_OK;
 }
@@ -524,9 +556,10 @@ extern "C" int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stri
                              const int32_t* order, float softmax_scale, int32_t* dev_err,
                              void* stream) {
   clear_error();
-  CUtensorMap tmq;
-  int rc = attn_setup(q, q_rows_total, q_stride, H, D, n_pairs, &tmq);
+  QMaps qm;
+  int rc = attn_setup(q, q_rows_total, q_stride, H, D, n_pairs, &qm.q[0]);
   if (rc || n_pairs == 0) return rc;
+  qm.q[1] = qm.q[0];
   if (kv_rows_total > kRowMask) {
     set_error(HIER_EVALUE, "key/value pool of %lld rows exceeds %d", (long long)kv_rows_total,
               kRowMask);
@@ -536,8 +569,8 @@ extern "C" int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stri
   rc = make_tmap_bf16_2d(&kv.k[0], k, (uint64_t)H * D, (uint64_t)kv_rows_total, kv_stride, 64, 64);
   if (!rc) rc = make_tmap_bf16_2d(&kv.v[0], v, (uint64_t)H * D, (uint64_t)kv_rows_total, kv_stride, 64, 64);
   if (rc) return rc;
-  return attn_launch<1>(tmq, kv, out, out_stride, nullptr, H, q_pairs, n_pairs, kv_tiles, row_masks, kBM,
-                        order, softmax_scale, nullptr, dev_err, stream);
+  return attn_launch<1>(qm, INT_MAX, kv, out, out_stride, nullptr, H, q_pairs, n_pairs, kv_tiles,
+                        row_masks, kBM, order, softmax_scale, nullptr, nullptr, dev_err, stream);
 }
 
 extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_t q_stride,
@@ -547,7 +580,8 @@ extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_
                                      int32_t H, int32_t D, const int32_t* q_pairs, int32_t n_pairs,
                                      const int32_t* kv_tiles, const uint32_t* tile_masks,
                                      int32_t mask_rows, const int32_t* order,
-                                     float softmax_scale, float* lse, int32_t* dev_err,
+                                     float softmax_scale, float* lse,
+                                     const hier_partial_out* part, int32_t* dev_err,
                                      void* stream) {
   clear_error();
   if (mask_rows != 1 && mask_rows != kBM) {
@@ -558,9 +592,26 @@ extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_
     set_error(HIER_EVALUE, "need 1..%d key/value streams; got %d", HIER_MAX_KV_STREAMS, n_streams);
     return HIER_EVALUE;
   }
-  CUtensorMap tmq;
-  int rc = attn_setup(q, q_rows_total, q_stride, H, D, n_pairs, &tmq);
+  QMaps qm;
+  int rc = attn_setup(q, q_rows_total, q_stride, H, D, n_pairs, &qm.q[0]);
   if (rc || n_pairs == 0) return rc;
+  int q2_row0 = INT_MAX;
+  qm.q[1] = qm.q[0];
+  if (part && part->q2) {
+    if (part->q2_row0 < 0 || part->q2_row0 > INT_MAX / 2 || part->q2_rows <= 0) {
+      set_error(HIER_EVALUE, "invalid second query block (row0 %lld, %lld rows)",
+                (long long)part->q2_row0, (long long)part->q2_rows);
+      return HIER_EVALUE;
+    }
+    rc = make_tmap_bf16_2d(&qm.q[1], part->q2, (uint64_t)H * D, (uint64_t)part->q2_rows,
+                           part->q2_stride, 64, 128);
+    if (rc) return rc;
+    q2_row0 = (int)part->q2_row0;
+  }
+  if (part && part->o && (part->row0 < 0 || part->row0 > INT_MAX / 2)) {
+    set_error(HIER_EVALUE, "invalid partial-row offset %lld", (long long)part->row0);
+    return HIER_EVALUE;
+  }
   // Streams without rows are never addressed by a plan; their slots (and the
   // unused ones) repeat the first non-empty stream's maps.
   int first = -1;
@@ -590,48 +641,109 @@ extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_
       kv.v[s] = kv.v[first];
     }
   }
-  return attn_launch<HIER_MAX_KV_STREAMS>(tmq, kv, out, out_stride, out_rows, H, q_pairs, n_pairs, kv_tiles,
+  return attn_launch<HIER_MAX_KV_STREAMS>(qm, q2_row0, kv, out, out_stride, out_rows, H, q_pairs, n_pairs, kv_tiles,
                                           tile_masks, mask_rows, order, softmax_scale, lse,
-                                          dev_err, stream);
+                                          part, dev_err, stream);
 }
 
 // ---------------------------------------------------------------------------
 // Merge of partial attention rows computed over disjoint key sets
 // ---------------------------------------------------------------------------
+//
+// Target row t has partial rows rows[off[t] .. off[t+1]) (bf16 outputs o,
+// each normalised over its own keys, and their log2-sum-exp lse); the merged
+// row is sum_i 2^(lse_i - M) o_i / sum_i 2^(lse_i - M) with M the largest
+// lse_i (0 without any key).  Over several ranks: M from a max all-reduce of
+// hier_lse_gather_max, then hier_lse_gather_prepare's x, w summed by an
+// all-reduce, then hier_lse_finish.  In one process hier_lse_gather_merge
+// does all three.
 
 namespace hier {
 namespace {
 
-// x[r, h*D + i] = w * o[r, h*D + i], w[r, h] = 2^(lse - lse_max) (0 if no keys)
-__global__ void lse_prepare_kernel(const __nv_bfloat16* o, int64_t o_stride, const float* lse,
-                                   const float* lse_max, int64_t rows, int H, int D, float* x,
-                                   float* w) {
-  const int per = D / 8;  // threads per (row, head)
-  const int64_t n = rows * H * per;
+__device__ __forceinline__ void bf16x8_load(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 v = __bfloat1622float2(p2[i]);
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
+}
+
+__device__ __forceinline__ void bf16x8_store(__nv_bfloat16* p, const float (&f)[8], float s) {
+  uint4 v;
+  v.x = pack_bf16x2(f[0] * s, f[1] * s);
+  v.y = pack_bf16x2(f[2] * s, f[3] * s);
+  v.z = pack_bf16x2(f[4] * s, f[5] * s);
+  v.w = pack_bf16x2(f[6] * s, f[7] * s);
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+__device__ __forceinline__ float gather_max(const float* lse, int H, int h, const int32_t* rows,
+                                            int b, int e) {
+  float m = -INFINITY;
+  for (int i = b; i < e; ++i) m = fmaxf(m, lse[(int64_t)rows[i] * H + h]);
+  return m;
+}
+
+__global__ void lse_gather_max_kernel(const float* lse, int H, const int32_t* off,
+                                      const int32_t* rows, int64_t n_targets, float* lse_max) {
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n_targets * H;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = t / H;
+    const int h = (int)(t % H);
+    lse_max[t] = gather_max(lse, H, h, rows, off[r], off[r + 1]);
+  }
+}
+
+// Per (target, head, 8 channels): the weighted sum of the partials; kFinal
+// writes the normalised bf16 row, otherwise x (fp32) and w.
+template <bool kFinal>
+__global__ void lse_gather_kernel(const __nv_bfloat16* o, int64_t o_stride, const float* lse,
+                                  const float* lse_max, int H, int D, const int32_t* off,
+                                  const int32_t* rows, int64_t n_targets, float* x, float* w,
+                                  __nv_bfloat16* out, int64_t out_stride,
+                                  const int32_t* out_rows) {
+  const int per = D / 8;
+  const int64_t n = n_targets * H * per;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n;
        t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t rh = t / per;
     const int part = (int)(t % per);
     const int64_t r = rh / H;
     const int h = (int)(rh % H);
-    const float l = lse[rh], m = lse_max[rh];
-    const float wt = (l == -INFINITY || m == -INFINITY) ? 0.f : exp2f(l - m);
-    const uint4 raw = *reinterpret_cast<const uint4*>(o + r * o_stride + h * D + part * 8);
-    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-    float4 a, b;
-    float2 f0 = __bfloat1622float2(p2[0]), f1 = __bfloat1622float2(p2[1]);
-    float2 f2 = __bfloat1622float2(p2[2]), f3 = __bfloat1622float2(p2[3]);
-    a = make_float4(f0.x * wt, f0.y * wt, f1.x * wt, f1.y * wt);
-    b = make_float4(f2.x * wt, f2.y * wt, f3.x * wt, f3.y * wt);
-    float4* dst = reinterpret_cast<float4*>(x + (r * H + h) * D + part * 8);
-    dst[0] = a;
-    dst[1] = b;
-    if (part == 0) w[rh] = wt;
+    const int b = off[r], e = off[r + 1];
+    const float m = kFinal ? gather_max(lse, H, h, rows, b, e) : lse_max[rh];
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float ws = 0.f;
+    for (int i = b; i < e; ++i) {
+      const int64_t pr = rows[i];
+      const float l = lse[pr * H + h];
+      if (l == -INFINITY || m == -INFINITY) continue;
+      const float wt = exp2f(l - m);
+      float f[8];
+      bf16x8_load(o + pr * o_stride + h * D + part * 8, f);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] = fmaf(wt, f[q], acc[q]);
+      ws += wt;
+    }
+    if (kFinal) {
+      const int64_t dr = out_rows ? (int64_t)out_rows[r] : r;
+      bf16x8_store(out + dr * out_stride + h * D + part * 8, acc, ws > 0.f ? 1.f / ws : 0.f);
+    } else {
+      float4* dst = reinterpret_cast<float4*>(x + (r * H + h) * D + part * 8);
+      dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      if (part == 0) w[rh] = ws;
+    }
   }
 }
 
 __global__ void lse_finish_kernel(const float* x, const float* w, int64_t rows, int H, int D,
-                                  __nv_bfloat16* out, int64_t out_stride) {
+                                  __nv_bfloat16* out, int64_t out_stride,
+                                  const int32_t* out_rows) {
   const int per = D / 8;
   const int64_t n = rows * H * per;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n;
@@ -641,15 +753,11 @@ __global__ void lse_finish_kernel(const float* x, const float* w, int64_t rows, 
     const int64_t r = rh / H;
     const int h = (int)(rh % H);
     const float ws = w[rh];
-    const float inv = ws > 0.f ? 1.f / ws : 0.f;
     const float4* src = reinterpret_cast<const float4*>(x + (r * H + h) * D + part * 8);
     const float4 a = src[0], b = src[1];
-    uint4 v;
-    v.x = pack_bf16x2(a.x * inv, a.y * inv);
-    v.y = pack_bf16x2(a.z * inv, a.w * inv);
-    v.z = pack_bf16x2(b.x * inv, b.y * inv);
-    v.w = pack_bf16x2(b.z * inv, b.w * inv);
-    *reinterpret_cast<uint4*>(out + r * out_stride + h * D + part * 8) = v;
+    const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const int64_t dr = out_rows ? (int64_t)out_rows[r] : r;
+    bf16x8_store(out + dr * out_stride + h * D + part * 8, f, ws > 0.f ? 1.f / ws : 0.f);
   }
 }
 
@@ -658,36 +766,66 @@ int merge_grid(int64_t n) {
   return (int)(b < 1 ? 1 : (b > 148 * 32 ? 148 * 32 : b));
 }
 
-}  // namespace
-}  // namespace hier
-
-extern "C" int hier_lse_prepare(const void* o, int64_t o_stride, const float* lse,
-                                const float* lse_max, int64_t rows, int32_t H, int32_t D, float* x,
-                                float* w, void* stream) {
-  clear_error();
-  if (rows < 0 || H <= 0 || D <= 0 || D % 8 || o_stride % 8) {
+int merge_check(int64_t rows, int H, int D, int64_t stride) {
+  if (rows < 0 || H <= 0 || D <= 0 || D % 8 || stride % 8) {
     set_error(HIER_EVALUE, "invalid merge shape rows=%lld H=%d D=%d", (long long)rows, H, D);
     return HIER_EVALUE;
   }
-  if (rows == 0) return HIER_OK;
-  const int64_t n = rows * H * (D / 8);
-  lse_prepare_kernel<<<merge_grid(n), 256, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(o), o_stride, lse, lse_max, rows, H, D, x, w);
-  HIER_CHECK_CUDA(cudaGetLastError(), "lse_prepare_kernel launch");
+  return HIER_OK;
+}
+
+}  // namespace
+}  // namespace hier
+
+extern "C" int hier_lse_gather_max(const float* lse, int32_t H, const int32_t* off,
+                                   const int32_t* rows, int64_t n_targets, float* lse_max,
+                                   void* stream) {
+  clear_error();
+  int rc = merge_check(n_targets, H, 8, 0);
+  if (rc || n_targets == 0) return rc;
+  lse_gather_max_kernel<<<merge_grid(n_targets * H), 256, 0, (cudaStream_t)stream>>>(
+      lse, H, off, rows, n_targets, lse_max);
+  HIER_CHECK_CUDA(cudaGetLastError(), "lse_gather_max_kernel launch");
+  return HIER_OK;
+}
+
+extern "C" int hier_lse_gather_prepare(const void* o, int64_t o_stride, const float* lse,
+                                       const float* lse_max, int32_t H, int32_t D,
+                                       const int32_t* off, const int32_t* rows, int64_t n_targets,
+                                       float* x, float* w, void* stream) {
+  clear_error();
+  int rc = merge_check(n_targets, H, D, o_stride);
+  if (rc || n_targets == 0) return rc;
+  lse_gather_kernel<false><<<merge_grid(n_targets * H * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o), o_stride, lse, lse_max, H, D, off, rows,
+      n_targets, x, w, nullptr, 0, nullptr);
+  HIER_CHECK_CUDA(cudaGetLastError(), "lse_gather_kernel launch");
   return HIER_OK;
 }
 
 extern "C" int hier_lse_finish(const float* x, const float* w, int64_t rows, int32_t H, int32_t D,
-                               void* out, int64_t out_stride, void* stream) {
+                               void* out, int64_t out_stride, const int32_t* out_rows,
+                               void* stream) {
   clear_error();
-  if (rows < 0 || H <= 0 || D <= 0 || D % 8 || out_stride % 8) {
-    set_error(HIER_EVALUE, "invalid merge shape rows=%lld H=%d D=%d", (long long)rows, H, D);
-    return HIER_EVALUE;
-  }
-  if (rows == 0) return HIER_OK;
-  const int64_t n = rows * H * (D / 8);
-  lse_finish_kernel<<<merge_grid(n), 256, 0, (cudaStream_t)stream>>>(
-      x, w, rows, H, D, reinterpret_cast<__nv_bfloat16*>(out), out_stride);
+  int rc = merge_check(rows, H, D, out_stride);
+  if (rc || rows == 0) return rc;
+  lse_finish_kernel<<<merge_grid(rows * H * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
+      x, w, rows, H, D, reinterpret_cast<__nv_bfloat16*>(out), out_stride, out_rows);
   HIER_CHECK_CUDA(cudaGetLastError(), "lse_finish_kernel launch");
+  return HIER_OK;
+}
+
+extern "C" int hier_lse_gather_merge(const void* o, int64_t o_stride, const float* lse, int32_t H,
+                                     int32_t D, const int32_t* off, const int32_t* rows,
+                                     int64_t n_targets, void* out, int64_t out_stride,
+                                     const int32_t* out_rows, void* stream) {
+  clear_error();
+  int rc = merge_check(n_targets, H, D, o_stride);
+  if (!rc) rc = merge_check(n_targets, H, D, out_stride);
+  if (rc || n_targets == 0) return rc;
+  lse_gather_kernel<true><<<merge_grid(n_targets * H * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o), o_stride, lse, nullptr, H, D, off, rows,
+      n_targets, nullptr, nullptr, reinterpret_cast<__nv_bfloat16*>(out), out_stride, out_rows);
+  HIER_CHECK_CUDA(cudaGetLastError(), "lse_gather_kernel launch");
   return HIER_OK;
 }

@@ -1,18 +1,30 @@
 // Attention plan of one player shard (a rank that owns players [p0, p1)),
 // and, with a single shard, of the whole full-sequence layer.
 //
-// Row order of the shard: its players' rows (player, frame, patch), then
-// every hub row group-major: local hub (g, f, slot) at
-// own_rows + (g*T + f)*K_L + slot, then global hub (f, slot) at
-// own_rows + T*N*K_L + f*K_G + slot.  Key/value streams: 0 = the shard's
-// player rows, 1 = the hub rows (same order), and for a remote group-mate
-// unit (o, f) the stream-packed first row remote_key[o*T + f].
+// Query rows of the shard (a row space over two query tensors):
+//   [0, own_rows)               its players' rows (player, frame, patch);
+//   [own_rows, V)               every hub row, group-major: local hub (g, f, slot)
+//                               at own_rows + (g*T + f)*K_L + slot, then global
+//                               hub (f, slot) at own_rows + T*N*K_L + f*K_G + slot;
+//   [V, V + n_own*T*K_L)        per own player p and frame t the K_L local-hub
+//                               rows of p's group at t (second query tensor).
+// Key/value streams: 0 = the shard's player rows, 1 = the hub rows (same
+// order as above), and for a remote group-mate unit (o, f) the
+// stream-packed first row remote_key[o*T + f].
+//
+// A hub row's attention is split by key set into partial rows merged from
+// their log-sum-exp: per member player p of its group, the row of the third
+// block over p's frames (on the rank that owns p), and over the hub tokens
+// the row of the second block (on the rank with hub_keys).  Each partial
+// then needs exactly one player's history, which keeps its tiles dense when
+// groups change from frame to frame.
 //
 // Query pairs are two consecutive 128-row tiles of one query block:
-//   * a player's T*L rows, cut into 256-row strips (frames f_lo..f_hi);
-//   * one group's T*K_L local-hub rows, or the T*K_G global-hub rows.
-// Per pair one CTA enumerates the key units any of its rows may attend to
-// (own frames, group-mate frames of the blocks the rows touch, hub units),
+//   * a player's T*L rows, cut into 256-row strips;
+//   * a player's T*K_L hub-partial rows, cut into 256-row strips;
+//   * one group's T*K_L local-hub rows, or the T*K_G global-hub rows (hub
+//     keys only; on the hub_keys rank).
+// Per pair one CTA enumerates the key units any of its rows may attend to,
 // keeps those with an edge from some row, merges consecutive rows of a
 // stream into runs, covers the runs with 64-row key boxes (two per 128-key
 // tile) and evaluates, per tile and query row, the 128-bit key mask from the
@@ -31,9 +43,7 @@
 // skipped by a half whose rows see none of its keys, and otherwise carries a
 // 128-row mask for that half.  A first pass counts key tiles and masks per
 // pair (the caller sizes the tables from the totals); the second writes the
-// plan.  Hub rows get the keys the shard holds (its players, plus the hub
-// rows when hub_keys is set): the ranks' partial rows merge from their
-// log-sum-exp.
+// plan.  Pairs of hub rows are flagged in q_pairs[7] (partial rows).
 
 #include <limits.h>
 #include <string.h>
@@ -60,12 +70,14 @@ constexpr int kSelSkip = -2;
 struct SDims {
   int P, T, L, N, KL, KG, nb, win, direct;
   int p0, p1, n_own, hub_keys;
-  int nps;             // strip pairs per player
-  int npl, npg;        // hub pairs per group, global hub pairs
-  int n_pairs;         // all pairs: players' strips, then hub pairs
-  int nf_mate;         // mate frames enumerated per strip pair
-  int c_player, c_hub; // candidates per strip / hub pair
-  int own_rows;
+  int nps;             // player strips per player
+  int nph;             // hub-partial strips per player
+  int npl, npg;        // hub-key pairs per group, global hub-key pairs (hub_keys rank)
+  int n_hh;            // hub-key pairs
+  int n_pairs;         // all pairs: player strips, hub-partial strips, hub-key pairs
+  int nf_mate;         // mate frames enumerated per player strip
+  int c_player, c_hub; // candidates per player strip / hub-key pair
+  int own_rows, hub_rows;
 };
 
 __device__ __forceinline__ int fdiv(int a, int b) {
@@ -83,8 +95,10 @@ __device__ __forceinline__ int unit_code(int kind, int id, int f) {
   return (kind << 24) | (id << 12) | f;
 }
 
+constexpr int kPairPlayer = 0, kPairLocal = 1, kPairGlobal = 2, kPairHubOfPlayer = 3;
+
 struct Pair {
-  int kind;    // 0 player strip, 1 local hubs of group id, 2 global hubs
+  int kind;    // kPair*: player strip, local / global hub-key pair, hub-partial strip
   int id;      // player (absolute) or group
   int j0;      // first row within the block of rows (player / group / global)
   int n0, n1;  // rows of the two halves
@@ -97,24 +111,32 @@ struct Pair {
 __device__ Pair pair_of(const SDims& d, int i) {
   Pair r;
   int rows;
+  const int n_hp = d.n_own * d.nph;
   if (i < d.n_own * d.nps) {
-    r.kind = 0;
+    r.kind = kPairPlayer;
     r.id = d.p0 + i / d.nps;
     r.j0 = kStripRows * (i % d.nps);
     rows = d.T * d.L;
     r.unit = d.L;
     r.q0 = (r.id - d.p0) * rows + r.j0;
-  } else if (i < d.n_own * d.nps + d.N * d.npl) {
-    const int h = i - d.n_own * d.nps;
-    r.kind = 1;
+  } else if ((i -= d.n_own * d.nps) < n_hp) {
+    r.kind = kPairHubOfPlayer;
+    r.id = d.p0 + i / d.nph;
+    r.j0 = kStripRows * (i % d.nph);
+    rows = d.T * d.KL;
+    r.unit = d.KL;
+    r.q0 = d.own_rows + d.hub_rows + (r.id - d.p0) * rows + r.j0;
+  } else if ((i -= n_hp) < d.N * d.npl) {
+    const int h = i;
+    r.kind = kPairLocal;
     r.id = h / d.npl;
     r.j0 = kStripRows * (h % d.npl);
     rows = d.T * d.KL;
     r.unit = d.KL;
     r.q0 = d.own_rows + r.id * rows + r.j0;
   } else {
-    const int h = i - d.n_own * d.nps - d.N * d.npl;
-    r.kind = 2;
+    const int h = i - d.N * d.npl;
+    r.kind = kPairGlobal;
     r.id = 0;
     r.j0 = kStripRows * h;
     rows = d.T * d.KG;
@@ -141,7 +163,10 @@ __device__ __forceinline__ bool active(const hier_shard_desc& g, int t, int gi) 
 __device__ bool edge(const hier_shard_desc& g, const SDims& d, int qkind, int qid, int t,
                      int u) {
   const int kind = u >> 24, id = (u >> 12) & 0xfff, f = u & 0xfff;
-  if (qkind == 0) {
+  if (qkind == kPairHubOfPlayer)  // local hub of qid's group at t -> qid's frames
+    return kind == kUnitPlayer && id == qid && temporal(d, t, f) &&
+           active(g, t, label(g, t, qid));
+  if (qkind == kPairPlayer) {
     if (kind == kUnitPlayer) {
       if (id == qid) return temporal(d, t, f);
       return d.direct && fdiv(f, d.nb) == fdiv(t, d.nb) && label(g, t, id) == label(g, t, qid);
@@ -149,7 +174,7 @@ __device__ bool edge(const hier_shard_desc& g, const SDims& d, int qkind, int qi
     if (kind == kUnitLocal) return temporal(d, t, f) && active(g, f, id) && label(g, t, qid) == id;
     return false;
   }
-  if (qkind == 1) {
+  if (qkind == kPairLocal) {
     if (!active(g, t, qid)) return false;
     if (kind == kUnitPlayer) return temporal(d, t, f) && label(g, t, id) == qid;
     if (kind == kUnitLocal) return temporal(d, t, f) && id == qid && active(g, f, qid);
@@ -170,7 +195,13 @@ __device__ void candidate(const hier_shard_desc& g, const SDims& d, const Pair& 
   auto player_key = [&](int o, int f) {
     return (o - d.p0) * d.T * d.L + f * d.L;
   };
-  if (pr.kind == 0) {
+  if (pr.kind == kPairHubOfPlayer) {  // the player's frames
+    *code = unit_code(kUnitPlayer, pr.id, c);
+    *key = player_key(pr.id, c);
+    *width = d.L;
+    return;
+  }
+  if (pr.kind == kPairPlayer) {
     if (c < d.T) {  // own frames
       *code = unit_code(kUnitPlayer, pr.id, c);
       *key = player_key(pr.id, c);
@@ -205,15 +236,7 @@ __device__ void candidate(const hier_shard_desc& g, const SDims& d, const Pair& 
     *width = d.KL;
     return;
   }
-  if (c < d.n_own * d.T) {  // the shard's player frames
-    const int o = d.p0 + c / d.T, f = c % d.T;
-    *code = unit_code(kUnitPlayer, o, f);
-    *key = player_key(o, f);
-    *width = d.L;
-    return;
-  }
-  c -= d.n_own * d.T;
-  if (c < d.T * d.N) {
+  if (c < d.T * d.N) {  // hub-key pairs: hub units only
     const int gi = c / d.T, f = c % d.T;
     *code = unit_code(kUnitLocal, gi, f);
     *key = s1 | ((gi * d.T + f) * d.KL);
@@ -231,7 +254,7 @@ __device__ void candidate(const hier_shard_desc& g, const SDims& d, const Pair& 
 __device__ bool pair_sees(const hier_shard_desc& g, const SDims& d, const Pair& pr, int u) {
   for (int t = pr.f_lo; t <= pr.f_hi; ++t) {
     if (edge(g, d, pr.kind, pr.id, t, u)) return true;
-    if (pr.kind == 1 && !active(g, t, pr.id) && u == unit_code(kUnitLocal, pr.id, t))
+    if (pr.kind == kPairLocal && !active(g, t, pr.id) && u == unit_code(kUnitLocal, pr.id, t))
       return true;
   }
   return false;
@@ -241,14 +264,13 @@ __device__ bool pair_sees(const hier_shard_desc& g, const SDims& d, const Pair& 
 // codes, m.dw / m.doff the attended candidates and their key offsets.
 __device__ void analyse_pair(const hier_shard_desc& g, const SDims& d, const Pair& pr,
                              const SegSmem& m, int* status) {
-  const int C = pr.kind == 0 ? d.c_player : d.c_hub;
+  const int C = pr.kind == kPairPlayer ? d.c_player : pr.kind == kPairHubOfPlayer ? d.T : d.c_hub;
   int missing = 0;
   for (int c = threadIdx.x; c < C; c += kThreads) {
     int code, key, width;
     bool remote;
     candidate(g, d, pr, c, &code, &key, &width, &remote);
-    bool seen = width > 0 && (pr.kind == 0 || c < d.n_own * d.T || d.hub_keys) &&
-                pair_sees(g, d, pr, code);
+    bool seen = width > 0 && pair_sees(g, d, pr, code);
     if (seen && remote && key < 0) {
       missing = 1;
       seen = false;
@@ -291,7 +313,7 @@ __device__ uint64_t box_bits(const hier_shard_desc& g, const SDims& d, const Pai
     if (m.doff[mid] <= k0) lo = mid;
     else hi = mid - 1;
   }
-  const bool self_only = pr.kind == 1 && !active(g, t, pr.id);
+  const bool self_only = pr.kind == kPairLocal && !active(g, t, pr.id);
   uint64_t bits = 0;
   int pos = 0;
   for (int a = lo; pos < valid && a < n_att; ++a) {
@@ -435,8 +457,8 @@ __global__ void __launch_bounds__(kThreads)
     rec[3] = pr.n1;
     rec[4] = tile_base;
     rec[5] = tile_base + n_tiles;
-    rec[6] = 1;  // 128-row masks
-    rec[7] = 0;
+    rec[6] = 1;                                // 128-row masks
+    rec[7] = pr.kind == kPairPlayer ? 0 : 1;  // hub rows: partial rows
   }
 }
 
@@ -479,11 +501,18 @@ int make_sdims(const hier_shard_desc* g, SDims* d) {
     return HIER_EVALUE;
   }
   d->own_rows = (int)own_rows;
+  d->hub_rows = (int)hub_rows;
   auto cdiv = [](int64_t a, int64_t b) { return (int)((a + b - 1) / b); };
   d->nps = cdiv((int64_t)d->T * d->L, kStripRows);
+  d->nph = d->KL > 0 ? cdiv((int64_t)d->T * d->KL, kStripRows) : 0;
   d->npl = d->KL > 0 ? cdiv((int64_t)d->T * d->KL, kStripRows) : 0;
   d->npg = d->KG > 0 ? cdiv((int64_t)d->T * d->KG, kStripRows) : 0;
-  d->n_pairs = d->n_own * d->nps + d->N * d->npl + d->npg;
+  d->n_hh = d->hub_keys ? d->N * d->npl + d->npg : 0;
+  d->n_pairs = d->n_own * (d->nps + d->nph) + d->n_hh;
+  if ((int64_t)own_rows + hub_rows + (int64_t)d->n_own * d->T * d->KL > INT_MAX / 2) {
+    set_error(HIER_EVALUE, "shard query rows exceed the row range");
+    return HIER_EVALUE;
+  }
   // mate frames of the blocks a strip's rows touch (the same for every player)
   int nf = 0;
   for (int i = 0; i < d->nps; ++i) {
@@ -494,7 +523,7 @@ int make_sdims(const hier_shard_desc* g, SDims* d) {
   }
   d->nf_mate = d->direct ? nf : 0;
   d->c_player = d->T + (d->P - 1) * d->nf_mate + d->T * d->N;
-  d->c_hub = d->n_own * d->T + (d->hub_keys ? d->T * d->N + d->T : 0);
+  d->c_hub = d->T * d->N + d->T;
   if (d->c_player > kMaxCand || d->c_hub > kMaxCand) {
     set_error(HIER_EVALUE, "shard too large for the plan builder (%d / %d key units per pair)",
               d->c_player, d->c_hub);
@@ -528,7 +557,8 @@ extern "C" int hier_shard_sizes(const hier_shard_desc* g, hier_shard_sizes_t* ou
   out->n_pairs = d.n_pairs;
   out->n_counts = 2 * d.n_pairs;
   out->own_rows = d.own_rows;
-  out->q_rows = (int64_t)d.own_rows + (int64_t)d.T * (d.N * d.KL + d.KG);
+  out->hub_rows = d.hub_rows;
+  out->hub_partial_rows = (int64_t)d.n_own * d.T * d.KL;
   return HIER_OK;
 }
 

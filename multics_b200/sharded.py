@@ -32,10 +32,9 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import HierShardDesc, HierShardSizes, check, ptr, stream_ptr
+from ._lib import HierPartialOut, HierShardDesc, HierShardSizes, check, ptr, stream_ptr
 
-__all__ = ["split_players", "ShardTopology", "ShardedHierAttention", "merge_hub_partials",
-           "exchange_mate_frames"]
+__all__ = ["split_players", "ShardTopology", "ShardedHierAttention", "exchange_mate_frames"]
 
 
 def split_players(P: int, world: int) -> List[Tuple[int, int]]:
@@ -142,6 +141,29 @@ class ShardTopology:
         own = np.arange(self.p0 * self.T * self.L, self.p1 * self.T * self.L)
         return np.concatenate([own, self.hub_rows_order()])
 
+    def hub_partial_src(self) -> np.ndarray:
+        """Hub row (in :meth:`hub_rows_order`) of each player-partial row: own
+        player ``p``, frame ``t``, slot ``s`` -> the local hub of ``p``'s group
+        at ``t``."""
+        T, KL = self.T, self.KL
+        p_i, t_i, s_i = np.meshgrid(np.arange(self.p0, self.p1), np.arange(T), np.arange(KL),
+                                    indexing="ij")
+        g = self.labels[t_i, p_i]
+        return ((g * T + t_i) * KL + s_i).reshape(-1).astype(np.int64)
+
+    def hub_partials(self, hub_keys: bool):
+        """CSR of the partial rows of every hub row on this rank: ``off``
+        ``[hub_rows+1]``, ``rows`` (partial-row indices: hub-key partials
+        ``[0, hub_rows)`` when ``hub_keys``, then the player partials)."""
+        src = self.hub_partial_src()
+        lists = [[r] if hub_keys else [] for r in range(self.hub_rows)]
+        for i, r in enumerate(src):
+            lists[r].append(self.hub_rows + i)
+        off = np.zeros(self.hub_rows + 1, dtype=np.int32)
+        off[1:] = np.cumsum([len(x) for x in lists])
+        rows = np.array([x for lst in lists for x in lst], dtype=np.int32)
+        return off, rows
+
 
 def _stream_arrays(streams):
     n = len(streams)
@@ -169,30 +191,6 @@ def exchange_mate_frames(topo: ShardTopology, k, v, remote, group=None, send_row
     dist.all_to_all_single(remote[:n_recv], send, [n * t.L for n in t.recv_units],
                            [len(u) * t.L for u in t.send_units], group=group)
     return remote
-
-
-def merge_hub_partials(o_hub, lse_hub, H, D, group=None, world=1):
-    """Merge hub-row partial results across ranks in place.
-
-    ``o_hub`` bf16 ``[rows, H*D]`` (normalised over this rank's keys),
-    ``lse_hub`` fp32 ``[rows, H]`` (log2 units, -inf without keys)."""
-    if world == 1:
-        return o_hub
-    import torch.distributed as dist
-
-    rows = o_hub.shape[0]
-    lse_max = lse_hub.clone()
-    dist.all_reduce(lse_max, op=dist.ReduceOp.MAX, group=group)
-    buf = torch.empty(rows * H * D + rows * H, dtype=torch.float32, device=o_hub.device)
-    x = buf[: rows * H * D]
-    w = buf[rows * H * D:]
-    lib = _lib.lib()
-    s = stream_ptr(o_hub.device)
-    check(lib.hier_lse_prepare(ptr(o_hub), o_hub.stride(0), ptr(lse_hub), ptr(lse_max), rows, H,
-                               D, ptr(x), ptr(w), s))
-    dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
-    check(lib.hier_lse_finish(ptr(x), ptr(w), rows, H, D, ptr(o_hub), o_hub.stride(0), s))
-    return o_hub
 
 
 class ShardedHierAttention:
@@ -247,7 +245,8 @@ class ShardedHierAttention:
         lib = _lib.lib()
         check(lib.hier_shard_sizes(ctypes.byref(d), ctypes.byref(sz)))
         self.n_pairs = int(sz.n_pairs)
-        self.q_rows = int(sz.q_rows)
+        self.q_rows = int(sz.own_rows + sz.hub_rows)
+        self.hp_rows = int(sz.hub_partial_rows)
         # plan: count key tiles and masks, size the tables (one host read), build
         self.counts = torch.empty(max(sz.n_counts, 1), dtype=torch.int32, device=dev)
         totals = torch.zeros(2, dtype=torch.int32, device=dev)
@@ -268,7 +267,16 @@ class ShardedHierAttention:
         self.n_recv = sum(t.recv_units) * t.L if self.transport == "exchange" else 0
         self.remote = torch.zeros((max(self.n_recv, 1), 2 * self.dim), dtype=torch.bfloat16,
                                   device=dev)
-        self.lse = torch.empty((self.q_rows, self.H), dtype=torch.float32, device=dev)
+        # hub rows: partial rows (hub-key part, then per own player) and their merge
+        n_part = t.hub_rows + self.hp_rows
+        self.part_o = torch.empty((max(n_part, 1), self.dim), dtype=torch.bfloat16, device=dev)
+        self.part_lse = torch.empty((max(n_part, 1), self.H), dtype=torch.float32, device=dev)
+        self.q_hp = torch.empty((max(self.hp_rows, 1), self.dim), dtype=torch.bfloat16,
+                                device=dev)
+        self.hp_src = torch.from_numpy(t.hub_partial_src()).to(dev)
+        off, rows = t.hub_partials(bool(d.hub_keys))
+        self.csr_off = torch.from_numpy(off).to(dev)
+        self.csr_rows = torch.from_numpy(rows if rows.size else np.zeros(1, np.int32)).to(dev)
         from .attention import _dev_err
         self.err = _dev_err(dev)
         self._sym = None
@@ -338,16 +346,17 @@ class ShardedHierAttention:
             self.remote[i * t.L:(i + 1) * t.L, :self.dim] = k_all[src:src + t.L]
             self.remote[i * t.L:(i + 1) * t.L, self.dim:] = v_all[src:src + t.L]
 
-    def attend(self, q, k, v, out, *, v_hub=None, out_rows=None, lse=True):
-        """One attention launch over this rank's query rows.  ``v_hub``
-        replaces ``v``'s hub rows (a group-major copy when ``v`` keeps the
-        sequence order); ``out_rows`` (int32 per query row) sends each row's
-        output (and log-sum-exp) to that row of ``out``; ``lse=False`` skips
-        the log-sum-exp (nothing to merge)."""
+    def attend(self, q, k, v, out, *, v_hub=None, out_rows=None):
+        """One attention launch over this rank's query rows: player rows into
+        ``out`` (row ``out_rows[r]`` when given), hub rows as partial rows
+        (merged by :meth:`merge`).  ``v_hub`` replaces ``v``'s hub rows (a
+        group-major copy when ``v`` keeps the sequence order)."""
         t = self.topo
         own, hub = t.own_rows, t.hub_rows
         if self.transport == "peer":
             k, v = self.k_buffer(), self.v_buffer()
+        if self.hp_rows:
+            torch.index_select(q[own:own + hub], 0, self.hp_src, out=self.q_hp)
         streams = [(k[:own], v[:own]),
                    (k[own:own + hub], v[own:own + hub] if v_hub is None else v_hub)]
         if self.transport == "peer":
@@ -355,11 +364,71 @@ class ShardedHierAttention:
         else:
             streams.append((self.remote[:, :self.dim], self.remote[:, self.dim:]))
         n, kp, vp, rows, strides = _stream_arrays(streams)
+        part = HierPartialOut()
+        part.q2, part.q2_rows, part.q2_stride = self.q_hp.data_ptr(), self.q_hp.shape[0], \
+            self.q_hp.stride(0)
+        part.q2_row0 = own + hub
+        part.o, part.o_stride = self.part_o.data_ptr(), self.part_o.stride(0)
+        part.lse, part.row0 = self.part_lse.data_ptr(), own
         check(_lib.lib().hier_attn_fwd_streams(
             ptr(q), q.shape[0], q.stride(0), n, kp, vp, rows, strides, ptr(out), out.stride(0),
             ptr(out_rows), self.H, self.D, ptr(self.q_pairs), self.n_pairs, ptr(self.kv_tiles),
-            ptr(self.tile_masks), 128, ptr(self.order), 1.0 / math.sqrt(self.D),
-            ptr(self.lse) if lse else None, ptr(self.err), stream_ptr(q.device)))
+            ptr(self.tile_masks), 128, ptr(self.order), 1.0 / math.sqrt(self.D), None,
+            ctypes.byref(part), ptr(self.err), stream_ptr(q.device)))
+
+    # ---- hub merge: partial rows -> hub rows ---------------------------------
+    def partial_max(self):
+        """Per hub row and head, the largest log-sum-exp of this rank's partials."""
+        t = self.topo
+        m = torch.empty((t.hub_rows, self.H), dtype=torch.float32, device=self.device)
+        check(_lib.lib().hier_lse_gather_max(ptr(self.part_lse), self.H, ptr(self.csr_off),
+                                             ptr(self.csr_rows), t.hub_rows, ptr(m),
+                                             stream_ptr(self.device)))
+        return m
+
+    def partial_sums(self, lse_max, buf=None):
+        """``x`` (fp32 ``[hub_rows, H*D]``) and ``w`` (``[hub_rows, H]``): this
+        rank's partials weighted by ``2^(lse - lse_max)``, in one buffer."""
+        t = self.topo
+        n = t.hub_rows
+        if buf is None:
+            buf = torch.empty(n * self.dim + n * self.H, dtype=torch.float32, device=self.device)
+        x, w = buf[:n * self.dim], buf[n * self.dim:]
+        check(_lib.lib().hier_lse_gather_prepare(
+            ptr(self.part_o), self.part_o.stride(0), ptr(self.part_lse), ptr(lse_max), self.H,
+            self.D, ptr(self.csr_off), ptr(self.csr_rows), n, ptr(x), ptr(w),
+            stream_ptr(self.device)))
+        return buf
+
+    def finish(self, buf, out, out_rows=None):
+        """Hub rows ``x / w`` into ``out`` (row ``out_rows[r]``, else ``r``)."""
+        n = self.topo.hub_rows
+        x, w = buf[:n * self.dim], buf[n * self.dim:]
+        check(_lib.lib().hier_lse_finish(ptr(x), ptr(w), n, self.H, self.D, ptr(out),
+                                         out.stride(0), ptr(out_rows), stream_ptr(self.device)))
+
+    def merge(self, out_hub, out_rows=None):
+        """Merged hub rows into ``out_hub`` (``[hub_rows, H*D]``, or rows
+        ``out_rows[r]`` of it): in one process one gather kernel; over ranks a
+        max all-reduce of the log-sum-exp and a sum all-reduce of the
+        weighted partials."""
+        t = self.topo
+        if t.hub_rows == 0:
+            return out_hub
+        if t.world == 1:
+            check(_lib.lib().hier_lse_gather_merge(
+                ptr(self.part_o), self.part_o.stride(0), ptr(self.part_lse), self.H, self.D,
+                ptr(self.csr_off), ptr(self.csr_rows), t.hub_rows, ptr(out_hub),
+                out_hub.stride(0), ptr(out_rows), stream_ptr(self.device)))
+            return out_hub
+        import torch.distributed as dist
+
+        m = self.partial_max()
+        dist.all_reduce(m, op=dist.ReduceOp.MAX, group=self.group)
+        buf = self.partial_sums(m)
+        dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group)
+        self.finish(buf, out_hub, out_rows)
+        return out_hub
 
     def forward(self, q, k, v, out=None):
         t = self.topo
@@ -370,6 +439,5 @@ class ShardedHierAttention:
             out = torch.empty_like(q)
         self.exchange(k, v)
         self.attend(q, k, v, out)
-        merge_hub_partials(out[t.own_rows:], self.lse[t.own_rows:], self.H, self.D,
-                           group=self.group, world=t.world)
+        self.merge(out[t.own_rows:])
         return out

@@ -324,7 +324,7 @@ def hierarchical_tiled_full_sequence_attention(*, roped_q: torch.Tensor, roped_k
             check(lib.hier_attn_fwd_streams(
                 ptr(q), seq_len, q.stride(0), 1, kp, vp, rows, strides, ptr(out), out.stride(0),
                 None, heads, head_dim, ptr(qp), p1 - p0, ptr(plan.kv_tiles), ptr(plan.tile_masks), 1,
-                ptr(order), 1.0 / math.sqrt(head_dim), None, ptr(err), stream_ptr(q.device)))
+                ptr(order), 1.0 / math.sqrt(head_dim), None, None, ptr(err), stream_ptr(q.device)))
     return out.reshape(batch, seq_len, heads * head_dim)
 
 

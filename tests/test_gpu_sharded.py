@@ -4,8 +4,6 @@ merge sums the partials), and the assembled output is compared with the
 oracle's dense-mask fp32 attention.  The NCCL version runs in
 test_gpu_multi.py when a box has two GPUs."""
 
-import ctypes
-
 import numpy as np
 import pytest
 import torch
@@ -33,15 +31,15 @@ def _case(P, T, L, N, KL, KG, labels, H, seed, n_block=1, win=-1):
 
 
 def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v, n_block=1, win=-1):
-    from multics_b200 import _lib
-    from multics_b200._lib import ptr, stream_ptr
+    """Every rank's plan and attention launch in one process; the hub merge
+    does what the two all-reduces compute (max of the ranks' log-sum-exp,
+    then the sum of their weighted partials)."""
     from multics_b200.sharded import ShardedHierAttention, ShardTopology
 
     S = q.shape[0]
     qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
     out = torch.zeros((S, H * 128), dtype=torch.float32, device="cuda")
-    hub_rows = S - P * T * L
-    lses, parts = [], []
+    shards = []
     for rank in range(world):
         t = ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=n_block, local_attn=win,
                           direct=True, labels=labels, world=world, rank=rank)
@@ -53,24 +51,12 @@ def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v, n_block=1, win=-
         sh.attend(ql, kl, vl, o)
         sh.check_status()
         out[t.p0 * T * L:t.p1 * T * L] = o[:t.own_rows].float()
-        parts.append(o[t.own_rows:].clone())
-        lses.append(sh.lse[t.own_rows:].clone())
-    # hub merge: what the two all-reduces compute
-    lse_max = torch.stack(lses).amax(0)
-    lib = _lib.lib()
-    xs = torch.zeros((hub_rows, H * 128), dtype=torch.float32, device="cuda")
-    ws = torch.zeros((hub_rows, H), dtype=torch.float32, device="cuda")
-    for o_h, l_h in zip(parts, lses):
-        x = torch.empty_like(xs)
-        w = torch.empty_like(ws)
-        _lib.check(lib.hier_lse_prepare(ptr(o_h), o_h.stride(0), ptr(l_h), ptr(lse_max), hub_rows,
-                                        H, 128, ptr(x), ptr(w), stream_ptr()))
-        xs += x
-        ws += w
-    merged = torch.empty((hub_rows, H * 128), dtype=torch.bfloat16, device="cuda")
-    _lib.check(lib.hier_lse_finish(ptr(xs), ptr(ws), hub_rows, H, 128, ptr(merged),
-                                   merged.stride(0), stream_ptr()))
-    out[torch.from_numpy(t.hub_rows_order()).cuda()] = merged.float()
+        shards.append(sh)
+    lse_max = torch.stack([sh.partial_max() for sh in shards]).amax(0)
+    buf = sum(sh.partial_sums(lse_max).clone() for sh in shards)
+    merged = torch.empty((shards[0].topo.hub_rows, H * 128), dtype=torch.bfloat16, device="cuda")
+    shards[0].finish(buf, merged)
+    out[torch.from_numpy(shards[0].topo.hub_rows_order()).cuda()] = merged.float()
     return out.cpu().numpy()
 
 

@@ -131,3 +131,34 @@ def test_local_rows_hubs_group_major():
     expect = [f_major(f, g, s) for g in range(N) for f in range(T) for s in range(KL)]
     expect += list(range(T * N * KL, T * (N * KL + KG)))
     assert list(hub) == expect
+
+
+@pytest.mark.parametrize("world,rank", [(1, 0), (2, 0), (2, 1), (4, 3)])
+def test_hub_partials_cover_each_hub_row_once_per_key_set(world, rank):
+    """Every local hub row has one partial per member player on this rank
+    (that player's row of the hub-partial block) and, on the rank holding
+    the hub keys, one over the hub tokens; global hub rows only the latter."""
+    from multics_b200.sharded import ShardTopology
+
+    P, T, L, N, KL, KG = 8, 6, 3, 4, 2, 3
+    lab = _regrouped_labels(P, T, 3, seed=7)
+    t = ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=1, local_attn=-1, direct=True,
+                      labels=lab, world=world, rank=rank)
+    hub_keys = rank == 0
+    off, rows = t.hub_partials(hub_keys)
+    src = t.hub_partial_src()
+    assert len(src) == t.n_own * T * KL
+    for r in range(t.hub_rows):
+        part = rows[off[r]:off[r + 1]]
+        own_part = [x for x in part if x >= t.hub_rows]
+        assert (r in part) == hub_keys
+        if r < T * N * KL:
+            g, f = r // (T * KL), (r % (T * KL)) // KL
+            members = [p for p in range(t.p0, t.p1) if lab[f, p] == g]
+            assert len(own_part) == len(members)
+            for x in own_part:
+                i = x - t.hub_rows
+                p = t.p0 + i // (T * KL)
+                assert p in members and src[i] == r
+        else:
+            assert own_part == []
