@@ -393,10 +393,12 @@ int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_boxes, const
  *                           at own_rows + (g*T + f)*K_L + slot, then global hub
  *                           (f, slot) at own_rows + T*N*K_L + f*K_G + slot
  *                           (V = own_rows + hub_rows);
- *   [V, V + hub_partial_rows) per own player p and frame t the K_L rows of the
- *                           local hub of p's group at t, row
- *                           V + ((p - p0)*T + t)*K_L + slot (a second query
- *                           tensor: hier_partial_out.q2 with q2_row0 = V).
+ *   [V + o, V + o + hub_partial_rows) per own player p and frame t the K_L
+ *                           rows of the local hub of p's group at t, row
+ *                           V + o + ((p - p0)*T + t)*K_L + slot (a second query
+ *                           tensor: hier_partial_out.q2 with q2_row0 = V + o;
+ *                           o = hub_partial_row0 places the rank's partials in
+ *                           a buffer gathered from every rank).
  * Key/value streams for hier_attn_fwd_streams: 0 = its players' rows, 1 =
  * the hub rows (same order), and for each remote group-mate unit (o, f) (the
  * L rows of player o at frame f) the stream-packed first row
@@ -405,11 +407,11 @@ int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_boxes, const
  * its GPU (read in place over NVLink).
  * Player rows get their full key sets.  A hub row is split into partial rows
  * over disjoint key sets: per member player (third block, on the member's
- * rank) and over the hub tokens (second block, on the hub_keys rank only);
- * hub pairs are flagged in q_pairs[7] and written as partial rows
+ * rank) and over the hub tokens (second block, when hub_keys is set); hub
+ * pairs are flagged in q_pairs[7] and written as partial rows
  * (hier_partial_out.row0 = own_rows: hub-key partials at [0, hub_rows),
- * player partials after), then merged with hier_lse_gather_* /
- * hier_lse_finish.  Query pairs are two 128-row tiles of 256-row strips of
+ * player partials at hub_rows + o onwards), then merged with
+ * hier_lse_gather_merge.  Query pairs are two 128-row tiles of 256-row strips of
  * one block; their key tiles cover exactly the key units some row attends
  * to and carry a 128-row mask per half where a half sees part of a tile
  * (q_pairs[6] = 1; launch with mask_rows 128).  An inactive local hub
@@ -420,7 +422,7 @@ typedef struct hier_shard_desc {
   int32_t P, N, L, KL, KG, T, n_block, local_attn, direct;
   int32_t p0, p1;
   int32_t hub_keys;
-  int32_t reserved;
+  int32_t hub_partial_row0; /* o: first hub-partial row (0 for one shard) */
   const int64_t* labels;      /* [T, P] */
   const uint8_t* active;      /* [T, N] */
   const int32_t* remote_key;  /* [P*T] */
@@ -452,22 +454,9 @@ int hier_shard_build(const hier_shard_desc* g, const int32_t* counts, int32_t* q
 
 /* Merge of partial rows over disjoint key sets.  Target t has the partial
  * rows rows[off[t] .. off[t+1]) of o (bf16 [.., H*D], row stride o_stride)
- * with log2-sum-exp lse ([..][H]); merged row = sum_i 2^(lse_i - M) o_i /
- * sum_i 2^(lse_i - M), 0 without keys.
- *   hier_lse_gather_max:     lse_max[t][h] = max_i lse_i (-inf if none);
- *   hier_lse_gather_prepare: x = sum_i 2^(lse_i - lse_max) o_i (fp32
- *                            [n_targets, H*D]), w = sum_i 2^(lse_i - lse_max);
- *   hier_lse_finish:         out[out_rows ? out_rows[t] : t] = x / w (bf16);
- * over ranks: max all-reduce of lse_max, sum all-reduce of x and w between
- * the steps.  hier_lse_gather_merge does the three in one process. */
-int hier_lse_gather_max(const float* lse, int32_t H, const int32_t* off, const int32_t* rows,
-                        int64_t n_targets, float* lse_max, void* stream);
-int hier_lse_gather_prepare(const void* o, int64_t o_stride, const float* lse,
-                            const float* lse_max, int32_t H, int32_t D, const int32_t* off,
-                            const int32_t* rows, int64_t n_targets, float* x, float* w,
-                            void* stream);
-int hier_lse_finish(const float* x, const float* w, int64_t rows, int32_t H, int32_t D, void* out,
-                    int64_t out_stride, const int32_t* out_rows, void* stream);
+ * with log2-sum-exp lse ([..][H]); out[out_rows ? out_rows[t] : t] =
+ * sum_i 2^(lse_i - M) o_i / sum_i 2^(lse_i - M) (bf16, M the largest lse_i,
+ * 0 without keys).  Across ranks the partial rows are all-gathered first. */
 int hier_lse_gather_merge(const void* o, int64_t o_stride, const float* lse, int32_t H, int32_t D,
                           const int32_t* off, const int32_t* rows, int64_t n_targets, void* out,
                           int64_t out_stride, const int32_t* out_rows, void* stream);

@@ -90,7 +90,7 @@ class HierShardDesc(ctypes.Structure):
     _fields_ = [
         ("P", c_int32), ("N", c_int32), ("L", c_int32), ("KL", c_int32), ("KG", c_int32),
         ("T", c_int32), ("n_block", c_int32), ("local_attn", c_int32), ("direct", c_int32),
-        ("p0", c_int32), ("p1", c_int32), ("hub_keys", c_int32), ("reserved", c_int32),
+        ("p0", c_int32), ("p1", c_int32), ("hub_keys", c_int32), ("hub_partial_row0", c_int32),
         ("labels", c_void_p), ("active", c_void_p), ("remote_key", c_void_p),
     ]
 
@@ -148,10 +148,6 @@ _SIGS = {
     "hier_shard_count": (c_int, [ctypes.POINTER(HierShardDesc), _P, _P, _P, _P]),
     "hier_shard_build": (c_int, [ctypes.POINTER(HierShardDesc), _P, _P, _P, c_int32, _P, c_int64,
                                  _P, _P, _P]),
-    "hier_lse_gather_max": (c_int, [_P, c_int32, _P, _P, c_int64, _P, _P]),
-    "hier_lse_gather_prepare": (c_int, [_P, c_int64, _P, _P, c_int32, c_int32, _P, _P, c_int64,
-                                        _P, _P, _P]),
-    "hier_lse_finish": (c_int, [_P, _P, c_int64, c_int32, c_int32, _P, c_int64, _P, _P]),
     "hier_lse_gather_merge": (c_int, [_P, c_int64, _P, c_int32, c_int32, _P, _P, c_int64, _P,
                                       c_int64, _P, _P]),
     "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),

@@ -653,10 +653,8 @@ extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_
 // Target row t has partial rows rows[off[t] .. off[t+1]) (bf16 outputs o,
 // each normalised over its own keys, and their log2-sum-exp lse); the merged
 // row is sum_i 2^(lse_i - M) o_i / sum_i 2^(lse_i - M) with M the largest
-// lse_i (0 without any key).  Over several ranks: M from a max all-reduce of
-// hier_lse_gather_max, then hier_lse_gather_prepare's x, w summed by an
-// all-reduce, then hier_lse_finish.  In one process hier_lse_gather_merge
-// does all three.
+// lse_i (0 without any key).  Across ranks the partial rows are gathered to
+// every rank first.
 
 namespace hier {
 namespace {
@@ -681,30 +679,10 @@ __device__ __forceinline__ void bf16x8_store(__nv_bfloat16* p, const float (&f)[
   *reinterpret_cast<uint4*>(p) = v;
 }
 
-__device__ __forceinline__ float gather_max(const float* lse, int H, int h, const int32_t* rows,
-                                            int b, int e) {
-  float m = -INFINITY;
-  for (int i = b; i < e; ++i) m = fmaxf(m, lse[(int64_t)rows[i] * H + h]);
-  return m;
-}
-
-__global__ void lse_gather_max_kernel(const float* lse, int H, const int32_t* off,
-                                      const int32_t* rows, int64_t n_targets, float* lse_max) {
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n_targets * H;
-       t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = t / H;
-    const int h = (int)(t % H);
-    lse_max[t] = gather_max(lse, H, h, rows, off[r], off[r + 1]);
-  }
-}
-
-// Per (target, head, 8 channels): the weighted sum of the partials; kFinal
-// writes the normalised bf16 row, otherwise x (fp32) and w.
-template <bool kFinal>
+// Per (target, head, 8 channels): the normalised weighted sum of the partials.
 __global__ void lse_gather_kernel(const __nv_bfloat16* o, int64_t o_stride, const float* lse,
-                                  const float* lse_max, int H, int D, const int32_t* off,
-                                  const int32_t* rows, int64_t n_targets, float* x, float* w,
-                                  __nv_bfloat16* out, int64_t out_stride,
+                                  int H, int D, const int32_t* off, const int32_t* rows,
+                                  int64_t n_targets, __nv_bfloat16* out, int64_t out_stride,
                                   const int32_t* out_rows) {
   const int per = D / 8;
   const int64_t n = n_targets * H * per;
@@ -715,7 +693,8 @@ __global__ void lse_gather_kernel(const __nv_bfloat16* o, int64_t o_stride, cons
     const int64_t r = rh / H;
     const int h = (int)(rh % H);
     const int b = off[r], e = off[r + 1];
-    const float m = kFinal ? gather_max(lse, H, h, rows, b, e) : lse_max[rh];
+    float m = -INFINITY;
+    for (int i = b; i < e; ++i) m = fmaxf(m, lse[(int64_t)rows[i] * H + h]);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     float ws = 0.f;
     for (int i = b; i < e; ++i) {
@@ -729,35 +708,8 @@ __global__ void lse_gather_kernel(const __nv_bfloat16* o, int64_t o_stride, cons
       for (int q = 0; q < 8; ++q) acc[q] = fmaf(wt, f[q], acc[q]);
       ws += wt;
     }
-    if (kFinal) {
-      const int64_t dr = out_rows ? (int64_t)out_rows[r] : r;
-      bf16x8_store(out + dr * out_stride + h * D + part * 8, acc, ws > 0.f ? 1.f / ws : 0.f);
-    } else {
-      float4* dst = reinterpret_cast<float4*>(x + (r * H + h) * D + part * 8);
-      dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-      if (part == 0) w[rh] = ws;
-    }
-  }
-}
-
-__global__ void lse_finish_kernel(const float* x, const float* w, int64_t rows, int H, int D,
-                                  __nv_bfloat16* out, int64_t out_stride,
-                                  const int32_t* out_rows) {
-  const int per = D / 8;
-  const int64_t n = rows * H * per;
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n;
-       t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t rh = t / per;
-    const int part = (int)(t % per);
-    const int64_t r = rh / H;
-    const int h = (int)(rh % H);
-    const float ws = w[rh];
-    const float4* src = reinterpret_cast<const float4*>(x + (r * H + h) * D + part * 8);
-    const float4 a = src[0], b = src[1];
-    const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     const int64_t dr = out_rows ? (int64_t)out_rows[r] : r;
-    bf16x8_store(out + dr * out_stride + h * D + part * 8, f, ws > 0.f ? 1.f / ws : 0.f);
+    bf16x8_store(out + dr * out_stride + h * D + part * 8, acc, ws > 0.f ? 1.f / ws : 0.f);
   }
 }
 
@@ -777,44 +729,6 @@ int merge_check(int64_t rows, int H, int D, int64_t stride) {
 }  // namespace
 }  // namespace hier
 
-extern "C" int hier_lse_gather_max(const float* lse, int32_t H, const int32_t* off,
-                                   const int32_t* rows, int64_t n_targets, float* lse_max,
-                                   void* stream) {
-  clear_error();
-  int rc = merge_check(n_targets, H, 8, 0);
-  if (rc || n_targets == 0) return rc;
-  lse_gather_max_kernel<<<merge_grid(n_targets * H), 256, 0, (cudaStream_t)stream>>>(
-      lse, H, off, rows, n_targets, lse_max);
-  HIER_CHECK_CUDA(cudaGetLastError(), "lse_gather_max_kernel launch");
-  return HIER_OK;
-}
-
-extern "C" int hier_lse_gather_prepare(const void* o, int64_t o_stride, const float* lse,
-                                       const float* lse_max, int32_t H, int32_t D,
-                                       const int32_t* off, const int32_t* rows, int64_t n_targets,
-                                       float* x, float* w, void* stream) {
-  clear_error();
-  int rc = merge_check(n_targets, H, D, o_stride);
-  if (rc || n_targets == 0) return rc;
-  lse_gather_kernel<false><<<merge_grid(n_targets * H * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(o), o_stride, lse, lse_max, H, D, off, rows,
-      n_targets, x, w, nullptr, 0, nullptr);
-  HIER_CHECK_CUDA(cudaGetLastError(), "lse_gather_kernel launch");
-  return HIER_OK;
-}
-
-extern "C" int hier_lse_finish(const float* x, const float* w, int64_t rows, int32_t H, int32_t D,
-                               void* out, int64_t out_stride, const int32_t* out_rows,
-                               void* stream) {
-  clear_error();
-  int rc = merge_check(rows, H, D, out_stride);
-  if (rc || rows == 0) return rc;
-  lse_finish_kernel<<<merge_grid(rows * H * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
-      x, w, rows, H, D, reinterpret_cast<__nv_bfloat16*>(out), out_stride, out_rows);
-  HIER_CHECK_CUDA(cudaGetLastError(), "lse_finish_kernel launch");
-  return HIER_OK;
-}
-
 extern "C" int hier_lse_gather_merge(const void* o, int64_t o_stride, const float* lse, int32_t H,
                                      int32_t D, const int32_t* off, const int32_t* rows,
                                      int64_t n_targets, void* out, int64_t out_stride,
@@ -823,9 +737,9 @@ extern "C" int hier_lse_gather_merge(const void* o, int64_t o_stride, const floa
   int rc = merge_check(n_targets, H, D, o_stride);
   if (!rc) rc = merge_check(n_targets, H, D, out_stride);
   if (rc || n_targets == 0) return rc;
-  lse_gather_kernel<true><<<merge_grid(n_targets * H * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(o), o_stride, lse, nullptr, H, D, off, rows,
-      n_targets, nullptr, nullptr, reinterpret_cast<__nv_bfloat16*>(out), out_stride, out_rows);
+  lse_gather_kernel<<<merge_grid(n_targets * H * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o), o_stride, lse, H, D, off, rows, n_targets,
+      reinterpret_cast<__nv_bfloat16*>(out), out_stride, out_rows);
   HIER_CHECK_CUDA(cudaGetLastError(), "lse_gather_kernel launch");
   return HIER_OK;
 }

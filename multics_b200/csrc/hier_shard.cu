@@ -6,8 +6,10 @@
 //   [own_rows, V)               every hub row, group-major: local hub (g, f, slot)
 //                               at own_rows + (g*T + f)*K_L + slot, then global
 //                               hub (f, slot) at own_rows + T*N*K_L + f*K_G + slot;
-//   [V, V + n_own*T*K_L)        per own player p and frame t the K_L local-hub
-//                               rows of p's group at t (second query tensor).
+//   [V + o, V + o + n_own*T*K_L) per own player p and frame t the K_L local-hub
+//                               rows of p's group at t (second query tensor;
+//                               V = own_rows + hub_rows, o = hub_partial_row0,
+//                               the shard's slot in an all-gathered buffer).
 // Key/value streams: 0 = the shard's player rows, 1 = the hub rows (same
 // order as above), and for a remote group-mate unit (o, f) the
 // stream-packed first row remote_key[o*T + f].
@@ -70,6 +72,7 @@ constexpr int kSelSkip = -2;
 struct SDims {
   int P, T, L, N, KL, KG, nb, win, direct;
   int p0, p1, n_own, hub_keys;
+  int hp_row0;         // offset of this shard's hub-partial rows in the partial-row space
   int nps;             // player strips per player
   int nph;             // hub-partial strips per player
   int npl, npg;        // hub-key pairs per group, global hub-key pairs (hub_keys rank)
@@ -125,7 +128,7 @@ __device__ Pair pair_of(const SDims& d, int i) {
     r.j0 = kStripRows * (i % d.nph);
     rows = d.T * d.KL;
     r.unit = d.KL;
-    r.q0 = d.own_rows + d.hub_rows + (r.id - d.p0) * rows + r.j0;
+    r.q0 = d.own_rows + d.hub_rows + d.hp_row0 + (r.id - d.p0) * rows + r.j0;
   } else if ((i -= n_hp) < d.N * d.npl) {
     const int h = i;
     r.kind = kPairLocal;
@@ -493,6 +496,11 @@ int make_sdims(const hier_shard_desc* g, SDims* d) {
     return HIER_EVALUE;
   }
   d->p0 = g->p0, d->p1 = g->p1, d->n_own = g->p1 - g->p0, d->hub_keys = g->hub_keys != 0;
+  if (g->hub_partial_row0 < 0) {
+    set_error(HIER_EVALUE, "negative hub-partial row offset %d", g->hub_partial_row0);
+    return HIER_EVALUE;
+  }
+  d->hp_row0 = g->hub_partial_row0;
   const int64_t own_rows = (int64_t)d->n_own * d->T * d->L;
   const int64_t hub_rows = (int64_t)d->T * (d->N * d->KL + d->KG);
   if (own_rows >= (1 << segplan::kStreamShift) || hub_rows >= (1 << segplan::kStreamShift)) {
@@ -509,7 +517,8 @@ int make_sdims(const hier_shard_desc* g, SDims* d) {
   d->npg = d->KG > 0 ? cdiv((int64_t)d->T * d->KG, kStripRows) : 0;
   d->n_hh = d->hub_keys ? d->N * d->npl + d->npg : 0;
   d->n_pairs = d->n_own * (d->nps + d->nph) + d->n_hh;
-  if ((int64_t)own_rows + hub_rows + (int64_t)d->n_own * d->T * d->KL > INT_MAX / 2) {
+  if ((int64_t)own_rows + hub_rows + d->hp_row0 + (int64_t)d->n_own * d->T * d->KL >
+      INT_MAX / 2) {
     set_error(HIER_EVALUE, "shard query rows exceed the row range");
     return HIER_EVALUE;
   }

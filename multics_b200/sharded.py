@@ -142,23 +142,37 @@ class ShardTopology:
         return np.concatenate([own, self.hub_rows_order()])
 
     def hub_partial_src(self) -> np.ndarray:
-        """Hub row (in :meth:`hub_rows_order`) of each player-partial row: own
-        player ``p``, frame ``t``, slot ``s`` -> the local hub of ``p``'s group
-        at ``t``."""
+        """Hub row (in :meth:`hub_rows_order`) of each of this rank's
+        player-partial rows: own player ``p``, frame ``t``, slot ``s`` -> the
+        local hub of ``p``'s group at ``t``."""
         T, KL = self.T, self.KL
         p_i, t_i, s_i = np.meshgrid(np.arange(self.p0, self.p1), np.arange(T), np.arange(KL),
                                     indexing="ij")
         g = self.labels[t_i, p_i]
         return ((g * T + t_i) * KL + s_i).reshape(-1).astype(np.int64)
 
-    def hub_partials(self, hub_keys: bool):
-        """CSR of the partial rows of every hub row on this rank: ``off``
-        ``[hub_rows+1]``, ``rows`` (partial-row indices: hub-key partials
-        ``[0, hub_rows)`` when ``hub_keys``, then the player partials)."""
-        src = self.hub_partial_src()
-        lists = [[r] if hub_keys else [] for r in range(self.hub_rows)]
-        for i, r in enumerate(src):
-            lists[r].append(self.hub_rows + i)
+    @property
+    def hub_partial_slot(self) -> int:
+        """Rows of one rank's player-partial block in the gathered buffer (the
+        largest rank's ``n_own*T*K_L``)."""
+        return max(b - a for a, b in self.bounds) * self.T * self.KL
+
+    def hub_partials(self):
+        """CSR of the partial rows of every hub row, in the partial-row buffer
+        every rank assembles: ``[0, hub_rows)`` the hub-token partials (each
+        rank computes them), then per rank a slot of
+        :attr:`hub_partial_slot` rows with its players' partials.  Returns
+        ``off [hub_rows+1]`` and ``rows``."""
+        T, KL = self.T, self.KL
+        lists = [[r] for r in range(self.hub_rows)]
+        slot = self.hub_partial_slot
+        for r, (a, b) in enumerate(self.bounds):
+            for p in range(a, b):
+                for t in range(T):
+                    g = int(self.labels[t, p])
+                    base = self.hub_rows + r * slot + ((p - a) * T + t) * KL
+                    for s in range(KL):
+                        lists[(g * T + t) * KL + s].append(base + s)
         off = np.zeros(self.hub_rows + 1, dtype=np.int32)
         off[1:] = np.cumsum([len(x) for x in lists])
         rows = np.array([x for lst in lists for x in lst], dtype=np.int32)
@@ -237,7 +251,10 @@ class ShardedHierAttention:
         d = HierShardDesc()
         d.P, d.N, d.L, d.KL, d.KG, d.T = t.P, t.N, t.L, t.KL, t.KG, t.T
         d.n_block, d.local_attn, d.direct = t.n_block, t.local_attn, int(t.direct)
-        d.p0, d.p1, d.hub_keys = t.p0, t.p1, int(t.rank == 0)
+        # every rank computes the hub-token partials (a few key tiles per hub
+        # row), so only the per-player hub partials cross GPUs
+        d.p0, d.p1, d.hub_keys = t.p0, t.p1, 1
+        d.hub_partial_row0 = t.rank * t.hub_partial_slot
         d.labels, d.active, d.remote_key = (self._labels.data_ptr(), self._active.data_ptr(),
                                             self._keys.data_ptr())
         self.desc = d
@@ -267,14 +284,17 @@ class ShardedHierAttention:
         self.n_recv = sum(t.recv_units) * t.L if self.transport == "exchange" else 0
         self.remote = torch.zeros((max(self.n_recv, 1), 2 * self.dim), dtype=torch.bfloat16,
                                   device=dev)
-        # hub rows: partial rows (hub-key part, then per own player) and their merge
-        n_part = t.hub_rows + self.hp_rows
-        self.part_o = torch.empty((max(n_part, 1), self.dim), dtype=torch.bfloat16, device=dev)
-        self.part_lse = torch.empty((max(n_part, 1), self.H), dtype=torch.float32, device=dev)
+        # hub rows as partial rows: the hub-token part, then one slot per rank
+        # for its players' partials (all-gathered in place before the merge)
+        slot = t.hub_partial_slot
+        n_part = t.hub_rows + t.world * slot
+        self.part_o = torch.zeros((max(n_part, 1), self.dim), dtype=torch.bfloat16, device=dev)
+        self.part_lse = torch.full((max(n_part, 1), self.H), float("-inf"), dtype=torch.float32,
+                                   device=dev)
         self.q_hp = torch.empty((max(self.hp_rows, 1), self.dim), dtype=torch.bfloat16,
                                 device=dev)
         self.hp_src = torch.from_numpy(t.hub_partial_src()).to(dev)
-        off, rows = t.hub_partials(bool(d.hub_keys))
+        off, rows = t.hub_partials()
         self.csr_off = torch.from_numpy(off).to(dev)
         self.csr_rows = torch.from_numpy(rows if rows.size else np.zeros(1, np.int32)).to(dev)
         from .attention import _dev_err
@@ -367,7 +387,7 @@ class ShardedHierAttention:
         part = HierPartialOut()
         part.q2, part.q2_rows, part.q2_stride = self.q_hp.data_ptr(), self.q_hp.shape[0], \
             self.q_hp.stride(0)
-        part.q2_row0 = own + hub
+        part.q2_row0 = own + hub + t.rank * t.hub_partial_slot
         part.o, part.o_stride = self.part_o.data_ptr(), self.part_o.stride(0)
         part.lse, part.row0 = self.part_lse.data_ptr(), own
         check(_lib.lib().hier_attn_fwd_streams(
@@ -377,58 +397,38 @@ class ShardedHierAttention:
             ctypes.byref(part), ptr(self.err), stream_ptr(q.device)))
 
     # ---- hub merge: partial rows -> hub rows ---------------------------------
-    def partial_max(self):
-        """Per hub row and head, the largest log-sum-exp of this rank's partials."""
+    def gather_partials(self):
+        """All-gather every rank's player-partial slot (rows and log-sum-exp)
+        into this rank's partial-row buffer, in place."""
         t = self.topo
-        m = torch.empty((t.hub_rows, self.H), dtype=torch.float32, device=self.device)
-        check(_lib.lib().hier_lse_gather_max(ptr(self.part_lse), self.H, ptr(self.csr_off),
-                                             ptr(self.csr_rows), t.hub_rows, ptr(m),
-                                             stream_ptr(self.device)))
-        return m
-
-    def partial_sums(self, lse_max, buf=None):
-        """``x`` (fp32 ``[hub_rows, H*D]``) and ``w`` (``[hub_rows, H]``): this
-        rank's partials weighted by ``2^(lse - lse_max)``, in one buffer."""
-        t = self.topo
-        n = t.hub_rows
-        if buf is None:
-            buf = torch.empty(n * self.dim + n * self.H, dtype=torch.float32, device=self.device)
-        x, w = buf[:n * self.dim], buf[n * self.dim:]
-        check(_lib.lib().hier_lse_gather_prepare(
-            ptr(self.part_o), self.part_o.stride(0), ptr(self.part_lse), ptr(lse_max), self.H,
-            self.D, ptr(self.csr_off), ptr(self.csr_rows), n, ptr(x), ptr(w),
-            stream_ptr(self.device)))
-        return buf
-
-    def finish(self, buf, out, out_rows=None):
-        """Hub rows ``x / w`` into ``out`` (row ``out_rows[r]``, else ``r``)."""
-        n = self.topo.hub_rows
-        x, w = buf[:n * self.dim], buf[n * self.dim:]
-        check(_lib.lib().hier_lse_finish(ptr(x), ptr(w), n, self.H, self.D, ptr(out),
-                                         out.stride(0), ptr(out_rows), stream_ptr(self.device)))
-
-    def merge(self, out_hub, out_rows=None):
-        """Merged hub rows into ``out_hub`` (``[hub_rows, H*D]``, or rows
-        ``out_rows[r]`` of it): in one process one gather kernel; over ranks a
-        max all-reduce of the log-sum-exp and a sum all-reduce of the
-        weighted partials."""
-        t = self.topo
-        if t.hub_rows == 0:
-            return out_hub
-        if t.world == 1:
-            check(_lib.lib().hier_lse_gather_merge(
-                ptr(self.part_o), self.part_o.stride(0), ptr(self.part_lse), self.H, self.D,
-                ptr(self.csr_off), ptr(self.csr_rows), t.hub_rows, ptr(out_hub),
-                out_hub.stride(0), ptr(out_rows), stream_ptr(self.device)))
-            return out_hub
+        if t.world == 1 or t.hub_partial_slot == 0:
+            return
         import torch.distributed as dist
 
-        m = self.partial_max()
-        dist.all_reduce(m, op=dist.ReduceOp.MAX, group=self.group)
-        buf = self.partial_sums(m)
-        dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group)
-        self.finish(buf, out_hub, out_rows)
+        h0, slot = t.hub_rows, t.hub_partial_slot
+        o_all = self.part_o[h0:h0 + t.world * slot]
+        l_all = self.part_lse[h0:h0 + t.world * slot]
+        r0 = t.rank * slot
+        dist.all_gather_into_tensor(o_all, o_all[r0:r0 + slot], group=self.group)
+        dist.all_gather_into_tensor(l_all, l_all[r0:r0 + slot], group=self.group)
+
+    def merge_partials(self, out_hub, out_rows=None):
+        """Merged hub rows from the assembled partial-row buffer into
+        ``out_hub`` (``[hub_rows, H*D]``, or rows ``out_rows[r]`` of it)."""
+        t = self.topo
+        check(_lib.lib().hier_lse_gather_merge(
+            ptr(self.part_o), self.part_o.stride(0), ptr(self.part_lse), self.H, self.D,
+            ptr(self.csr_off), ptr(self.csr_rows), t.hub_rows, ptr(out_hub), out_hub.stride(0),
+            ptr(out_rows), stream_ptr(self.device)))
         return out_hub
+
+    def merge(self, out_hub, out_rows=None):
+        """Hub rows: all-gather the ranks' player partials, then one gather
+        kernel merges every hub row's partials by log-sum-exp."""
+        if self.topo.hub_rows == 0:
+            return out_hub
+        self.gather_partials()
+        return self.merge_partials(out_hub, out_rows)
 
     def forward(self, q, k, v, out=None):
         t = self.topo

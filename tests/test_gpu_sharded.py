@@ -31,9 +31,9 @@ def _case(P, T, L, N, KL, KG, labels, H, seed, n_block=1, win=-1):
 
 
 def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v, n_block=1, win=-1):
-    """Every rank's plan and attention launch in one process; the hub merge
-    does what the two all-reduces compute (max of the ranks' log-sum-exp,
-    then the sum of their weighted partials)."""
+    """Every rank's plan and attention launch in one process; the ranks'
+    player-partial slots are copied together as the all-gather would, then
+    merged."""
     from multics_b200.sharded import ShardedHierAttention, ShardTopology
 
     S = q.shape[0]
@@ -52,11 +52,16 @@ def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v, n_block=1, win=-
         sh.check_status()
         out[t.p0 * T * L:t.p1 * T * L] = o[:t.own_rows].float()
         shards.append(sh)
-    lse_max = torch.stack([sh.partial_max() for sh in shards]).amax(0)
-    buf = sum(sh.partial_sums(lse_max).clone() for sh in shards)
-    merged = torch.empty((shards[0].topo.hub_rows, H * 128), dtype=torch.bfloat16, device="cuda")
-    shards[0].finish(buf, merged)
-    out[torch.from_numpy(shards[0].topo.hub_rows_order()).cuda()] = merged.float()
+    # the all-gather: every rank's player-partial slot into rank 0's buffer
+    s0 = shards[0]
+    h0, slot = s0.topo.hub_rows, s0.topo.hub_partial_slot
+    for r, sh in enumerate(shards[1:], start=1):
+        rows = slice(h0 + r * slot, h0 + (r + 1) * slot)
+        s0.part_o[rows] = sh.part_o[rows]
+        s0.part_lse[rows] = sh.part_lse[rows]
+    merged = torch.empty((h0, H * 128), dtype=torch.bfloat16, device="cuda")
+    s0.merge_partials(merged)
+    out[torch.from_numpy(s0.topo.hub_rows_order()).cuda()] = merged.float()
     return out.cpu().numpy()
 
 

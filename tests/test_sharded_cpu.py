@@ -133,32 +133,33 @@ def test_local_rows_hubs_group_major():
     assert list(hub) == expect
 
 
-@pytest.mark.parametrize("world,rank", [(1, 0), (2, 0), (2, 1), (4, 3)])
-def test_hub_partials_cover_each_hub_row_once_per_key_set(world, rank):
-    """Every local hub row has one partial per member player on this rank
-    (that player's row of the hub-partial block) and, on the rank holding
-    the hub keys, one over the hub tokens; global hub rows only the latter."""
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_hub_partials_cover_each_hub_row_once_per_key_set(world):
+    """In the assembled partial-row buffer every local hub row has its
+    hub-token partial and one partial per member player, in the slot of the
+    rank that owns the player; global hub rows only the hub-token one."""
     from multics_b200.sharded import ShardTopology
 
     P, T, L, N, KL, KG = 8, 6, 3, 4, 2, 3
     lab = _regrouped_labels(P, T, 3, seed=7)
-    t = ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=1, local_attn=-1, direct=True,
-                      labels=lab, world=world, rank=rank)
-    hub_keys = rank == 0
-    off, rows = t.hub_partials(hub_keys)
-    src = t.hub_partial_src()
-    assert len(src) == t.n_own * T * KL
+    tops = [ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=1, local_attn=-1,
+                          direct=True, labels=lab, world=world, rank=r) for r in range(world)]
+    t = tops[0]
+    off, rows = t.hub_partials()
+    assert all((x.hub_partials()[1] == rows).all() for x in tops)  # the same on every rank
+    slot = t.hub_partial_slot
     for r in range(t.hub_rows):
-        part = rows[off[r]:off[r + 1]]
-        own_part = [x for x in part if x >= t.hub_rows]
-        assert (r in part) == hub_keys
+        part = list(rows[off[r]:off[r + 1]])
+        assert part[0] == r
+        players = part[1:]
         if r < T * N * KL:
             g, f = r // (T * KL), (r % (T * KL)) // KL
-            members = [p for p in range(t.p0, t.p1) if lab[f, p] == g]
-            assert len(own_part) == len(members)
-            for x in own_part:
-                i = x - t.hub_rows
-                p = t.p0 + i // (T * KL)
-                assert p in members and src[i] == r
+            members = [p for p in range(P) if lab[f, p] == g]
+            assert len(players) == len(members)
+            for x in players:
+                rk, i = divmod(x - t.hub_rows, slot)
+                tr = tops[rk]
+                src = tr.hub_partial_src()
+                assert src[i] == r and tr.p0 + i // (T * KL) in members
         else:
-            assert own_part == []
+            assert players == []
