@@ -202,13 +202,10 @@ def run_sharded(args, rank, world, local_rank):
                      out=(q_buf, k_buf))
         if i is not None:
             marks["a"][i].record(stream)
-        sh.exchange(k_buf, v)
-        if i is not None:
-            marks["b"][i].record(stream)
-        sh.attend(q_buf, k_buf, v, o_buf)
-        if i is not None:
-            marks["c"][i].record(stream)
-        sh.merge(o_buf[topo.own_rows:])
+        # exchange, hub pairs, partial all-gather overlapped with the player
+        # strips, hub merge (events after the exchange and the launches)
+        sh.forward(q_buf, k_buf, v, o_buf,
+                   events=None if i is None else (marks["b"][i], marks["c"][i]))
 
     for _ in range(args.warmup):
         step()

@@ -430,7 +430,9 @@ typedef struct hier_shard_desc {
 
 typedef struct hier_shard_sizes_t {
   int32_t n_pairs;          /* player strips, hub-partial strips, hub-key pairs */
+  int32_t n_player_pairs;   /* the player strips, pairs [0, n_player_pairs) */
   int32_t n_counts;         /* int32 entries of the per-pair counts */
+  int32_t reserved;
   int64_t own_rows;         /* the rank's player rows */
   int64_t hub_rows;         /* T*(N*K_L + K_G) */
   int64_t hub_partial_rows; /* (p1 - p0)*T*K_L */
@@ -447,7 +449,10 @@ int hier_shard_count(const hier_shard_desc* g, int32_t* counts, int32_t* totals,
                      int32_t* status, void* stream);
 
 /* Second pass: the plan (q_pairs [n_pairs][8], kv_tiles, tile_masks, order
- * [n_pairs] or NULL); status bit 1: tile capacity, bit 4: mask capacity. */
+ * [n_pairs] or NULL); status bit 1: tile capacity, bit 4: mask capacity.
+ * order lists the player strips first, then the hub pairs, each part by
+ * descending work, so the two parts can run as separate launches (e.g. the
+ * hub pairs first, their partials exchanged while the strips run). */
 int hier_shard_build(const hier_shard_desc* g, const int32_t* counts, int32_t* q_pairs,
                      int32_t* kv_tiles, int32_t tile_capacity, uint32_t* tile_masks,
                      int64_t mask_capacity, int32_t* order, int32_t* status, void* stream);

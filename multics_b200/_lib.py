@@ -99,7 +99,8 @@ class HierShardSizes(ctypes.Structure):
     """Mirror of ``hier_shard_sizes_t``."""
 
     _fields_ = [
-        ("n_pairs", c_int32), ("n_counts", c_int32), ("own_rows", c_int64), ("hub_rows", c_int64),
+        ("n_pairs", c_int32), ("n_player_pairs", c_int32), ("n_counts", c_int32),
+        ("reserved", c_int32), ("own_rows", c_int64), ("hub_rows", c_int64),
         ("hub_partial_rows", c_int64),
     ]
 

@@ -564,6 +564,7 @@ extern "C" int hier_shard_sizes(const hier_shard_desc* g, hier_shard_sizes_t* ou
   if (rc) return rc;
   memset(out, 0, sizeof(*out));
   out->n_pairs = d.n_pairs;
+  out->n_player_pairs = d.n_own * d.nps;
   out->n_counts = 2 * d.n_pairs;
   out->own_rows = d.own_rows;
   out->hub_rows = d.hub_rows;
@@ -608,8 +609,12 @@ extern "C" int hier_shard_build(const hier_shard_desc* g, const int32_t* counts,
   pair_build_kernel<<<d.n_pairs, kThreads, plan_smem_bytes(), s>>>(
       *g, d, counts, q_pairs, kv_tiles, tile_capacity, tile_masks, mask_capacity, status);
   HIER_CHECK_CUDA(cudaGetLastError(), "pair_build_kernel launch");
-  if (order) {
-    order_by_work_kernel<8><<<(d.n_pairs + 127) / 128, 128, 0, s>>>(q_pairs, d.n_pairs, order);
+  if (order) {  // player strips, then hub pairs, each by descending work
+    const int ns = d.n_own * d.nps, nh = d.n_pairs - ns;
+    if (ns > 0) order_by_work_kernel<8><<<(ns + 127) / 128, 128, 0, s>>>(q_pairs, ns, order);
+    if (nh > 0)
+      order_by_work_kernel<8><<<(nh + 127) / 128, 128, 0, s>>>(q_pairs + (int64_t)ns * 8, nh,
+                                                                 order + ns, ns);
     HIER_CHECK_CUDA(cudaGetLastError(), "order_by_work_kernel launch");
   }
   return HIER_OK;
