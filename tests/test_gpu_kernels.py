@@ -290,6 +290,36 @@ def test_sequence_plan_random_configs_vs_torch_fp32(dev, case):
     assert _cos(out.float(), ref) >= MIN_COS
 
 
+def test_sequence_plan_caller_active_groups(dev):
+    """Caller-given active groups: an active group without members (its hub
+    rows attend to hub tokens only) and an inactive group with members (its
+    hub rows attend to themselves, players do not see them)."""
+    from multics_b200.attention import sequence_plan
+    from multics_b200.hier_masks import build_stage2_hier_flex_block_mask
+
+    P, T, L, N, KL, KG, H = 4, 4, 40, 3, 4, 3, 2
+    labels = torch.tensor([[0, 0, 1, 1]] * T)
+    active = torch.tensor([[True, True, True], [True, False, True], [True, True, False],
+                           [False, True, True]])
+    g = torch.Generator().manual_seed(11)
+    S = P * T * L + T * (N * KL + KG)
+    q, k, v = (torch.randn(S, H * 128, generator=g).mul(0.5).to(torch.bfloat16).to(dev)
+               for _ in range(3))
+    bm, _, _ = build_stage2_hier_flex_block_mask(P, T, L, N, KL, KG, 1, -1, labels.to(dev),
+                                                 active.to(dev), True, dev)
+    sp = sequence_plan(bm, H)
+    assert sp is not None
+    src = sp.plan_to_seq.long()
+    out = sp.attend(q[src].contiguous(), k[src].contiguous(), v)
+    mask = torch.from_numpy(O.dense_mask(P, T, L, N, KL, KG, 1, -1, labels=labels.numpy(),
+                                         active=active.numpy(), direct=True)).to(dev)
+    ref = torch_masked_attention(q, k, v, mask, H)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    assert float((out.float() - ref).abs().max()) <= MAX_ABS
+    assert _cos(out.float(), ref) >= MIN_COS
+
+
 @pytest.mark.parametrize("plan", ["segments", "blocks"])
 @pytest.mark.parametrize("name", [n for n in case_names("num") if "d128" in n])
 def test_layer_entry_matches_reference_fp32(dev, name, plan, monkeypatch):
