@@ -28,6 +28,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "hier-attn useful TFLOP/s"
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one attention
+# launch of the config-2 sequence plan, from an ncu capture of this bench's
+# command (1.09x the algorithmic Q, K, V read + O write of 0.95 GB)
+CFG2_SEQUENCE_TRAFFIC_BYTES = 1.032e9
 UNIT = "TFLOP/s"
 
 
@@ -445,7 +449,9 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_b,
                      "unit": "TFLOP/s", "frac": round(achieved / peak_b, 4),
                      "peak_kind": f"{peak_kind} bf16 burst", "frac_vs_sustained":
-                         round(achieved / peak_s, 4), "traffic": None,
+                         round(achieved / peak_s, 4),
+                     "traffic": (CFG2_SEQUENCE_TRAFFIC_BYTES
+                                 if (sp is not None and cfg.name == "cfg2") else None),
                      "kernel": "hier_attn_kernel",
                      "algorithmic": "useful FLOPs = 4*H*D*unmasked pairs per launch"},
         "gpu_launches": 2 * args.steps,
