@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(384, 1) prep_qk_kernel(PrepArgs a) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ uint64_t full[kPrepStages];
   __shared__ float red[R][12];
+  __shared__ float rsq[R];
   __shared__ float camv[R][CAM > 0 ? CAM : 1];
   const bool is_k = blockIdx.y == 1;
   const __nv_bfloat16* x = is_k ? a.kx : a.qx;
@@ -197,21 +198,41 @@ __global__ void __launch_bounds__(384, 1) prep_qk_kernel(PrepArgs a) {
         ss[r] = r < nr ? sq : 0.f;
       }
     }
+    // warp sums of the R = 8 rows by a halving exchange: after the offsets
+    // 16, 8, 4 each lane holds one row's partial (row = lane bits 4, 3, 2),
+    // then offsets 2 and 1 finish it (9 shuffles instead of 40)
+    static_assert(R == 8, "the row-sum exchange below assumes 8 rows per chunk");
+    {
+      const int lane = t & 31;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
+      for (int k = 0; k < 3; ++k) {
+        const int o = 16 >> k, keep = (lane & o) ? 1 : 0;
+        const int n = 4 >> k;  // values kept after this step
 #pragma unroll
-      for (int r = 0; r < R; ++r) ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], o);
-    if ((t & 31) == 0) {
-#pragma unroll
-      for (int r = 0; r < R; ++r) red[r][t >> 5] = ss[r];
+        for (int i = 0; i < n; ++i) {
+          const float send = keep ? ss[i] : ss[i + n];
+          const float recv = __shfl_xor_sync(0xffffffffu, send, o);
+          ss[i] = (keep ? ss[i + n] : ss[i]) + recv;
+        }
+      }
+      ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], 2);
+      ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], 1);
+      if ((lane & 3) == 0) {
+        const int row = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+        red[row][t >> 5] = ss[0];
+      }
+    }
+    __syncthreads();
+    if (t < R) {  // row scales once per chunk
+      float tot = 0.f;
+      for (int w = 0; w < nwarps; ++w) tot += red[t][w];
+      rsq[t] = rsqrtf(tot / a.dim + a.eps);
     }
     __syncthreads();
     // pass 2: normalise, rotate, store
     const float4* fr = reinterpret_cast<const float4*>(st + R * row_bytes);
     auto finish = [&](int r) {
-      float tot = 0.f;
-      for (int w = 0; w < nwarps; ++w) tot += red[r][w];
-      const float rs = rsqrtf(tot / a.dim + a.eps);
+      const float rs = rsq[r];
       float xv[8];
       bf16x8_to_f32(*reinterpret_cast<const uint4*>(st + r * row_bytes + d0 * 2), xv);
       if (CAM > 0) {
