@@ -236,10 +236,16 @@ def run_sharded(args, rank, world, local_rank):
         "hub_merge": statistics.mean(marks["c"][i].elapsed_time(ends[i]) for i in range(K)),
     }
     t = torch.tensor([total_ms, parts["attention"]], device=dev)
+    stages = torch.tensor([parts[k] for k in sorted(parts)], device=dev)
+    stages_min = stages.clone()
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(stages, op=dist.ReduceOp.MAX)
+        dist.all_reduce(stages_min, op=dist.ReduceOp.MIN)
         dist.barrier()
     total_ms, attn_max = float(t[0]), float(t[1])
+    stage_range = {k: [round(float(a), 4), round(float(b), 4)]
+                   for k, a, b in zip(sorted(parts), stages_min.tolist(), stages.tolist())}
     ms_per_step = total_ms / K
     value = useful_flops / (ms_per_step * 1e-3) / 1e12
     e2e = None
@@ -268,6 +274,7 @@ def run_sharded(args, rank, world, local_rank):
                    "tile_gflop_per_step_rank0": round(tile_flops / 1e9, 1),
                    "l2": "inputs larger than L2"},
         "breakdown_ms": {k: round(v_, 4) for k, v_ in parts.items()},
+        "breakdown_ms_min_max_over_ranks": stage_range,
         "plan_once_ms": round(plan_ms, 3),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_b,
                      "unit": "TFLOP/s", "frac": round(achieved / peak_b, 4),

@@ -461,10 +461,28 @@ int hier_shard_build(const hier_shard_desc* g, const int32_t* counts, int32_t* q
  * rows rows[off[t] .. off[t+1]) of o (bf16 [.., H*D], row stride o_stride)
  * with log2-sum-exp lse ([..][H]); out[out_rows ? out_rows[t] : t] =
  * sum_i 2^(lse_i - M) o_i / sum_i 2^(lse_i - M) (bf16, M the largest lse_i,
- * 0 without keys).  Across ranks the partial rows are all-gathered first. */
+ * 0 without keys).  Across ranks the partial rows are all-gathered first, or
+ * read in place (hier_lse_gather_merge_peers). */
 int hier_lse_gather_merge(const void* o, int64_t o_stride, const float* lse, int32_t H, int32_t D,
                           const int32_t* off, const int32_t* rows, int64_t n_targets, void* out,
                           int64_t out_stride, const int32_t* out_rows, void* stream);
+
+/* hier_lse_gather_merge over partial rows that stay in the memory of the
+ * rank that computed them: o_bases / lse_bases are device arrays of n_ranks
+ * pointers (this rank's own buffers and the other ranks' buffers mapped into
+ * this GPU's address space, e.g. symmetric memory); partial row pr < local_rows
+ * is read from rank self, a higher row from rank (pr - local_rows) / slot_rows,
+ * at the same row of that rank's buffer.  The caller orders the reads after
+ * every rank's writes (a collective on the stream after the attention).
+ * (Having the attention kernels write each partial row into every rank's
+ * buffer instead was measured slower at 8 GPUs: the NVLink stores slow the
+ * attention launch more than the merge saves.) */
+int hier_lse_gather_merge_peers(const void* const* o_bases, const float* const* lse_bases,
+                                int32_t n_ranks, int32_t self, int64_t local_rows,
+                                int64_t slot_rows, int64_t o_stride, int32_t H, int32_t D,
+                                const int32_t* off, const int32_t* rows, int64_t n_targets,
+                                void* out, int64_t out_stride, const int32_t* out_rows,
+                                void* stream);
 
 /* ---------------------------------------------------------------------------
  * Self-test of the tensor-core operand encodings (no reference counterpart):

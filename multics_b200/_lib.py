@@ -151,6 +151,9 @@ _SIGS = {
                                  _P, _P, _P]),
     "hier_lse_gather_merge": (c_int, [_P, c_int64, _P, c_int32, c_int32, _P, _P, c_int64, _P,
                                       c_int64, _P, _P]),
+    "hier_lse_gather_merge_peers": (c_int, [_P, _P, c_int32, c_int32, c_int64, c_int64, c_int64,
+                                            c_int32, c_int32, _P, _P, c_int64, _P, c_int64, _P,
+                                            _P]),
     "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "hier_selftest_exp2": (c_int, [_P, _P, c_int64, _P]),
 }

@@ -653,8 +653,9 @@ extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_
 // Target row t has partial rows rows[off[t] .. off[t+1]) (bf16 outputs o,
 // each normalised over its own keys, and their log2-sum-exp lse); the merged
 // row is sum_i 2^(lse_i - M) o_i / sum_i 2^(lse_i - M) with M the largest
-// lse_i (0 without any key).  Across ranks the partial rows are gathered to
-// every rank first.
+// lse_i (0 without any key).  Across ranks the partial rows are either
+// gathered to every rank first, or read in place from the owning rank's
+// memory (symmetric buffers mapped over NVLink).
 
 namespace hier {
 namespace {
@@ -679,10 +680,36 @@ __device__ __forceinline__ void bf16x8_store(__nv_bfloat16* p, const float (&f)[
   *reinterpret_cast<uint4*>(p) = v;
 }
 
+// Where partial row pr lives: in one buffer, or (kPeers) in the buffer of
+// its owner: rows below local_rows in this rank's, then one slot of
+// slot_rows rows per rank, read in place from that rank's memory.
+struct PartialSrc {
+  const __nv_bfloat16* o;
+  const float* lse;
+  const __nv_bfloat16* const* o_bases;  // per rank (kPeers)
+  const float* const* lse_bases;
+  int self;
+  int64_t local_rows, slot_rows;
+};
+
+template <bool kPeers>
+__device__ __forceinline__ void partial_at(const PartialSrc& p, int64_t pr,
+                                           const __nv_bfloat16** o, const float** lse) {
+  if (!kPeers) {
+    *o = p.o;
+    *lse = p.lse;
+    return;
+  }
+  const int owner = pr < p.local_rows ? p.self : (int)((pr - p.local_rows) / p.slot_rows);
+  *o = p.o_bases[owner];
+  *lse = p.lse_bases[owner];
+}
+
 // Per (target, head, 8 channels): the normalised weighted sum of the partials.
-__global__ void lse_gather_kernel(const __nv_bfloat16* o, int64_t o_stride, const float* lse,
-                                  int H, int D, const int32_t* off, const int32_t* rows,
-                                  int64_t n_targets, __nv_bfloat16* out, int64_t out_stride,
+template <bool kPeers>
+__global__ void lse_gather_kernel(PartialSrc src, int64_t o_stride, int H, int D,
+                                  const int32_t* off, const int32_t* rows, int64_t n_targets,
+                                  __nv_bfloat16* out, int64_t out_stride,
                                   const int32_t* out_rows) {
   const int per = D / 8;
   const int64_t n = n_targets * H * per;
@@ -694,11 +721,19 @@ __global__ void lse_gather_kernel(const __nv_bfloat16* o, int64_t o_stride, cons
     const int h = (int)(rh % H);
     const int b = off[r], e = off[r + 1];
     float m = -INFINITY;
-    for (int i = b; i < e; ++i) m = fmaxf(m, lse[(int64_t)rows[i] * H + h]);
+    for (int i = b; i < e; ++i) {
+      const __nv_bfloat16* o;
+      const float* lse;
+      partial_at<kPeers>(src, rows[i], &o, &lse);
+      m = fmaxf(m, lse[(int64_t)rows[i] * H + h]);
+    }
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     float ws = 0.f;
     for (int i = b; i < e; ++i) {
       const int64_t pr = rows[i];
+      const __nv_bfloat16* o;
+      const float* lse;
+      partial_at<kPeers>(src, pr, &o, &lse);
       const float l = lse[pr * H + h];
       if (l == -INFINITY || m == -INFINITY) continue;
       const float wt = exp2f(l - m);
@@ -737,9 +772,41 @@ extern "C" int hier_lse_gather_merge(const void* o, int64_t o_stride, const floa
   int rc = merge_check(n_targets, H, D, o_stride);
   if (!rc) rc = merge_check(n_targets, H, D, out_stride);
   if (rc || n_targets == 0) return rc;
-  lse_gather_kernel<<<merge_grid(n_targets * H * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(o), o_stride, lse, H, D, off, rows, n_targets,
-      reinterpret_cast<__nv_bfloat16*>(out), out_stride, out_rows);
+  PartialSrc src{};
+  src.o = reinterpret_cast<const __nv_bfloat16*>(o);
+  src.lse = lse;
+  lse_gather_kernel<false><<<merge_grid(n_targets * H * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
+      src, o_stride, H, D, off, rows, n_targets, reinterpret_cast<__nv_bfloat16*>(out),
+      out_stride, out_rows);
+  HIER_CHECK_CUDA(cudaGetLastError(), "lse_gather_kernel launch");
+  return HIER_OK;
+}
+
+extern "C" int hier_lse_gather_merge_peers(const void* const* o_bases, const float* const* lse_bases,
+                                           int32_t n_ranks, int32_t self, int64_t local_rows,
+                                           int64_t slot_rows, int64_t o_stride, int32_t H,
+                                           int32_t D, const int32_t* off, const int32_t* rows,
+                                           int64_t n_targets, void* out, int64_t out_stride,
+                                           const int32_t* out_rows, void* stream) {
+  clear_error();
+  int rc = merge_check(n_targets, H, D, o_stride);
+  if (!rc) rc = merge_check(n_targets, H, D, out_stride);
+  if (rc || n_targets == 0) return rc;
+  if (!o_bases || !lse_bases || n_ranks <= 0 || self < 0 || self >= n_ranks || local_rows < 0 ||
+      slot_rows <= 0) {
+    set_error(HIER_EVALUE, "invalid peer partial buffers (%d ranks, self %d, slot %lld)", n_ranks,
+              self, (long long)slot_rows);
+    return HIER_EVALUE;
+  }
+  PartialSrc src{};
+  src.o_bases = reinterpret_cast<const __nv_bfloat16* const*>(o_bases);
+  src.lse_bases = lse_bases;
+  src.self = self;
+  src.local_rows = local_rows;
+  src.slot_rows = slot_rows;
+  lse_gather_kernel<true><<<merge_grid(n_targets * H * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
+      src, o_stride, H, D, off, rows, n_targets, reinterpret_cast<__nv_bfloat16*>(out),
+      out_stride, out_rows);
   HIER_CHECK_CUDA(cudaGetLastError(), "lse_gather_kernel launch");
   return HIER_OK;
 }

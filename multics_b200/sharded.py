@@ -329,6 +329,29 @@ class ShardedHierAttention:
             n = (b - a) * t.T * t.L
             self._peers.append((buf[0, :n], buf[1, :n]))
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        # hub partial rows in symmetric memory too: the merge reads the other
+        # ranks' player partials in place
+        shape_o, shape_l = tuple(self.part_o.shape), tuple(self.part_lse.shape)
+        self.part_o = symm.empty(shape_o, dtype=torch.bfloat16, device=self.device)
+        self.part_lse = symm.empty(shape_l, dtype=torch.float32, device=self.device)
+        self.part_o.zero_()
+        self.part_lse.fill_(float("-inf"))
+        h_o = symm.rendezvous(self.part_o, group)
+        h_l = symm.rendezvous(self.part_lse, group)
+        self._part_handles = (h_o, h_l)
+        o_bases, l_bases = [], []
+        self._part_peers = []
+        for r in range(t.world):
+            if r == t.rank:
+                po, pl = self.part_o, self.part_lse
+            else:
+                po = h_o.get_buffer(r, shape_o, torch.bfloat16)
+                pl = h_l.get_buffer(r, shape_l, torch.float32)
+                self._part_peers.append((po, pl))
+            o_bases.append(po.data_ptr())
+            l_bases.append(pl.data_ptr())
+        self._part_o_bases = torch.tensor(o_bases, dtype=torch.int64, device=self.device)
+        self._part_lse_bases = torch.tensor(l_bases, dtype=torch.int64, device=self.device)
 
     def k_buffer(self):
         """Where K of this rank's rows should be written (peer transport)."""
@@ -430,16 +453,29 @@ class ShardedHierAttention:
         return out_hub
 
     def merge(self, out_hub, out_rows=None):
-        """Hub rows: all-gather the ranks' player partials, then one gather
-        kernel merges every hub row's partials by log-sum-exp."""
-        if self.topo.hub_rows == 0:
+        """Hub rows: one gather kernel merges every hub row's partials by
+        log-sum-exp.  With the peer transport it reads the other ranks'
+        player partials in place after a one-element all-reduce (every rank's
+        partials written); otherwise they are all-gathered first."""
+        t = self.topo
+        if t.hub_rows == 0:
+            return out_hub
+        if t.world > 1 and self.transport == "peer":
+            import torch.distributed as dist
+
+            dist.all_reduce(self._flag, group=self.group)
+            check(_lib.lib().hier_lse_gather_merge_peers(
+                ptr(self._part_o_bases), ptr(self._part_lse_bases), t.world, t.rank, t.hub_rows,
+                max(t.hub_partial_slot, 1), self.part_o.stride(0), self.H, self.D,
+                ptr(self.csr_off), ptr(self.csr_rows), t.hub_rows, ptr(out_hub),
+                out_hub.stride(0), ptr(out_rows), stream_ptr(self.device)))
             return out_hub
         self.gather_partials()
         return self.merge_partials(out_hub, out_rows)
 
     def forward(self, q, k, v, out=None, events=None):
         """The layer's attention over this rank's rows: exchange, one
-        attention launch, all-gather of the player partials, hub merge.
+        attention launch, hub merge (:meth:`merge`).
         ``events`` (optional, two CUDA events) are recorded after the
         exchange and after the attention launch.  (Running the hub pairs as a
         first launch with the all-gather overlapping the player strips was
