@@ -280,7 +280,9 @@ def run_sharded(args, rank, world, local_rank):
                      "unit": "TFLOP/s", "frac": round(achieved / peak_b, 4),
                      "peak_kind": f"{peak_kind} bf16 burst", "traffic": None,
                      "kernel": "hier_attn_kernel (rank with the most players)"},
-        "gpu_launches": 4 * K,
+        # per step: prep_qk_kernel, hier_attn_kernel, the hub merge's
+        # lse_gather_kernel (NCCL's and torch's gather kernels not counted)
+        "gpu_launches": 3 * K,
         "device_error": device_error(dev),
     }
     if e2e is not None:
@@ -461,7 +463,9 @@ def run_ours(args, rank, world, local_rank):
                                  if (sp is not None and cfg.name == "cfg2") else None),
                      "kernel": "hier_attn_kernel",
                      "algorithmic": "useful FLOPs = 4*H*D*unmasked pairs per launch"},
-        "gpu_launches": 2 * args.steps,
+        # per step: prep_qk_kernel, hier_attn_kernel (+ the hub merge's
+        # lse_gather_kernel on the sequence plan; torch's V-row gather not counted)
+        "gpu_launches": (3 if sp is not None else 2) * args.steps,
         "device_error": err,
     }
     if e2e is not None:
