@@ -255,7 +255,7 @@ def run_sharded(args, rank, world, local_rank):
     peak_b, peak_s, hbm, peak_kind = load_peaks()
     # kernel roofline: this rank's share of the useful FLOPs over its slowest
     # attention launch (the players split evenly or nearly so)
-    share = topo.n_own / cfg.P
+    share = topo.work_share
     achieved = useful_flops * share / (attn_max * 1e-3) / 1e12
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
@@ -268,7 +268,8 @@ def run_sharded(args, rank, world, local_rank):
                                f"N={cfg.N} groups (regroup every {cfg.regroup_every} frames), "
                                f"K_L={cfg.KL}, K_G={cfg.KG}, H={cfg.H}x{cfg.D}",
                    "S": S, "useful_pairs": pairs, "useful_gflop_per_step": useful_flops / 1e9,
-                   "parallelism": f"players sharded x{world} (ranks own {topo.bounds}); "
+                   "parallelism": f"players sharded x{world} by 256-row strips "
+                                  f"(rank 0: {topo.segments[0]}); "
                                   f"mate frames: {sh.transport}",
                    "remote_units_rank0": len(topo.needs[0]),
                    "tile_gflop_per_step_rank0": round(tile_flops / 1e9, 1),
@@ -279,7 +280,7 @@ def run_sharded(args, rank, world, local_rank):
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_b,
                      "unit": "TFLOP/s", "frac": round(achieved / peak_b, 4),
                      "peak_kind": f"{peak_kind} bf16 burst", "traffic": None,
-                     "kernel": "hier_attn_kernel (rank with the most players)"},
+                     "kernel": "hier_attn_kernel (rank 0 share of the useful work over the slowest rank attention)"},
         # per step: prep_qk_kernel, hier_attn_kernel, the hub merge's
         # lse_gather_kernel (NCCL's and torch's gather kernels not counted)
         "gpu_launches": 3 * K,

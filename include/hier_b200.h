@@ -386,28 +386,34 @@ int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_boxes, const
  * ------------------------------------------------------------------------- */
 
 /* One rank's share of a full-sequence layer (labels mode), or with one
- * shard (p0 = 0, p1 = P, hub_keys = 1) the whole layer.  The rank owns
- * players [p0, p1).  Its query rows:
- *   [0, own_rows)           its players' rows (player, frame, patch);
+ * shard (every player local with all its strips and hub partials, hub_keys
+ * = 1) the whole layer.  The rank holds the rows of n_local players (row
+ * slots in local_player order) and computes the given 256-row strips of
+ * them, so players can be split between ranks by strips when their count
+ * does not divide the ranks.  Its query rows:
+ *   [0, own_rows)           its local players' rows (slot, frame, patch);
  *   [own_rows, V)           every hub row, group-major: local hub (g, f, slot)
  *                           at own_rows + (g*T + f)*K_L + slot, then global hub
  *                           (f, slot) at own_rows + T*N*K_L + f*K_G + slot
  *                           (V = own_rows + hub_rows);
- *   [V + o, V + o + hub_partial_rows) per own player p and frame t the K_L
- *                           rows of the local hub of p's group at t, row
- *                           V + o + ((p - p0)*T + t)*K_L + slot (a second query
+ *   [V + o, V + o + hub_partial_rows) per hub-partial player (k-th slot with
+ *                           hub_partials set) and frame t the K_L rows of the
+ *                           local hub of its group at t, row
+ *                           V + o + (k*T + t)*K_L + slot (a second query
  *                           tensor: hier_partial_out.q2 with q2_row0 = V + o;
  *                           o = hub_partial_row0 places the rank's partials in
- *                           a buffer gathered from every rank).
- * Key/value streams for hier_attn_fwd_streams: 0 = its players' rows, 1 =
+ *                           a buffer shared by the ranks).
+ * Key/value streams for hier_attn_fwd_streams: 0 = its local players' rows, 1 =
  * the hub rows (same order), and for each remote group-mate unit (o, f) (the
  * L rows of player o at frame f) the stream-packed first row
  * remote_key[o*T + f] = (stream << 24) | row (-1 if absent): a buffer of
  * frames fetched before the launch, or the owning rank's buffer mapped from
  * its GPU (read in place over NVLink).
- * Player rows get their full key sets.  A hub row is split into partial rows
- * over disjoint key sets: per member player (third block, on the member's
- * rank) and over the hub tokens (second block, when hub_keys is set); hub
+ * Player rows get their full key sets (a group-mate frame held by no local
+ * slot comes from remote_key).  A hub row is split into partial rows over
+ * disjoint key sets: per member player (third block, on the rank computing
+ * that player's hub partials) and over the hub tokens (second block, when
+ * hub_keys is set); hub
  * pairs are flagged in q_pairs[7] and written as partial rows
  * (hier_partial_out.row0 = own_rows: hub-key partials at [0, hub_rows),
  * player partials at hub_rows + o onwards), then merged with
@@ -418,14 +424,20 @@ int hier_tiled_build(const hier_tiled_grouping* g, const int32_t* n_boxes, const
  * attends to itself only.  The edges are those of the dense mask
  * (multics/models/hier_masks.py:364-507); no reference counterpart exists
  * for the sharding itself: the reference runs every player on one device. */
+#define HIER_SHARD_MAX_LOCAL 16
+
 typedef struct hier_shard_desc {
   int32_t P, N, L, KL, KG, T, n_block, local_attn, direct;
-  int32_t p0, p1;
+  int32_t n_local;          /* players whose rows this rank holds */
   int32_t hub_keys;
   int32_t hub_partial_row0; /* o: first hub-partial row (0 for one shard) */
   const int64_t* labels;      /* [T, P] */
   const uint8_t* active;      /* [T, N] */
   const int32_t* remote_key;  /* [P*T] */
+  int32_t local_player[HIER_SHARD_MAX_LOCAL]; /* absolute player of each local row slot */
+  int32_t strip_begin[HIER_SHARD_MAX_LOCAL];  /* the 256-row strips [begin, end) of the */
+  int32_t strip_end[HIER_SHARD_MAX_LOCAL];    /*   slot's player this rank computes */
+  int32_t hub_partials[HIER_SHARD_MAX_LOCAL]; /* 1: this rank computes the player's hub partials */
 } hier_shard_desc;
 
 typedef struct hier_shard_sizes_t {
@@ -435,7 +447,7 @@ typedef struct hier_shard_sizes_t {
   int32_t reserved;
   int64_t own_rows;         /* the rank's player rows */
   int64_t hub_rows;         /* T*(N*K_L + K_G) */
-  int64_t hub_partial_rows; /* (p1 - p0)*T*K_L */
+  int64_t hub_partial_rows; /* hub-partial players * T*K_L */
 } hier_shard_sizes_t;
 
 int hier_shard_sizes(const hier_shard_desc* g, hier_shard_sizes_t* out);

@@ -32,6 +32,7 @@ class HierGrouping(ctypes.Structure):
 
 
 MAX_KV_STREAMS = 32
+SHARD_MAX_LOCAL = 16
 
 
 class HierCachedGrouping(ctypes.Structure):
@@ -90,8 +91,10 @@ class HierShardDesc(ctypes.Structure):
     _fields_ = [
         ("P", c_int32), ("N", c_int32), ("L", c_int32), ("KL", c_int32), ("KG", c_int32),
         ("T", c_int32), ("n_block", c_int32), ("local_attn", c_int32), ("direct", c_int32),
-        ("p0", c_int32), ("p1", c_int32), ("hub_keys", c_int32), ("hub_partial_row0", c_int32),
+        ("n_local", c_int32), ("hub_keys", c_int32), ("hub_partial_row0", c_int32),
         ("labels", c_void_p), ("active", c_void_p), ("remote_key", c_void_p),
+        ("local_player", c_int32 * SHARD_MAX_LOCAL), ("strip_begin", c_int32 * SHARD_MAX_LOCAL),
+        ("strip_end", c_int32 * SHARD_MAX_LOCAL), ("hub_partials", c_int32 * SHARD_MAX_LOCAL),
     ]
 
 

@@ -1,15 +1,19 @@
-// Attention plan of one player shard (a rank that owns players [p0, p1)),
-// and, with a single shard, of the whole full-sequence layer.
+// Attention plan of one shard (a rank holding the rows of some players and
+// computing some 256-row strips of them), and, with a single shard, of the
+// whole full-sequence layer.
 //
 // Query rows of the shard (a row space over two query tensors):
-//   [0, own_rows)               its players' rows (player, frame, patch);
+//   [0, own_rows)               the rows of its local players, in slot order
+//                               (slot, frame, patch);
 //   [own_rows, V)               every hub row, group-major: local hub (g, f, slot)
 //                               at own_rows + (g*T + f)*K_L + slot, then global
 //                               hub (f, slot) at own_rows + T*N*K_L + f*K_G + slot;
-//   [V + o, V + o + n_own*T*K_L) per own player p and frame t the K_L local-hub
-//                               rows of p's group at t (second query tensor;
-//                               V = own_rows + hub_rows, o = hub_partial_row0,
-//                               the shard's slot in an all-gathered buffer).
+//   [V + o, V + o + n_hp*T*K_L) per hub-partial player p (those the shard
+//                               computes hub partials for) and frame t the K_L
+//                               local-hub rows of p's group at t (second query
+//                               tensor; V = own_rows + hub_rows, o =
+//                               hub_partial_row0, the shard's slot in a buffer
+//                               shared by the ranks).
 // Key/value streams: 0 = the shard's player rows, 1 = the hub rows (same
 // order as above), and for a remote group-mate unit (o, f) the
 // stream-packed first row remote_key[o*T + f].
@@ -22,7 +26,7 @@
 // groups change from frame to frame.
 //
 // Query pairs are two consecutive 128-row tiles of one query block:
-//   * a player's T*L rows, cut into 256-row strips;
+//   * the shard's strips of a local player's T*L rows (256 rows each);
 //   * a player's T*K_L hub-partial rows, cut into 256-row strips;
 //   * one group's T*K_L local-hub rows, or the T*K_G global-hub rows (hub
 //     keys only; on the hub_keys rank).
@@ -71,10 +75,16 @@ constexpr int kSelSkip = -2;
 
 struct SDims {
   int P, T, L, N, KL, KG, nb, win, direct;
-  int p0, p1, n_own, hub_keys;
+  int n_local, hub_keys;
+  int player[HIER_SHARD_MAX_LOCAL];     // local player slot -> absolute player
+  int strip0[HIER_SHARD_MAX_LOCAL];     // this shard's strips of that player
+  int strip_pre[HIER_SHARD_MAX_LOCAL + 1];  // exclusive prefix of the strip counts
+  int hp_slot[HIER_SHARD_MAX_LOCAL];    // index among the hub-partial players, or -1
+  int hp_player[HIER_SHARD_MAX_LOCAL];  // hub-partial player k -> local slot
+  int n_hp_players, n_strips;
   int hp_row0;         // offset of this shard's hub-partial rows in the partial-row space
-  int nps;             // player strips per player
-  int nph;             // hub-partial strips per player
+  int nps;             // 256-row strips of one player's rows
+  int nph;             // hub-partial strips per hub-partial player
   int npl, npg;        // hub-key pairs per group, global hub-key pairs (hub_keys rank)
   int n_hh;            // hub-key pairs
   int n_pairs;         // all pairs: player strips, hub-partial strips, hub-key pairs
@@ -114,21 +124,24 @@ struct Pair {
 __device__ Pair pair_of(const SDims& d, int i) {
   Pair r;
   int rows;
-  const int n_hp = d.n_own * d.nph;
-  if (i < d.n_own * d.nps) {
+  const int n_hp = d.n_hp_players * d.nph;
+  if (i < d.n_strips) {
+    int slot = 0;
+    while (slot + 1 < d.n_local && d.strip_pre[slot + 1] <= i) ++slot;
     r.kind = kPairPlayer;
-    r.id = d.p0 + i / d.nps;
-    r.j0 = kStripRows * (i % d.nps);
+    r.id = d.player[slot];
+    r.j0 = kStripRows * (d.strip0[slot] + i - d.strip_pre[slot]);
     rows = d.T * d.L;
     r.unit = d.L;
-    r.q0 = (r.id - d.p0) * rows + r.j0;
-  } else if ((i -= d.n_own * d.nps) < n_hp) {
+    r.q0 = slot * rows + r.j0;
+  } else if ((i -= d.n_strips) < n_hp) {
+    const int k = i / d.nph;
     r.kind = kPairHubOfPlayer;
-    r.id = d.p0 + i / d.nph;
+    r.id = d.player[d.hp_player[k]];
     r.j0 = kStripRows * (i % d.nph);
     rows = d.T * d.KL;
     r.unit = d.KL;
-    r.q0 = d.own_rows + d.hub_rows + d.hp_row0 + (r.id - d.p0) * rows + r.j0;
+    r.q0 = d.own_rows + d.hub_rows + d.hp_row0 + k * rows + r.j0;
   } else if ((i -= n_hp) < d.N * d.npl) {
     const int h = i;
     r.kind = kPairLocal;
@@ -188,6 +201,13 @@ __device__ bool edge(const hier_shard_desc& g, const SDims& d, int qkind, int qi
   return temporal(d, t, f);
 }
 
+// Local row slot of player o (-1: not held by this shard).
+__device__ __forceinline__ int local_slot(const SDims& d, int o) {
+  for (int i = 0; i < d.n_local; ++i)
+    if (d.player[i] == o) return i;
+  return -1;
+}
+
 // Candidate c of a pair: unit code, stream-packed first key row and width
 // (0 for an unused slot).  *remote marks a remote mate frame, whose key is
 // remote_key[o*T + f] (-1 when the shard has no slot for it).
@@ -196,7 +216,7 @@ __device__ void candidate(const hier_shard_desc& g, const SDims& d, const Pair& 
   *remote = false;
   const int s1 = 1 << segplan::kStreamShift;
   auto player_key = [&](int o, int f) {
-    return (o - d.p0) * d.T * d.L + f * d.L;
+    return local_slot(d, o) * d.T * d.L + f * d.L;
   };
   if (pr.kind == kPairHubOfPlayer) {  // the player's frames
     *code = unit_code(kUnitPlayer, pr.id, c);
@@ -224,7 +244,7 @@ __device__ void candidate(const hier_shard_desc& g, const SDims& d, const Pair& 
       }
       *code = unit_code(kUnitPlayer, o, f);
       *width = d.L;
-      if (o >= d.p0 && o < d.p1) {
+      if (local_slot(d, o) >= 0) {
         *key = player_key(o, f);
       } else {
         *key = g.remote_key[o * d.T + f];
@@ -487,21 +507,50 @@ int make_sdims(const hier_shard_desc* g, SDims* d) {
     set_error(HIER_EVALUE, "shard plan supports at most 4095 players, groups and frames");
     return HIER_EVALUE;
   }
-  if (g->p0 < 0 || g->p1 > g->P || g->p0 >= g->p1) {
-    set_error(HIER_EVALUE, "invalid player shard [%d, %d) of %d players", g->p0, g->p1, g->P);
+  if (g->n_local <= 0 || g->n_local > HIER_SHARD_MAX_LOCAL) {
+    set_error(HIER_EVALUE, "a shard holds 1..%d players; got %d", HIER_SHARD_MAX_LOCAL,
+              g->n_local);
     return HIER_EVALUE;
   }
   if (d->direct && !g->remote_key) {
     set_error(HIER_EVALUE, "direct player edges need the remote unit table");
     return HIER_EVALUE;
   }
-  d->p0 = g->p0, d->p1 = g->p1, d->n_own = g->p1 - g->p0, d->hub_keys = g->hub_keys != 0;
+  d->n_local = g->n_local, d->hub_keys = g->hub_keys != 0;
+  const int nps_all = (int)(((int64_t)d->T * d->L + kStripRows - 1) / kStripRows);
+  d->strip_pre[0] = 0;
+  for (int i = 0; i < d->n_local; ++i) {
+    const int o = g->local_player[i];
+    if (o < 0 || o >= d->P) {
+      set_error(HIER_EVALUE, "local player %d out of range [0, %d)", o, d->P);
+      return HIER_EVALUE;
+    }
+    for (int j = 0; j < i; ++j)
+      if (g->local_player[j] == o) {
+        set_error(HIER_EVALUE, "player %d listed twice in a shard", o);
+        return HIER_EVALUE;
+      }
+    const int b = g->strip_begin[i], e = g->strip_end[i];
+    if (b < 0 || e < b || e > nps_all) {
+      set_error(HIER_EVALUE, "strips [%d, %d) of player %d outside [0, %d)", b, e, o, nps_all);
+      return HIER_EVALUE;
+    }
+    d->player[i] = o;
+    d->strip0[i] = b;
+    d->strip_pre[i + 1] = d->strip_pre[i] + (e - b);
+    d->hp_slot[i] = -1;
+    if (g->hub_partials[i]) {
+      d->hp_slot[i] = d->n_hp_players;
+      d->hp_player[d->n_hp_players++] = i;
+    }
+  }
+  d->n_strips = d->strip_pre[d->n_local];
   if (g->hub_partial_row0 < 0) {
     set_error(HIER_EVALUE, "negative hub-partial row offset %d", g->hub_partial_row0);
     return HIER_EVALUE;
   }
   d->hp_row0 = g->hub_partial_row0;
-  const int64_t own_rows = (int64_t)d->n_own * d->T * d->L;
+  const int64_t own_rows = (int64_t)d->n_local * d->T * d->L;
   const int64_t hub_rows = (int64_t)d->T * (d->N * d->KL + d->KG);
   if (own_rows >= (1 << segplan::kStreamShift) || hub_rows >= (1 << segplan::kStreamShift)) {
     set_error(HIER_EVALUE, "shard of %lld player rows / %lld hub rows exceeds %d",
@@ -516,8 +565,8 @@ int make_sdims(const hier_shard_desc* g, SDims* d) {
   d->npl = d->KL > 0 ? cdiv((int64_t)d->T * d->KL, kStripRows) : 0;
   d->npg = d->KG > 0 ? cdiv((int64_t)d->T * d->KG, kStripRows) : 0;
   d->n_hh = d->hub_keys ? d->N * d->npl + d->npg : 0;
-  d->n_pairs = d->n_own * (d->nps + d->nph) + d->n_hh;
-  if ((int64_t)own_rows + hub_rows + d->hp_row0 + (int64_t)d->n_own * d->T * d->KL >
+  d->n_pairs = d->n_strips + d->n_hp_players * d->nph + d->n_hh;
+  if ((int64_t)own_rows + hub_rows + d->hp_row0 + (int64_t)d->n_hp_players * d->T * d->KL >
       INT_MAX / 2) {
     set_error(HIER_EVALUE, "shard query rows exceed the row range");
     return HIER_EVALUE;
@@ -564,11 +613,11 @@ extern "C" int hier_shard_sizes(const hier_shard_desc* g, hier_shard_sizes_t* ou
   if (rc) return rc;
   memset(out, 0, sizeof(*out));
   out->n_pairs = d.n_pairs;
-  out->n_player_pairs = d.n_own * d.nps;
+  out->n_player_pairs = d.n_strips;
   out->n_counts = 2 * d.n_pairs;
   out->own_rows = d.own_rows;
   out->hub_rows = d.hub_rows;
-  out->hub_partial_rows = (int64_t)d.n_own * d.T * d.KL;
+  out->hub_partial_rows = (int64_t)d.n_hp_players * d.T * d.KL;
   return HIER_OK;
 }
 
@@ -610,7 +659,7 @@ extern "C" int hier_shard_build(const hier_shard_desc* g, const int32_t* counts,
       *g, d, counts, q_pairs, kv_tiles, tile_capacity, tile_masks, mask_capacity, status);
   HIER_CHECK_CUDA(cudaGetLastError(), "pair_build_kernel launch");
   if (order) {  // player strips, then hub pairs, each by descending work
-    const int ns = d.n_own * d.nps, nh = d.n_pairs - ns;
+    const int ns = d.n_strips, nh = d.n_pairs - ns;
     if (ns > 0) order_by_work_kernel<8><<<(ns + 127) / 128, 128, 0, s>>>(q_pairs, ns, order);
     if (nh > 0)
       order_by_work_kernel<8><<<(nh + 127) / 128, 128, 0, s>>>(q_pairs + (int64_t)ns * 8, nh,

@@ -37,6 +37,9 @@ from ._lib import HierPartialOut, HierShardDesc, HierShardSizes, check, ptr, str
 __all__ = ["split_players", "ShardTopology", "ShardedHierAttention", "exchange_mate_frames"]
 
 
+STRIP_ROWS = 256  # query rows of one attention work item (two 128-row tiles)
+
+
 def split_players(P: int, world: int) -> List[Tuple[int, int]]:
     """Contiguous player ranges per rank, the first ``P % world`` ranks one larger."""
     if world < 1 or world > P:
@@ -50,14 +53,48 @@ def split_players(P: int, world: int) -> List[Tuple[int, int]]:
     return out
 
 
+def split_strips(P: int, T: int, L: int, world: int) -> List[List[Tuple[int, int, int]]]:
+    """Balanced split of every player's 256-row strips over the ranks: the
+    strips of players 0..P-1 in order, each weighted by its last frame + 2
+    (its key count grows with the history it attends to), cut into ``world``
+    contiguous runs of equal weight.  Returns per rank ``(player, first
+    strip, end strip)`` segments; whole players per rank when ``world``
+    divides ``P``."""
+    if world < 1 or world > P:
+        raise ValueError(f"cannot shard {P} players over {world} ranks")
+    nps = -(-T * L // STRIP_ROWS)
+    w = np.array([(min((s + 1) * STRIP_ROWS, T * L) - 1) // L + 2 for s in range(nps)],
+                 dtype=np.float64)
+    weights = np.tile(w, P)
+    cum = np.concatenate([[0.0], np.cumsum(weights)])
+    total = cum[-1]
+    cuts = [0] + [int(np.argmin(np.abs(cum - total * r / world))) for r in range(1, world)] + \
+        [P * nps]
+    out = []
+    for r in range(world):
+        segs = []
+        i0, i1 = cuts[r], cuts[r + 1]
+        for p in range(P):
+            b, e = max(i0, p * nps), min(i1, (p + 1) * nps)
+            if b < e:
+                segs.append((p, b - p * nps, e - p * nps))
+        out.append(segs)
+    return out
+
+
 class ShardTopology:
     """Host-side description of one sharded layer (identical on every rank).
 
-    ``labels``: int64 ``[T, P]`` group labels (constant inside each block of
-    ``n_block`` frames).  ``needs[r]`` lists the remote units ``(o, f)`` (L rows
-    of player ``o`` at frame ``f``) rank ``r`` attends to through direct
-    edges, ordered by (owner rank, player, frame): the order of its remote
-    buffer and of the ``all_to_all`` receive splits."""
+    ``labels``: int64 ``[T, P]`` group labels.  Work is split by 256-row
+    strips (:func:`split_strips`): rank ``r`` computes ``segments[r]`` and
+    holds the rows of every player it computes strips of (its *local*
+    players, in increasing order).  Each player's *home* is the rank holding
+    its last strip: it computes the player's hub partial rows and serves its
+    frames to ranks that need them as group-mate keys.  ``needs[r]`` lists
+    the units ``(o, f)`` (L rows of player ``o`` at frame ``f``) rank ``r``
+    reads from another rank through direct edges, ordered by (home rank,
+    player, frame): the order of its remote buffer and of the ``all_to_all``
+    receive splits."""
 
     def __init__(self, *, P, T, L, N, KL, KG, n_block, local_attn, direct, labels, world, rank):
         self.P, self.T, self.L, self.N, self.KL, self.KG = P, T, L, N, KL, KG
@@ -65,33 +102,45 @@ class ShardTopology:
         self.world, self.rank = world, rank
         lab = np.asarray(labels, dtype=np.int64).reshape(T, P)
         self.labels = lab
-        self.bounds = split_players(P, world)
-        self.owner = np.zeros(P, dtype=np.int64)
-        for r, (a, b) in enumerate(self.bounds):
-            self.owner[a:b] = r
-        self.p0, self.p1 = self.bounds[rank]
-        self.n_own = self.p1 - self.p0
+        self.nps = -(-T * L // STRIP_ROWS)
+        self.segments = split_strips(P, T, L, world)
+        self.local = [[p for p, _, _ in segs] for segs in self.segments]
+        self.home = np.zeros(P, dtype=np.int64)
+        for r, segs in enumerate(self.segments):
+            for p, _, e in segs:
+                if e == self.nps:
+                    self.home[p] = r
+        self.hp_players = [[p for p in self.local[r] if self.home[p] == r] for r in range(world)]
+        self.local_players = self.local[rank]
+        self.n_local = len(self.local_players)
+        if self.n_local > _lib.SHARD_MAX_LOCAL:
+            raise ValueError(f"a rank would hold {self.n_local} players; at most "
+                             f"{_lib.SHARD_MAX_LOCAL}")
         self.hub_rows = T * (N * KL + KG)
-        self.own_rows = self.n_own * T * L
+        self.own_rows = self.n_local * T * L
+        w = self._strip_weights()
+        self.work_share = sum(w[b:e].sum() for _, b, e in self.segments[rank]) / (P * w.sum())
         self.needs = [self._needs(r) for r in range(world)]
         mine = self.needs[rank]
-        self.remote_slot = np.full(P * T, -1, dtype=np.int32)
-        for i, (o, f) in enumerate(mine):
-            self.remote_slot[o * T + f] = i
-        self.recv_units = [sum(1 for o, _ in mine if self.owner[o] == i) for i in range(world)]
-        self.send_units = [[u for u in self.needs[j] if self.owner[u[0]] == rank]
+        self.recv_units = [sum(1 for o, _ in mine if self.home[o] == i) for i in range(world)]
+        self.send_units = [[u for u in self.needs[j] if self.home[u[0]] == rank]
                            for j in range(world)]
         rows = []
         for j in range(world):
             for o, f in self.send_units[j]:
-                start = (o - self.p0) * T * L + f * L
+                start = self.local_players.index(o) * T * L + f * L
                 rows.append(np.arange(start, start + L))
         self.send_rows = (np.concatenate(rows) if rows else np.zeros(0, np.int64)).astype(np.int64)
+
+    def _strip_weights(self):
+        T, L = self.T, self.L
+        return np.array([(min((s + 1) * STRIP_ROWS, T * L) - 1) // L + 2 for s in range(self.nps)],
+                        dtype=np.float64)
 
     def remote_keys(self, transport: str) -> np.ndarray:
         """int32 ``[P*T]``: stream-packed first row of every remote unit this
         rank reads (-1 elsewhere).  ``"exchange"``: slot ``i`` of the received
-        buffer (stream 2); ``"peer"``: the owning rank's own rows, stream
+        buffer (stream 2); ``"peer"``: the home rank's own rows, stream
         ``2 + j`` for the ``j``-th other rank."""
         keys = np.full(self.P * self.T, -1, dtype=np.int64)
         others = [r for r in range(self.world) if r != self.rank]
@@ -99,29 +148,37 @@ class ShardTopology:
             if transport == "exchange":
                 keys[o * self.T + f] = (2 << 24) | (i * self.L)
             else:
-                owner = int(self.owner[o])
-                p0 = self.bounds[owner][0]
-                keys[o * self.T + f] = ((2 + others.index(owner)) << 24) | \
-                    ((o - p0) * self.T * self.L + f * self.L)
+                h = int(self.home[o])
+                slot = self.local[h].index(o)
+                keys[o * self.T + f] = ((2 + others.index(h)) << 24) | \
+                    (slot * self.T * self.L + f * self.L)
         return keys.astype(np.int32)
 
     def _needs(self, r):
-        a, b = self.bounds[r]
         if not self.direct:
             return []
-        n, T = self.n_block, self.T
+        n, T, L = self.n_block, self.T, self.L
+        local = set(self.local[r])
         units = set()
-        for p in range(a, b):
-            for qf in range(T):
+        for p, b, e in self.segments[r]:
+            f_lo, f_hi = (b * STRIP_ROWS) // L, (min(e * STRIP_ROWS, T * L) - 1) // L
+            for qf in range(f_lo, f_hi + 1):
                 bs = (qf // n) * n
                 for o in range(self.P):
-                    if o == p or self.labels[qf, o] != self.labels[qf, p]:
-                        continue
-                    if a <= o < b:
+                    if o == p or o in local or self.labels[qf, o] != self.labels[qf, p]:
                         continue
                     for kf in range(bs, min(bs + n, T)):
                         units.add((o, kf))
-        return sorted(units, key=lambda u: (self.owner[u[0]], u[0], u[1]))
+        return sorted(units, key=lambda u: (self.home[u[0]], u[0], u[1]))
+
+    def computed_rows(self) -> np.ndarray:
+        """Local rows (player slots) this rank computes: its strips' rows."""
+        T, L = self.T, self.L
+        rows = []
+        for p, b, e in self.segments[self.rank]:
+            slot = self.local_players.index(p)
+            rows.append(slot * T * L + np.arange(b * STRIP_ROWS, min(e * STRIP_ROWS, T * L)))
+        return np.concatenate(rows).astype(np.int64)
 
     def hub_rows_order(self) -> np.ndarray:
         """Sequence rows of the hub rows in the shard's order: local hubs
@@ -136,26 +193,30 @@ class ShardTopology:
         return np.concatenate([local, glob]).astype(np.int64)
 
     def local_rows(self) -> np.ndarray:
-        """Sequence rows of this rank's query rows: its players' rows, then
-        every hub row in :meth:`hub_rows_order`."""
-        own = np.arange(self.p0 * self.T * self.L, self.p1 * self.T * self.L)
-        return np.concatenate([own, self.hub_rows_order()])
+        """Sequence rows of this rank's query rows: its local players' rows
+        (slot order), then every hub row in :meth:`hub_rows_order`."""
+        TL = self.T * self.L
+        own = [np.arange(p * TL, (p + 1) * TL) for p in self.local_players]
+        return np.concatenate(own + [self.hub_rows_order()]).astype(np.int64)
 
-    def hub_partial_src(self) -> np.ndarray:
-        """Hub row (in :meth:`hub_rows_order`) of each of this rank's
-        player-partial rows: own player ``p``, frame ``t``, slot ``s`` -> the
-        local hub of ``p``'s group at ``t``."""
+    def hub_partial_src(self, r=None) -> np.ndarray:
+        """Hub row (in :meth:`hub_rows_order`) of each player-partial row of
+        rank ``r`` (default this rank): hub-partial player ``p`` (k-th),
+        frame ``t``, slot ``s`` -> the local hub of ``p``'s group at ``t``."""
         T, KL = self.T, self.KL
-        p_i, t_i, s_i = np.meshgrid(np.arange(self.p0, self.p1), np.arange(T), np.arange(KL),
+        players = self.hp_players[self.rank if r is None else r]
+        if not players:
+            return np.zeros(0, np.int64)
+        p_i, t_i, s_i = np.meshgrid(np.array(players), np.arange(T), np.arange(KL),
                                     indexing="ij")
         g = self.labels[t_i, p_i]
         return ((g * T + t_i) * KL + s_i).reshape(-1).astype(np.int64)
 
     @property
     def hub_partial_slot(self) -> int:
-        """Rows of one rank's player-partial block in the gathered buffer (the
-        largest rank's ``n_own*T*K_L``)."""
-        return max(b - a for a, b in self.bounds) * self.T * self.KL
+        """Rows of one rank's player-partial block in the shared partial-row
+        buffer (the largest rank's hub-partial players x ``T*K_L``)."""
+        return max(len(x) for x in self.hp_players) * self.T * self.KL
 
     def hub_partials(self):
         """CSR of the partial rows of every hub row, in the partial-row buffer
@@ -166,11 +227,11 @@ class ShardTopology:
         T, KL = self.T, self.KL
         lists = [[r] for r in range(self.hub_rows)]
         slot = self.hub_partial_slot
-        for r, (a, b) in enumerate(self.bounds):
-            for p in range(a, b):
+        for r in range(self.world):
+            for k, p in enumerate(self.hp_players[r]):
                 for t in range(T):
                     g = int(self.labels[t, p])
-                    base = self.hub_rows + r * slot + ((p - a) * T + t) * KL
+                    base = self.hub_rows + r * slot + (k * T + t) * KL
                     for s in range(KL):
                         lists[(g * T + t) * KL + s].append(base + s)
         off = np.zeros(self.hub_rows + 1, dtype=np.int32)
@@ -210,10 +271,12 @@ def exchange_mate_frames(topo: ShardTopology, k, v, remote, group=None, send_row
 class ShardedHierAttention:
     """One rank's sharded attention layer (inputs already projected and roped).
 
-    ``forward(q, k, v)`` takes this rank's rows in local order (its players'
-    ``n_own*T*L`` rows then all ``T*(N*K_L+K_G)`` hub rows), bf16
-    ``[rows, H*128]``, and returns the attention output for the same rows;
-    hub rows are identical on every rank after the merge.
+    ``forward(q, k, v)`` takes this rank's rows in local order (its local
+    players' ``T*L`` rows each, then all ``T*(N*K_L+K_G)`` hub rows), bf16
+    ``[rows, H*128]``, and returns the attention output for the same rows:
+    the rows of its strips (``topo.computed_rows()``) and every hub row,
+    identical on every rank after the merge; a local player's rows computed
+    by another rank are left as they were in ``out``.
 
     ``transport`` selects how group-mate frames on other ranks are read:
     ``"exchange"`` fetches them with ``all_to_all`` before the launch;
@@ -253,8 +316,12 @@ class ShardedHierAttention:
         d.n_block, d.local_attn, d.direct = t.n_block, t.local_attn, int(t.direct)
         # every rank computes the hub-token partials (a few key tiles per hub
         # row), so only the per-player hub partials cross GPUs
-        d.p0, d.p1, d.hub_keys = t.p0, t.p1, 1
+        d.n_local, d.hub_keys = t.n_local, 1
         d.hub_partial_row0 = t.rank * t.hub_partial_slot
+        for i, p in enumerate(t.local_players):
+            b, e = next(((b_, e_) for p_, b_, e_ in t.segments[t.rank] if p_ == p), (0, 0))
+            d.local_player[i], d.strip_begin[i], d.strip_end[i] = p, b, e
+            d.hub_partials[i] = int(t.home[p] == t.rank)
         d.labels, d.active, d.remote_key = (self._labels.data_ptr(), self._active.data_ptr(),
                                             self._keys.data_ptr())
         self.desc = d
@@ -316,7 +383,7 @@ class ShardedHierAttention:
                 symm.enable_symm_mem_for_group(group.group_name)
             except Exception:  # already enabled / not needed in this torch version
                 pass
-        rows = max(b - a for a, b in t.bounds) * t.T * t.L + t.hub_rows
+        rows = max(len(x) for x in t.local) * t.T * t.L + t.hub_rows
         self._sym_rows = rows
         self._sym = symm.empty((2, rows, self.dim), dtype=torch.bfloat16, device=self.device)
         self._sym.zero_()
@@ -325,8 +392,7 @@ class ShardedHierAttention:
             if r == t.rank:
                 continue
             buf = self._handle.get_buffer(r, (2, rows, self.dim), torch.bfloat16)
-            a, b = t.bounds[r]
-            n = (b - a) * t.T * t.L
+            n = len(t.local[r]) * t.T * t.L
             self._peers.append((buf[0, :n], buf[1, :n]))
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
         # hub partial rows in symmetric memory too: the merge reads the other

@@ -50,7 +50,8 @@ def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v, n_block=1, win=-
         o = torch.empty_like(ql)
         sh.attend(ql, kl, vl, o)
         sh.check_status()
-        out[t.p0 * T * L:t.p1 * T * L] = o[:t.own_rows].float()
+        mine = torch.from_numpy(t.computed_rows()).cuda()
+        out[loc[mine]] = o[mine].float()
         shards.append(sh)
     # the all-gather: every rank's player-partial slot into rank 0's buffer
     s0 = shards[0]
@@ -83,9 +84,10 @@ def test_sharded_dynamic_groups_match_oracle(world):
     _check(_run_sharded(P, T, L, N, KL, KG, lab, H, world, q, k, v), ref)
 
 
-@pytest.mark.parametrize("world", [3, 8])
+@pytest.mark.parametrize("world", [3, 4, 8])
 def test_sharded_uneven_players_match_oracle(world):
-    """Config-5 grouping in miniature: 10 players in groups (3,3,2,2)."""
+    """Config-5 grouping in miniature: 10 players in groups (3,3,2,2), split
+    between the ranks by 256-row strips (players shared by two ranks)."""
     P, T, L, N, KL, KG, H = 10, 4, 24, 4, 3, 2, 2
     lab = np.array([[0, 0, 0, 1, 1, 1, 2, 2, 3, 3]] * T)
     q, k, v, ref = _case(P, T, L, N, KL, KG, lab, H, seed=2)
@@ -111,3 +113,13 @@ def test_sharded_blocks_and_window_match_oracle(world):
     lab = _regrouped_labels(P, T, 3, seed=5)
     q, k, v, ref = _case(P, T, L, N, KL, KG, lab, H, seed=5, n_block=3, win=3)
     _check(_run_sharded(P, T, L, N, KL, KG, lab, H, world, q, k, v, n_block=3, win=3), ref)
+
+
+@pytest.mark.parametrize("world", [3, 5])
+def test_sharded_strip_split_dynamic_groups_match_oracle(world):
+    """Players split between ranks by strips while groups change every 3
+    frames: mate frames come from the players' home ranks."""
+    P, T, L, N, KL, KG, H = 8, 6, 100, 4, 4, 3, 2
+    lab = _regrouped_labels(P, T, 3, seed=9)
+    q, k, v, ref = _case(P, T, L, N, KL, KG, lab, H, seed=9)
+    _check(_run_sharded(P, T, L, N, KL, KG, lab, H, world, q, k, v), ref)

@@ -44,18 +44,20 @@ def test_remote_units_match_dense_mask(world, n_block):
     for rank in range(world):
         t = ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=n_block, local_attn=-1,
                           direct=True, labels=lab, world=world, rank=rank)
-        rows = np.arange(t.p0 * T * L, t.p1 * T * L)
+        rows = np.concatenate([p * T * L + np.arange(b * 256, min(e * 256, T * L))
+                               for p, b, e in t.segments[rank]])
         cols = np.nonzero(dense[rows].any(0))[0]
         want = set()
         for c in cols:
             if c < P * T * L:
                 o, f = c // (T * L), (c % (T * L)) // L
-                if not (t.p0 <= o < t.p1):
+                if o not in t.local_players:
                     want.add((o, f))
         assert set(t.needs[rank]) == want
-        # every slot of the remote table points at its own unit
+        # every entry of the exchange table points at its own slot
+        keys = t.remote_keys("exchange")
         for i, (o, f) in enumerate(t.needs[rank]):
-            assert t.remote_slot[o * T + f] == i
+            assert keys[o * T + f] == (2 << 24) | (i * L)
 
 
 def test_static_groups_on_one_rank_exchange_nothing():
@@ -97,20 +99,23 @@ def _exchange_rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_exchange_with_two_gloo_ranks():
+@pytest.mark.parametrize("world", [2, 3])
+def test_exchange_with_gloo_ranks(world):
+    """All-to-all of the mate frames with whole players per rank (2 ranks)
+    and with players split between ranks by strips (3 ranks)."""
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
-    port = 29600 + os.getpid() % 200
-    procs = [ctx.Process(target=_exchange_rank, args=(r, 2, port, q)) for r in range(2)]
+    port = 29600 + os.getpid() % 200 + world
+    procs = [ctx.Process(target=_exchange_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(120)
-    res = sorted(q.get() for _ in range(2))
+    res = sorted(q.get() for _ in range(world))
     assert all(p.exitcode == 0 for p in procs)
-    assert [r[1] for r in res] == [True, True]
+    assert all(r[1] for r in res)
     assert all(r[2] > 0 for r in res)  # dynamic groups do cross ranks
 
 
@@ -131,6 +136,33 @@ def test_local_rows_hubs_group_major():
     expect = [f_major(f, g, s) for g in range(N) for f in range(T) for s in range(KL)]
     expect += list(range(T * N * KL, T * (N * KL + KG)))
     assert list(hub) == expect
+
+
+@pytest.mark.parametrize("P,T,L,world", [(8, 6, 3, 2), (8, 42, 220, 8), (10, 42, 220, 8),
+                                         (10, 42, 220, 4), (5, 6, 40, 3), (4, 3, 16, 1)])
+def test_split_strips_covers_and_balances(P, T, L, world):
+    """Every strip of every player on exactly one rank, contiguous runs per
+    rank, whole players when the ranks divide the players, work within one
+    strip of equal."""
+    from multics_b200.sharded import split_strips
+
+    nps = -(-T * L // 256)
+    segs = split_strips(P, T, L, world)
+    seen = np.zeros((P, nps), np.int64)
+    w = np.array([(min((s + 1) * 256, T * L) - 1) // L + 2 for s in range(nps)], np.float64)
+    loads = []
+    for r in range(world):
+        load = 0.0
+        for p, b, e in segs[r]:
+            seen[p, b:e] += 1
+            load += w[b:e].sum()
+        loads.append(load)
+    assert (seen == 1).all()
+    if P % world == 0:
+        per = P // world
+        assert all([p for p, _, _ in segs[r]] == list(range(r * per, (r + 1) * per))
+                   and all(b == 0 and e == nps for _, b, e in segs[r]) for r in range(world))
+    assert max(loads) - min(loads) <= 2 * w.max() + 1e-9
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 8])
@@ -160,6 +192,6 @@ def test_hub_partials_cover_each_hub_row_once_per_key_set(world):
                 rk, i = divmod(x - t.hub_rows, slot)
                 tr = tops[rk]
                 src = tr.hub_partial_src()
-                assert src[i] == r and tr.p0 + i // (T * KL) in members
+                assert src[i] == r and tr.hp_players[rk][i // (T * KL)] in members
         else:
             assert players == []
