@@ -53,19 +53,32 @@ def split_players(P: int, world: int) -> List[Tuple[int, int]]:
     return out
 
 
-def split_strips(P: int, T: int, L: int, world: int) -> List[List[Tuple[int, int, int]]]:
-    """Balanced split of every player's 256-row strips over the ranks: the
-    strips of players 0..P-1 in order, each weighted by its last frame + 2
-    (its key count grows with the history it attends to), cut into ``world``
-    contiguous runs of equal weight.  Returns per rank ``(player, first
-    strip, end strip)`` segments; whole players per rank when ``world``
-    divides ``P``."""
-    if world < 1 or world > P:
-        raise ValueError(f"cannot shard {P} players over {world} ranks")
+def strip_weights(T: int, L: int, KL: int = 0) -> np.ndarray:
+    """Work weight of each of a player's 256-row strips: its last frame + 2
+    (its key count grows with the history it attends to).  With ``K_L`` the
+    player's hub-partial strips (its group's hub rows of every frame, over
+    the same history) are added to its last strip, which decides the rank
+    that computes them."""
     nps = -(-T * L // STRIP_ROWS)
     w = np.array([(min((s + 1) * STRIP_ROWS, T * L) - 1) // L + 2 for s in range(nps)],
                  dtype=np.float64)
-    weights = np.tile(w, P)
+    if KL > 0:
+        nph = -(-T * KL // STRIP_ROWS)
+        w[-1] += sum((min((s + 1) * STRIP_ROWS, T * KL) - 1) // KL + 2 for s in range(nph))
+    return w
+
+
+def split_strips(P: int, T: int, L: int, world: int, KL: int = 0
+                 ) -> List[List[Tuple[int, int, int]]]:
+    """Balanced split of every player's 256-row strips over the ranks: the
+    strips of players 0..P-1 in order, weighted by :func:`strip_weights`, cut
+    into ``world`` contiguous runs of equal weight.  Returns per rank
+    ``(player, first strip, end strip)`` segments; whole players per rank
+    when ``world`` divides ``P``."""
+    if world < 1 or world > P:
+        raise ValueError(f"cannot shard {P} players over {world} ranks")
+    nps = -(-T * L // STRIP_ROWS)
+    weights = np.tile(strip_weights(T, L, KL), P)
     cum = np.concatenate([[0.0], np.cumsum(weights)])
     total = cum[-1]
     cuts = [0] + [int(np.argmin(np.abs(cum - total * r / world))) for r in range(1, world)] + \
@@ -103,7 +116,7 @@ class ShardTopology:
         lab = np.asarray(labels, dtype=np.int64).reshape(T, P)
         self.labels = lab
         self.nps = -(-T * L // STRIP_ROWS)
-        self.segments = split_strips(P, T, L, world)
+        self.segments = split_strips(P, T, L, world, KL)
         self.local = [[p for p, _, _ in segs] for segs in self.segments]
         self.home = np.zeros(P, dtype=np.int64)
         for r, segs in enumerate(self.segments):
@@ -118,7 +131,7 @@ class ShardTopology:
                              f"{_lib.SHARD_MAX_LOCAL}")
         self.hub_rows = T * (N * KL + KG)
         self.own_rows = self.n_local * T * L
-        w = self._strip_weights()
+        w = strip_weights(T, L, KL)
         self.work_share = sum(w[b:e].sum() for _, b, e in self.segments[rank]) / (P * w.sum())
         self.needs = [self._needs(r) for r in range(world)]
         mine = self.needs[rank]
@@ -131,11 +144,6 @@ class ShardTopology:
                 start = self.local_players.index(o) * T * L + f * L
                 rows.append(np.arange(start, start + L))
         self.send_rows = (np.concatenate(rows) if rows else np.zeros(0, np.int64)).astype(np.int64)
-
-    def _strip_weights(self):
-        T, L = self.T, self.L
-        return np.array([(min((s + 1) * STRIP_ROWS, T * L) - 1) // L + 2 for s in range(self.nps)],
-                        dtype=np.float64)
 
     def remote_keys(self, transport: str) -> np.ndarray:
         """int32 ``[P*T]``: stream-packed first row of every remote unit this

@@ -138,18 +138,19 @@ def test_local_rows_hubs_group_major():
     assert list(hub) == expect
 
 
-@pytest.mark.parametrize("P,T,L,world", [(8, 6, 3, 2), (8, 42, 220, 8), (10, 42, 220, 8),
-                                         (10, 42, 220, 4), (5, 6, 40, 3), (4, 3, 16, 1)])
-def test_split_strips_covers_and_balances(P, T, L, world):
+@pytest.mark.parametrize("P,T,L,world,KL", [(8, 6, 3, 2, 2), (8, 42, 220, 8, 16),
+                                            (10, 42, 220, 8, 16), (10, 42, 220, 4, 16),
+                                            (5, 6, 40, 3, 0), (4, 3, 16, 1, 8)])
+def test_split_strips_covers_and_balances(P, T, L, world, KL):
     """Every strip of every player on exactly one rank, contiguous runs per
-    rank, whole players when the ranks divide the players, work within one
-    strip of equal."""
-    from multics_b200.sharded import split_strips
+    rank, whole players when the ranks divide the players, work (hub
+    partials counted on the home rank) within two strips of equal."""
+    from multics_b200.sharded import split_strips, strip_weights
 
     nps = -(-T * L // 256)
-    segs = split_strips(P, T, L, world)
+    segs = split_strips(P, T, L, world, KL)
     seen = np.zeros((P, nps), np.int64)
-    w = np.array([(min((s + 1) * 256, T * L) - 1) // L + 2 for s in range(nps)], np.float64)
+    w = strip_weights(T, L, KL)
     loads = []
     for r in range(world):
         load = 0.0
