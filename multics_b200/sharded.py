@@ -361,7 +361,8 @@ class ShardedHierAttention:
         self.remote = torch.zeros((max(self.n_recv, 1), 2 * self.dim), dtype=torch.bfloat16,
                                   device=dev)
         # hub rows as partial rows: the hub-token part, then one slot per rank
-        # for its players' partials (all-gathered in place before the merge)
+        # for its home players' partials (read in place from the other ranks
+        # with the peer transport, all-gathered in place otherwise)
         slot = t.hub_partial_slot
         n_part = t.hub_rows + t.world * slot
         self.part_o = torch.zeros((max(n_part, 1), self.dim), dtype=torch.bfloat16, device=dev)
