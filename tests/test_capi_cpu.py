@@ -58,3 +58,38 @@ def test_group_validation_messages_match_reference():
     with pytest.raises(NotImplementedError, match="CUDA"):
         make_grouping_spec(4, 3, 2, 2, 1, 1, 1, -1, torch.zeros(3, 4, dtype=torch.long),
                            device="cpu")
+
+
+def test_shard_descriptor_validation_and_sizes():
+    """hier_shard_sizes checks the shard descriptor on the host and sizes the
+    plan: strips of the local players, hub-partial strips of its home
+    players, hub-token pairs."""
+    h = _lib.lib()
+
+    def desc(players, strips, hp):
+        d = _lib.HierShardDesc()
+        d.P, d.N, d.L, d.KL, d.KG, d.T = 4, 2, 220, 16, 6, 42
+        d.n_block, d.local_attn, d.direct = 1, -1, 1
+        d.n_local, d.hub_keys = len(players), 1
+        # grouping tables are device pointers, not read by the host checks
+        d.labels = d.active = d.remote_key = 16
+        for i, (p, (b, e), f) in enumerate(zip(players, strips, hp)):
+            d.local_player[i], d.strip_begin[i], d.strip_end[i], d.hub_partials[i] = p, b, e, f
+        return d
+
+    sz = _lib.HierShardSizes()
+    nps = -(-42 * 220 // 256)   # 37 strips of a player
+    nph = -(-42 * 16 // 256)    # 3 hub-partial strips
+    n_hh = 2 * nph + -(-42 * 6 // 256)
+    d = desc([1, 2], [(20, nps), (0, 5)], [1, 0])
+    _lib.check(h.hier_shard_sizes(ctypes.byref(d), ctypes.byref(sz)))
+    assert sz.n_player_pairs == (nps - 20) + 5
+    assert sz.n_pairs == sz.n_player_pairs + nph + n_hh
+    assert sz.own_rows == 2 * 42 * 220 and sz.hub_partial_rows == 42 * 16
+    assert sz.hub_rows == 42 * (2 * 16 + 6)
+    for bad, msg in [(desc([], [], []), "holds 1..16 players"),
+                     (desc([1, 1], [(0, 1), (1, 2)], [0, 0]), "listed twice"),
+                     (desc([0], [(0, nps + 1)], [1]), "outside"),
+                     (desc([7], [(0, 1)], [1]), "out of range")]:
+        with pytest.raises(ValueError, match=msg):
+            _lib.check(h.hier_shard_sizes(ctypes.byref(bad), ctypes.byref(sz)))
