@@ -79,7 +79,6 @@ struct SDims {
   int player[HIER_SHARD_MAX_LOCAL];     // local player slot -> absolute player
   int strip0[HIER_SHARD_MAX_LOCAL];     // this shard's strips of that player
   int strip_pre[HIER_SHARD_MAX_LOCAL + 1];  // exclusive prefix of the strip counts
-  int hp_slot[HIER_SHARD_MAX_LOCAL];    // index among the hub-partial players, or -1
   int hp_player[HIER_SHARD_MAX_LOCAL];  // hub-partial player k -> local slot
   int n_hp_players, n_strips;
   int hp_row0;         // offset of this shard's hub-partial rows in the partial-row space
@@ -538,11 +537,7 @@ int make_sdims(const hier_shard_desc* g, SDims* d) {
     d->player[i] = o;
     d->strip0[i] = b;
     d->strip_pre[i + 1] = d->strip_pre[i] + (e - b);
-    d->hp_slot[i] = -1;
-    if (g->hub_partials[i]) {
-      d->hp_slot[i] = d->n_hp_players;
-      d->hp_player[d->n_hp_players++] = i;
-    }
+    if (g->hub_partials[i]) d->hp_player[d->n_hp_players++] = i;
   }
   d->n_strips = d->strip_pre[d->n_local];
   if (g->hub_partial_row0 < 0) {
