@@ -461,10 +461,8 @@ int hier_shard_count(const hier_shard_desc* g, int32_t* counts, int32_t* totals,
                      int32_t* status, void* stream);
 
 /* Second pass: the plan (q_pairs [n_pairs][8], kv_tiles, tile_masks, order
- * [n_pairs] or NULL); status bit 1: tile capacity, bit 4: mask capacity.
- * order lists the player strips first, then the hub pairs, each part by
- * descending work, so the two parts can run as separate launches (e.g. the
- * hub pairs first, their partials exchanged while the strips run). */
+ * [n_pairs] or NULL: every pair by descending work); status bit 1: tile
+ * capacity, bit 4: mask capacity. */
 int hier_shard_build(const hier_shard_desc* g, const int32_t* counts, int32_t* q_pairs,
                      int32_t* kv_tiles, int32_t tile_capacity, uint32_t* tile_masks,
                      int64_t mask_capacity, int32_t* order, int32_t* status, void* stream);

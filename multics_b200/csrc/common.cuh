@@ -298,10 +298,10 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
-// order[rank] = base + work item, by descending key-tile count (ties: lower
-// index first); item i's count is rec[i*kStride + 5] - rec[i*kStride + 4].
+// order[rank] = work item, by descending key-tile count (ties: lower index
+// first); item i's count is rec[i*kStride + 5] - rec[i*kStride + 4].
 template <int kStride>
-__global__ void order_by_work_kernel(const int32_t* rec, int n, int32_t* order, int base = 0) {
+__global__ void order_by_work_kernel(const int32_t* rec, int n, int32_t* order) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int ci = rec[i * kStride + 5] - rec[i * kStride + 4];
     int rank = 0;
@@ -309,7 +309,7 @@ __global__ void order_by_work_kernel(const int32_t* rec, int n, int32_t* order, 
       const int cj = rec[j * kStride + 5] - rec[j * kStride + 4];
       rank += (cj > ci) || (cj == ci && j < i);
     }
-    order[rank] = base + i;
+    order[rank] = i;
   }
 }
 

@@ -653,12 +653,8 @@ extern "C" int hier_shard_build(const hier_shard_desc* g, const int32_t* counts,
   pair_build_kernel<<<d.n_pairs, kThreads, plan_smem_bytes(), s>>>(
       *g, d, counts, q_pairs, kv_tiles, tile_capacity, tile_masks, mask_capacity, status);
   HIER_CHECK_CUDA(cudaGetLastError(), "pair_build_kernel launch");
-  if (order) {  // player strips, then hub pairs, each by descending work
-    const int ns = d.n_strips, nh = d.n_pairs - ns;
-    if (ns > 0) order_by_work_kernel<8><<<(ns + 127) / 128, 128, 0, s>>>(q_pairs, ns, order);
-    if (nh > 0)
-      order_by_work_kernel<8><<<(nh + 127) / 128, 128, 0, s>>>(q_pairs + (int64_t)ns * 8, nh,
-                                                                 order + ns, ns);
+  if (order) {  // every pair by descending work: the long hub-partial strips start early
+    order_by_work_kernel<8><<<(d.n_pairs + 127) / 128, 128, 0, s>>>(q_pairs, d.n_pairs, order);
     HIER_CHECK_CUDA(cudaGetLastError(), "order_by_work_kernel launch");
   }
   return HIER_OK;

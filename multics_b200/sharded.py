@@ -465,22 +465,18 @@ class ShardedHierAttention:
             self.remote[i * t.L:(i + 1) * t.L, :self.dim] = k_all[src:src + t.L]
             self.remote[i * t.L:(i + 1) * t.L, self.dim:] = v_all[src:src + t.L]
 
-    def attend(self, q, k, v, out, *, v_hub=None, out_rows=None, pairs="all"):
-        """Attention over this rank's query rows: player rows into ``out``
-        (row ``out_rows[r]`` when given), hub rows as partial rows (merged by
-        :meth:`merge`).  ``v_hub`` replaces ``v``'s hub rows (a group-major
-        copy when ``v`` keeps the sequence order).  ``pairs``: ``"all"`` (one
-        launch), ``"hubs"`` or ``"players"`` (the two halves of the plan)."""
+    def attend(self, q, k, v, out, *, v_hub=None, out_rows=None):
+        """One attention launch over this rank's query rows: player rows into
+        ``out`` (row ``out_rows[r]`` when given), hub rows as partial rows
+        (merged by :meth:`merge`).  ``v_hub`` replaces ``v``'s hub rows (a
+        group-major copy when ``v`` keeps the sequence order)."""
         t = self.topo
         own, hub = t.own_rows, t.hub_rows
         if self.transport == "peer":
             k, v = self.k_buffer(), self.v_buffer()
-        first, count = {"all": (0, self.n_pairs),
-                        "players": (0, self.n_player_pairs),
-                        "hubs": (self.n_player_pairs, self.n_pairs - self.n_player_pairs)}[pairs]
-        if count == 0:
+        if self.n_pairs == 0:
             return
-        if self.hp_rows and pairs != "players":
+        if self.hp_rows:
             torch.index_select(q[own:own + hub], 0, self.hp_src, out=self.q_hp)
         streams = [(k[:own], v[:own]),
                    (k[own:own + hub], v[own:own + hub] if v_hub is None else v_hub)]
@@ -497,8 +493,8 @@ class ShardedHierAttention:
         part.lse, part.row0 = self.part_lse.data_ptr(), own
         check(_lib.lib().hier_attn_fwd_streams(
             ptr(q), q.shape[0], q.stride(0), n, kp, vp, rows, strides, ptr(out), out.stride(0),
-            ptr(out_rows), self.H, self.D, ptr(self.q_pairs), count, ptr(self.kv_tiles),
-            ptr(self.tile_masks), 128, ptr(self.order[first:]), 1.0 / math.sqrt(self.D), None,
+            ptr(out_rows), self.H, self.D, ptr(self.q_pairs), self.n_pairs, ptr(self.kv_tiles),
+            ptr(self.tile_masks), 128, ptr(self.order), 1.0 / math.sqrt(self.D), None,
             ctypes.byref(part), ptr(self.err), stream_ptr(q.device)))
 
     # ---- hub merge: partial rows -> hub rows ---------------------------------
