@@ -251,6 +251,31 @@ def logical_pairs(P, T, L, N, KL, KG, n_block, local_attn, **kw):
     return total
 
 
+def logical_pairs_units(P, T, L, N, KL, KG, n_block, local_attn, **kw):
+    """The same count from the mask at unit scale (one token per player frame,
+    local hub and global hub; L = K_L = K_G = 1), each unit pair weighted by
+    its unit sizes.  The mask is uniform inside a unit pair except for an
+    inactive local hub's self edge (``hier_masks.py:476-480``), a diagonal of
+    K_L tokens rather than K_L x K_L."""
+    if KL == 0 and KG == 0:
+        return logical_pairs(P, T, L, N, KL, KG, n_block, local_attn, **kw)
+    unit = dense_mask(P, T, 1, N, 1 if KL else 0, 1 if KG else 0, n_block, local_attn, **kw)
+    sizes = np.concatenate([np.full(P * T, L), np.full(T * N if KL else 0, KL),
+                            np.full(T if KG else 0, KG)]).astype(np.int64)
+    w = sizes[:, None] * sizes[None, :]
+    total = int((unit * w).sum())
+    labels, active, _, _ = prepare_grouping(P, T, N, kw.get("labels"), kw.get("active"),
+                                            kw.get("membership"), kw.get("global_only"))
+    if KL:
+        for t in range(T):
+            for g in range(N):
+                if not active[t, g]:
+                    u = P * T + t * N + g
+                    if unit[u, u]:
+                        total -= KL * KL - KL
+    return total
+
+
 # ---------------------------------------------------------------------------
 # segmented metadata (kernels/hier_segmented_attention.py:117-395)
 # ---------------------------------------------------------------------------

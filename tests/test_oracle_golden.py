@@ -107,3 +107,42 @@ def test_rope_tables_match_reference(name):
 def test_oracle_rejects_bad_labels():
     with pytest.raises(ValueError, match=r"must be in \[0,2\)"):
         O.dense_mask(4, 3, 2, 2, 1, 1, 3, 7, labels=np.array([[-1, 0, 0, 1]] * 3), direct=True)
+
+
+def test_benchmark_useful_pairs_from_the_oracle():
+    """The useful-FLOP count bench.py reports for config 2 (unmasked pairs of
+    the block plan, counted on the GPU: 209 222 076) equals the oracle's
+    unit-scale count of the reference mask."""
+    import torch
+
+    from multics_b200.synth import CONFIGS, group_labels
+
+    cfg = CONFIGS["cfg2"]  # static groups: labels do not depend on the generator
+    lab = group_labels(cfg, torch.Generator().manual_seed(cfg.seed)).numpy()
+    pairs = O.logical_pairs_units(cfg.P, cfg.T, cfg.L, cfg.N, cfg.KL, cfg.KG, cfg.n_block,
+                                  cfg.local_attn, labels=lab, direct=cfg.direct)
+    assert pairs == 209222076
+
+
+@pytest.mark.parametrize("case", [
+    dict(P=4, T=3, L=5, N=2, KL=3, KG=2, n=1, win=-1, labels=[[0, 0, 1, 1]] * 3),
+    dict(P=3, T=6, L=4, N=3, KL=2, KG=3, n=2, win=3, labels=[[0, 1, 1], [0, 1, 1], [2, 2, 0],
+                                                              [2, 2, 0], [1, 0, 0], [1, 0, 0]]),
+    dict(P=3, T=4, L=3, N=2, KL=4, KG=0, n=1, win=-1, labels=[[0, 0, 0]] * 4),
+])
+def test_unit_scale_pair_count_equals_dense_popcount(case):
+    """Unit-scale count (with the inactive-hub self edge as a diagonal) equals
+    the token-level popcount, labels and membership groupings."""
+    c = dict(case)
+    lab = np.array(c.pop("labels"))
+    dims = (c["P"], c["T"], c["L"], c["N"], c["KL"], c["KG"], c["n"], c["win"])
+    assert O.logical_pairs_units(*dims, labels=lab, direct=True) == \
+        O.logical_pairs(*dims, labels=lab, direct=True)
+    mem = np.zeros((c["T"], c["N"], c["P"]), bool)
+    for t in range(c["T"]):
+        for p in range(c["P"]):
+            mem[t, lab[t, p], p] = True
+    go = ~mem.any(1)
+    go[:, 0] = True  # a global-only player
+    assert O.logical_pairs_units(*dims, membership=mem, global_only=go, direct=True) == \
+        O.logical_pairs(*dims, membership=mem, global_only=go, direct=True)
