@@ -93,3 +93,28 @@ def test_shard_descriptor_validation_and_sizes():
                      (desc([7], [(0, 1)], [1]), "out of range")]:
         with pytest.raises(ValueError, match=msg):
             _lib.check(h.hier_shard_sizes(ctypes.byref(bad), ctypes.byref(sz)))
+
+
+def test_sequence_plan_selection_rules(monkeypatch):
+    """Which groupings the full-sequence entry points run on the sequence
+    plan (labels, no no-local topology, T % n == 0, window -1 or >= n), and
+    the environment switch to the block plan."""
+    from types import SimpleNamespace
+
+    from multics_b200.attention import FULL_SEQUENCE_PLAN_ENV, HierSequencePlan, sequence_plan
+
+    base = dict(membership=None, labels=torch.zeros(6, 4, dtype=torch.long), no_local=False,
+                T=6, n_block=3, local_attn=-1)
+    ok = SimpleNamespace(**base)
+    assert HierSequencePlan.supports(ok)
+    for change in (dict(membership=torch.zeros(6, 2, 4, dtype=torch.bool)), dict(no_local=True),
+                   dict(n_block=4), dict(local_attn=2), dict(labels=None)):
+        assert not HierSequencePlan.supports(SimpleNamespace(**{**base, **change})), change
+    assert HierSequencePlan.supports(SimpleNamespace(**{**base, "local_attn": 3}))
+    mask = SimpleNamespace(spec=SimpleNamespace(**{**base, "no_local": True}))
+    assert sequence_plan(mask, 2) is None  # unsupported grouping: block plan, no device work
+    monkeypatch.setenv(FULL_SEQUENCE_PLAN_ENV, "blocks")
+    assert sequence_plan(SimpleNamespace(spec=ok), 2) is None
+    monkeypatch.setenv(FULL_SEQUENCE_PLAN_ENV, "tiles")
+    with pytest.raises(ValueError, match="segments"):
+        sequence_plan(SimpleNamespace(spec=ok), 2)
