@@ -196,3 +196,49 @@ def test_hub_partials_cover_each_hub_row_once_per_key_set(world):
                 assert src[i] == r and tr.hp_players[rk][i // (T * KL)] in members
         else:
             assert players == []
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_random_strip_splits_cover_needs_and_partials(seed):
+    """Random shapes and rank counts: every strip computed once, every mate
+    unit a rank's strips attend to (dense mask) is local or listed in its
+    needs and served by the player's home rank, and every member player of
+    every local hub row has exactly one partial row."""
+    from multics_b200.sharded import STRIP_ROWS, ShardTopology
+
+    rng = np.random.default_rng(seed)
+    P = int(rng.integers(2, 7))
+    world = int(rng.integers(1, P + 1))
+    T, L = int(rng.integers(2, 6)), int(rng.integers(20, 140))
+    N, KL, KG = 2, int(rng.integers(1, 4)), int(rng.integers(0, 3))
+    n_block = int(rng.choice([1, 2])) if T % 2 == 0 else 1
+    lab = rng.integers(0, N, size=(T, P))
+    for t0 in range(0, T, n_block):
+        lab[t0:t0 + n_block] = lab[t0]
+    dense = O.dense_mask(P, T, L, N, KL, KG, n_block, -1, labels=lab, direct=True)
+    tops = [ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=n_block, local_attn=-1,
+                          direct=True, labels=lab, world=world, rank=r) for r in range(world)]
+    computed = np.zeros(P * T * L, np.int64)
+    for r, t in enumerate(tops):
+        rows = []
+        for p, b, e in t.segments[r]:
+            rows.append(p * T * L + np.arange(b * STRIP_ROWS, min(e * STRIP_ROWS, T * L)))
+        rows = np.concatenate(rows)
+        computed[rows] += 1
+        assert set(t.local_rows()[t.computed_rows()]) == set(rows)
+        cols = np.nonzero(dense[rows].any(0))[0]
+        need = {(c // (T * L), (c % (T * L)) // L) for c in cols if c < P * T * L}
+        need = {u for u in need if u[0] not in t.local_players}
+        assert set(t.needs[r]) == need
+        for o, _ in t.needs[r]:
+            assert o in tops[int(t.home[o])].local_players
+    assert (computed == 1).all()
+    off, rows = tops[0].hub_partials()
+    slot = tops[0].hub_partial_slot
+    for h in range(T * N * KL):
+        g, f = h // (T * KL), (h % (T * KL)) // KL
+        players = []
+        for x in rows[off[h] + 1:off[h + 1]]:
+            rk, i = divmod(int(x) - tops[0].hub_rows, slot)
+            players.append(tops[rk].hp_players[rk][i // (T * KL)])
+        assert sorted(players) == [p for p in range(P) if lab[f, p] == g]
