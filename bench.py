@@ -147,6 +147,22 @@ def plan_tile_flops(q_pairs, kv_tiles, H, D):
     return 4.0 * 128 * 128 * D * H * float(used.sum())
 
 
+def workload_config(cfg, world, sharded):
+    """``config`` object shared by both arms of one command line."""
+    if sharded:
+        wl = (f"{cfg.name}: hierarchical attention layer forward, players sharded over "
+              f"{world} GPU(s) (prologue + mate-frame exchange + attention + hub merge), "
+              f"P={cfg.P} x T={cfg.T} x L={cfg.L}, N={cfg.N} groups"
+              + (f" (regroup every {cfg.regroup_every} frames)" if cfg.regroup_every else "")
+              + f", K_L={cfg.KL}, K_G={cfg.KG}, H={cfg.H}x{cfg.D}")
+    else:
+        wl = (f"{cfg.name}: hierarchical attention layer forward (prologue + attention), "
+              f"P={cfg.P} players x T={cfg.T} frames x L={cfg.L} tokens, N={cfg.N} groups, "
+              f"K_L={cfg.KL}, K_G={cfg.KG}, H={cfg.H}x{cfg.D}, n_block={cfg.n_block}, "
+              f"local_attn={cfg.local_attn}, direct={cfg.direct}")
+    return {"workload": wl, "S": cfg.S}
+
+
 def run_sharded(args, rank, world, local_rank):
     """Players sharded over the ranks (strong scaling of one layer): each rank
     runs the prologue of its rows (its players, then the replicated hub
@@ -262,12 +278,8 @@ def run_sharded(args, rank, world, local_rank):
         "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; shapes of the reference configs)",
-        "config": {"workload": f"{cfg.name}: hierarchical attention layer forward, players "
-                               f"sharded over {world} GPUs (prologue + mate-frame all_to_all + "
-                               f"attention + hub merge), P={cfg.P} x T={cfg.T} x L={cfg.L}, "
-                               f"N={cfg.N} groups (regroup every {cfg.regroup_every} frames), "
-                               f"K_L={cfg.KL}, K_G={cfg.KG}, H={cfg.H}x{cfg.D}",
-                   "S": S, "useful_pairs": pairs, "useful_gflop_per_step": useful_flops / 1e9,
+        "config": {**workload_config(cfg, world, True),
+                   "useful_pairs": pairs, "useful_gflop_per_step": useful_flops / 1e9,
                    "parallelism": f"players sharded x{world} by 256-row strips "
                                   f"(rank 0: {topo.segments[0]}); "
                                   f"mate frames: {sh.transport}",
@@ -442,12 +454,8 @@ def run_ours(args, rank, world, local_rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; shapes of the reference configs)",
-        "config": {"workload": f"{cfg.name}: hierarchical attention layer forward "
-                               f"(prologue + attention), P={cfg.P} players x T={cfg.T} frames x "
-                               f"L={cfg.L} tokens, N={cfg.N} groups, K_L={cfg.KL}, K_G={cfg.KG}, "
-                               f"H={cfg.H}x{cfg.D}, n_block={cfg.n_block}, "
-                               f"local_attn={cfg.local_attn}, direct={cfg.direct}",
-                   "S": S, "useful_pairs": pairs, "useful_gflop_per_step": useful_flops / 1e9,
+        "config": {**workload_config(cfg, world, False),
+                   "useful_pairs": pairs, "useful_gflop_per_step": useful_flops / 1e9,
                    "tile_gflop_per_step": tile_flops / 1e9,
                    "parallelism": f"players sharded x{world}" if world > 1 else "single GPU",
                    "plan": ("sequence plan: 256-row player strips and 128-row group tiles of "
@@ -554,90 +562,54 @@ def run_e2e(args, cfg, inp, bm, ft, dev, useful_flops, world):
                          "while step i computes"}
 
 
-class CPUPath:
-    """The reference's CPU attention path, restated by the oracle port: dense
-    hierarchical mask rows + fp32 masked-softmax attention, on prologue
-    outputs (fp32 camera add, RMSNorm over the full row, float64 RoPE) for
-    head 0.  Inputs are prepared once; :meth:`sample` times a bounded number
-    of query-row chunks, walking backwards from the last frames of player 0
-    (the rows with the most keys)."""
-
-    def __init__(self, cfg):
-        import numpy as np
-
-        from oracle import hier_oracle as O
-        from multics_b200.synth import make_inputs
-
-        self.O = O
-        self.cfg = cfg
-        inp = make_inputs(cfg, device="cpu")
-        self.labels = inp.labels.numpy()
-        f32 = lambda t: t.float().numpy()  # noqa: E731
-        freqs = np.ascontiguousarray(np.stack([inp.freqs[:, 0].real.numpy(),
-                                               inp.freqs[:, 0].imag.numpy()], -1))
-        cam = f32(inp.cam)
-        self.q = O.prologue_head(f32(inp.qx), cam, f32(inp.wcq), f32(inp.nqw), freqs, cfg.H, 0)
-        self.k = O.prologue_head(f32(inp.kx), cam, f32(inp.wck), f32(inp.nkw), freqs, cfg.H, 0)
-        self.v = np.ascontiguousarray(f32(inp.v)[:, : cfg.D])
-        self.cursor = cfg.T * cfg.L
-
-    def sample(self, seconds, rows_per_chunk=512):
-        cfg, O = self.cfg, self.O
-        pairs, elapsed = 0, 0.0
-        while elapsed < seconds:
-            if self.cursor <= 0:
-                self.cursor = cfg.T * cfg.L
-            a, r = max(0, self.cursor - rows_per_chunk), self.cursor
-            t = time.perf_counter()
-            m = O.dense_mask(cfg.P, cfg.T, cfg.L, cfg.N, cfg.KL, cfg.KG, cfg.n_block,
-                             cfg.local_attn, labels=self.labels, direct=cfg.direct,
-                             rows=slice(a, r))
-            O.masked_attention(self.q[a:r], self.k, self.v, 1, lambda x, y: m[x:y],
-                               row_chunk=rows_per_chunk)
-            elapsed += time.perf_counter() - t
-            pairs += int(m.sum())
-            self.cursor = a
-        return pairs, elapsed
-
-    def value(self, seconds):
-        pairs, elapsed = self.sample(seconds)
-        return 4.0 * self.cfg.D * pairs / elapsed / 1e12, pairs, elapsed
-
-
 def cpu_baseline(cfg, sample_seconds=15.0):
-    """cpu_baseline object of the JSON line (rank 0, N=1)."""
-    path = CPUPath(cfg)
-    v, pairs, el = path.value(sample_seconds)
-    return {"value": round(v, 6), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-            "sample": f"oracle port (dense mask + fp32 masked attention, head 0) over {pairs} "
-                      f"unmasked pairs of the last frames of player 0 in {el:.1f} s; useful "
-                      f"FLOP/s = 4*D*pairs/time"}
+    """cpu_baseline object of the JSON line (rank 0, N=1): the reference's CPU
+    path (torch calls in fp32, all host threads) over a bounded sample of the
+    same layer."""
+    from oracle.ref_cpu_path import RefCPULayer, cpu_model
+
+    path = RefCPULayer(cfg)
+    flops, el, units, rows = path.sample(sample_seconds)
+    return {"value": round(flops / el / 1e12, 6), "unit": UNIT, "cores": path.threads,
+            "cpu": cpu_model(), "kind": "port", "sample": path.describe(units, rows)}
 
 
 def run_reference(args, rank, world):
-    """Reference arm: the reference's CPU path (oracle port; the reference is
-    pure Python and cannot be installed on the GPU box) on host cores."""
+    """Reference arm: the reference's CPU path for this layer (the same torch
+    calls, fp32, float64 RoPE; the reference package itself does not install)
+    on all host threads, rank 0 only.  Each step is a bounded sample of the
+    layer; the value is the useful FLOPs of all timed steps over their time."""
     from multics_b200.synth import CONFIGS
+    from oracle.ref_cpu_path import RefCPULayer, cpu_model
 
     cfg = CONFIGS[args.config]
     if rank != 0:
         return None
-    path = CPUPath(cfg)
-    per_step = min(10.0, max(1.0, 90.0 / max(1, args.steps + args.warmup)))
+    path = RefCPULayer(cfg)
+    per_step = min(10.0, max(0.5, 90.0 / max(1, args.steps + args.warmup)))
     for _ in range(args.warmup):
-        path.value(per_step / 2)
+        path.sample(per_step / 2)
     t = time.perf_counter()
-    vals = [path.value(per_step)[0] for _ in range(args.steps)]
+    tot_f = tot_s = 0.0
+    tot_u = tot_r = 0
+    for _ in range(args.steps):
+        f, s_, u, r = path.sample(per_step)
+        tot_f, tot_s, tot_u, tot_r = tot_f + f, tot_s + s_, tot_u + u, tot_r + r
     wall = time.perf_counter() - t
-    v = statistics.mean(vals)
-    return {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(wall * 1e3 / args.steps, 1),
+    v = tot_f / tot_s / 1e12
+    desc = path.describe(tot_u, tot_r)
+    return {"metric": METRIC, "value": round(v, 6), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(wall * 1e3 / max(1, args.steps), 1),
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
-            "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)", "impl": "reference",
-            "config": {"workload": f"{cfg.name} (bounded CPU sample)"},
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"{per_step:.0f} s of dense-mask fp32 attention rows per step"},
-            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
+            "impl": "reference",
+            "config": workload_config(cfg, world, args.path == "shard"),
+            "layer_seconds_estimate": round(tot_s / max(1, tot_r) * cfg.S * cfg.H, 2),
+            "cpu_baseline": {"value": round(v, 6), "unit": UNIT, "cores": path.threads,
+                             "cpu": cpu_model(), "kind": "port", "sample": desc},
+            "e2e": {"value": round(v, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
 
 
 def main():
@@ -645,8 +617,15 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    # Under torch.distributed.run (the scaling runs) every N, N=1 included,
+    # runs config 4 through the sharded layer, so that the per-N values divide
+    # one workload; a plain single-GPU run measures config 2 (the metric's
+    # configuration).
+    under_launcher = "TORCHELASTIC_RUN_ID" in os.environ or "LOCAL_WORLD_SIZE" in os.environ
     if args.config is None:
-        args.config = "cfg2" if world == 1 else "cfg4"
+        args.config = "cfg2" if (world == 1 and not under_launcher) else "cfg4"
+    if args.path is None:
+        args.path = "segments" if (world == 1 and args.config == "cfg2") else "shard"
     if args.impl == "reference":
         line = run_reference(args, rank, world)
         if line is not None:
@@ -674,8 +653,6 @@ def main():
             sys.stdout.flush()
             os.dup2(saved, 1)
             os.close(saved)
-    if args.path is None:
-        args.path = "segments" if (world == 1 and args.config == "cfg2") else "shard"
     if args.path == "block":
         os.environ["MULTICS_B200_FULL_SEQUENCE_PLAN"] = "blocks"
     if world == 1 and args.path in ("segments", "block"):

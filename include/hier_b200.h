@@ -141,6 +141,29 @@ int hier_block_plan_build(const hier_grouping* g, void* workspace, const int32_t
                           int32_t* q_pairs, int32_t* kv_tiles, uint32_t* row_masks,
                           int32_t* order, int32_t* n_kv_tiles, void* stream);
 
+/* Workspace bytes for hier_dense_block_mask_build / hier_dense_block_plan_build. */
+int hier_dense_block_workspace_size(int64_t S, size_t* bytes);
+
+/* The same block classification and lists as hier_block_mask_build, read
+ * from a caller's dense mask instead of a grouping: mask is uint8/bool
+ * [S, ld] on the device (row stride ld >= S; any non-zero byte allows the
+ * pair, as flash_attention's mask.to(bool) does), or NULL for no mask (every
+ * pair inside [0,S)^2 allowed).  Replaces the dense-mask and unmasked calls
+ * of flash_attention (multics/models/attention.py:39-54, the sdpa path of
+ * SelfAttention.forward, attention.py:436-442). */
+int hier_dense_block_mask_build(const uint8_t* mask, int64_t S, int64_t ld, void* workspace,
+                                int32_t* kv_num, int32_t* kv_off, int32_t* kv_idx,
+                                int32_t* full_num, int32_t* full_off, int32_t* full_idx,
+                                int32_t* totals, void* stream);
+
+/* Attention work plan (the formats of hier_block_plan_build, no page table)
+ * of the classification hier_dense_block_mask_build left in the workspace;
+ * row_masks hold the mask's own bits of every partial block. */
+int hier_dense_block_plan_build(const uint8_t* mask, int64_t S, int64_t ld, void* workspace,
+                                const int32_t* kv_off, const int32_t* kv_idx, int32_t* q_pairs,
+                                int32_t* kv_tiles, uint32_t* row_masks, int32_t* order,
+                                int32_t* n_kv_tiles, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Fused Q/K prologue
  * ------------------------------------------------------------------------- */

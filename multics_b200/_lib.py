@@ -129,6 +129,11 @@ _SIGS = {
                                       _P, _P, _P]),
     "hier_block_mask_build_static": (c_int, [ctypes.POINTER(HierGrouping), _P, _P, _P, _P, _P, _P, _P,
                                              _P]),
+    "hier_dense_block_workspace_size": (c_int, [c_int64, ctypes.POINTER(c_size_t)]),
+    "hier_dense_block_mask_build": (c_int, [_P, c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P, _P,
+                                            _P]),
+    "hier_dense_block_plan_build": (c_int, [_P, c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P, _P,
+                                            _P]),
     "hier_prep_qk": (c_int, [_P, _P, c_int64, _P, c_int32, _P, _P, _P, _P, _P, c_int64, c_int32,
                              c_int32, c_float, _P, _P, c_int64, _P, _P]),
     "hier_attn_fwd": (c_int, [_P, c_int64, c_int64, _P, _P, c_int64, c_int64, _P, c_int64, c_int32,

@@ -26,11 +26,11 @@ import torch.nn as nn
 
 from . import _lib
 from ._lib import check, ptr, stream_ptr
-from .hier_masks import HierBlockMask
+from .hier_masks import HierBlockMask, block_mask_for_spec, build_dense_block_plan
 
 __all__ = ["hier_prep_qk", "hier_block_attention", "freqs_table", "RMSNorm", "SelfAttention",
            "AttentionPlan", "attention_from_plan", "HierSequencePlan", "sequence_plan",
-           "hier_attention_layer"]
+           "hier_attention_layer", "attention_mask_plan"]
 
 # Work plan of the full-sequence layer entry points: "segments" (the
 # HierSequencePlan wherever the grouping allows it) or "blocks" (always the
@@ -211,7 +211,7 @@ class HierSequencePlan:
 
     @staticmethod
     def supports(spec) -> bool:
-        return (spec.membership is None and spec.labels is not None and not spec.no_local
+        return (spec is not None and spec.membership is None and spec.labels is not None and not spec.no_local
                 and spec.T % spec.n_block == 0
                 and (spec.local_attn == -1 or spec.local_attn >= spec.n_block))
 
@@ -256,6 +256,7 @@ def hier_attention_layer(qx, kx, v, freqs, block_mask: HierBlockMask, num_heads,
     camera + RMSNorm + RoPE prologue, then block-sparse attention.  Equivalent
     to the reference's ``_project_self_attn_qkv`` tail + ``flash_attention(mask)``
     (``attention.py:355-365,39-54``); returns ``[S, H*D]`` bf16."""
+    block_mask = attention_mask_plan(block_mask, _rows(qx).shape[0], qx.device)
     sp = sequence_plan(block_mask, num_heads)
     q, k = hier_prep_qk(qx, kx, freqs, num_heads, norm_q_weight=norm_q_weight,
                         norm_k_weight=norm_k_weight, cam_tokens=cam_tokens,
@@ -264,6 +265,39 @@ def hier_attention_layer(qx, kx, v, freqs, block_mask: HierBlockMask, num_heads,
     if sp is not None:
         return sp.attend(q, k, _rows(v), out)
     return attention_from_plan(q, k, v, block_mask, num_heads, out=out)
+
+
+_DENSE_PLANS: list = []  # [(weakref to mask or None, version, S, device, HierBlockMask)]
+
+
+def attention_mask_plan(mask, S: int, device) -> HierBlockMask:
+    """The block mask / work plan for ``mask`` as :meth:`SelfAttention.forward`
+    accepts it.  Plans of dense masks are kept for the two most recent masks
+    (and for no mask per length), like the reference's bounded mask caches,
+    and rebuilt when the mask tensor is modified in place."""
+    import weakref
+
+    if isinstance(mask, HierBlockMask):
+        return mask
+    spec = getattr(mask, "hier_spec", None)
+    if spec is not None:
+        return block_mask_for_spec(spec)
+    if mask is not None and not isinstance(mask, torch.Tensor):
+        raise TypeError(f"mask must be a HierBlockMask, a dense [S,S] tensor or None; got "
+                        f"{type(mask).__name__}")
+    dev = torch.device(device)
+    for ref, ver, s_, d_, bm in _DENSE_PLANS:
+        if s_ != S or d_ != dev:
+            continue
+        if mask is None and ref is None:
+            return bm
+        if mask is not None and ref is not None and ref() is mask and mask._version == ver:
+            return bm
+    bm = build_dense_block_plan(mask, S, dev)
+    _DENSE_PLANS.insert(0, (None if mask is None else weakref.ref(mask),
+                            None if mask is None else mask._version, S, dev, bm))
+    del _DENSE_PLANS[2:]
+    return bm
 
 
 class RMSNorm(nn.Module):
@@ -285,9 +319,10 @@ class SelfAttention(nn.Module):
     ``forward(x, freqs, mask=None, cam_tokens=None)`` signature
     (``attention.py:255-442``).
 
-    ``mask`` is the :class:`HierBlockMask` returned by
-    ``multics_b200.hier_masks.build_stage2_hier_flex_block_mask`` (the
-    reference passes a dense bool mask or a Flex BlockMask).  The q/k/v/o
+    ``mask`` is a :class:`HierBlockMask`
+    (``multics_b200.hier_masks.build_stage2_hier_flex_block_mask``), a dense
+    bool mask (``build_stage2_hier_self_attn_mask`` or any other) or None, as
+    the reference's Flex and sdpa call sites pass.  The q/k/v/o
     projections run as cuBLAS GEMMs; the camera add, both RMSNorms and RoPE
     run in one prologue kernel and the attention in the tcgen05 kernel."""
 
@@ -350,9 +385,13 @@ class SelfAttention(nn.Module):
         return q, k, _rows(v)
 
     def forward(self, x, freqs, mask=None, cam_tokens=None):
-        if not isinstance(mask, HierBlockMask):
-            raise TypeError("multics_b200 SelfAttention.forward requires a HierBlockMask "
-                            "(build_stage2_hier_flex_block_mask)")
+        """``attention.py:436-442``.  ``mask`` is what the reference's call
+        sites pass: the :class:`HierBlockMask` of
+        ``build_stage2_hier_flex_block_mask`` (the Flex path), the dense bool
+        mask of ``build_stage2_hier_self_attn_mask`` (the sdpa path; it
+        carries its grouping and runs on the grouping's plan), any other dense
+        ``[S,S]`` mask (block plan built from its bytes), or None (unmasked)."""
+        mask = attention_mask_plan(mask, x.shape[1], x.device)
         sp = sequence_plan(mask, self.num_heads)
         q, k, v = self.project_qkv(x, freqs, cam_tokens,
                                    out_rows=None if sp is None else sp.seq_to_plan)

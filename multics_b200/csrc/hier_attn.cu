@@ -515,13 +515,13 @@ int attn_launch(const QMaps& qm, int q2_row0, const KVMaps<kMaps>& kv, void* out
                 int32_t n_pairs, const int32_t* kv_tiles, const uint32_t* row_masks,
                 int mask_rows, const int32_t* order, float softmax_scale, float* lse,
                 const hier_partial_out* part, int32_t* dev_err, void* stream) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    HIER_CHECK_CUDA(cudaFuncSetAttribute(hier_attn_kernel<kMaps>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
-                    "cudaFuncSetAttribute(hier_attn_kernel)");
-    attr_set = true;
-  }
+  // The shared-memory limit is a per-device attribute of the function: set
+  // it on every launch (a host call of about a microsecond), as the other
+  // launchers do, so that a process driving several devices or host threads
+  // needs no shared flag.
+  HIER_CHECK_CUDA(cudaFuncSetAttribute(hier_attn_kernel<kMaps>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+                  "cudaFuncSetAttribute(hier_attn_kernel)");
   AttnArgs args;
   args.pairs = reinterpret_cast<const int4*>(q_pairs);
   args.kv_tiles = reinterpret_cast<const int4*>(kv_tiles);

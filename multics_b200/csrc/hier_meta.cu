@@ -11,6 +11,7 @@
 // matrix and only partial blocks are expanded to token bitmasks.
 
 #include <stdio.h>
+#include <string.h>
 
 #include "common.cuh"
 
@@ -538,6 +539,169 @@ extern "C" int hier_block_plan_build(const hier_grouping* g, void* workspace,
   if (row_masks) rowmask_kernel<<<nb, 128, 0, s>>>(d, M, kv_off, kv_idx, (uint4*)row_masks);
   if (order) order_by_work_kernel<8><<<grid_for(np, 128), 128, 0, s>>>(q_pairs, np, order);
   HIER_CHECK_CUDA(cudaGetLastError(), "block plan kernels launch");
+  return HIER_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Block plan of a caller's dense bool mask, or of no mask
+// ---------------------------------------------------------------------------
+//
+// The reference's full-sequence attention also runs with a plain dense bool
+// mask [S,S] (flash_attention(q, k, v, num_heads, mask=...),
+// multics/models/attention.py:39-54) or with none.  The same 128x128 block
+// plan is built from the mask bytes themselves: blocks are classified by
+// reading every byte once (coalesced 128-byte row segments per warp), and
+// partial blocks get per-row key bitmasks by warp ballots.  A NULL mask
+// means every (query, key) pair inside [0,S)^2 is allowed.
+
+namespace hier {
+
+// Byte (r, c) of the mask as a bool; outside [0,S)^2 false.
+__device__ __forceinline__ bool dense_at(const uint8_t* mask, int64_t ld, int64_t S, int64_t r,
+                                         int64_t c) {
+  if (r >= S || c >= S) return false;
+  return mask ? mask[r * ld + c] != 0 : true;
+}
+
+// One 128-thread block per 128x128 block (grid-stride): each warp reads 32
+// rows of the block, one 128-byte row segment per step (lane l: columns
+// 4l..4l+3, one 32-bit load when the rows are 4-byte aligned).
+__global__ void dense_classify_kernel(const uint8_t* mask, int64_t ld, int64_t S, int nb,
+                                      bool vec4, uint8_t* cls) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int any_s[4], all_s[4];
+  for (int64_t e = blockIdx.x; e < (int64_t)nb * nb; e += gridDim.x) {
+    const int qb = (int)(e / nb), kb = (int)(e % nb);
+    const int64_t r0 = (int64_t)qb * 128, c0 = (int64_t)kb * 128 + 4 * lane;
+    bool any = false, all = true;
+    for (int i = 0; i < 32; ++i) {
+      const int64_t r = r0 + 32 * w + i;
+      bool b[4];
+      if (mask && vec4 && r < S && c0 + 3 < S) {
+        const uint32_t x = *reinterpret_cast<const uint32_t*>(mask + r * ld + c0);
+        b[0] = (x & 0xffu) != 0, b[1] = (x & 0xff00u) != 0;
+        b[2] = (x & 0xff0000u) != 0, b[3] = (x & 0xff000000u) != 0;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b[j] = dense_at(mask, ld, S, r, c0 + j);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        any |= b[j];
+        all &= b[j];
+      }
+    }
+    any = __any_sync(0xffffffffu, any);
+    all = __all_sync(0xffffffffu, all);
+    if (lane == 0) {
+      any_s[w] = any;
+      all_s[w] = all;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const bool a = any_s[0] | any_s[1] | any_s[2] | any_s[3];
+      const bool f = all_s[0] & all_s[1] & all_s[2] & all_s[3];
+      cls[e] = a ? (f ? 2 : 1) : 0;
+    }
+    __syncthreads();
+  }
+}
+
+// One 128-thread block per query block; warp w builds the bitmasks of rows
+// 32w..32w+31 of every partial block of the row (lane l reads columns l,
+// l+32, l+64, l+96; ballots give the four 32-bit words).
+__global__ void dense_rowmask_kernel(const uint8_t* mask, int64_t ld, int64_t S,
+                                     const int32_t* kv_off, const int32_t* kv_idx,
+                                     uint4* row_masks) {
+  const int qb = blockIdx.x;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int32_t pi = kv_off[qb]; pi < kv_off[qb + 1]; ++pi) {
+    const int64_t c0 = (int64_t)kv_idx[pi] * 128;
+    for (int i = 0; i < 32; ++i) {
+      const int rr = 32 * w + i;
+      const int64_t r = (int64_t)qb * 128 + rr;
+      uint32_t word[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        word[j] = __ballot_sync(0xffffffffu, dense_at(mask, ld, S, r, c0 + 32 * j + lane));
+      if (lane == 0) row_masks[(int64_t)pi * 128 + rr] = make_uint4(word[0], word[1], word[2], word[3]);
+    }
+  }
+}
+
+static int check_dense(const uint8_t* mask, int64_t S, int64_t ld) {
+  if (S <= 0 || S > (int64_t)INT32_MAX / 2) {
+    set_error(HIER_EVALUE, "dense mask plan: sequence length %lld out of range", (long long)S);
+    return HIER_EVALUE;
+  }
+  if (mask && ld < S) {
+    set_error(HIER_EVALUE, "dense mask row stride %lld is shorter than S=%lld", (long long)ld,
+              (long long)S);
+    return HIER_EVALUE;
+  }
+  return HIER_OK;
+}
+
+}  // namespace hier
+
+extern "C" int hier_dense_block_workspace_size(int64_t S, size_t* bytes) {
+  clear_error();
+  int rc = check_dense(nullptr, S, S);
+  if (rc) return rc;
+  const int64_t nb = (S + 127) / 128;
+  const int64_t np = (nb + 1) / 2;
+  *bytes = align256((size_t)(nb * nb)) + 2 * align256((size_t)(np + 1) * sizeof(int32_t));
+  return HIER_OK;
+}
+
+extern "C" int hier_dense_block_mask_build(const uint8_t* mask, int64_t S, int64_t ld,
+                                           void* workspace, int32_t* kv_num, int32_t* kv_off,
+                                           int32_t* kv_idx, int32_t* full_num,
+                                           int32_t* full_off, int32_t* full_idx,
+                                           int32_t* totals, void* stream) {
+  clear_error();
+  int rc = check_dense(mask, S, ld);
+  if (rc) return rc;
+  const int nb = (int)((S + 127) / 128);
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* cls = (uint8_t*)workspace;
+  const bool vec4 = mask && ((uintptr_t)mask % 4 == 0) && (ld % 4 == 0);
+  const int64_t blocks = (int64_t)nb * nb;
+  dense_classify_kernel<<<(int)(blocks < 148 * 16 ? blocks : 148 * 16), 128, 0, s>>>(
+      mask, ld, S, nb, vec4, cls);
+  block_count_kernel<<<(nb + 7) / 8, 256, 0, s>>>(cls, nb, kv_num, full_num);
+  scan_kernel<<<1, 1024, 0, s>>>(kv_num, nb, kv_off, totals);
+  scan_kernel<<<1, 1024, 0, s>>>(full_num, nb, full_off, totals ? totals + 1 : nullptr);
+  block_fill_kernel<<<(nb + 7) / 8, 256, 0, s>>>(cls, nb, kv_off, kv_idx, full_off, full_idx);
+  HIER_CHECK_CUDA(cudaGetLastError(), "dense block mask kernels launch");
+  return HIER_OK;
+}
+
+extern "C" int hier_dense_block_plan_build(const uint8_t* mask, int64_t S, int64_t ld,
+                                           void* workspace, const int32_t* kv_off,
+                                           const int32_t* kv_idx, int32_t* q_pairs,
+                                           int32_t* kv_tiles, uint32_t* row_masks,
+                                           int32_t* order, int32_t* n_kv_tiles, void* stream) {
+  clear_error();
+  int rc = check_dense(mask, S, ld);
+  if (rc) return rc;
+  const int nb = (int)((S + 127) / 128);
+  const int np = (nb + 1) / 2;
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* cls = (uint8_t*)workspace;
+  int32_t* pair_cnt = (int32_t*)(cls + align256((size_t)nb * nb));
+  int32_t* pair_off = (int32_t*)((uint8_t*)pair_cnt + align256((size_t)(np + 1) * sizeof(int32_t)));
+  Dims d;
+  memset(&d, 0, sizeof(d));
+  d.S = S;
+  pair_count_kernel<<<(np + 7) / 8, 256, 0, s>>>(cls, nb, np, pair_cnt);
+  scan_kernel<<<1, 1024, 0, s>>>(pair_cnt, np, pair_off, n_kv_tiles);
+  pair_plan_fill_kernel<<<(np + 7) / 8, 256, 0, s>>>(d, cls, nb, np, kv_off, pair_off, nullptr,
+                                                     q_pairs, kv_tiles);
+  if (row_masks)
+    dense_rowmask_kernel<<<nb, 128, 0, s>>>(mask, ld, S, kv_off, kv_idx, (uint4*)row_masks);
+  if (order) order_by_work_kernel<8><<<grid_for(np, 128), 128, 0, s>>>(q_pairs, np, order);
+  HIER_CHECK_CUDA(cudaGetLastError(), "dense block plan kernels launch");
   return HIER_OK;
 }
 

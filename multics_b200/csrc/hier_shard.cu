@@ -465,9 +465,22 @@ __global__ void __launch_bounds__(kThreads)
   const int n_tiles = (m.misc[2] + 1) >> 1;
   if (n_tiles != counts[2 * pi] || tile_base + n_tiles > tile_capacity ||
       (int64_t)mask_base + counts[2 * pi + 1] > mask_capacity) {
-    if (threadIdx.x == 0 && status)
-      atomicOr(status, tile_base + n_tiles > tile_capacity ? kStatusTileOverflow
-                                                           : kStatusMaskOverflow);
+    if (threadIdx.x == 0) {
+      if (status)
+        atomicOr(status, tile_base + n_tiles > tile_capacity ? kStatusTileOverflow
+                                                             : kStatusMaskOverflow);
+      // still a well-formed record: an empty pair, so that ordering and an
+      // attention launch over this plan read no key tile outside the table
+      int32_t* rec = q_pairs + (int64_t)pi * 8;
+      rec[0] = pr.q0;
+      rec[1] = pr.n0;
+      rec[2] = pr.q0 + 128;
+      rec[3] = pr.n1;
+      rec[4] = 0;
+      rec[5] = 0;
+      rec[6] = 1;
+      rec[7] = pr.kind == kPairPlayer ? 0 : 1;
+    }
     return;
   }
   emit_tiles<true>(g, d, pr, m, tile_base, mask_base, kv_tiles, tile_masks);

@@ -272,7 +272,25 @@ def build_stage2_hier_self_attn_mask(num_players, num_frames, num_patches, num_g
                               num_local_hub_tokens, num_global_hub_tokens, num_frame_per_block,
                               local_attn_size, group_labels, active_group, direct_player, device,
                               membership, global_only, hier_no_local_hub)
-    return dense_mask_rows(spec, 0, spec.S)
+    return HierDenseMask.wrap(dense_mask_rows(spec, 0, spec.S), spec)
+
+
+class HierDenseMask(torch.Tensor):
+    """The dense ``[S,S]`` bool mask of :func:`build_stage2_hier_self_attn_mask`
+    (a plain bool tensor for every torch operation, whose results are plain
+    tensors) that also carries the grouping it was built from, so that
+    :class:`multics_b200.attention.SelfAttention` runs it on the grouping's
+    work plan instead of reading the mask's bytes."""
+
+    hier_spec: "HierGroupingSpec"
+
+    __torch_function__ = torch._C._disabled_torch_function_impl
+
+    @staticmethod
+    def wrap(mask: torch.Tensor, spec: "HierGroupingSpec") -> "HierDenseMask":
+        m = mask.as_subclass(HierDenseMask)
+        m.hier_spec = spec
+        return m
 
 
 def dense_mask_rows(spec: HierGroupingSpec, row0: int, nrows: int) -> torch.Tensor:
@@ -314,7 +332,7 @@ class HierBlockMask:
     n_partial: int
     n_full: int
     n_kv_tiles: torch.Tensor
-    spec: HierGroupingSpec
+    spec: Optional[HierGroupingSpec]
 
     @property
     def shape(self):
@@ -370,12 +388,19 @@ def build_block_plan(spec: HierGroupingSpec, page_table: Optional[torch.Tensor] 
     check(L.hier_block_plan_build(ctypes.byref(g), ptr(ws), ptr(kv_off), ptr(kv_flat),
                                   ptr(full_off), ptr(full_flat), ptr(pt), ptr(q_pairs),
                                   ptr(kv_tiles), ptr(row_masks), ptr(order), ptr(n_kv_tiles), s))
-    kv_flat = kv_flat[:n_partial]
-    full_flat = full_flat[:n_full]
+    return _block_mask_from_lists(S, nb, kv_num, kv_off, kv_flat[:n_partial], full_num,
+                                  full_off, full_flat[:n_full], q_pairs, kv_tiles, row_masks,
+                                  order, n_partial, n_full, n_kv_tiles, spec)
+
+
+def _block_mask_from_lists(S, nb, kv_num, kv_off, kv_flat, full_num, full_off, full_flat,
+                           q_pairs, kv_tiles, row_masks, order, n_partial, n_full, n_kv_tiles,
+                           spec) -> HierBlockMask:
+    dev = kv_num.device
 
     def padded(flat, off, num):
         # Flex-shaped [1,1,nb,nb] index tensor holding each row's list as prefix
-        out = torch.zeros(nb, nb, **i32)
+        out = torch.zeros(nb, nb, dtype=torch.int32, device=dev)
         if flat.numel():
             rows = torch.repeat_interleave(torch.arange(nb, device=dev), num.long())
             cols = torch.arange(flat.numel(), device=dev) - off[:-1].long()[rows]
@@ -389,6 +414,61 @@ def build_block_plan(spec: HierGroupingSpec, page_table: Optional[torch.Tensor] 
         full_offsets=full_off, kv_flat=kv_flat, full_flat=full_flat, q_pairs=q_pairs,
         kv_tiles=kv_tiles, row_masks=row_masks, order=order, n_partial=n_partial,
         n_full=n_full, n_kv_tiles=n_kv_tiles, spec=spec)
+
+
+def build_dense_block_plan(mask: Optional[torch.Tensor], S: int, device=None) -> HierBlockMask:
+    """128x128 block plan of a caller's dense mask (``[S,S]``, or with leading
+    unit dims; any non-zero element allows the pair, as ``flash_attention``'s
+    ``mask.to(bool)`` does, ``attention.py:47-54``) or of no mask (``None``:
+    every pair allowed).  The returned :class:`HierBlockMask` has no grouping
+    (``spec`` is None), so it always runs on the block plan."""
+    if mask is not None:
+        m = mask
+        while m.dim() > 2:
+            if m.shape[0] != 1:
+                raise NotImplementedError(
+                    f"the B200 attention takes one [S,S] mask for all batches and heads; got "
+                    f"{tuple(mask.shape)}")
+            m = m[0]
+        if tuple(m.shape) != (S, S):
+            raise ValueError(f"mask must be [S={S},S={S}], got {tuple(mask.shape)}")
+        if m.dtype != torch.bool and m.dtype != torch.uint8:
+            m = m.to(torch.bool)
+        dev = m.device if device is None else torch.device(device)
+        m = m.to(dev)
+        if m.stride(1) != 1:
+            m = m.contiguous()
+        ld = m.stride(0)
+    else:
+        dev = torch.device("cuda") if device is None else torch.device(device)
+        m, ld = None, S
+    nb = (S + 127) // 128
+    L = _lib.lib()
+    ws_bytes = ctypes.c_size_t()
+    check(L.hier_dense_block_workspace_size(S, ctypes.byref(ws_bytes)))
+    ws = torch.empty(max(ws_bytes.value, 1), dtype=torch.uint8, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    kv_num, full_num = torch.empty(nb, **i32), torch.empty(nb, **i32)
+    kv_off, full_off = torch.empty(nb + 1, **i32), torch.empty(nb + 1, **i32)
+    kv_flat, full_flat = torch.empty(nb * nb, **i32), torch.empty(nb * nb, **i32)
+    totals = torch.zeros(2, **i32)
+    s = stream_ptr(dev)
+    check(L.hier_dense_block_mask_build(ptr(m), S, ld, ptr(ws), ptr(kv_num), ptr(kv_off),
+                                        ptr(kv_flat), ptr(full_num), ptr(full_off),
+                                        ptr(full_flat), ptr(totals), s))
+    n_partial, n_full = (int(x) for x in totals.tolist())
+    n_pairs = (nb + 1) // 2
+    q_pairs = torch.empty(n_pairs, 8, **i32)
+    kv_tiles = torch.empty(max(n_partial + n_full, 1), 4, **i32)
+    row_masks = torch.empty(max(n_partial, 1), 128, 4, **i32)
+    order = torch.empty(n_pairs, **i32)
+    n_kv_tiles = torch.zeros(1, **i32)
+    check(L.hier_dense_block_plan_build(ptr(m), S, ld, ptr(ws), ptr(kv_off), ptr(kv_flat),
+                                        ptr(q_pairs), ptr(kv_tiles), ptr(row_masks), ptr(order),
+                                        ptr(n_kv_tiles), s))
+    return _block_mask_from_lists(S, nb, kv_num, kv_off, kv_flat[:n_partial], full_num,
+                                  full_off, full_flat[:n_full], q_pairs, kv_tiles, row_masks,
+                                  order, n_partial, n_full, n_kv_tiles, None)
 
 
 def _cache_size():
@@ -409,19 +489,25 @@ def build_stage2_hier_flex_block_mask(num_players, num_frames, num_patches, num_
                               num_local_hub_tokens, num_global_hub_tokens, num_frame_per_block,
                               local_attn_size, group_labels, active_group, direct_player, device,
                               membership, global_only, hier_no_local_hub)
+    bm = block_mask_for_spec(spec)
+    return bm, bm.S, bm.S_pad
+
+
+def block_mask_for_spec(spec: HierGroupingSpec) -> HierBlockMask:
+    """The :class:`HierBlockMask` of a grouping, from the cache of
+    :func:`build_stage2_hier_flex_block_mask` (keyed by grouping value)."""
     key = ("hier",) + spec.key()
     hit = _BLOCK_PLAN_CACHE.get(key)
     if hit is not None:
         _BLOCK_PLAN_CACHE.move_to_end(key)
-        return hit
+        return hit[0]
     bm = build_block_plan(spec)
-    res = (bm, bm.S, bm.S_pad)
     limit = _cache_size()
     if limit != 0:
-        _BLOCK_PLAN_CACHE[key] = res
+        _BLOCK_PLAN_CACHE[key] = (bm, bm.S, bm.S_pad)
         while limit > 0 and len(_BLOCK_PLAN_CACHE) > limit:
             _BLOCK_PLAN_CACHE.popitem(last=False)
-    return res
+    return bm
 
 
 def clear_block_mask_cache():

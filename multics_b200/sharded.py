@@ -378,6 +378,8 @@ class ShardedHierAttention:
         self.err = _dev_err(dev)
         self._sym = None
         self._peers = []
+        # a plan whose tables overflowed is refused here, before any launch
+        self.check_status()
         if self.transport == "peer":
             self._setup_peer()
 

@@ -378,3 +378,19 @@ def test_paged_pool_matches_contiguous(dev):
     o2 = attention_from_plan(q, kp, vp, paged, H)
     torch.cuda.synchronize()
     assert torch.equal(o1, o2)
+
+
+@pytest.mark.parametrize("name", case_names("mask"))
+def test_dense_mask_block_plan_bit_exact(dev, name):
+    """The block plan built from the reference's dense mask bytes has the
+    Flex block lists of the reference and re-expands to the same mask."""
+    from multics_b200.hier_masks import build_dense_block_plan
+
+    c = mask_case(name)
+    bm = build_dense_block_plan(torch.from_numpy(c["dense"]).to(dev), c["S"])
+    assert bm.S_pad == c["S_pad"]
+    assert np.array_equal(bm.kv_num_blocks.flatten().cpu().numpy(), c["kv_num_blocks"])
+    assert np.array_equal(bm.kv_flat.cpu().numpy(), c["kv_indices"])
+    assert np.array_equal(bm.full_kv_num_blocks.flatten().cpu().numpy(), c["full_kv_num_blocks"])
+    assert np.array_equal(bm.full_flat.cpu().numpy(), c["full_kv_indices"])
+    assert np.array_equal(expand_plan(bm), c["dense"])

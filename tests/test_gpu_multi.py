@@ -1,6 +1,9 @@
-"""Player-sharded layer over NCCL: one process per GPU (2 GPUs), exchange by
-all_to_all and hub merge by all-reduce, checked against the oracle.  Skipped
-on boxes with fewer than two GPUs."""
+"""Player-sharded layer over NCCL: one process per GPU (2 GPUs), group-mate
+frames by all_to_all or read in place from the peer's memory, hub rows merged
+by log-sum-exp over the ranks' partial rows (all-gathered, or read in place
+from the peers), checked against the oracle.  Skipped on boxes with fewer
+than two GPUs.  NVLink multicast is switched off in NCCL and in torch's
+symmetric memory: the test needs only plain peer pointers."""
 
 import os
 
@@ -22,7 +25,8 @@ def _rank_main(rank, world, port, q, transport):
     from multics_b200.sharded import ShardedHierAttention, ShardTopology
     from test_sharded_cpu import _regrouped_labels
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      TORCH_SYMM_MEM_DISABLE_MULTICAST="1")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60),
