@@ -46,226 +46,176 @@ __device__ __forceinline__ void bf16x8_to_f32(uint4 v, float (&f)[8]) {
   }
 }
 
-// One thread owns 8 consecutive channels of a token row (blockDim = dim/8);
-// blockIdx.y selects Q (0) or K (1).  The CTA walks chunks of kPrepRows
-// consecutive tokens; thread 0 streams each chunk's rows and RoPE rows into a
-// kPrepStages-deep shared-memory ring with bulk async copies, so several
-// chunks of loads are in flight per SM while the block computes one.  The
-// camera weights of a thread's 8 channels sit in registers.
-constexpr int kPrepRows = 8;
-constexpr int kPrepStages = 3;
+// One warp per token row.  Lane l owns the 8-channel chunks starting at
+// channels 8l + 256i (i = 0..dim/256-1): every load and store of a row is
+// one coalesced 512-byte access per chunk, the row's sum of squares is a
+// warp reduction (no block barrier), and the RoPE pairs of a lane are the
+// same for all its chunks (channel offsets 256i are whole heads apart), so
+// a lane reads 4 (cos, sin) pairs per row.  A warp walks a contiguous run of
+// rows; the camera projection W cam_r of its channels (camera weights
+// transposed into shared memory, fp32 sums, kept as bf16 in the warp's slice
+// of shared memory) is recomputed only when the camera row changes: the rows
+// of a player frame share one camera row and hub rows have none.
+constexpr int kPrepWarps = 12;
+constexpr int kPrepMaxChunks = 12;  // dim <= 256 * 12 = 3072
 
-__device__ int g_prep_err;  // pipeline wait timeouts of the prologue kernel
+// chunk i of a lane exists (a row of dim = 256k + 128 leaves the upper half of
+// the lanes without a last chunk)
+__device__ __forceinline__ bool chunk_ok(int dim, int lane, int i) { return 8 * lane + 256 * i < dim; }
 
-__host__ __device__ constexpr int align16i(int x) { return (x + 15) & ~15; }
-
-template <int CAM>
-__global__ void __launch_bounds__(384, 1) prep_qk_kernel(PrepArgs a) {
-  constexpr int R = kPrepRows;
-  extern __shared__ __align__(128) uint8_t ring[];
-  __shared__ uint64_t full[kPrepStages];
-  __shared__ float red[R][12];
-  __shared__ float rsq[R];
-  __shared__ float camv[R][CAM > 0 ? CAM : 1];
+template <int CAM, int NCH>
+__global__ void __launch_bounds__(kPrepWarps * 32, 1) prep_qk_kernel(PrepArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  // [CAM][dim] bf16 transposed camera weights, [dim] bf16 norm weights, then
+  // per warp its projection [NCH][32 lanes][8 channels] bf16
+  __nv_bfloat16* wt = reinterpret_cast<__nv_bfloat16*>(smem);
+  __nv_bfloat16* nws = wt + CAM * a.dim;
+  uint4* proj = reinterpret_cast<uint4*>(nws + a.dim) + (threadIdx.x >> 5) * (NCH * 32);
   const bool is_k = blockIdx.y == 1;
   const __nv_bfloat16* x = is_k ? a.kx : a.qx;
   const __nv_bfloat16* wc = is_k ? a.wck : a.wcq;
   const __nv_bfloat16* nw = is_k ? a.nkw : a.nqw;
   __nv_bfloat16* out = is_k ? a.k_out : a.q_out;
-  const int t = threadIdx.x;
-  const int d0 = t * 8;
-  const int nt = blockDim.x;
-  const int nwarps = nt / 32;
-  const int half = a.D / 2;
-  const int row_bytes = a.dim * 2;
-  const int fr_bytes = half * 8;  // (cos, sin) float pairs of one token
-  const int stage_bytes = align16i(R * (row_bytes + fr_bytes));
-  // camera weights W[d0 + i][c] of this thread's channels, bf16 pairs
-  constexpr int kc = CAM > 0 ? CAM : 1;
-  uint32_t wr[kc][4];
-  if (CAM > 0) {
-    const uint16_t* w16 = reinterpret_cast<const uint16_t*>(wc);
-#pragma unroll
-    for (int c = 0; c < CAM; ++c)
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        wr[c][i] = (uint32_t)w16[(int64_t)(d0 + 2 * i) * CAM + c] |
-                   ((uint32_t)w16[(int64_t)(d0 + 2 * i + 1) * CAM + c] << 16);
+  for (int e = threadIdx.x; e < CAM * a.dim; e += blockDim.x) {
+    const int d = e / CAM, c = e % CAM;  // coalesced reads of W[d][c]
+    wt[c * a.dim + d] = wc[e];
   }
-  float nv[8];
-  bf16x8_to_f32(*reinterpret_cast<const uint4*>(nw + d0), nv);
-  const int pair0 = (d0 % a.D) / 2;
-  const int64_t n_chunks = (a.S + R - 1) / R;
-  if (t == 0) {
-    for (int s = 0; s < kPrepStages; ++s) mbar_init(full + s, 1);
-    fence_mbar_init();
-  }
+  for (int e = threadIdx.x; e < a.dim / 8; e += blockDim.x)
+    reinterpret_cast<uint4*>(nws)[e] = reinterpret_cast<const uint4*>(nw)[e];
   __syncthreads();
-  // chunk i of this CTA is chunk blockIdx.x + i * gridDim.x of the sequence
-  auto issue = [&](int64_t i) {
-    const int64_t c = blockIdx.x + i * (int64_t)gridDim.x;
-    if (c >= n_chunks) return;
-    const int64_t r0 = c * R;
-    const int nr = (int)min((int64_t)R, a.S - r0);
-    uint8_t* st = ring + (i % kPrepStages) * stage_bytes;
-    uint64_t* bar = full + (i % kPrepStages);
-    mbar_arrive_expect_tx(bar, nr * (row_bytes + fr_bytes));
-    for (int r = 0; r < nr; ++r)
-      bulk_load(st + r * row_bytes, x + (r0 + r) * a.x_stride, row_bytes, bar);
-    bulk_load(st + R * row_bytes, a.freqs + r0 * half, nr * fr_bytes, bar);
-  };
-  if (t == 0)
-    for (int i = 0; i < kPrepStages - 1; ++i) issue(i);
-  // camera rows are tiny: plain loads, one chunk ahead, through registers
-  const int n_cam = CAM > 0 ? R * CAM : 0;
-  // R*CAM <= 128 camera values per chunk, >= 32 threads per block
-  constexpr int kCamPer = (R * kMaxCam + 31) / 32;
-  float cam_r[kCamPer];
-  auto fetch_cam = [&](int64_t i) {
-    const int64_t r0 = (blockIdx.x + i * (int64_t)gridDim.x) * R;
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * kPrepWarps + (threadIdx.x >> 5);
+  const int64_t nw_total = (int64_t)gridDim.x * kPrepWarps;
+  const int64_t per = (a.S + nw_total - 1) / nw_total;
+  const int64_t r_begin = gw * per, r_end = min(a.S, r_begin + per);
+  const int half = a.D / 2;
+  const int pair0 = (8 * lane % a.D) / 2;  // first RoPE pair of every chunk of this lane
+  float cam_prev = 0.f;  // lane c < CAM: camera value c of the projected row
+  bool have_proj = false;
+  const float inv_dim = 1.f / (float)a.dim;
+  for (int64_t r = r_begin; r < r_end; ++r) {
+    const __nv_bfloat16* xr = x + r * a.x_stride;
+    uint4 xv[NCH];
 #pragma unroll
-    for (int k = 0; k < kCamPer; ++k) {
-      const int j = t + k * nt;
-      cam_r[k] = 0.f;
-      if (j < n_cam && r0 + j / kc < a.S) cam_r[k] = __bfloat162float(a.cam[(r0 + j / kc) * CAM + j % kc]);
-    }
-  };
-  if (CAM > 0) fetch_cam(0);
-  for (int64_t i = 0;; ++i) {
-    const int64_t row0 = (blockIdx.x + i * (int64_t)gridDim.x) * R;
-    if (row0 >= a.S) break;
-    if (t == 0) issue(i + kPrepStages - 1);  // into the stage freed by iteration i-1
+    for (int i = 0; i < NCH; ++i)
+      xv[i] = chunk_ok(a.dim, lane, i) ? *reinterpret_cast<const uint4*>(xr + 8 * lane + 256 * i)
+                                       : make_uint4(0u, 0u, 0u, 0u);
+    const float4* fr = reinterpret_cast<const float4*>(a.freqs + r * half + pair0);
+    const float4 f0 = fr[0], f1 = fr[1];
     if (CAM > 0) {
+      const float cv = lane < CAM ? __bfloat162float(a.cam[r * CAM + lane]) : 0.f;
+      const bool same = __all_sync(0xffffffffu, cv == cam_prev);
+      if (!(same && have_proj)) {
+        const bool zero = __all_sync(0xffffffffu, cv == 0.f);
+        const bool ok_last = chunk_ok(a.dim, lane, NCH - 1);
 #pragma unroll
-      for (int k = 0; k < kCamPer; ++k) {
-        const int j = t + k * nt;
-        if (j < n_cam) camv[j / kc][j % kc] = cam_r[k];
-      }
-      fetch_cam(i + 1);
-    }
-    const uint8_t* st = ring + (i % kPrepStages) * stage_bytes;
-    mbar_wait(full + (i % kPrepStages), (uint32_t)((i / kPrepStages) & 1), &g_prep_err, 1);
-    __syncthreads();  // camv visible
-    const int nr = (int)min((int64_t)R, a.S - row0);
-    // rows of one player frame share their camera row: project it once
-    bool shared_cam = true;
-    float proj[8];
+        for (int i = 0; i < NCH; ++i) {
+          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (!zero) {
 #pragma unroll
-    for (int q = 0; q < 8; ++q) proj[q] = 0.f;
-    auto project = [&](int r) {  // proj = W cam_r for this thread's 8 channels
+            for (int c = 0; c < CAM; ++c) {
+              // every lane takes part in the shuffle, lanes without a last chunk too
+              const float cc = __shfl_sync(0xffffffffu, cv, c);
+              if (i + 1 < NCH || ok_last) {
+                float w[8];
+                bf16x8_to_f32(*reinterpret_cast<const uint4*>(wt + c * a.dim + 8 * lane + 256 * i), w);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) proj[q] = 0.f;
-#pragma unroll
-      for (int c = 0; c < CAM; ++c) {
-        float w[8];
-        bf16x8_to_f32(make_uint4(wr[c][0], wr[c][1], wr[c][2], wr[c][3]), w);
-        const float cv = camv[r][c];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) proj[q] = fmaf(cv, w[q], proj[q]);
-      }
-    };
-    if (CAM > 0) {
-#pragma unroll
-      for (int r = 1; r < R; ++r)
-#pragma unroll
-        for (int c = 0; c < CAM; ++c) shared_cam &= camv[r][c] == camv[0][c];
-      if (shared_cam) project(0);
-    }
-    // pass 1: sums of squares of all rows, reduced together
-    float ss[R];
-    if (CAM == 0 || shared_cam) {
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        float xv[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(st + r * row_bytes + d0 * 2), xv);
-        float sq = 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float v = CAM > 0 ? xv[q] + proj[q] : xv[q];
-          sq = fmaf(v, v, sq);
+                for (int q = 0; q < 8; ++q) acc[q] = fmaf(cc, w[q], acc[q]);
+              }
+            }
+          }
+          proj[i * 32 + lane] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                           pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
         }
-        ss[r] = r < nr ? sq : 0.f;
-      }
-    } else {  // a chunk across a frame boundary: one projection per row
-#pragma unroll 1
-      for (int r = 0; r < R; ++r) {
-        project(r);
-        float xv[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(st + r * row_bytes + d0 * 2), xv);
-        float sq = 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) sq = fmaf(xv[q] + proj[q], xv[q] + proj[q], sq);
-        ss[r] = r < nr ? sq : 0.f;
+        cam_prev = cv;
+        have_proj = true;
       }
     }
-    // warp sums of the R = 8 rows by a halving exchange: after the offsets
-    // 16, 8, 4 each lane holds one row's partial (row = lane bits 4, 3, 2),
-    // then offsets 2 and 1 finish it (9 shuffles instead of 40)
-    static_assert(R == 8, "the row-sum exchange below assumes 8 rows per chunk");
-    {
-      const int lane = t & 31;
+    // pass 1: sum of squares of (x + proj) over the row
+    float ss = 0.f;
 #pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        const int o = 16 >> k, keep = (lane & o) ? 1 : 0;
-        const int n = 4 >> k;  // values kept after this step
-#pragma unroll
-        for (int i = 0; i < n; ++i) {
-          const float send = keep ? ss[i] : ss[i + n];
-          const float recv = __shfl_xor_sync(0xffffffffu, send, o);
-          ss[i] = (keep ? ss[i + n] : ss[i]) + recv;
-        }
-      }
-      ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], 2);
-      ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], 1);
-      if ((lane & 3) == 0) {
-        const int row = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-        red[row][t >> 5] = ss[0];
-      }
-    }
-    __syncthreads();
-    if (t < R) {  // row scales once per chunk
-      float tot = 0.f;
-      for (int w = 0; w < nwarps; ++w) tot += red[t][w];
-      rsq[t] = rsqrtf(tot / a.dim + a.eps);
-    }
-    __syncthreads();
-    // pass 2: normalise, rotate, store
-    const float4* fr = reinterpret_cast<const float4*>(st + R * row_bytes);
-    auto finish = [&](int r) {
-      const float rs = rsq[r];
-      float xv[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(st + r * row_bytes + d0 * 2), xv);
+    for (int i = 0; i < NCH; ++i) {
+      float xf[8], pf[8];
+      bf16x8_to_f32(xv[i], xf);
       if (CAM > 0) {
+        bf16x8_to_f32(proj[i * 32 + lane], pf);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) xv[q] += proj[q];
+        for (int q = 0; q < 8; ++q) xf[q] += pf[q];
       }
-      const float4 f0 = fr[r * (half / 2) + pair0 / 2], f1 = fr[r * (half / 2) + pair0 / 2 + 1];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ss = fmaf(xf[q], xf[q], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rs = rsqrtf(ss * inv_dim + a.eps);
+    // pass 2: normalise, rotate, store
+    const int64_t dst = a.out_rows ? (int64_t)a.out_rows[r] : r;
+    __nv_bfloat16* orow = out + dst * a.out_stride;
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      float xf[8], pf[8], wf[8];
+      bf16x8_to_f32(xv[i], xf);
+      if (CAM > 0) {
+        bf16x8_to_f32(proj[i * 32 + lane], pf);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) xf[q] += pf[q];
+      }
+      bf16x8_to_f32(chunk_ok(a.dim, lane, i)
+                        ? *reinterpret_cast<const uint4*>(nws + 8 * lane + 256 * i)
+                        : make_uint4(0u, 0u, 0u, 0u), wf);
       uint4 o;
       uint32_t* po = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const float4 f2 = q < 2 ? f0 : f1;
-        const float c = (q & 1) ? f2.z : f2.x;
-        const float s = (q & 1) ? f2.w : f2.y;
-        const float a0 = xv[2 * q] * rs * nv[2 * q], a1 = xv[2 * q + 1] * rs * nv[2 * q + 1];
+        const float4 f = q < 2 ? f0 : f1;
+        const float c = (q & 1) ? f.z : f.x;
+        const float s = (q & 1) ? f.w : f.y;
+        const float a0 = xf[2 * q] * rs * wf[2 * q], a1 = xf[2 * q + 1] * rs * wf[2 * q + 1];
         po[q] = pack_bf16x2(a0 * c - a1 * s, a0 * s + a1 * c);
       }
-      const int64_t dst = a.out_rows ? (int64_t)a.out_rows[row0 + r] : row0 + r;
-      *reinterpret_cast<uint4*>(out + dst * a.out_stride + d0) = o;
-    };
-    if (CAM == 0 || shared_cam) {  // proj still holds the chunk's shared projection
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-        if (r < nr) finish(r);
-    } else {
-#pragma unroll 1
-      for (int r = 0; r < nr; ++r) {
-        project(r);
-        finish(r);
-      }
+      if (chunk_ok(a.dim, lane, i)) *reinterpret_cast<uint4*>(orow + 8 * lane + 256 * i) = o;
     }
-    __syncthreads();  // stage and red free for the next chunks
   }
+}
+
+template <int CAM>
+int prep_launch(const PrepArgs& p, int sms, cudaStream_t st) {
+  const int nch = (p.dim + 255) / 256;
+  // weights and norm, then per warp NCH chunks x 32 lanes x 16 bytes of projection
+  const size_t smem = (size_t)(CAM + 1) * p.dim * 2 + (CAM > 0 ? (size_t)kPrepWarps * nch * 512 : 0);
+  const int64_t warps = (p.S + 3) / 4;  // at least 4 rows per warp
+  int64_t blocks = (warps + kPrepWarps - 1) / kPrepWarps;
+  if (blocks > (sms + 1) / 2) blocks = (sms + 1) / 2;  // with Q and K: one CTA per SM
+  const dim3 grid((unsigned)blocks, 2);
+  switch (nch) {
+#define HIER_PREP_CASE(n)                                                                     \
+  case n:                                                                                     \
+    HIER_CHECK_CUDA(cudaFuncSetAttribute(prep_qk_kernel<CAM, n>,                              \
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,         \
+                                         (int)smem),                                          \
+                    "cudaFuncSetAttribute(prep_qk_kernel)");                                  \
+    prep_qk_kernel<CAM, n><<<grid, kPrepWarps * 32, smem, st>>>(p);                           \
+    break;
+    HIER_PREP_CASE(1)
+    HIER_PREP_CASE(2)
+    HIER_PREP_CASE(3)
+    HIER_PREP_CASE(4)
+    HIER_PREP_CASE(5)
+    HIER_PREP_CASE(6)
+    HIER_PREP_CASE(7)
+    HIER_PREP_CASE(8)
+    HIER_PREP_CASE(9)
+    HIER_PREP_CASE(10)
+    HIER_PREP_CASE(11)
+    HIER_PREP_CASE(12)
+#undef HIER_PREP_CASE
+    default:
+      set_error(HIER_ENOTIMPL, "hier_prep_qk supports dim = 128..3072 in steps of 128; got %d",
+                p.dim);
+      return HIER_ENOTIMPL;
+  }
+  HIER_CHECK_CUDA(cudaGetLastError(), "prep_qk_kernel launch");
+  return HIER_OK;
 }
 
 }  // namespace hier
@@ -279,8 +229,10 @@ extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, co
                             const int32_t* out_rows, void* stream) {
   clear_error();
   const int dim = H * D;
-  if (dim % 8 != 0 || dim / 8 > 384 || dim / 8 < 32 || (dim / 8) % 32 != 0 || D % 8 != 0) {
-    set_error(HIER_ENOTIMPL, "hier_prep_qk needs dim = H*D with dim/8 a multiple of 32 and <= 384; got dim=%d", dim);
+  if (dim % 128 != 0 || dim > 256 * kPrepMaxChunks || D <= 0 || D % 8 != 0 || 256 % D != 0) {
+    set_error(HIER_ENOTIMPL,
+              "hier_prep_qk needs dim = H*D a multiple of 128 up to %d and head_dim dividing 256; "
+              "got dim=%d head_dim=%d", 256 * kPrepMaxChunks, dim, D);
     return HIER_ENOTIMPL;
   }
   if (cam && (cam_dim <= 0 || cam_dim > kMaxCam || !wcq || !wck)) {
@@ -307,9 +259,10 @@ extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, co
   p.k_out = (__nv_bfloat16*)k_out;
   p.out_stride = out_stride;
   p.out_rows = out_rows;
-  const int threads = dim / 8;
   if (x_stride % 8 || out_stride % 8 || (reinterpret_cast<uintptr_t>(qx) & 15) ||
-      (reinterpret_cast<uintptr_t>(kx) & 15) || (reinterpret_cast<uintptr_t>(freqs) & 15)) {
+      (reinterpret_cast<uintptr_t>(kx) & 15) || (reinterpret_cast<uintptr_t>(freqs) & 15) ||
+      (reinterpret_cast<uintptr_t>(q_out) & 15) || (reinterpret_cast<uintptr_t>(k_out) & 15) ||
+      (reinterpret_cast<uintptr_t>(nqw) & 15) || (reinterpret_cast<uintptr_t>(nkw) & 15)) {
     set_error(HIER_EVALUE, "hier_prep_qk needs 16-byte aligned rows (strides %lld, %lld)",
               (long long)x_stride, (long long)out_stride);
     return HIER_EVALUE;
@@ -317,31 +270,10 @@ extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, co
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // one resident block per SM for each of Q and K
-  const int64_t chunks = (S + kPrepRows - 1) / kPrepRows;
-  const int64_t blocks = chunks < (sms + 1) / 2 ? chunks : (sms + 1) / 2;
-  const dim3 grid((unsigned)blocks, 2);
   cudaStream_t st = (cudaStream_t)stream;
-  const size_t ring = (size_t)kPrepStages * align16i(kPrepRows * (dim * 2 + (D / 2) * 8));
-  if (!cam) {
-    HIER_CHECK_CUDA(cudaFuncSetAttribute(prep_qk_kernel<0>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ring),
-                    "cudaFuncSetAttribute(prep_qk_kernel)");
-    prep_qk_kernel<0><<<grid, threads, ring, st>>>(p);
-  } else if (cam_dim == 12) {
-    HIER_CHECK_CUDA(cudaFuncSetAttribute(prep_qk_kernel<12>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ring),
-                    "cudaFuncSetAttribute(prep_qk_kernel)");
-    prep_qk_kernel<12><<<grid, threads, ring, st>>>(p);
-  } else if (cam_dim == 16) {
-    HIER_CHECK_CUDA(cudaFuncSetAttribute(prep_qk_kernel<16>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ring),
-                    "cudaFuncSetAttribute(prep_qk_kernel)");
-    prep_qk_kernel<16><<<grid, threads, ring, st>>>(p);
-  } else {
-    set_error(HIER_ENOTIMPL, "hier_prep_qk supports cam_dim 12 or 16; got %d", cam_dim);
-    return HIER_ENOTIMPL;
-  }
-  HIER_CHECK_CUDA(cudaGetLastError(), "prep_qk_kernel launch");
-  return HIER_OK;
+  if (!cam) return prep_launch<0>(p, sms, st);
+  if (cam_dim == 12) return prep_launch<12>(p, sms, st);
+  if (cam_dim == 16) return prep_launch<16>(p, sms, st);
+  set_error(HIER_ENOTIMPL, "hier_prep_qk supports cam_dim 12 or 16; got %d", cam_dim);
+  return HIER_ENOTIMPL;
 }

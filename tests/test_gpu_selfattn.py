@@ -151,7 +151,8 @@ def test_selfattention_forward_accepts_every_mask_form():
     cd = cam.unsqueeze(0).to(dev)
     outs = {}
     for name, m in (("block", bm), ("dense_spec", dm), ("plain", plain), ("float", as_float)):
-        outs[name] = layer(xd, fd, m, cd)
+        with torch.no_grad():
+            outs[name] = layer(xd, fd, m, cd)
         torch.cuda.synchronize()
         _check(outs[name].float().cpu().numpy()[0], ref)
     # the grouping-carrying mask runs on the grouping's own plan: same bits
@@ -166,8 +167,9 @@ def test_selfattention_forward_unmasked(shape):
     layer, x, cam, freqs, S = _layer_and_inputs(P, T, h, w, N, KL, KG, H, seed=9)
     _, ref, _ = _fp32_forward(layer, x, cam, freqs, H, None)
     dev = torch.device("cuda")
-    out = layer(x.to(dev), torch.from_numpy(freqs).float().to(dev), None,
-                cam.unsqueeze(0).to(dev))
+    with torch.no_grad():
+        out = layer(x.to(dev), torch.from_numpy(freqs).float().to(dev), None,
+                    cam.unsqueeze(0).to(dev))
     torch.cuda.synchronize()
     _check(out.float().cpu().numpy()[0], ref)
 
@@ -194,7 +196,8 @@ def test_dense_plan_of_random_mask_with_empty_rows():
     has = dense.any(1)
     f = lambda t: t.detach().float().cpu().numpy()  # noqa: E731
     xf = x.to(dev)[0]
-    qx, kx, v = layer.q(xf), layer.k(xf), layer.v(xf)
+    with torch.no_grad():
+        qx, kx, v = layer.q(xf), layer.k(xf), layer.v(xf)
     got = hier_attention_layer(qx, kx, v, torch.from_numpy(freqs).float().to(dev),
                                torch.from_numpy(dense).to(dev), H,
                                norm_q_weight=layer.norm_q.weight, norm_k_weight=layer.norm_k.weight,
