@@ -196,9 +196,16 @@ int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, const void* c
  *       by q_pairs are written; rows whose key set is empty are written as 0
  *       (the cached backends' contract, hier_segmented_attention.py:104-109).
  *   q_pairs [n_pairs][8], kv_tiles [][4], row_masks, order [n_pairs] (or
- *       NULL) in the format of hier_block_plan_build: each CTA computes the
- *       two 128-row query tiles of a pair for one head.
+ *       NULL) in the format of hier_block_plan_build: a work item is the two
+ *       128-row query tiles of a pair for one head, taken in the order
+ *       (head, rank in order[]) by one persistent CTA per SM.
  *   dev_err: device int32, set non-zero if a pipeline wait timed out.
+ * The CTAs claim work items from a counter in a fixed device array of the
+ * library (64 counters per device, one per launch in turn, zeroed on the
+ * launch stream; nothing is allocated).  Up to 64 attention launches may be
+ * in flight at the same time on one device.  The first launch on a device
+ * looks the array up (cudaGetSymbolAddress) and should come before any
+ * stream capture.
  * Replaces the attention kernels of the reference backends: masked SDPA
  * (attention.py:39-54), FlexAttention (attention.py:322-353), the Triton
  * segmented / tiled128 kernels (kernels/hier_segmented_attention.py:27-114,
@@ -527,10 +534,15 @@ int hier_lse_gather_merge_peers(const void* const* o_bases, const float* const* 
 int hier_selftest_umma(const void* a, const void* b, float* c_ss, float* c_mn, float* c_ts,
                        int32_t* dev_err, void* stream);
 
-/* Self-test of the FMA-pipe exp2 used for part of the softmax exponentials
- * (no reference counterpart): y[i] = 2^x[i] for n fp32 values, 0 for
- * x <= -127. */
-int hier_selftest_exp2(const float* x, float* y, int64_t n, void* stream);
+/* Self-test of the bounded pipeline wait (no reference counterpart; the
+ * reference has no device-side waits): one thread waits, giving up after
+ * limit_cycles SM clock cycles (1 .. 4e9, the kernels' own limit), on a
+ * barrier phase that nothing completes.  Afterwards *dev_err holds
+ * 1 (wait timed out) | (30 << 8) (wait site) if it was 0, and *dev_cycles the
+ * cycles waited (-1 if the wait had not given up).  This is how every kernel
+ * of the library reports a stalled pipeline instead of hanging the device. */
+int hier_selftest_wait_timeout(int64_t limit_cycles, int32_t* dev_err, int64_t* dev_cycles,
+                               void* stream);
 
 #ifdef __cplusplus
 }

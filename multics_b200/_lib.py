@@ -163,7 +163,7 @@ _SIGS = {
                                             c_int32, c_int32, _P, _P, c_int64, _P, c_int64, _P,
                                             _P]),
     "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),
-    "hier_selftest_exp2": (c_int, [_P, _P, c_int64, _P]),
+    "hier_selftest_wait_timeout": (c_int, [c_int64, _P, _P, _P]),
 }
 
 _LIB = None

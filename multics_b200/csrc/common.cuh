@@ -70,20 +70,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase.  Gives up after roughly two seconds of
-// SM clock, records DEV_WAIT_TIMEOUT (with the wait site) in *err and
-// returns false, so a broken pipeline ends the kernel instead of hanging the
-// device.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site) {
+// Bounded wait on an mbarrier phase.  Gives up after `limit` SM clock
+// cycles, records DEV_WAIT_TIMEOUT (with the wait site) in *err and returns
+// false, so a broken pipeline ends the kernel instead of hanging the device.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* err,
+                                                int site, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > 4000000000LL) {
+    if (clock64() - t0 > limit) {
       if (err) atomicCAS(err, 0, DEV_WAIT_TIMEOUT | (site << 8));
       return false;
     }
   }
+}
+
+// The kernels' waits: roughly two seconds of SM clock.
+constexpr long long kWaitLimitCycles = 4000000000LL;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site) {
+  return mbar_wait_limit(bar, parity, err, site, kWaitLimitCycles);
 }
 
 // 2-D tiled TMA load (no multicast) into shared memory, completing on `bar`.
@@ -249,35 +255,6 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
-}
-
-// 2^x for two packed fp32 lanes on the FMA pipe, for moving part of the
-// softmax exponentials off the MUFU unit.  Cody-Waite range reduction
-// x = n + f with n = rint(x) (by adding 1.5 * 2^23, which leaves n in the low
-// mantissa bits) and f in [-1/2, 1/2], then a degree-3 minimax polynomial for
-// 2^f on [-1/2, 1/2] (coefficients fitted for this library with the Remez
-// exchange algorithm on the relative error; max relative error 7.5e-5), then
-// scaling by 2^n built directly as the float with exponent field n + 127.
-// Inputs are clamped to >= -127 so that masked (-inf) entries give exactly 0.
-__device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t x) {
-  float x0, x1;
-  f2_unpack(x, x0, x1);
-  x0 = fmaxf(x0, -127.f);
-  x1 = fmaxf(x1, -127.f);
-  const uint64_t xc = f2_pack(x0, x1);
-  const uint64_t magic = f2_pack(12582912.f, 12582912.f);
-  const uint64_t t = f2_add(xc, magic);
-  const uint64_t nf = f2_add(t, f2_pack(-12582912.f, -12582912.f));
-  const uint64_t f = f2_fma(nf, f2_pack(-1.f, -1.f), xc);
-  uint64_t p = f2_fma(f2_pack(0.0551716685f, 0.0551716685f), f, f2_pack(0.242611125f, 0.242611125f));
-  p = f2_fma(p, f, f2_pack(0.693260968f, 0.693260968f));
-  p = f2_fma(p, f, f2_pack(0.999928057f, 0.999928057f));
-  float t0, t1;
-  f2_unpack(t, t0, t1);
-  // bits(t) = 0x4B400000 + n; exponent field n + 127 shifted into place
-  const uint32_t e0 = (__float_as_uint(t0) << 23) - 0xC0800000u;
-  const uint32_t e1 = (__float_as_uint(t1) << 23) - 0xC0800000u;
-  return f2_mul(p, f2_pack(__uint_as_float(e0), __uint_as_float(e1)));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(kPrepWarps * 32, 1) prep_qk_kernel(PrepArgs a)
   const __nv_bfloat16* nw = is_k ? a.nkw : a.nqw;
   __nv_bfloat16* out = is_k ? a.k_out : a.q_out;
   for (int e = threadIdx.x; e < CAM * a.dim; e += blockDim.x) {
-    const int d = e / CAM, c = e % CAM;  // coalesced reads of W[d][c]
+    const int d = e / (CAM > 0 ? CAM : 1), c = e % (CAM > 0 ? CAM : 1);  // coalesced reads of W[d][c]
     wt[c * a.dim + d] = wc[e];
   }
   for (int e = threadIdx.x; e < a.dim / 8; e += blockDim.x)

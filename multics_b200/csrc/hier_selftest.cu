@@ -1,6 +1,8 @@
-// Self-test of the tcgen05 operand encodings used by the attention kernel:
-// SS form with K-major A and B, SS form with an MN-major B, and the TS form
-// with A read from tensor memory (bf16 pairs packed per 32-bit column).
+// Self-tests: the tcgen05 operand encodings used by the attention kernel (SS
+// form with K-major A and B, SS form with an MN-major B, and the TS form with
+// A read from tensor memory, bf16 pairs packed per 32-bit column), and the
+// bounded mbarrier wait that every pipeline wait uses (it must give up and
+// report, never hang).
 
 #include <stdio.h>
 
@@ -122,26 +124,30 @@ extern "C" int hier_selftest_umma(const void* a, const void* b, float* c_ss, flo
 }
 
 namespace hier {
-__global__ void selftest_exp2_kernel(const float* x, float* y, int64_t n) {
-  const int64_t i = 2 * (blockIdx.x * (int64_t)blockDim.x + threadIdx.x);
-  if (i + 1 < n) {
-    float a, b;
-    f2_unpack(exp2_poly_x2(f2_pack(x[i], x[i + 1])), a, b);
-    y[i] = a;
-    y[i + 1] = b;
-  } else if (i < n) {
-    float a, b;
-    f2_unpack(exp2_poly_x2(f2_pack(x[i], 0.f)), a, b);
-    y[i] = a;
-  }
+// One thread waits, with the given limit, on a fresh mbarrier phase that
+// nothing completes: the wait must give up, record DEV_WAIT_TIMEOUT with the
+// site in *err and report the cycles it waited.
+__global__ void selftest_wait_kernel(long long limit, int* err, long long* cycles) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  const long long t0 = clock64();
+  const bool done = mbar_wait_limit(&bar, 0, err, 30, limit);
+  *cycles = done ? -1 : clock64() - t0;
 }
 }  // namespace hier
 
-extern "C" int hier_selftest_exp2(const float* x, float* y, int64_t n, void* stream) {
+extern "C" int hier_selftest_wait_timeout(int64_t limit_cycles, int32_t* dev_err,
+                                          int64_t* dev_cycles, void* stream) {
   clear_error();
-  if (n <= 0) return HIER_OK;
-  const int64_t pairs = (n + 1) / 2;
-  selftest_exp2_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, (cudaStream_t)stream>>>(x, y, n);
-  HIER_CHECK_CUDA(cudaGetLastError(), "selftest_exp2_kernel launch");
+  if (limit_cycles <= 0 || limit_cycles > kWaitLimitCycles || !dev_err || !dev_cycles) {
+    set_error(HIER_EVALUE, "wait limit must be 1..%lld cycles with both outputs given",
+              (long long)kWaitLimitCycles);
+    return HIER_EVALUE;
+  }
+  selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(
+      (long long)limit_cycles, dev_err, reinterpret_cast<long long*>(dev_cycles));
+  HIER_CHECK_CUDA(cudaGetLastError(), "selftest_wait_kernel launch");
   return HIER_OK;
 }

@@ -62,28 +62,6 @@ def test_umma_operand_selftest(dev):
     torch.testing.assert_close(outs[2], af @ bf, atol=1e-2, rtol=1e-3)
 
 
-def test_poly_exp2_matches_exp2f(dev):
-    """The FMA-pipe exp2 used for part of the softmax vs CUDA exp2f (torch.exp2)
-    and a float64 reference: relative error < 1e-4, exactly 0 at and below -127
-    (masked keys)."""
-    from multics_b200 import _lib
-    from multics_b200._lib import ptr, stream_ptr
-
-    x = torch.cat([torch.linspace(-126.0, 12.0, 1 << 20), torch.rand(1 << 16) * 2 - 1,
-                   torch.tensor([-127.0, -130.0, -1e30, float("-inf"), 0.0, 1.0, -0.5, 0.5])])
-    x = x.to(dev)
-    y = torch.empty_like(x)
-    _lib.check(_lib.lib().hier_selftest_exp2(ptr(x), ptr(y), x.numel(), stream_ptr()))
-    torch.cuda.synchronize()
-    fin = x > -126.5
-    ref64 = torch.exp2(x.double())
-    rel = ((y.double() - ref64) / ref64)[fin].abs().max().item()
-    assert rel < 1e-4, rel
-    rel_f = ((y - torch.exp2(x)) / torch.exp2(x))[fin].abs().max().item()
-    assert rel_f < 1e-4, rel_f
-    assert torch.all(y[x <= -127.0] == 0)
-
-
 @pytest.mark.parametrize("name", case_names("mask"))
 def test_dense_mask_bit_exact(dev, name):
     from multics_b200.hier_masks import build_stage2_hier_self_attn_mask
