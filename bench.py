@@ -45,6 +45,8 @@ def parse():
                     help="cfg2 (default at 1 GPU) or cfg4/cfg5 (default cfg4 when sharded)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-dit", action="store_true",
+                    help="skip the configuration-3 DiT denoising-step measurement")
     ap.add_argument("--transport", default="peer", choices=["peer", "exchange"],
                     help="sharded runs: how group-mate frames on other GPUs are read")
     ap.add_argument("--path", default=None, choices=["segments", "block", "shard"],
@@ -484,6 +486,13 @@ def run_ours(args, rank, world, local_rank):
         line["clocks"] = clocks
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, sample_seconds=15.0)
+    if world == 1:
+        line["cached_step"] = run_cached_step()
+        line["plans_rebuild_ms"] = plans_rebuild(cfg, dev)
+    if world == 1 and not args.no_dit:
+        del inp, q_buf, k_buf, o_buf
+        torch.cuda.empty_cache()
+        line["dit_step"] = run_dit()
     return line
 
 
@@ -560,6 +569,135 @@ def run_e2e(args, cfg, inp, bm, ft, dev, useful_flops, world):
             "d2h_bytes_per_step": ho[0].numel() * ho[0].element_size(), "steps": steps,
             "pipelined": "inputs of step i+1 upload and outputs of step i-1 download "
                          "while step i computes"}
+
+
+def plans_rebuild(cfg, dev):
+    """A second build of the block mask and the sequence plan for a fresh
+    grouping value (the first build in the run also pays the lazy loading of
+    the builder kernels): host wall time with the device synchronised on
+    both sides, and the device time between CUDA events."""
+    import torch
+
+    from multics_b200.attention import sequence_plan
+    from multics_b200.hier_masks import build_stage2_hier_flex_block_mask, clear_block_mask_cache
+
+    labels = torch.tensor([cfg.groups[::-1] if cfg.groups else [0] * cfg.P] * cfg.T, device=dev)
+    clear_block_mask_cache()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    a.record()
+    bm, _, _ = build_stage2_hier_flex_block_mask(cfg.P, cfg.T, cfg.L, cfg.N, cfg.KL, cfg.KG,
+                                                 cfg.n_block, cfg.local_attn, labels, None,
+                                                 cfg.direct, dev)
+    t1 = time.perf_counter()
+    sequence_plan(bm, cfg.H)
+    b.record()
+    torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    return {"block_mask_wall_ms": round((t1 - t0) * 1e3, 3),
+            "sequence_plan_wall_ms": round((t2 - t1) * 1e3, 3),
+            "total_device_span_ms": round(a.elapsed_time(b), 3)}
+
+
+def run_cached_step(steps=20, warmup=3):
+    """The released cached-inference step (``WAN_HIER_INFER_KERNEL`` plugin):
+    one 3-frame block of 4 players x 220 tokens + hubs, 24x128 heads, against
+    rolling caches of 24 retained frames.  Times the whole plugin call (its
+    per-call plan from the frame lists, then the attention) and the plan
+    build alone."""
+    import torch
+
+    from multics_b200 import cached as C
+    from multics_b200.synth import cached_step_inputs
+
+    kw = cached_step_inputs()
+    dev = kw["roped_q"].device
+    g = None
+
+    def plugin():
+        return C.hierarchical_cached_attention(sync_checks=False, **kw)
+
+    for _ in range(warmup):
+        plugin()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    a.record()
+    for _ in range(steps):
+        plugin()
+    b.record()
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) * 1e3 / steps
+    step_ms = a.elapsed_time(b) / steps
+    # plan alone: the grouping object the plugin builds, then only the plan
+    agent = [f.reshape(-1) for f in kw["agent_frames"]]
+    local = [f.reshape(-1) for f in kw["local_frames"]]
+    lact = [t.view(torch.uint8) for t in kw["local_active_tokens"]]
+    g = C._Grouping(P=kw["P"], N=kw["N"], L=kw["L"], KL=kw["KL"], KG=kw["KG"],
+                    n_frames=kw["n_frames"], n_block=kw["n_block"], local_attn=kw["local_attn"],
+                    direct=True, no_local=False, agent_frames=agent, local_frames=local,
+                    local_active=lact, global_frames=kw["global_frames"].reshape(-1),
+                    labels=kw["labels"], q_active=kw["active"].view(torch.uint8),
+                    membership=None, global_only=None)
+    a.record()
+    for _ in range(steps):
+        C.build_cached_plan(g, dev)
+    b.record()
+    torch.cuda.synchronize()
+    plan_ms = a.elapsed_time(b) / steps
+    plan = C.build_cached_plan(g, dev)
+    return {"workload": "cached inference step (plugin signature): P=4 x n=3 frames x L=220 + "
+                        "hubs (N=2 x K_L=16, K_G=6) = %d query rows, 24x128 heads, caches of 24 "
+                        "retained frames, window 21" % kw["roped_q"].shape[1],
+            "ms_per_step": round(step_ms, 4), "host_wall_ms_per_step": round(wall, 4),
+            "plan_ms": round(plan_ms, 4), "query_pairs": int(plan.n_pairs),
+            "key_streams": int(plan.n_streams)}
+
+
+def run_dit(steps=3, warmup=1):
+    """Configuration 3: one denoising step (one model evaluation, 30 blocks)
+    of the Multics-shaped DiT on this GPU, random N(0, 0.02) weights, with
+    CUDA events around every block's hierarchical self-attention."""
+    import torch
+
+    from multics_b200.dit import DiTConfig, HierDiT, dit_inputs, init_weights
+
+    cfg = DiTConfig()
+    dev = torch.device("cuda")
+    with torch.device(dev):
+        model = HierDiT(cfg).to(torch.bfloat16)
+    init_weights(model)
+    inputs = dit_inputs(cfg, dev)
+    consts = model.prepare(inputs, dev)
+    n_params = sum(p.numel() for p in model.parameters())
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(cfg.blocks)]
+    with torch.no_grad():
+        for _ in range(warmup):
+            model(inputs, consts)
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        attn = []
+        a.record()
+        for _ in range(steps):
+            model(inputs, consts, attn_events=ev)
+            b.record()
+            torch.cuda.synchronize()
+            attn.append(sum(e0.elapsed_time(e1) for e0, e1 in ev))
+        ms = a.elapsed_time(b) / steps
+    attn_ms = statistics.mean(attn)
+    del model
+    torch.cuda.empty_cache()
+    return {"workload": "cfg3: one denoising step of a Wan2.2-TI2V-5B-shaped Multics DiT, "
+                        f"{cfg.blocks} blocks, dim {cfg.dim}, FFN {cfg.ffn}, {cfg.heads}x128 heads, "
+                        f"{cfg.players} players x {cfg.frames} x {cfg.height}x{cfg.width} latents, "
+                        f"text {cfg.text_len}x{cfg.text_dim}, hierarchical self-attention in every "
+                        "block", "n_gpus": 1, "params": n_params, "dtype": "bf16",
+            "ms_per_step": round(ms, 2), "hier_attention_ms_per_step": round(attn_ms, 2),
+            "hier_attention_share": round(attn_ms / ms, 4), "steps": steps, "warmup": warmup,
+            "note": "self-attention = q/k/v/o projections + fused prologue + tcgen05 attention "
+                    "(the module as called); other branches on cuBLAS / PyTorch SDPA"}
 
 
 def cpu_baseline(cfg, sample_seconds=15.0):

@@ -1,12 +1,8 @@
 // Block-sparse flash attention forward for sm_100a (tcgen05 + TMEM + TMA).
 //
-// A work item is (query pair, head): a query pair is two 128-row query tiles
+// One CTA per (query pair, head): a query pair is two 128-row query tiles
 // ("halves") that share one list of 128-key tiles; each key tile carries one
 // mask selector per half (full / skip / index of a per-row key bitmask).
-// The kernel is persistent: one CTA per SM walks its share of the items
-// (largest first), keeping its barriers, tensor memory and the K/V rings
-// across items, so that the next item's Q and first key tiles load while the
-// current item drains and its epilogue overlaps the next item's first MMAs.
 //
 // Per half h and key tile j the tensor pipe runs S_h(j) = Q_h K(j)^T
 // (128 x 128, fp32 in TMEM) and O_h += P_h(j) V(j); the softmax warpgroup of
@@ -17,10 +13,7 @@
 //   S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | PV0(1) S0(2) PV1(1) S1(2) | ...
 //
 // which keeps the two halves out of phase (with one issuer per half they
-// drift into phase and their softmaxes contend for the exp unit).  Measured
-// on B200, back-to-back 128x128x16 MMAs cost 107 cycles (both operands in
-// shared memory, S) and 94 cycles (A in tensor memory, PV); the inner loop
-// runs at that instruction rate.
+// drift into phase and their softmaxes contend for the exp unit).
 //
 // Warp roles (384 threads, three warpgroups):
 //   warp 0      TMA producer of Q0, Q1 and the K tiles (3-stage ring)
@@ -35,16 +28,13 @@
 // P (bf16, two per 32-bit column) is written over the first 64 columns of the
 // S buffer it came from and read by the TS-form MMA; S_h(j+1) is issued after
 // PV_h(j) by the same thread, and tcgen05 MMAs of one thread execute in issue
-// order, so it never overwrites P_h(j) before PV_h(j) has read it.  An item's
-// epilogue reads O_h into registers and hands it back (o_free) before the
-// next item's first PV_h overwrites it.
+// order, so it never overwrites P_h(j) before PV_h(j) has read it.
 //
 // Shared memory: Q0, Q1 (32 KiB each), K ring 3 x 32 KiB, V ring 2 x 32 KiB;
 // each tile is two 64-column halves in the 128-byte swizzled layout, loaded
 // as two 64-row TMA boxes whose pool rows come from the plan (contiguous,
 // paged or gathered pools use the same code).  Shared-memory descriptors are
-// assembled inside the MMA's PTX from 32-bit base addresses and constant
-// offsets.
+// built once per operand and advanced by adding constant offsets.
 //
 // Online softmax: fp32 running max/sum per row; O is rescaled in TMEM only
 // when the running max grows by more than 2^8 (the final O/l is exact for any
@@ -54,9 +44,6 @@
 #include <math.h>
 #include <stdio.h>
 #include <string.h>
-
-#include <atomic>
-#include <mutex>
 
 #include "common.cuh"
 #include "tmap.h"
@@ -75,9 +62,8 @@ constexpr int kSmemQ = 0;               // Q0, Q1
 constexpr int kSmemK = 2 * kTile;
 constexpr int kSmemV = kSmemK + kKStages * kTile;
 constexpr int kSmemBar = kSmemV + kVStages * kTile;
-constexpr int kNumBars = 2 + 2 * kKStages + 2 * kVStages + 2 + 2 + 2 + 2 + 2 * 4;
-constexpr int kSmemMisc = 512;  // barriers, TMEM address slot, item ring
-constexpr int kSmemBytes = kSmemBar + kSmemMisc + 1024;  // + slack for 1024-byte alignment
+constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 2 + 2 + 2;
+constexpr int kSmemBytes = kSmemBar + 256 + 1024;  // + slack for 1024-byte alignment
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;
 constexpr int kSkip = -2;  // mask selector: this half does not use the key tile
@@ -86,8 +72,8 @@ constexpr int kSkip = -2;  // mask selector: this half does not use the key tile
 constexpr int kMapShift = 24;
 constexpr int kRowMask = (1 << kMapShift) - 1;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-constexpr uint32_t kRegsControl = 56;
-constexpr uint32_t kRegsSoftmax = 216;
+constexpr uint32_t kRegsControl = 40;
+constexpr uint32_t kRegsSoftmax = 224;
 static_assert(4 * 32 * kRegsControl + 8 * 32 * kRegsSoftmax <= 384 * 168,
               "register split exceeds the launch allocation");
 
@@ -113,7 +99,6 @@ struct AttnArgs {
   float* lse;  // optional [q_rows_total][H]: log2-sum-exp of the scaled scores per row
   int n_heads;
   int* err;
-  int* work;  // item counter of this launch (zeroed before the launch)
 };
 
 // Query tensor maps: rows below q2_row0 from q[0], the others from q[1].
@@ -134,27 +119,15 @@ __device__ __forceinline__ int half_sel(const int4& e, int h, int use) {
   return ((use >> h) & 1) ? (h ? e.w : e.z) : kSkip;
 }
 
-// The two mask selectors (z, w) of key-tile entry i.
-__device__ __forceinline__ int2 tile_sel(const int4* kv_tiles, int i) {
-  return *reinterpret_cast<const int2*>(reinterpret_cast<const int*>(kv_tiles + i) + 2);
-}
-__device__ __forceinline__ int half_sel2(int2 e, int h, int use) {
-  return ((use >> h) & 1) ? (h ? e.y : e.x) : kSkip;
-}
-
 struct Bars {
   uint64_t* q_full;
-  uint64_t* q_empty;  // the S MMAs of an item have read Q
   uint64_t* k_full;
   uint64_t* k_empty;
   uint64_t* v_full;
   uint64_t* v_empty;
   uint64_t* s_full;   // [half]
   uint64_t* p_full;   // [half], 128 softmax threads
-  uint64_t* o_final;  // [half], one phase after the last PV of an item
-  uint64_t* o_free;   // [half], 128 softmax threads: O read out, may be overwritten
-  uint64_t* item_full;   // [kItemSlots], the producer published an item index
-  uint64_t* item_empty;  // [kItemSlots], every other role has read it
+  uint64_t* o_final;  // [half], one phase after the last PV
 };
 
 // Shared-memory descriptors are built once per operand base (low word) and
@@ -258,210 +231,98 @@ __device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* ma
   tma_load_2d(dst + kHalf + kBoxBytes, m1, bar, col + 64, r1);
 }
 
-// Work items of a launch are (query pair, head), head-major: item t is pair
-// rank t % n_pairs of head t / n_pairs (pairs ranked by descending key-tile
-// count), so the CTAs running at any time share one or two heads' keys and
-// values in L2.  CTAs claim items in that order from a counter (atomicAdd by
-// the Q/K producer, which runs ahead) and pass each claimed index to the
-// other roles through a ring of kItemSlots shared-memory slots; a negative
-// index ends the walk.
-struct Item {
-  int4 pq;  // (q_start0, q_rows0, q_start1, q_rows1)
-  int4 pk;  // (kv_begin, kv_end, 128-row-mask flag, partial-row flag)
-  int4 e0;  // first key-tile entry (when kv_end > kv_begin)
-  int t;    // item index, -1: no more items
-  int col;  // first channel of the head
-  int pad[2];
-};
-
-__device__ __forceinline__ Item load_item(const AttnArgs& a, int t) {
-  Item it;
-  it.t = t;
-  if (t < 0) return it;
-  const int rank = t % a.n_pairs, head = t / a.n_pairs;
-  const int pr = a.order ? a.order[rank] : rank;
-  it.pq = a.pairs[2 * pr];
-  it.pk = a.pairs[2 * pr + 1];
-  it.e0 = it.pk.y > it.pk.x ? a.kv_tiles[it.pk.x] : make_int4(0, 0, kSkip, kSkip);
-  it.col = head * kHD;
-  return it;
-}
-
-__device__ __forceinline__ int item_use(const Item& it) {
-  return (it.pq.y > 0 ? 1 : 0) | (it.pq.w > 0 ? 2 : 0);  // halves with query rows
-}
-
-constexpr int kItemSlots = 4;
-constexpr int kItemConsumers = 2 + 256;  // V producer, MMA issuer, softmax threads
-
-// The i-th item of this CTA for a consumer role, from the producer's ring
-// (t < 0 when the walk is over, or when the wait gave up).
-__device__ __forceinline__ Item next_item(const Bars& B, const Item* ring, int i, int* err) {
-  const int slot = i % kItemSlots;
-  Item it;
-  if (!mbar_wait(B.item_full + slot, (i / kItemSlots) & 1, err, 14)) {
-    it.t = -1;
-    return it;
-  }
-  it = ring[slot];
-  mbar_arrive(B.item_empty + slot);
-  return it;
-}
-
-// Producer side: claim the next item, read its descriptor, publish it as the
-// i-th item of this CTA.
-__device__ __forceinline__ bool publish_item(const AttnArgs& a, const Bars& B, Item* ring,
-                                             int i, int n_items) {
-  const int slot = i % kItemSlots;
-  if (i >= kItemSlots && !mbar_wait(B.item_empty + slot, ((i / kItemSlots) - 1) & 1, a.err, 15))
-    return false;
-  int t = atomicAdd(a.work, 1);
-  if (t >= n_items) t = -1;
-  ring[slot] = load_item(a, t);
-  mbar_arrive(B.item_full + slot);
-  return true;
-}
-
-
-// Barrier phases run on across the items of a CTA: every counter below is
-// the number of completed phases of its barrier so far, so a parity wait
-// always names the next phase.
 template <int kMaps>
-__device__ __forceinline__ void control_role(const AttnArgs& a, int n_items, uint32_t tbase,
-                                             int warp, int lane, uint8_t* smem, const QMaps& qm,
-                                             const KVMaps<kMaps>& kv, const Bars& B, Item* ring) {
-  if (warp == 0 && lane == 0) {
-    // ------------------------------------------------- Q + K producer
+__device__ __forceinline__ void control_role(const AttnArgs& a, int4 pq, int kv_begin, int n_kv,
+                                             uint32_t tbase, int warp, int lane, uint8_t* smem,
+                                             const QMaps& qm, const KVMaps<kMaps>& kv,
+                                             const Bars& B, int col, int use) {
+  if (n_kv > 0 && warp == 0 && lane == 0) {
+    // -------------------------------------------------------- Q + K producer
+    const bool q2a = pq.x >= a.q2_row0, q2b = pq.z >= a.q2_row0;
+    const CUtensorMap* qa = &qm.q[q2a ? 1 : 0];
+    const CUtensorMap* qb = &qm.q[q2b ? 1 : 0];
+    const int ra = pq.x - (q2a ? a.q2_row0 : 0), rb = pq.z - (q2b ? a.q2_row0 : 0);
+    prefetch_tmap(qa);
     if (kMaps == 1) prefetch_tmap(&kv.k[0]);
-    int kc = 0, qi = 0;  // K tiles loaded, Q loads
-    if (!publish_item(a, B, ring, 0, n_items)) return;
-    for (int i = 0;; ++i) {
-      // the producer's own copy of item i: its ring slot is not reused before
-      // item i + kItemSlots is published
-      const Item& it = ring[i % kItemSlots];
-      if (it.t < 0) break;
-      const int kv_begin = it.pk.x, n_kv = it.pk.y - it.pk.x;
-      if (n_kv > 0) {
-        const int4 pq = it.pq;
-        const bool q2a = pq.x >= a.q2_row0, q2b = pq.z >= a.q2_row0;
-        const CUtensorMap* qa = &qm.q[q2a ? 1 : 0];
-        const CUtensorMap* qb = &qm.q[q2b ? 1 : 0];
-        const int ra = pq.x - (q2a ? a.q2_row0 : 0), rb = pq.z - (q2b ? a.q2_row0 : 0);
-        // the previous item's S MMAs have read Q
-        if (qi > 0 && !mbar_wait(B.q_empty, (qi - 1) & 1, a.err, 1)) return;
-        mbar_arrive_expect_tx(B.q_full, 2 * kTile);
-        tma_load_2d(smem + kSmemQ, qa, B.q_full, it.col, ra);
-        tma_load_2d(smem + kSmemQ + kHalf, qa, B.q_full, it.col + 64, ra);
-        tma_load_2d(smem + kSmemQ + kTile, qb, B.q_full, it.col, rb);
-        tma_load_2d(smem + kSmemQ + kTile + kHalf, qb, B.q_full, it.col + 64, rb);
-        ++qi;
-      }
-      bool claimed = false;
-      for (int j = 0; j < n_kv; ++j, ++kc) {
-        const int st = kc % kKStages;
-        // once the ring is primed, claim and publish the next item while this
-        // one's loads wait for free stages
-        if (j == kKStages && !claimed) {
-          if (!publish_item(a, B, ring, i + 1, n_items)) return;
-          claimed = true;
-        }
-        if (kc >= kKStages && !mbar_wait(B.k_empty + st, ((kc / kKStages) - 1) & 1, a.err, 1))
-          return;
-        const int4 e = j == 0 ? it.e0 : a.kv_tiles[kv_begin + j];
-        load_kv_tile<kMaps>(smem + kSmemK + st * kTile, kv.k, B.k_full + st, it.col, e.x, e.y);
-      }
-      if (!claimed && !publish_item(a, B, ring, i + 1, n_items)) return;
+    mbar_arrive_expect_tx(B.q_full, 2 * kTile);
+    tma_load_2d(smem + kSmemQ, qa, B.q_full, col, ra);
+    tma_load_2d(smem + kSmemQ + kHalf, qa, B.q_full, col + 64, ra);
+    tma_load_2d(smem + kSmemQ + kTile, qb, B.q_full, col, rb);
+    tma_load_2d(smem + kSmemQ + kTile + kHalf, qb, B.q_full, col + 64, rb);
+    for (int j = 0; j < n_kv; ++j) {
+      const int st = j % kKStages;
+      if (j >= kKStages && !mbar_wait(B.k_empty + st, ((j / kKStages) - 1) & 1, a.err, 1)) break;
+      const int4 e = a.kv_tiles[kv_begin + j];
+      load_kv_tile<kMaps>(smem + kSmemK + st * kTile, kv.k, B.k_full + st, col, e.x, e.y);
     }
-  } else if (warp == 2 && lane == 0) {
-    // ---------------------------------------------------- V producer
+  } else if (n_kv > 0 && warp == 2 && lane == 0) {
+    // ------------------------------------------------------------ V producer
     if (kMaps == 1) prefetch_tmap(&kv.v[0]);
-    int vc = 0;
-    for (int i = 0;; ++i) {
-      const Item it = next_item(B, ring, i, a.err);
-      if (it.t < 0) break;
-      const int kv_begin = it.pk.x, n_kv = it.pk.y - it.pk.x;
-      for (int j = 0; j < n_kv; ++j, ++vc) {
-        const int st = vc % kVStages;
-        if (vc >= kVStages && !mbar_wait(B.v_empty + st, ((vc / kVStages) - 1) & 1, a.err, 2))
-          return;
-        const int4 e = j == 0 ? it.e0 : a.kv_tiles[kv_begin + j];
-        load_kv_tile<kMaps>(smem + kSmemV + st * kTile, kv.v, B.v_full + st, it.col, e.x, e.y);
-      }
+    for (int j = 0; j < n_kv; ++j) {
+      const int st = j % kVStages;
+      if (j >= kVStages && !mbar_wait(B.v_empty + st, ((j / kVStages) - 1) & 1, a.err, 2)) break;
+      const int4 e = a.kv_tiles[kv_begin + j];
+      load_kv_tile<kMaps>(smem + kSmemV + st * kTile, kv.v, B.v_full + st, col, e.x, e.y);
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------------------------------------------- MMA issuer
+  } else if (n_kv > 0 && warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
     const uint32_t q_lo[2] = {sdesc_lo_kmajor(smem_u32(smem + kSmemQ)),
                               sdesc_lo_kmajor(smem_u32(smem + kSmemQ + kTile))};
     const uint32_t k_lo0 = sdesc_lo_kmajor(smem_u32(smem + kSmemK));
     const uint32_t v_lo0 = sdesc_lo_mnmajor(smem_u32(smem + kSmemV));
-    int kc = 0, vc = 0, qi = 0;
-    int pc[2] = {0, 0};  // P hand-offs consumed per half
-    int oc[2] = {0, 0};  // items with PVs per half (O hand-backs expected)
-    for (int i = 0;; ++i) {
-      const Item it = next_item(B, ring, i, a.err);
-      if (it.t < 0) break;
-      const int kv_begin = it.pk.x, n_kv = it.pk.y - it.pk.x;
-      if (n_kv <= 0) continue;
-      const int use = item_use(it);
-      if (!mbar_wait(B.q_full, qi & 1, a.err, 3)) return;
-      int2 e_cur = make_int2(it.e0.z, it.e0.w);
-      if (!mbar_wait(B.k_full + kc % kKStages, (kc / kKStages) & 1, a.err, 4)) return;
-      tc_fence_after();
-      // S_h(0) overwrites P_h of the previous item, which that item's last
-      // PV_h, issued earlier by this thread, reads first (in-order execution).
+    int cp[2] = {0, 0};  // PVs issued per half
+    if (!mbar_wait(B.q_full, 0, a.err, 3)) return;
+    // Every phase of the stage barriers is waited for, used or not, so a
+    // parity wait never matches an older phase.
+    int4 e_cur = a.kv_tiles[kv_begin];
+    if (!mbar_wait(B.k_full, 0, a.err, 4)) return;
+    tc_fence_after();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (half_sel(e_cur, h, use) == kSkip) continue;
+      issue_s(tbase + h * kBN, q_lo[h], k_lo0);
+      umma_commit(B.s_full + h);
+    }
+    umma_commit(B.k_empty);
+    for (int j = 0; j < n_kv; ++j) {
+      const bool more = j + 1 < n_kv;
+      const int4 e_next = more ? a.kv_tiles[kv_begin + j + 1] : e_cur;
+      const int stv = j % kVStages, stk = (j + 1) % kKStages;
+      if (!mbar_wait(B.v_full + stv, (j / kVStages) & 1, a.err, 5)) return;
+      // PV0(j) S0(j+1) PV1(j) S1(j+1): S_h(j+1) overwrites P_h(j), which the
+      // PV_h(j) issued just before it reads first (in-order execution).
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        if (half_sel2(e_cur, h, use) == kSkip) continue;
-        issue_s(tbase + h * kBN, q_lo[h], k_lo0 + (((kc % kKStages) * kTile) >> 4));
-        umma_commit(B.s_full + h);
-      }
-      umma_commit(B.k_empty + kc % kKStages);
-      int cp[2] = {0, 0};  // PVs of this item per half
-      for (int j = 0; j < n_kv; ++j) {
-        const bool more = j + 1 < n_kv;
-        const int2 e_next = more ? tile_sel(a.kv_tiles, kv_begin + j + 1) : e_cur;
-        const int stv = vc % kVStages, kn = kc + 1, stk = kn % kKStages;
-        if (!mbar_wait(B.v_full + stv, (vc / kVStages) & 1, a.err, 5)) return;
-        // PV0(j) S0(j+1) PV1(j) S1(j+1): S_h(j+1) overwrites P_h(j), which the
-        // PV_h(j) issued just before it reads first (in-order execution).
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (half_sel2(e_cur, h, use) != kSkip) {
-            if (!mbar_wait(B.p_full + h, pc[h] & 1, a.err, 6 + h)) return;
-            // the first PV of an item overwrites O_h: the previous item's
-            // epilogue must have read it
-            if (cp[h] == 0 && oc[h] > 0 && !mbar_wait(B.o_free + h, (oc[h] - 1) & 1, a.err, 8 + h))
-              return;
-            tc_fence_after();
-            issue_pv(tbase + kColO + h * kBN, tbase + h * kBN, v_lo0 + ((stv * kTile) >> 4),
-                     cp[h] > 0);
-            ++pc[h];
-            ++cp[h];
-          }
-          if (!more) continue;
-          if (h == 0 && !mbar_wait(B.k_full + stk, (kn / kKStages) & 1, a.err, 4)) return;
-          if (half_sel2(e_next, h, use) != kSkip) {
-            tc_fence_after();
-            issue_s(tbase + h * kBN, q_lo[h], k_lo0 + ((stk * kTile) >> 4));
-            umma_commit(B.s_full + h);
-          }
+        if (half_sel(e_cur, h, use) != kSkip) {
+          if (!mbar_wait(B.p_full + h, cp[h] & 1, a.err, 6 + h)) return;
+          tc_fence_after();
+          issue_pv(tbase + kColO + h * kBN, tbase + h * kBN, v_lo0 + ((stv * kTile) >> 4),
+                   cp[h] > 0);
+          ++cp[h];
         }
-        umma_commit(B.v_empty + stv);
-        ++vc;
-        if (more) umma_commit(B.k_empty + stk);
-        ++kc;
-        e_cur = e_next;
-      }
-      umma_commit(B.q_empty);  // every S of this item issued: Q may be replaced
-      ++qi;
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-        if (cp[h] > 0) {
-          umma_commit(B.o_final + h);
-          ++oc[h];
+        if (!more) continue;
+        if (h == 0 && !mbar_wait(B.k_full + stk, ((j + 1) / kKStages) & 1, a.err, 4)) return;
+        if (half_sel(e_next, h, use) != kSkip) {
+          tc_fence_after();
+          issue_s(tbase + h * kBN, q_lo[h], k_lo0 + ((stk * kTile) >> 4));
+          umma_commit(B.s_full + h);
         }
+      }
+      umma_commit(B.v_empty + stv);
+      if (more) umma_commit(B.k_empty + stk);
+      e_cur = e_next;
     }
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (cp[h] > 0) umma_commit(B.o_final + h);
   }
+}
+
+// 32 bytes (8 words) to a 32-byte aligned global address.
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t* w) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(w[0]),
+               "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
 }
 
 // O (128 x 128 fp32 in TMEM) rescaled by alpha, 8 columns at a time (few
@@ -484,158 +345,149 @@ __device__ __forceinline__ void rescale_o(uint32_t o_col, float alpha) {
   }
 }
 
-__device__ __forceinline__ void softmax_role(const AttnArgs& a, uint32_t tbase, int warp,
-                                             const Bars& B, const Item* ring) {
+__device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_begin, int n_kv,
+                                             uint32_t tbase, int warp, const Bars& B, int col,
+                                             int use, bool row_masks128, bool partial_rows) {
   const int h = (warp >> 2) - 1;  // 0 for warps 4-7, 1 for warps 8-11
   const int row = threadIdx.x - 128 * (h + 1);
   const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
   const uint32_t s_col = tbase + lane_base + h * kBN;
   const uint32_t o_col = tbase + lane_base + kColO + h * kBN;
+  const int q_start = h ? pq.z : pq.x;
+  const int q_rows = h ? pq.w : pq.y;
+  const bool store_row = row < q_rows;
+  int64_t dst_row;
+  __nv_bfloat16* orow;
+  float* lse_out;
+  if (partial_rows) {
+    dst_row = (int64_t)(q_start + row) - a.part_row0;
+    orow = a.part_out + dst_row * a.part_stride + col;
+    lse_out = a.part_lse;
+  } else {
+    dst_row = (a.out_rows && store_row) ? (int64_t)a.out_rows[q_start + row]
+                                        : (int64_t)(q_start + row);
+    orow = a.out + dst_row * a.out_stride + col;
+    lse_out = a.lse;
+  }
+  // a pair flagged in q_pairs[6] carries one mask per query row whatever the
+  // launch's mask format
+  const int mask_stride = row_masks128 ? kBM : a.mask_stride;
+  const int mask_row_and = row_masks128 ? kBM - 1 : a.mask_row_and;
+  float m_run = -INFINITY, l_run = 0.f;  // running max in scaled log2 units
+  int c = 0;                             // key tiles processed by this half
   const float sc = a.scale_log2;
-  int c = 0;   // S tiles of this half so far (all items)
-  int of = 0;  // items with tiles of this half so far
-  for (int i = 0;; ++i) {
-    const Item it = next_item(B, ring, i, a.err);
-    if (it.t < 0) break;
-    const int4 pq = it.pq;
-    const int kv_begin = it.pk.x, n_kv = it.pk.y - it.pk.x;
-    const int use = item_use(it);
-    const bool row_masks128 = it.pk.z == 1, partial_rows = (it.pk.w & 1) != 0;
-    const int col = it.col;
-    const int q_start = h ? pq.z : pq.x;
-    const int q_rows = h ? pq.w : pq.y;
-    const bool store_row = row < q_rows;
-    int64_t dst_row;
-    __nv_bfloat16* orow;
-    float* lse_out;
-    if (partial_rows) {
-      dst_row = (int64_t)(q_start + row) - a.part_row0;
-      orow = a.part_out + dst_row * a.part_stride + col;
-      lse_out = a.part_lse;
-    } else {
-      dst_row = (a.out_rows && store_row) ? (int64_t)a.out_rows[q_start + row]
-                                          : (int64_t)(q_start + row);
-      orow = a.out + dst_row * a.out_stride + col;
-      lse_out = a.lse;
-    }
-    // a pair flagged in q_pairs[6] carries one mask per query row whatever the
-    // launch's mask format
-    const int mask_stride = row_masks128 ? kBM : a.mask_stride;
-    const int mask_row_and = row_masks128 ? kBM - 1 : a.mask_row_and;
-    float m_run = -INFINITY, l_run = 0.f;  // running max in scaled log2 units
-    int ci = 0;                            // key tiles of this item for this half
-    // Entries are loaded one tile ahead and a partial tile's row mask is
-    // requested before the S wait, keeping both global loads off the S -> P path.
-    int4 e_next = it.e0;
-    for (int j = 0; j < n_kv; ++j) {
-      const int4 e = e_next;
-      if (j + 1 < n_kv) e_next = a.kv_tiles[kv_begin + j + 1];
-      const int mi = half_sel(e, h, use);
-      if (mi == kSkip) continue;
-      const bool partial = mi >= 0;  // uniform across the CTA
-      uint4 mk = make_uint4(~0u, ~0u, ~0u, ~0u);
-      if (partial) mk = a.row_masks[(int64_t)mi * mask_stride + (row & mask_row_and)];
-      // S_h(c) is committed after PV_h(c-1), so once it is visible O holds
-      // every earlier P V product and can be rescaled without another wait.
-      if (!mbar_wait(B.s_full + h, c & 1, a.err, 11)) return;
-      tc_fence_after();
-      float sv[kBN];
-      {
-        uint32_t* r = reinterpret_cast<uint32_t*>(sv);
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          tmem_ld32(s_col + q * 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32 * q));
-        tmem_wait_ld();
-      }
-      if (partial) {
-        const uint32_t w[4] = {mk.x, mk.y, mk.z, mk.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            sv[32 * q + i] = ((w[q] >> i) & 1u) ? sv[32 * q + i] : -INFINITY;
-      }
-      float m8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = sv[i];
-#pragma unroll
-      for (int i = 8; i < kBN; ++i) m8[i & 7] = fmaxf(m8[i & 7], sv[i]);
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sc;
-      const bool grow = mx > m_run + kRescaleThreshold;
-      const bool rescale = grow && m_run != -INFINITY;
-      if (__any_sync(0xffffffffu, rescale)) {
-        const float alpha = rescale ? ex2_approx(m_run - mx) : 1.f;
-        rescale_o(o_col, alpha);
-        l_run *= alpha;
-      }
-      if (grow) m_run = mx;
-      const float nref = m_run == -INFINITY ? 0.f : -m_run;
-      // exponent arguments and row sums two lanes at a time (fp32x2 FMA / add)
-      const uint64_t sc2 = f2_pack(sc, sc), nref2 = f2_pack(nref, nref);
-      uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const uint64_t arg =
-              f2_fma(f2_pack(sv[64 * half + 2 * i], sv[64 * half + 2 * i + 1]), sc2, nref2);
-          float a0, a1;
-          f2_unpack(arg, a0, a1);
-          const float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
-          acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
-          pk[i] = pack_bf16x2(p0, p1);
-        }
-        tmem_st32(s_col + 32 * half, pk);
-      }
-      {
-        const uint64_t s2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
-        float s0, s1;
-        f2_unpack(s2, s0, s1);
-        l_run += s0 + s1;
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(B.p_full + h);
-      ++c;
-      ++ci;
-    }
-    if (ci == 0) {
-      if (store_row) {
-        const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-        for (int q = 0; q < kHD / 8; ++q) reinterpret_cast<uint4*>(orow)[q] = z;
-        if (lse_out) lse_out[dst_row * a.n_heads + col / kHD] = -INFINITY;
-      }
-      continue;
-    }
-    if (!mbar_wait(B.o_final + h, of & 1, a.err, 13)) return;
-    ++of;
+  // Entries are loaded one tile ahead and a partial tile's row mask is
+  // requested before the S wait, keeping both global loads off the S -> P path.
+  int4 e_next = n_kv > 0 ? a.kv_tiles[kv_begin] : make_int4(0, 0, kSkip, kSkip);
+  for (int j = 0; j < n_kv; ++j) {
+    const int4 e = e_next;
+    if (j + 1 < n_kv) e_next = a.kv_tiles[kv_begin + j + 1];
+    const int mi = half_sel(e, h, use);
+    if (mi == kSkip) continue;
+    const bool partial = mi >= 0;  // uniform across the CTA
+    uint4 mk = make_uint4(~0u, ~0u, ~0u, ~0u);
+    if (partial) mk = a.row_masks[(int64_t)mi * mask_stride + (row & mask_row_and)];
+    // S_h(c) is committed after PV_h(c-1), so once it is visible O holds
+    // every earlier P V product and can be rescaled without another wait.
+    if (!mbar_wait(B.s_full + h, c & 1, a.err, 11)) return;
     tc_fence_after();
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    // O -> registers (bf16), then O is handed back to the MMA issuer for the
-    // next item before the row is written out
-    uint32_t ow[kHD / 2];
+    float sv[kBN];
+    {
+      uint32_t* r = reinterpret_cast<uint32_t*>(sv);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t r[32];
-      tmem_ld32(o_col + q * 32, r);
+      for (int q = 0; q < 4; ++q)
+        tmem_ld32(s_col + q * 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32 * q));
       tmem_wait_ld();
+    }
+    if (partial) {
+      const uint32_t w[4] = {mk.x, mk.y, mk.z, mk.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          sv[32 * q + i] = ((w[q] >> i) & 1u) ? sv[32 * q + i] : -INFINITY;
+    }
+    float m8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m8[i] = sv[i];
+#pragma unroll
+    for (int i = 8; i < kBN; ++i) m8[i & 7] = fmaxf(m8[i & 7], sv[i]);
+    const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                           fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sc;
+    const bool grow = mx > m_run + kRescaleThreshold;
+    const bool need_rescale = grow && m_run != -INFINITY;
+    if (__any_sync(0xffffffffu, need_rescale)) {
+      const float alpha = need_rescale ? ex2_approx(m_run - mx) : 1.f;
+      rescale_o(o_col, alpha);
+      l_run *= alpha;
+    }
+    if (grow) m_run = mx;
+    const float nref = m_run == -INFINITY ? 0.f : -m_run;
+    // exponent arguments and row sums two lanes at a time (fp32x2 FMA / add)
+    const uint64_t sc2 = f2_pack(sc, sc), nref2 = f2_pack(nref, nref);
+    uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint64_t arg =
+            f2_fma(f2_pack(sv[64 * half + 2 * i], sv[64 * half + 2 * i + 1]), sc2, nref2);
+        float a0, a1;
+        f2_unpack(arg, a0, a1);
+        const float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
+        acc[i & 3] = f2_add(acc[i & 3], f2_pack(p0, p1));
+        pk[i] = pack_bf16x2(p0, p1);
+      }
+      tmem_st32(s_col + 32 * half, pk);
+    }
+    {
+      const uint64_t s2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
+      float s0, s1;
+      f2_unpack(s2, s0, s1);
+      l_run += s0 + s1;
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(B.p_full + h);
+    ++c;
+  }
+  if (c == 0) {
+    if (store_row) {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int q = 0; q < kHD / 8; ++q) reinterpret_cast<uint4*>(orow)[q] = z;
+      if (lse_out) lse_out[dst_row * a.n_heads + col / kHD] = -INFINITY;
+    }
+    return;
+  }
+  if (!mbar_wait(B.o_final + h, 0, a.err, 13)) return;
+  tc_fence_after();
+  const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+  if (lse_out && store_row)  // O = sum_j 2^(s_j - lse) v_j
+    lse_out[dst_row * a.n_heads + col / kHD] =
+        l_run > 0.f ? m_run + __log2f(l_run) : -INFINITY;
+  // each thread writes its own 256-byte row; 32-byte stores fill whole
+  // sectors (half as many transactions as 16-byte ones)
+  const bool v8 = (reinterpret_cast<uintptr_t>(orow) & 31) == 0;
+  uint32_t r[32];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    tmem_ld32(o_col + q * 32, r);
+    tmem_wait_ld();
+    if (store_row) {
+      uint32_t w[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i)
-        ow[16 * q + i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv,
-                                     __uint_as_float(r[2 * i + 1]) * inv);
-    }
-    tc_fence_before();
-    mbar_arrive(B.o_free + h);
-    if (store_row) {
-      if (lse_out)  // O = sum_j 2^(s_j - lse) v_j
-        lse_out[dst_row * a.n_heads + col / kHD] = l_run > 0.f ? m_run + __log2f(l_run) : -INFINITY;
-      uint4* dst = reinterpret_cast<uint4*>(orow);
+        w[i] = pack_bf16x2(__uint_as_float(r[2 * i]) * inv, __uint_as_float(r[2 * i + 1]) * inv);
+      if (v8) {
+        st_global_v8(orow + q * 32, w);
+        st_global_v8(orow + q * 32 + 16, w + 8);
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(orow + q * 32);
 #pragma unroll
-      for (int w = 0; w < kHD / 8; ++w)
-        dst[w] = make_uint4(ow[4 * w], ow[4 * w + 1], ow[4 * w + 2], ow[4 * w + 3]);
+        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+      }
     }
   }
 }
@@ -650,28 +502,28 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
   Bars B;
   B.q_full = bars;
-  B.q_empty = B.q_full + 1;
-  B.k_full = B.q_empty + 1;
+  B.k_full = B.q_full + 1;
   B.k_empty = B.k_full + kKStages;
   B.v_full = B.k_empty + kKStages;
   B.v_empty = B.v_full + kVStages;
   B.s_full = B.v_empty + kVStages;
   B.p_full = B.s_full + 2;
   B.o_final = B.p_full + 2;
-  B.o_free = B.o_final + 2;
-  B.item_full = B.o_free + 2;
-  B.item_empty = B.item_full + kItemSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
-  Item* ring = reinterpret_cast<Item*>(tmem_slot + 4);
-  static_assert(kNumBars * 8 + 16 + kItemSlots * sizeof(Item) <= kSmemMisc, "misc area overflow");
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int n_items = a.n_pairs * a.n_heads;
+  const int head = blockIdx.x / a.n_pairs;
+  const int rank = blockIdx.x % a.n_pairs;
+  const int pr = a.order ? a.order[rank] : rank;
+  const int4 pq = a.pairs[2 * pr];
+  const int4 pk = a.pairs[2 * pr + 1];
+  const int kv_begin = pk.x;
+  const int n_kv = pk.y - pk.x;
+  const int use = (pq.y > 0 ? 1 : 0) | (pq.w > 0 ? 2 : 0);  // halves with query rows
 
   if (threadIdx.x == 0) {
     mbar_init(B.q_full, 1);
-    mbar_init(B.q_empty, 1);
     for (int s = 0; s < kKStages; ++s) {
       mbar_init(B.k_full + s, 1);
       mbar_init(B.k_empty + s, 1);
@@ -684,11 +536,6 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(B.s_full + i, 1);
       mbar_init(B.p_full + i, 128);
       mbar_init(B.o_final + i, 1);
-      mbar_init(B.o_free + i, 128);
-    }
-    for (int i = 0; i < kItemSlots; ++i) {
-      mbar_init(B.item_full + i, 1);
-      mbar_init(B.item_empty + i, kItemConsumers);
     }
     fence_mbar_init();
   }
@@ -698,12 +545,13 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
+  const int col = head * kHD;
   if (warp >= 4) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-    softmax_role(a, tbase, warp, B, ring);
+    softmax_role(a, pq, kv_begin, n_kv, tbase, warp, B, col, use, pk.z == 1, (pk.w & 1) != 0);
   } else {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
-    control_role<kMaps>(a, n_items, tbase, warp, lane, smem, qm, kv, B, ring);
+    control_role<kMaps>(a, pq, kv_begin, n_kv, tbase, warp, lane, smem, qm, kv, B, col, use);
   }
 
   tc_fence_before();
@@ -719,40 +567,6 @@ __global__ void __launch_bounds__(384, 1)
 using namespace hier;
 
 namespace {
-
-// Item counters of the persistent attention launches: each launch takes the
-// next of kWorkSlots counters of its device (file-scope device memory, no
-// allocation) and zeroes it on its stream before the kernel.  Launches in
-// flight at the same time use different counters as long as fewer than
-// kWorkSlots of them overlap.  The first launch on a device looks the array
-// up (cudaGetSymbolAddress) and should come before any stream capture.
-constexpr int kWorkSlots = 64;
-constexpr int kMaxWorkDevices = 64;
-__device__ int g_work_counters[kWorkSlots];
-std::mutex g_work_mu;
-int* g_work_base[kMaxWorkDevices] = {};
-std::atomic<unsigned> g_work_seq{0};
-
-int work_counter(cudaStream_t stream, int** out) {
-  int dev = 0;
-  HIER_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxWorkDevices) {
-    set_error(HIER_EVALUE, "device ordinal %d beyond %d", dev, kMaxWorkDevices);
-    return HIER_EVALUE;
-  }
-  {
-    std::lock_guard<std::mutex> lock(g_work_mu);
-    if (!g_work_base[dev]) {
-      void* p = nullptr;
-      HIER_CHECK_CUDA(cudaGetSymbolAddress(&p, g_work_counters), "cudaGetSymbolAddress(work)");
-      g_work_base[dev] = static_cast<int*>(p);
-    }
-  }
-  int* c = g_work_base[dev] + (g_work_seq.fetch_add(1) % kWorkSlots);
-  HIER_CHECK_CUDA(cudaMemsetAsync(c, 0, sizeof(int), stream), "cudaMemsetAsync(work)");
-  *out = c;
-  return HIER_OK;
-}
 
 int attn_setup(const void* q, int64_t q_rows_total, int64_t q_stride, int32_t H, int32_t D,
                int32_t n_pairs, CUtensorMap* tmq) {
@@ -805,19 +619,7 @@ int attn_launch(const QMaps& qm, int q2_row0, const KVMaps<kMaps>& kv, void* out
   args.lse = lse;
   args.n_heads = H;
   args.err = dev_err;
-  {
-    const int rc = work_counter((cudaStream_t)stream, &args.work);
-    if (rc) return rc;
-  }
-  // persistent: one CTA per SM (224 KB of shared memory, all of TMEM), each
-  // walking its share of the (pair, head) items
-  int dev = 0, sms = 148;
-  HIER_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-  HIER_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
-                  "cudaDeviceGetAttribute");
-  const int64_t items = (int64_t)n_pairs * H;
-  const int grid = (int)(items < sms ? items : sms);
-  hier_attn_kernel<kMaps><<<grid, 384, kSmemBytes, (cudaStream_t)stream>>>(qm, kv, args);
+  hier_attn_kernel<kMaps><<<n_pairs * H, 384, kSmemBytes, (cudaStream_t)stream>>>(qm, kv, args);
   HIER_CHECK_CUDA(cudaGetLastError(), "hier_attn_kernel launch");
   return HIER_OK;
 }

@@ -159,3 +159,42 @@ def make_inputs(cfg: HierConfig, device="cpu") -> LayerInputs:
                                      cfg.D, pool_size=max(10, cfg.P) if cfg.P <= 17 else cfg.P)
     labels = group_labels(cfg, g)
     return LayerInputs(qx, kx, v, cam, wcq, wck, nqw, nkw, freqs.to(device), labels.to(device))
+
+
+def cached_step_inputs(P=4, N=2, L=220, KL=16, KG=6, n_frames=3, local_attn=21, retained=24,
+                       H=24, device="cuda", seed=0) -> dict:
+    """Keyword arguments of the cached-backend plugin
+    (``multics_b200.cached.hierarchical_cached_attention``) for one block of
+    ``n_frames`` new frames against rolling caches holding ``retained``
+    frames per stream (the released inference shape: 4 players, 3-frame
+    blocks, window 21 + 3 retained frames), with seeded random roped queries
+    and cache contents ~ N(0,1)*0.5, groups {0,1},{2,3} and every hub active."""
+    g = torch.Generator().manual_seed(seed)
+    dim = H * 128
+    S = P * n_frames * L + n_frames * (N * KL + KG)
+    fr = torch.arange(retained, dtype=torch.int64)
+
+    def frames(w):
+        return fr.repeat_interleave(max(w, 1)).to(device)
+
+    def rnd(rows):
+        return (torch.randn((1, rows, dim), generator=g) * 0.5).to(torch.bfloat16).to(device)
+
+    kw = dict(P=P, N=N, L=L, KL=KL, KG=KG, n_frames=n_frames, n_block=n_frames,
+              local_attn=local_attn, direct_player=True, hier_no_local_hub=False)
+    kw["agent_frames"] = [frames(L) for _ in range(P)]
+    kw["agent_keys"] = [rnd(retained * L) for _ in range(P)]
+    kw["agent_vals"] = [rnd(retained * L) for _ in range(P)]
+    kw["local_frames"] = [frames(KL) for _ in range(N)]
+    kw["local_keys"] = [rnd(retained * KL) for _ in range(N)]
+    kw["local_vals"] = [rnd(retained * KL) for _ in range(N)]
+    kw["local_active_tokens"] = [torch.ones(retained * KL, dtype=torch.bool, device=device)
+                                 for _ in range(N)]
+    kw["global_frames"] = frames(KG)
+    kw["global_keys"] = rnd(retained * KG)
+    kw["global_vals"] = rnd(retained * KG)
+    kw["labels"] = torch.tensor([[p * N // P for p in range(P)]] * n_frames, dtype=torch.long,
+                                device=device)
+    kw["active"] = torch.ones((n_frames, N), dtype=torch.bool, device=device)
+    kw["roped_q"] = (torch.randn((1, S, H, 128), generator=g) * 0.5).to(torch.bfloat16).to(device)
+    return kw
