@@ -196,16 +196,10 @@ int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, const void* c
  *       by q_pairs are written; rows whose key set is empty are written as 0
  *       (the cached backends' contract, hier_segmented_attention.py:104-109).
  *   q_pairs [n_pairs][8], kv_tiles [][4], row_masks, order [n_pairs] (or
- *       NULL) in the format of hier_block_plan_build: a work item is the two
- *       128-row query tiles of a pair for one head, taken in the order
- *       (head, rank in order[]) by one persistent CTA per SM.
+ *       NULL) in the format of hier_block_plan_build: each CTA computes the
+ *       two 128-row query tiles of a pair for one head, pairs taken in the
+ *       order of order[] for every head.
  *   dev_err: device int32, set non-zero if a pipeline wait timed out.
- * The CTAs claim work items from a counter in a fixed device array of the
- * library (64 counters per device, one per launch in turn, zeroed on the
- * launch stream; nothing is allocated).  Up to 64 attention launches may be
- * in flight at the same time on one device.  The first launch on a device
- * looks the array up (cudaGetSymbolAddress) and should come before any
- * stream capture.
  * Replaces the attention kernels of the reference backends: masked SDPA
  * (attention.py:39-54), FlexAttention (attention.py:322-353), the Triton
  * segmented / tiled128 kernels (kernels/hier_segmented_attention.py:27-114,
