@@ -199,16 +199,33 @@ def run_sharded(args, rank, world, local_rank):
     useful_flops = 4.0 * cfg.H * cfg.D * pairs
     w = {k: getattr(inp, k) for k in ("wcq", "wck", "nqw", "nkw")}
     del bm, inp
+    # configuration 5 on one GPU: the player rows' keys and values in 64-token
+    # pages shuffled by seed (the reference's paged KV layout)
+    from multics_b200.synth import page_table as _page_table
+
+    pages = _page_table(cfg) if (cfg.page_size and world == 1) else None
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    sh = ShardedHierAttention(topo, cfg.H, dev, transport=args.transport)
+    sh = ShardedHierAttention(topo, cfg.H, dev, transport=args.transport, page_table=pages)
     torch.cuda.synchronize()
     plan_ms = (time.perf_counter() - t0) * 1e3
     sh.check_status()
     tile_flops = plan_tile_flops(sh.q_pairs[:sh.n_pairs], sh.kv_tiles, cfg.H, cfg.D)
     q_buf = torch.empty_like(qx)
     o_buf = torch.empty_like(qx)
-    if sh.transport == "peer":
+    k_rows = None
+    if pages is not None:
+        own = topo.own_rows
+        r = torch.arange(qx.shape[0], device=dev)
+        pt = pages.to(dev).long()
+        k_rows = torch.where(r < own, pt[torch.clamp(r, max=own - 1) // 64] * 64 + r % 64,
+                             sh.page_rows + r - own).to(torch.int32)
+        k_buf = torch.empty((sh.page_rows + topo.hub_rows, qx.shape[1]), dtype=qx.dtype,
+                            device=dev)
+        v_pool = torch.zeros_like(k_buf)
+        v_pool.index_copy_(0, k_rows.long(), v)
+        v = v_pool
+    elif sh.transport == "peer":
         # K is produced straight into the rank's symmetric buffer; V (a layer
         # input) lives there as well
         k_buf = sh.k_buffer()
@@ -221,7 +238,7 @@ def run_sharded(args, rank, world, local_rank):
     def step(i=None):
         hier_prep_qk(qx, kx, ft, cfg.H, norm_q_weight=w["nqw"], norm_k_weight=w["nkw"],
                      cam_tokens=cam, cam_q_weight=w["wcq"], cam_k_weight=w["wck"],
-                     out=(q_buf, k_buf))
+                     out=(q_buf, k_buf), k_out_rows=k_rows)
         if i is not None:
             marks["a"][i].record(stream)
         # exchange, hub pairs, partial all-gather overlapped with the player
@@ -269,7 +286,7 @@ def run_sharded(args, rank, world, local_rank):
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e_sharded(args, cfg, topo, sh, qx, kx, v, cam, ft, w, dev, useful_flops,
-                              world)
+                              world, k_rows)
     peak_b, peak_s, hbm, peak_kind = load_peaks()
     # kernel roofline: this rank's share of the useful FLOPs over its slowest
     # attention launch (the players split evenly or nearly so)
@@ -286,6 +303,8 @@ def run_sharded(args, rank, world, local_rank):
                                   f"(rank 0: {topo.segments[0]}); "
                                   f"mate frames: {sh.transport}",
                    "remote_units_rank0": len(topo.needs[0]),
+                   "kv_layout": ("64-token pages shuffled by seed (%d pages)" % pages.numel()
+                                 if pages is not None else "rows in place"),
                    "tile_gflop_per_step_rank0": round(tile_flops / 1e9, 1),
                    "l2": "inputs larger than L2"},
         "breakdown_ms": {k: round(v_, 4) for k, v_ in parts.items()},
@@ -308,10 +327,13 @@ def run_sharded(args, rank, world, local_rank):
     return line
 
 
-def run_e2e_sharded(args, cfg, topo, sh, qx, kx, v, cam, ft, w, dev, useful_flops, world):
+def run_e2e_sharded(args, cfg, topo, sh, qx, kx, v, cam, ft, w, dev, useful_flops, world,
+                    k_rows=None):
     """The sharded layer through its public API with pinned host buffers: each
     rank copies its rows' projections and camera tokens in and its output
-    rows out every step."""
+    rows out every step.  With a page table (``k_rows``) the values arrive
+    in their pages, as a paged cache holds them, and the prologue writes the
+    keys into the same pages."""
     import torch
     import torch.distributed as dist
 
@@ -320,7 +342,7 @@ def run_e2e_sharded(args, cfg, topo, sh, qx, kx, v, cam, ft, w, dev, useful_flop
     hq, hk, hv, hc = (t.cpu().pin_memory() for t in (qx, kx, v, cam))
     ho = torch.empty_like(hq).pin_memory()
     dq, dk, dv, dc = (torch.empty_like(t, device=dev) for t in (hq, hk, hv, hc))
-    qb, kb = torch.empty_like(dq), torch.empty_like(dq)
+    qb, kb = torch.empty_like(dq), torch.empty_like(dv)
     if sh.transport == "peer":
         dv, kb = sh.v_buffer(), sh.k_buffer()
     stream = torch.cuda.current_stream(dev)
@@ -329,7 +351,8 @@ def run_e2e_sharded(args, cfg, topo, sh, qx, kx, v, cam, ft, w, dev, useful_flop
         for d_, h_ in ((dq, hq), (dk, hk), (dv, hv), (dc, hc)):
             d_.copy_(h_, non_blocking=True)
         hier_prep_qk(dq, dk, ft, cfg.H, norm_q_weight=w["nqw"], norm_k_weight=w["nkw"],
-                     cam_tokens=dc, cam_q_weight=w["wcq"], cam_k_weight=w["wck"], out=(qb, kb))
+                     cam_tokens=dc, cam_q_weight=w["wcq"], cam_k_weight=w["wck"], out=(qb, kb),
+                     k_out_rows=k_rows)
         o = sh.forward(qb, kb, dv)
         ho.copy_(o, non_blocking=True)
 

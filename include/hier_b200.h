@@ -177,12 +177,15 @@ int hier_dense_block_plan_build(const uint8_t* mask, int64_t S, int64_t ld, void
  * (multics/models/rope.py:248-254).  cam may be NULL (no camera tokens).
  * freqs: float32 [S, D/2, 2] (cos, sin) per token, shared by all heads.
  * Row strides are in elements.  out_rows (int32 [S], may be NULL) writes
- * token r's q and k to row out_rows[r] of q_out / k_out. */
+ * token r's q and k to row out_rows[r] of q_out / k_out; k_out_rows (may be
+ * NULL: out_rows) gives k its own rows, e.g. the physical rows of a paged
+ * key pool.  dim = H*D a multiple of 128 up to 3072, D dividing 256, cam_dim
+ * 12 or 16. */
 int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, const void* cam,
                  int32_t cam_dim, const void* wcq, const void* wck, const void* nqw,
                  const void* nkw, const float* freqs, int64_t S, int32_t H, int32_t D,
                  float eps, void* q_out, void* k_out, int64_t out_stride,
-                 const int32_t* out_rows, void* stream);
+                 const int32_t* out_rows, const int32_t* k_out_rows, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Attention
@@ -462,6 +465,13 @@ typedef struct hier_shard_desc {
   int32_t strip_begin[HIER_SHARD_MAX_LOCAL];  /* the 256-row strips [begin, end) of the */
   int32_t strip_end[HIER_SHARD_MAX_LOCAL];    /*   slot's player this rank computes */
   int32_t hub_partials[HIER_SHARD_MAX_LOCAL]; /* 1: this rank computes the player's hub partials */
+  /* Paged player rows (key/value stream 0) in pages of 64 rows: logical row
+   * r of stream 0 lives at physical row page_table[r / 64] * 64 + r % 64 of
+   * the stream's tensors (n_pages >= ceil(own_rows / 64) entries).  NULL: rows
+   * in place.  Paging needs a single shard holding every player. */
+  const int32_t* page_table;
+  int32_t n_pages;
+  int32_t reserved_paged;
 } hier_shard_desc;
 
 typedef struct hier_shard_sizes_t {
@@ -486,7 +496,12 @@ int hier_shard_count(const hier_shard_desc* g, int32_t* counts, int32_t* totals,
 
 /* Second pass: the plan (q_pairs [n_pairs][8], kv_tiles, tile_masks, order
  * [n_pairs] or NULL: every pair by descending work); status bit 1: tile
- * capacity, bit 4: mask capacity. */
+ * capacity, bit 4: mask capacity, bit 5: a pair touches more pages of the
+ * paged stream than the builder's page list holds.  With a page table the
+ * player keys of a pair are covered page by page (every row of a page it
+ * touches, masked by the unit-level edges), so each 64-row key box is one
+ * physical page, the reference's paged KV layout
+ * (kernels/hier_paged_attention.py:209-260) with 64-token pages. */
 int hier_shard_build(const hier_shard_desc* g, const int32_t* counts, int32_t* q_pairs,
                      int32_t* kv_tiles, int32_t tile_capacity, uint32_t* tile_masks,
                      int64_t mask_capacity, int32_t* order, int32_t* status, void* stream);

@@ -95,6 +95,7 @@ class HierShardDesc(ctypes.Structure):
         ("labels", c_void_p), ("active", c_void_p), ("remote_key", c_void_p),
         ("local_player", c_int32 * SHARD_MAX_LOCAL), ("strip_begin", c_int32 * SHARD_MAX_LOCAL),
         ("strip_end", c_int32 * SHARD_MAX_LOCAL), ("hub_partials", c_int32 * SHARD_MAX_LOCAL),
+        ("page_table", c_void_p), ("n_pages", c_int32), ("reserved_paged", c_int32),
     ]
 
 
@@ -135,7 +136,7 @@ _SIGS = {
     "hier_dense_block_plan_build": (c_int, [_P, c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P, _P,
                                             _P]),
     "hier_prep_qk": (c_int, [_P, _P, c_int64, _P, c_int32, _P, _P, _P, _P, _P, c_int64, c_int32,
-                             c_int32, c_float, _P, _P, c_int64, _P, _P]),
+                             c_int32, c_float, _P, _P, c_int64, _P, _P, _P]),
     "hier_attn_fwd": (c_int, [_P, c_int64, c_int64, _P, _P, c_int64, c_int64, _P, c_int64, c_int32,
                               c_int32, _P, c_int32, _P, _P, _P, c_float, _P, _P]),
     "hier_attn_fwd_streams": (c_int, [_P, c_int64, c_int64, c_int32, _P, _P, _P, _P, _P, c_int64,

@@ -80,13 +80,15 @@ def _rows(x):
 
 
 def hier_prep_qk(qx, kx, freqs, num_heads, *, norm_q_weight, norm_k_weight, cam_tokens=None,
-                 cam_q_weight=None, cam_k_weight=None, eps=1e-6, out=None, out_rows=None):
+                 cam_q_weight=None, cam_k_weight=None, eps=1e-6, out=None, out_rows=None,
+                 k_out_rows=None):
     """``q = rope(rmsnorm(qx + cam @ Wq^T) * wq)`` and the same for k, bf16.
 
     ``freqs``: complex ``[S,1,D/2]`` (as built by the reference's freq
     builders) or a float32 ``[S,D/2,2]`` table from :func:`freqs_table`.
-    ``out_rows`` (int32 ``[S]`` on the device, a permutation) writes token
-    ``r`` to row ``out_rows[r]`` of the outputs."""
+    ``out_rows`` (int32 ``[S]`` on the device) writes token ``r`` to row
+    ``out_rows[r]`` of the outputs; ``k_out_rows`` gives k its own rows (a
+    paged key pool), ``out`` then holds ``(q_out, k_out)`` sized for them."""
     q2, k2 = _rows(qx), _rows(kx)
     S, dim = q2.shape
     if q2.dtype != torch.bfloat16 or k2.dtype != torch.bfloat16:
@@ -117,13 +119,15 @@ def hier_prep_qk(qx, kx, freqs, num_heads, *, norm_q_weight, norm_k_weight, cam_
         cam_k_weight = cam_k_weight.to(torch.bfloat16).contiguous()
     nqw = norm_q_weight.to(torch.bfloat16).contiguous()
     nkw = norm_k_weight.to(torch.bfloat16).contiguous()
-    if out_rows is not None and (out_rows.dtype != torch.int32 or out_rows.numel() != S
-                                 or out_rows.device != q2.device):
-        raise ValueError(f"out_rows must be int32 [{S}] on {q2.device}")
+    for name, m in (("out_rows", out_rows), ("k_out_rows", k_out_rows)):
+        if m is not None and (m.dtype != torch.int32 or m.numel() != S or m.device != q2.device):
+            raise ValueError(f"{name} must be int32 [{S}] on {q2.device}")
+    if q_out.stride(0) != k_out.stride(0):
+        raise ValueError("q and k outputs must share a row stride")
     check(_lib.lib().hier_prep_qk(
         ptr(q2), ptr(k2), q2.stride(0), ptr(cam), cam_dim, ptr(cam_q_weight), ptr(cam_k_weight),
         ptr(nqw), ptr(nkw), ptr(ft), S, num_heads, D, float(eps), ptr(q_out), ptr(k_out),
-        q_out.stride(0), ptr(out_rows), stream_ptr(q2.device)))
+        q_out.stride(0), ptr(out_rows), ptr(k_out_rows), stream_ptr(q2.device)))
     return q_out, k_out
 
 
@@ -184,7 +188,7 @@ class HierSequencePlan:
     sequence rows from their log-sum-exp.  Same edges as the block plan, so the same
     results up to the order of floating-point sums."""
 
-    def __init__(self, spec, num_heads: int):
+    def __init__(self, spec, num_heads: int, page_table=None):
         from .sharded import ShardedHierAttention, ShardTopology
 
         if not HierSequencePlan.supports(spec):
@@ -197,7 +201,8 @@ class HierSequencePlan:
                              rank=0)
         self.topo = topo
         self.num_heads = num_heads
-        self.core = ShardedHierAttention(topo, num_heads, dev, active=spec.active)
+        self.core = ShardedHierAttention(topo, num_heads, dev, active=spec.active,
+                                         page_table=page_table)
         order = topo.local_rows()  # plan row -> sequence row
         inv = np.empty_like(order)
         inv[order] = np.arange(order.size)
@@ -207,7 +212,43 @@ class HierSequencePlan:
         self.seq_to_plan = torch.from_numpy(inv.astype(np.int32)).to(dev)
         self.hub_src = torch.from_numpy((order[self.A:] - self.A).astype(np.int64)).to(dev)
         self.hub_dst = self.plan_to_seq[self.A:].contiguous()
+        self.paged = page_table is not None
+        if self.paged:
+            # key/value pool: the player rows in 64-row pages, then the hub
+            # rows in plan order; pool_rows[r] = pool row of sequence row r
+            pt = torch.as_tensor(page_table).to(torch.int64).cpu()
+            if pt.numel() * 64 < self.A:
+                raise ValueError(f"page table of {pt.numel()} pages is short of {self.A} rows")
+            base = self.core.page_rows
+            plan = np.arange(self.S)
+            phys = np.empty(self.S, np.int64)
+            pr = plan[:self.A]
+            phys[:self.A] = pt.numpy()[pr // 64] * 64 + pr % 64
+            phys[self.A:] = base + (plan[self.A:] - self.A)
+            self.pool_size = base + (self.S - self.A)
+            self.pool_rows = torch.from_numpy(phys[inv].astype(np.int32)).to(dev)
         self.core.check_status()
+
+    def to_pool(self, x):
+        """A sequence-order ``[S, H*D]`` tensor laid out as this paged plan's
+        key/value pool (the layout the prologue writes k into)."""
+        pool = torch.zeros((self.pool_size, x.shape[1]), dtype=x.dtype, device=x.device)
+        pool.index_copy_(0, self.pool_rows.long(), _rows(x))
+        return pool
+
+    def attend_paged(self, q_plan, k_pool, v_pool, out=None):
+        """Attention of a paged plan: ``q_plan`` in plan row order, ``k_pool``
+        / ``v_pool`` in the pool layout (:meth:`to_pool`); returns ``out`` in
+        sequence order."""
+        if not self.paged:
+            raise ValueError("attend_paged needs a plan built with a page table")
+        if out is None:
+            out = torch.empty((self.S, q_plan.shape[1]), dtype=q_plan.dtype, device=q_plan.device)
+        base = self.core.page_rows
+        self.core.attend(q_plan, k_pool, v_pool, out, v_hub=v_pool[base:base + self.S - self.A],
+                         out_rows=self.plan_to_seq)
+        self.core.merge(out, out_rows=self.hub_dst)
+        return out
 
     @staticmethod
     def supports(spec) -> bool:

@@ -31,7 +31,8 @@ struct PrepArgs {
   __nv_bfloat16* q_out;
   __nv_bfloat16* k_out;
   int64_t out_stride;
-  const int32_t* out_rows;  // output row of each input row (NULL: the same row)
+  const int32_t* out_rows;    // output row of each input row (NULL: the same row)
+  const int32_t* k_out_rows;  // the same for k (NULL: out_rows)
 };
 
 constexpr int kMaxCam = 16;
@@ -149,7 +150,8 @@ __global__ void __launch_bounds__(kPrepWarps * 32, 1) prep_qk_kernel(PrepArgs a)
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float rs = rsqrtf(ss * inv_dim + a.eps);
     // pass 2: normalise, rotate, store
-    const int64_t dst = a.out_rows ? (int64_t)a.out_rows[r] : r;
+    const int32_t* rows_map = (is_k && a.k_out_rows) ? a.k_out_rows : a.out_rows;
+    const int64_t dst = rows_map ? (int64_t)rows_map[r] : r;
     __nv_bfloat16* orow = out + dst * a.out_stride;
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
@@ -226,7 +228,7 @@ extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, co
                             int32_t cam_dim, const void* wcq, const void* wck, const void* nqw,
                             const void* nkw, const float* freqs, int64_t S, int32_t H, int32_t D,
                             float eps, void* q_out, void* k_out, int64_t out_stride,
-                            const int32_t* out_rows, void* stream) {
+                            const int32_t* out_rows, const int32_t* k_out_rows, void* stream) {
   clear_error();
   const int dim = H * D;
   if (dim % 128 != 0 || dim > 256 * kPrepMaxChunks || D <= 0 || D % 8 != 0 || 256 % D != 0) {
@@ -259,6 +261,7 @@ extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, co
   p.k_out = (__nv_bfloat16*)k_out;
   p.out_stride = out_stride;
   p.out_rows = out_rows;
+  p.k_out_rows = k_out_rows;
   if (x_stride % 8 || out_stride % 8 || (reinterpret_cast<uintptr_t>(qx) & 15) ||
       (reinterpret_cast<uintptr_t>(kx) & 15) || (reinterpret_cast<uintptr_t>(freqs) & 15) ||
       (reinterpret_cast<uintptr_t>(q_out) & 15) || (reinterpret_cast<uintptr_t>(k_out) & 15) ||

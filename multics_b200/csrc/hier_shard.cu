@@ -67,6 +67,10 @@ using segplan::SegSmem;
 using segplan::block_scan;
 
 constexpr int kMaxCand = 2048;
+constexpr int kMaxPages = 32768;     // pages of the paged stream (bitmap bits)
+constexpr int kMaxPairPages = 2048;  // pages one pair's keys may touch
+constexpr int kPageRows = 64;
+constexpr int kStatusPageOverflow = 32;
 constexpr int kStripRows = 256;
 constexpr int kStatusTileOverflow = 2;
 constexpr int kStatusMissingRemote = 8;
@@ -90,6 +94,8 @@ struct SDims {
   int nf_mate;         // mate frames enumerated per player strip
   int c_player, c_hub; // candidates per player strip / hub-key pair
   int own_rows, hub_rows;
+  const int* page_table;  // stream 0 paged (NULL: in place)
+  int n_pages;
 };
 
 __device__ __forceinline__ int fdiv(int a, int b) {
@@ -282,10 +288,98 @@ __device__ bool pair_sees(const hier_shard_desc& g, const SDims& d, const Pair& 
   return false;
 }
 
+// Page bitmap and page list of the paged stream, after the run analysis.
+__device__ __forceinline__ uint32_t* page_bitmap(int* smem_i) {
+  return reinterpret_cast<uint32_t*>(smem_i + segplan::seg_smem_ints(kMaxCand));
+}
+__device__ __forceinline__ int* page_list(int* smem_i) {
+  return smem_i + segplan::seg_smem_ints(kMaxCand) + kMaxPages / 32;
+}
+
+// Paged stream 0: the boxes become the distinct pages the stream-0 runs
+// touch (ascending), numbered first; the other runs' boxes follow in run
+// order (m.rb recomputed, zero boxes for stream-0 runs).  m.misc[7] = pages.
+__device__ void page_boxes(const SDims& d, const SegSmem& m, int* smem_i, int* status) {
+  uint32_t* bm = page_bitmap(smem_i);
+  int* pl = page_list(smem_i);
+  const int words = (d.n_pages + 31) / 32;
+  for (int i = threadIdx.x; i < words; i += kThreads) bm[i] = 0u;
+  __syncthreads();
+  const int n_runs = m.misc[1];
+  for (int r = threadIdx.x; r < n_runs; r += kThreads) {
+    const int k = m.rk[r];
+    if ((k >> segplan::kStreamShift) != 0) continue;
+    const int row = k & ((1 << segplan::kStreamShift) - 1);
+    const int len = m.rf[r + 1] - m.rf[r];
+    for (int p = row / kPageRows; p <= (row + len - 1) / kPageRows; ++p)
+      atomicOr(bm + p / 32, 1u << (p % 32));
+  }
+  __syncthreads();
+  int* wtmp = m.misc + 8;
+  int carry = 0;
+  for (int base = 0; base < words; base += kThreads) {
+    const int i = base + threadIdx.x;
+    const uint32_t w = i < words ? bm[i] : 0u;
+    const int incl = block_scan<false>(__popc(w), wtmp) + carry;
+    int pos = incl - __popc(w);
+    for (uint32_t x = w; x; x &= x - 1, ++pos)
+      if (pos < kMaxPairPages) pl[pos] = 32 * i + __ffs(x) - 1;
+    if (threadIdx.x == kThreads - 1) m.misc[21] = incl;
+    __syncthreads();
+    carry = m.misc[21];
+    __syncthreads();
+  }
+  int n_paged = carry;
+  if (n_paged > kMaxPairPages) {
+    if (threadIdx.x == 0 && status) atomicOr(status, kStatusPageOverflow);
+    n_paged = kMaxPairPages;
+  }
+  // boxes of the other streams' runs, after the pages
+  int cb = 0;
+  for (int base = 0; base < n_runs; base += kThreads) {
+    const int r = base + threadIdx.x;
+    int nbx = 0;
+    if (r < n_runs && (m.rk[r] >> segplan::kStreamShift) != 0)
+      nbx = (m.rf[r + 1] - m.rf[r] + segplan::kBoxRows - 1) / segplan::kBoxRows;
+    const int incl = block_scan<false>(nbx, wtmp) + cb;
+    if (r < n_runs) m.rb[r] = n_paged + incl - nbx;
+    if (threadIdx.x == kThreads - 1) m.misc[21] = incl;
+    __syncthreads();
+    cb = m.misc[21];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    m.rb[n_runs] = n_paged + cb;
+    m.misc[2] = n_paged + cb;
+    m.misc[7] = n_paged;
+  }
+  __syncthreads();
+}
+
+// 64 mask bits of one query row (frame t) over page `page` of the paged
+// stream: each key row's bit is the unit-level edge to its own unit.
+__device__ uint64_t page_bits(const hier_shard_desc& g, const SDims& d, const Pair& pr, int t,
+                              int page) {
+  const int TL = d.T * d.L;
+  const int r0 = page * kPageRows, end = min(r0 + kPageRows, d.own_rows);
+  uint64_t bits = 0;
+  for (int r = r0; r < end;) {
+    const int slot = r / TL, f = (r % TL) / d.L;
+    const int e = min(end, slot * TL + (f + 1) * d.L);
+    if (edge(g, d, pr.kind, pr.id, t, unit_code(kUnitPlayer, d.player[slot], f))) {
+      const int a = r - r0, b = e - r0;
+      const uint64_t hi = b >= 64 ? ~0ull : ((1ull << b) - 1ull);
+      bits |= hi & ~((1ull << a) - 1ull);
+    }
+    r = e;
+  }
+  return bits;
+}
+
 // Candidates, runs and boxes of pair pr (all threads); m.pool holds unit
 // codes, m.dw / m.doff the attended candidates and their key offsets.
 __device__ void analyse_pair(const hier_shard_desc& g, const SDims& d, const Pair& pr,
-                             const SegSmem& m, int* status) {
+                             const SegSmem& m, int* smem_i, int* status) {
   const int C = pr.kind == kPairPlayer ? d.c_player : pr.kind == kPairHubOfPlayer ? d.T : d.c_hub;
   int missing = 0;
   for (int c = threadIdx.x; c < C; c += kThreads) {
@@ -304,6 +398,9 @@ __device__ void analyse_pair(const hier_shard_desc& g, const SDims& d, const Pai
   if (missing && status) atomicOr(status, kStatusMissingRemote);
   __syncthreads();
   segplan::analyse_runs(m, C);
+  if (threadIdx.x == 0) m.misc[7] = 0;
+  __syncthreads();
+  if (d.page_table) page_boxes(d, m, smem_i, status);
   // compact list of attended candidates with their key offsets
   int* wtmp = m.misc + 8;
   int carry = 0;
@@ -362,9 +459,11 @@ __device__ uint64_t box_bits(const hier_shard_desc& g, const SDims& d, const Pai
 // kWrite = false only counts the masked halves.
 template <bool kWrite>
 __device__ int emit_tiles(const hier_shard_desc& g, const SDims& d, const Pair& pr,
-                          const SegSmem& m, int tile_base, int mask_base, int32_t* kv_tiles,
-                          uint32_t* tile_masks) {
+                          const SegSmem& m, int* smem_i, int tile_base, int mask_base,
+                          int32_t* kv_tiles, uint32_t* tile_masks) {
   const int n_runs = m.misc[1], n_box = m.misc[2], n_tiles = (n_box + 1) >> 1;
+  const int n_paged = m.misc[7];
+  const int* pl = page_list(smem_i);
   const int h = threadIdx.x >> 7, r = threadIdx.x & 127;
   const int nrow = h ? pr.n1 : pr.n0;
   const bool row_ok = r < nrow;
@@ -372,21 +471,31 @@ __device__ int emit_tiles(const hier_shard_desc& g, const SDims& d, const Pair& 
   const int t = row_ok ? j / pr.unit : 0, slot = row_ok ? j % pr.unit : 0;
   int n_mask = 0;
   for (int i = 0; i < n_tiles; ++i) {
-    int key[2], k0[2], valid[2];
+    int key[2], k0[2], valid[2], page[2];
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
       const int b = 2 * i + s;
       const int bb = b < n_box ? b : b - 1;  // odd count: the last tile repeats a box, masked
-      const int ru = segplan::run_of_box(m, n_runs, bb);
-      const int k = bb - m.rb[ru];
-      key[s] = m.rk[ru] + segplan::kBoxRows * k;
-      k0[s] = m.rf[ru] + segplan::kBoxRows * k;
-      valid[s] = b < n_box ? min(segplan::kBoxRows, m.rf[ru + 1] - k0[s]) : 0;
+      page[s] = -1;
+      if (bb < n_paged) {  // one physical page of the paged stream
+        page[s] = pl[bb];
+        key[s] = d.page_table[page[s]] * kPageRows;
+        k0[s] = 0;
+        valid[s] = b < n_box ? kPageRows : 0;
+      } else {
+        const int ru = segplan::run_of_box(m, n_runs, bb);
+        const int k = bb - m.rb[ru];
+        key[s] = m.rk[ru] + segplan::kBoxRows * k;
+        k0[s] = m.rf[ru] + segplan::kBoxRows * k;
+        valid[s] = b < n_box ? min(segplan::kBoxRows, m.rf[ru + 1] - k0[s]) : 0;
+      }
     }
     uint64_t bits[2] = {0ull, 0ull};
     if (row_ok) {
 #pragma unroll
-      for (int s = 0; s < 2; ++s) bits[s] = box_bits(g, d, pr, m, t, slot, k0[s], valid[s]);
+      for (int s = 0; s < 2; ++s)
+        bits[s] = page[s] >= 0 ? (valid[s] ? page_bits(g, d, pr, t, page[s]) : 0ull)
+                               : box_bits(g, d, pr, m, t, slot, k0[s], valid[s]);
     }
     const bool all = (bits[0] & bits[1]) == ~0ull;
     const bool some = (bits[0] | bits[1]) != 0ull;
@@ -420,7 +529,10 @@ __device__ int emit_tiles(const hier_shard_desc& g, const SDims& d, const Pair& 
   return n_mask;
 }
 
-size_t plan_smem_bytes() { return segplan::seg_smem_ints(kMaxCand) * sizeof(int); }
+size_t plan_smem_bytes() {
+  return (segplan::seg_smem_ints(kMaxCand) + kMaxPages / 32 + kMaxPairPages + 32) * sizeof(int);
+}
+
 
 __global__ void __launch_bounds__(kThreads)
     pair_count_kernel(const hier_shard_desc g, const SDims d, int32_t* counts, int32_t* totals,
@@ -428,8 +540,8 @@ __global__ void __launch_bounds__(kThreads)
   extern __shared__ int smem_i[];
   const SegSmem m = segplan::seg_smem(smem_i, kMaxCand);
   const Pair pr = pair_of(d, blockIdx.x);
-  analyse_pair(g, d, pr, m, status);
-  const int n_mask = emit_tiles<false>(g, d, pr, m, 0, 0, nullptr, nullptr);
+  analyse_pair(g, d, pr, m, smem_i, status);
+  const int n_mask = emit_tiles<false>(g, d, pr, m, smem_i, 0, 0, nullptr, nullptr);
   if (threadIdx.x == 0) {
     const int n_tiles = (m.misc[2] + 1) >> 1;
     counts[2 * blockIdx.x] = n_tiles;
@@ -461,7 +573,7 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == kThreads - 1) bases[1] = mb;
   __syncthreads();
   const int tile_base = bases[0], mask_base = bases[1];
-  analyse_pair(g, d, pr, m, nullptr);
+  analyse_pair(g, d, pr, m, smem_i, nullptr);
   const int n_tiles = (m.misc[2] + 1) >> 1;
   if (n_tiles != counts[2 * pi] || tile_base + n_tiles > tile_capacity ||
       (int64_t)mask_base + counts[2 * pi + 1] > mask_capacity) {
@@ -483,7 +595,7 @@ __global__ void __launch_bounds__(kThreads)
     }
     return;
   }
-  emit_tiles<true>(g, d, pr, m, tile_base, mask_base, kv_tiles, tile_masks);
+  emit_tiles<true>(g, d, pr, m, smem_i, tile_base, mask_base, kv_tiles, tile_masks);
   if (threadIdx.x == 0) {
     int32_t* rec = q_pairs + (int64_t)pi * 8;
     rec[0] = pr.q0;
@@ -567,6 +679,19 @@ int make_sdims(const hier_shard_desc* g, SDims* d) {
   }
   d->own_rows = (int)own_rows;
   d->hub_rows = (int)hub_rows;
+  d->page_table = g->page_table;
+  d->n_pages = g->page_table ? g->n_pages : 0;
+  if (g->page_table) {
+    if (g->n_local != g->P) {
+      set_error(HIER_EVALUE, "paged player rows need a single shard holding all %d players", g->P);
+      return HIER_EVALUE;
+    }
+    if ((int64_t)g->n_pages * kPageRows < own_rows || g->n_pages > kMaxPages) {
+      set_error(HIER_EVALUE, "page table of %d pages for %lld player rows (at most %d pages)",
+                g->n_pages, (long long)own_rows, kMaxPages);
+      return HIER_EVALUE;
+    }
+  }
   auto cdiv = [](int64_t a, int64_t b) { return (int)((a + b - 1) / b); };
   d->nps = cdiv((int64_t)d->T * d->L, kStripRows);
   d->nph = d->KL > 0 ? cdiv((int64_t)d->T * d->KL, kStripRows) : 0;

@@ -78,7 +78,7 @@ __device__ __forceinline__ SegSmem seg_smem(int* base, int C) {
   return m;
 }
 
-inline size_t seg_smem_ints(int C) { return (size_t)9 * C + 3 + kMiscInts; }
+__host__ __device__ inline size_t seg_smem_ints(int C) { return (size_t)9 * C + 3 + kMiscInts; }
 
 // Key offsets, merged runs and box offsets from w / key (all threads).
 __device__ inline void analyse_runs(const SegSmem& m, int C) {

@@ -294,7 +294,7 @@ class ShardedHierAttention:
     :meth:`k_buffer` / :meth:`v_buffer` (other tensors are copied there)."""
 
     def __init__(self, topo: ShardTopology, num_heads: int, device, group=None,
-                 transport: str = "exchange", active=None):
+                 transport: str = "exchange", active=None, page_table=None):
         if transport not in ("exchange", "peer"):
             raise ValueError(f"unknown transport {transport!r}")
         self.topo = topo
@@ -332,6 +332,16 @@ class ShardedHierAttention:
             d.hub_partials[i] = int(t.home[p] == t.rank)
         d.labels, d.active, d.remote_key = (self._labels.data_ptr(), self._active.data_ptr(),
                                             self._keys.data_ptr())
+        # stream 0 (the shard's player rows) in 64-row pages: its key/value
+        # tensors hold page_table[p] * 64 + r % 64 for logical row r
+        self.page_rows = 0
+        if page_table is not None:
+            if t.world != 1:
+                raise ValueError("a page table is supported on a single rank (the mate-frame "
+                                 "exchange reads rows in place)")
+            self._pages = torch.as_tensor(page_table).to(device=dev, dtype=torch.int32).contiguous()
+            d.page_table, d.n_pages = self._pages.data_ptr(), int(self._pages.numel())
+            self.page_rows = (int(self._pages.max().item()) + 1) * 64
         self.desc = d
         sz = HierShardSizes()
         lib = _lib.lib()
@@ -480,8 +490,10 @@ class ShardedHierAttention:
             return
         if self.hp_rows:
             torch.index_select(q[own:own + hub], 0, self.hp_src, out=self.q_hp)
-        streams = [(k[:own], v[:own]),
-                   (k[own:own + hub], v[own:own + hub] if v_hub is None else v_hub)]
+        # key/value streams: player rows (in place, or a pool of pages), hub rows
+        n0 = self.page_rows or own
+        streams = [(k[:n0], v[:n0]),
+                   (k[n0:n0 + hub], v[n0:n0 + hub] if v_hub is None else v_hub)]
         if self.transport == "peer":
             streams += self._peers
         else:
@@ -554,8 +566,11 @@ class ShardedHierAttention:
         first launch with the all-gather overlapping the player strips was
         slower at 8 GPUs: 1.09 against 1.06 ms per config-4 layer.)"""
         t = self.topo
-        if q.shape != (self.q_rows, self.dim) or k.shape != q.shape or v.shape != q.shape:
-            raise ValueError(f"expected local rows [{self.q_rows}, {self.dim}], got "
+        kv_rows = (self.page_rows or t.own_rows) + t.hub_rows
+        if q.shape != (self.q_rows, self.dim) or k.shape != (kv_rows, self.dim) or \
+                v.shape != k.shape:
+            raise ValueError(f"expected query rows [{self.q_rows}, {self.dim}] and key/value "
+                             f"rows [{kv_rows}, {self.dim}], got "
                              f"{tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}")
         if out is None:
             out = torch.empty_like(q)

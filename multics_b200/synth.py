@@ -161,6 +161,15 @@ def make_inputs(cfg: HierConfig, device="cpu") -> LayerInputs:
     return LayerInputs(qx, kx, v, cam, wcq, wck, nqw, nkw, freqs.to(device), labels.to(device))
 
 
+def page_table(cfg: HierConfig) -> torch.Tensor:
+    """int32 logical page -> physical page of the player rows (64-token pages
+    for ``cfg.page_size``), a permutation shuffled by the config's seed."""
+    size = cfg.page_size or 64
+    n = -(-cfg.P * cfg.T * cfg.L // size)
+    g = torch.Generator().manual_seed(cfg.seed + 1)
+    return torch.randperm(n, generator=g).to(torch.int32)
+
+
 def cached_step_inputs(P=4, N=2, L=220, KL=16, KG=6, n_frames=3, local_attn=21, retained=24,
                        H=24, device="cuda", seed=0) -> dict:
     """Keyword arguments of the cached-backend plugin

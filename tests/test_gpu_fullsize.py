@@ -98,3 +98,49 @@ def test_full_size_layer_matches_fp32(name):
             assert err <= MAX_ABS, (label, h, err)
             assert cos >= MIN_COS, (label, h, cos)
     print(f"{name}: S={S} worst max_abs={worst[0]:.3g} cos={worst[1]:.6f}")
+
+
+def test_full_size_config5_paged():
+    """Configuration 5 with its 64-token pages shuffled by seed: the paged
+    sequence plan at full size against the same fp32 reference samples."""
+    from multics_b200.attention import HierSequencePlan, device_error, freqs_table, hier_prep_qk
+    from multics_b200.hier_masks import make_grouping_spec
+    from multics_b200.synth import CONFIGS, make_inputs, page_table
+
+    cfg = CONFIGS["cfg5"]
+    dev = torch.device("cuda")
+    inp = make_inputs(cfg, device=dev)
+    spec = make_grouping_spec(cfg.P, cfg.T, cfg.L, cfg.N, cfg.KL, cfg.KG, cfg.n_block,
+                              cfg.local_attn, inp.labels, None, cfg.direct, dev)
+    sp = HierSequencePlan(spec, cfg.H, page_table=page_table(cfg))
+    assert int(sp.core.status.item()) == 0
+    S = cfg.S
+    q_plan = torch.empty(S, cfg.dim, dtype=torch.bfloat16, device=dev)
+    k_pool = torch.empty(sp.pool_size, cfg.dim, dtype=torch.bfloat16, device=dev)
+    err0 = device_error(dev)
+    hier_prep_qk(inp.qx, inp.kx, freqs_table(inp.freqs), cfg.H, norm_q_weight=inp.nqw,
+                 norm_k_weight=inp.nkw, cam_tokens=inp.cam, cam_q_weight=inp.wcq,
+                 cam_k_weight=inp.wck, out=(q_plan, k_pool), out_rows=sp.seq_to_plan,
+                 k_out_rows=sp.pool_rows)
+    out = sp.attend_paged(q_plan, k_pool, sp.to_pool(inp.v))
+    torch.cuda.synchronize()
+    assert device_error(dev) == err0 == 0
+    D, H = cfg.D, cfg.H
+    freqs_c = inp.freqs.reshape(S, 1, D // 2).to(dev)
+    q32 = _fp32_prologue(inp.qx, inp.cam, inp.wcq, inp.nqw, freqs_c, H)
+    k32 = _fp32_prologue(inp.kx, inp.cam, inp.wck, inp.nkw, freqs_c, H)
+    v32 = inp.v.float()
+    um = UnitMask(cfg.P, cfg.T, cfg.L, cfg.N, cfg.KL, cfg.KG, cfg.n_block, cfg.local_attn,
+                  labels=inp.labels.cpu().numpy(), direct=cfg.direct)
+    scale = 1.0 / np.sqrt(D)
+    for label, r0, r1 in _sample_ranges(cfg)[::3] + [_sample_ranges(cfg)[-1]]:
+        m = torch.from_numpy(um.rows(r0, r1)).to(dev)
+        for h in (0, H - 1):
+            cols = slice(h * D, (h + 1) * D)
+            s = (q32[r0:r1, cols] @ k32[:, cols].t()) * scale
+            ref = torch.softmax(s.masked_fill(~m, float("-inf")), -1) @ v32[:, cols]
+            got = out[r0:r1, cols].float()
+            err = float((got - ref).abs().max())
+            cos = float((got * ref).sum() / (got.norm() * ref.norm()))
+            assert err <= MAX_ABS, (label, h, err)
+            assert cos >= MIN_COS, (label, h, cos)
