@@ -515,6 +515,7 @@ def run_ours(args, rank, world, local_rank):
     if world == 1 and not args.no_dit:
         del inp, q_buf, k_buf, o_buf
         torch.cuda.empty_cache()
+        line["action_attention"] = run_action()
         line["dit_step"] = run_dit()
     return line
 
@@ -678,6 +679,75 @@ def run_cached_step(steps=20, warmup=3):
             "key_streams": int(plan.n_streams)}
 
 
+def run_action(steps=20, warmup=3):
+    """Configuration 3's action-branch attentions at their real sizes, inputs
+    resident in HBM (each case's q/k/v/o exceed L2): the per-frame attention
+    (880 sequences of 42 frames, 1-frame block-causal mask) and the keyboard
+    cross-attention (4 players x 9 240 rows over 504 keyboard tokens, the
+    frame mask repeated), 24 heads.  Each is timed on the tcgen05 kernel
+    (``shared_mask_attention``, plan built once) and as the reference calls it
+    (``flash_attention(q, k, v, num_heads, mask)`` = rearrange + SDPA with the
+    bool mask + rearrange, bf16, ``attention.py:47-54``) on the same GPU.
+    Bound: HBM; algorithmic bytes = q, k, v read once and o written once."""
+    import torch
+    import torch.nn.functional as F
+
+    from multics_b200.action import (get_temporal_block_causal_mask, keyboard_frame_mask,
+                                     shared_mask_attention, shared_mask_plan)
+    from multics_b200.attention import device_error
+
+    _, _, hbm, peak_kind = load_peaks()
+    dev = torch.device("cuda")
+    H, Fr, L, K, P = 24, 42, 220, 12, 4
+    fm = get_temporal_block_causal_mask(Fr, 1, -1, device=dev)
+    cases = {"temporal": (P * L, Fr, Fr, fm), "keyboard": (P, Fr * L, Fr * K,
+                                                          keyboard_frame_mask(fm, L, K))}
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(5)
+    for name, (B, Lq, Lk, m) in cases.items():
+        q = torch.randn(B, Lq, H * 128, generator=g, device=dev).bfloat16()
+        k, v = (torch.randn(B, Lk, H * 128, generator=g, device=dev).bfloat16() for _ in range(2))
+        out = torch.empty_like(q)
+        plan = shared_mask_plan(m, B, Lq, Lk, dev)
+
+        def ours():
+            shared_mask_attention(q, k, v, H, m, out=out, plan=plan)
+
+        def reference():
+            qh, kh, vh = (t.view(B, t.shape[1], H, 128).transpose(1, 2) for t in (q, k, v))
+            o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=m)
+            return o.transpose(1, 2).reshape(B, Lq, H * 128)
+
+        times = {}
+        for arm, fn in (("ours", ours), ("sdpa", reference)):
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(steps)]
+            for a, b in evs:
+                a.record()
+                fn()
+                b.record()
+            torch.cuda.synchronize()
+            times[arm] = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        byts = 2 * (2 * B * Lq + 2 * B * Lk) * H * 128
+        gbs = byts / (times["ours"] * 1e-3) / 1e9
+        res[name] = {"B": B, "Lq": Lq, "Lk": Lk, "ms": round(times["ours"], 4),
+                     "reference_sdpa_ms": round(times["sdpa"], 4),
+                     "speedup_vs_sdpa": round(times["sdpa"] / times["ours"], 2),
+                     "algorithmic_mb": round(byts / 1e6, 1), "achieved_gbs": round(gbs, 1),
+                     "hbm_frac": round(gbs / hbm, 4), "n_pairs": plan.n_pairs}
+        del q, k, v, out
+        torch.cuda.empty_cache()
+    res["hbm_peak_gbs"] = hbm
+    res["peak_kind"] = f"{peak_kind} copy bandwidth"
+    res["device_error"] = device_error(dev)
+    res["note"] = ("kernel: hier_attn_kernel over the shared-mask plan (one launch per call); "
+                   "reference: torch SDPA with the bool mask on the same GPU")
+    return res
+
+
 def run_dit(steps=3, warmup=1):
     """Configuration 3: one denoising step (one model evaluation, 30 blocks)
     of the Multics-shaped DiT on this GPU, random N(0, 0.02) weights, with
@@ -694,22 +764,25 @@ def run_dit(steps=3, warmup=1):
     inputs = dit_inputs(cfg, dev)
     consts = model.prepare(inputs, dev)
     n_params = sum(p.numel() for p in model.parameters())
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(cfg.blocks)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(cfg.blocks)]
     with torch.no_grad():
         for _ in range(warmup):
             model(inputs, consts)
         torch.cuda.synchronize()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
-        attn = []
+        attn, temporal, keyboard = [], [], []
         a.record()
         for _ in range(steps):
             model(inputs, consts, attn_events=ev)
             b.record()
             torch.cuda.synchronize()
-            attn.append(sum(e0.elapsed_time(e1) for e0, e1 in ev))
+            attn.append(sum(e[0].elapsed_time(e[1]) for e in ev))
+            temporal.append(sum(e[2].elapsed_time(e[3]) for e in ev))
+            keyboard.append(sum(e[4].elapsed_time(e[5]) for e in ev))
         ms = a.elapsed_time(b) / steps
     attn_ms = statistics.mean(attn)
+    temporal_ms, keyboard_ms = statistics.mean(temporal), statistics.mean(keyboard)
     del model
     torch.cuda.empty_cache()
     return {"workload": "cfg3: one denoising step of a Wan2.2-TI2V-5B-shaped Multics DiT, "
@@ -718,9 +791,14 @@ def run_dit(steps=3, warmup=1):
                         f"text {cfg.text_len}x{cfg.text_dim}, hierarchical self-attention in every "
                         "block", "n_gpus": 1, "params": n_params, "dtype": "bf16",
             "ms_per_step": round(ms, 2), "hier_attention_ms_per_step": round(attn_ms, 2),
-            "hier_attention_share": round(attn_ms / ms, 4), "steps": steps, "warmup": warmup,
-            "note": "self-attention = q/k/v/o projections + fused prologue + tcgen05 attention "
-                    "(the module as called); other branches on cuBLAS / PyTorch SDPA"}
+            "hier_attention_share": round(attn_ms / ms, 4),
+            "action_temporal_ms_per_step": round(temporal_ms, 2),
+            "action_keyboard_ms_per_step": round(keyboard_ms, 2),
+            "steps": steps, "warmup": warmup,
+            "note": "self-attention and action temporal attention = q/k/v/o projections + fused "
+                    "prologue + tcgen05 attention (the modules as called); keyboard "
+                    "cross-attention = projections + RMSNorm + tcgen05 attention; other "
+                    "branches on cuBLAS / PyTorch SDPA"}
 
 
 def cpu_baseline(cfg, sample_seconds=15.0):

@@ -164,6 +164,29 @@ int hier_dense_block_plan_build(const uint8_t* mask, int64_t S, int64_t ld, void
                                 int32_t* kv_tiles, uint32_t* row_masks, int32_t* order,
                                 int32_t* n_kv_tiles, void* stream);
 
+/* Batched attention under one bool mask [Lq, Lk] shared by every batch entry
+ * (query row b*Lq + i sees key row b*Lk + j iff mask[i*ld + j] != 0): the
+ * reference's flash_attention(q, k, v, num_heads, mask) with a mask that
+ * broadcasts over the batch (multics/models/attention.py:39-54), as the DiT
+ * block's action branch calls it: the per-frame mouse attention with
+ * get_temporal_block_causal_mask (hier_masks.py:1152-1166, blocks.py:441-447,
+ * 684-686), the keyboard cross-attention with the repeated frame mask
+ * (blocks.py:446-448,693-697) and their cached forms (blocks.py:256-375).
+ * hier_shared_mask_plan_size gives the plan's extent: n_pairs query pairs and
+ * tiles_per_pair kv_tiles entries reserved per pair; the caller allocates
+ * q_pairs [n_pairs][8], kv_tiles [n_pairs * tiles_per_pair][4], tile_masks
+ * [n_pairs * tiles_per_pair * 2][128][4] uint32 and order [n_pairs] (or
+ * passes NULL for the identity order).  Sequences of at most 64 rows are
+ * packed several to a 128-row tile with block-diagonal masks.  The plan runs
+ * on hier_attn_fwd (keys and values [B*Lk, H*D]).  Errors: HIER_EVALUE for
+ * non-positive sizes, more than 2^24 - 256 key rows, or a NULL mask /
+ * ld < Lk. */
+int hier_shared_mask_plan_size(int64_t B, int64_t Lq, int64_t Lk, int32_t* n_pairs,
+                               int32_t* tiles_per_pair);
+int hier_shared_mask_plan_build(const uint8_t* mask, int64_t ld, int64_t B, int64_t Lq,
+                                int64_t Lk, int32_t* q_pairs, int32_t* kv_tiles,
+                                uint32_t* tile_masks, int32_t* order, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Fused Q/K prologue
  * ------------------------------------------------------------------------- */
@@ -175,7 +198,10 @@ int hier_dense_block_plan_build(const uint8_t* mask, int64_t S, int64_t ld, void
  * (_apply_camera_qk, attention.py:307-320, bias-free, cam_dim inputs),
  * RMSNorm over the full dim (attention.py:231-242, eps) and rope_apply
  * (multics/models/rope.py:248-254).  cam may be NULL (no camera tokens).
- * freqs: float32 [S, D/2, 2] (cos, sin) per token, shared by all heads.
+ * freqs: float32 [freqs_rows, D/2, 2] (cos, sin), shared by all heads; token
+ * r uses row r % freqs_rows (freqs_rows = S: one row per token; the frame
+ * count: a batch of sequences flattened to rows, as the per-frame action
+ * attention's [frames, 1, D/2] table broadcasts over its batch).
  * Row strides are in elements.  out_rows (int32 [S], may be NULL) writes
  * token r's q and k to row out_rows[r] of q_out / k_out; k_out_rows (may be
  * NULL: out_rows) gives k its own rows, e.g. the physical rows of a paged
@@ -183,8 +209,8 @@ int hier_dense_block_plan_build(const uint8_t* mask, int64_t S, int64_t ld, void
  * 12 or 16. */
 int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, const void* cam,
                  int32_t cam_dim, const void* wcq, const void* wck, const void* nqw,
-                 const void* nkw, const float* freqs, int64_t S, int32_t H, int32_t D,
-                 float eps, void* q_out, void* k_out, int64_t out_stride,
+                 const void* nkw, const float* freqs, int64_t freqs_rows, int64_t S, int32_t H,
+                 int32_t D, float eps, void* q_out, void* k_out, int64_t out_stride,
                  const int32_t* out_rows, const int32_t* k_out_rows, void* stream);
 
 /* ---------------------------------------------------------------------------

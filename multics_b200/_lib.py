@@ -135,7 +135,11 @@ _SIGS = {
                                             _P]),
     "hier_dense_block_plan_build": (c_int, [_P, c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P, _P,
                                             _P]),
-    "hier_prep_qk": (c_int, [_P, _P, c_int64, _P, c_int32, _P, _P, _P, _P, _P, c_int64, c_int32,
+    "hier_shared_mask_plan_size": (c_int, [c_int64, c_int64, c_int64, _P, _P]),
+    "hier_shared_mask_plan_build": (c_int, [_P, c_int64, c_int64, c_int64, c_int64, _P, _P, _P,
+                                            _P, _P]),
+    "hier_prep_qk": (c_int, [_P, _P, c_int64, _P, c_int32, _P, _P, _P, _P, _P, c_int64, c_int64,
+                             c_int32,
                              c_int32, c_float, _P, _P, c_int64, _P, _P, _P]),
     "hier_attn_fwd": (c_int, [_P, c_int64, c_int64, _P, _P, c_int64, c_int64, _P, c_int64, c_int32,
                               c_int32, _P, c_int32, _P, _P, _P, c_float, _P, _P]),
@@ -169,6 +173,9 @@ _SIGS = {
 
 _LIB = None
 
+# hier_abi_version() of the library these signatures describe
+ABI_VERSION = 2
+
 
 def lib():
     """Load the in-tree library (once) and declare the C signatures."""
@@ -183,6 +190,10 @@ def lib():
             fn = getattr(h, name)
             fn.restype = res
             fn.argtypes = args
+        if h.hier_abi_version() != ABI_VERSION:
+            raise RuntimeError(
+                f"{LIB_PATH.name} has ABI version {h.hier_abi_version()}, the package expects "
+                f"{ABI_VERSION}; rebuild it with `python -m multics_b200.build`")
         _LIB = h
     return _LIB
 

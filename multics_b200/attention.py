@@ -30,7 +30,7 @@ from .hier_masks import HierBlockMask, block_mask_for_spec, build_dense_block_pl
 
 __all__ = ["hier_prep_qk", "hier_block_attention", "freqs_table", "RMSNorm", "SelfAttention",
            "AttentionPlan", "attention_from_plan", "HierSequencePlan", "sequence_plan",
-           "hier_attention_layer", "attention_mask_plan"]
+           "hier_attention_layer", "attention_mask_plan", "CrossAttention"]
 
 # Work plan of the full-sequence layer entry points: "segments" (the
 # HierSequencePlan wherever the grouping allows it) or "blocks" (always the
@@ -99,8 +99,9 @@ def hier_prep_qk(qx, kx, freqs, num_heads, *, norm_q_weight, norm_k_weight, cam_
     D = dim // num_heads
     ft = freqs if (freqs.dtype == torch.float32 and freqs.dim() == 3
                    and freqs.shape[-1] == 2) else freqs_table(freqs)
-    if ft.shape[0] != S or ft.shape[1] * 2 != D:
-        raise ValueError(f"freqs must be [S={S},1,{D // 2}], got {tuple(freqs.shape)}")
+    if ft.shape[0] < 1 or S % ft.shape[0] or ft.shape[1] * 2 != D:
+        raise ValueError(f"freqs must be [S={S},1,{D // 2}] (or [F,1,{D // 2}] with F dividing S, "
+                         f"row r using entry r % F), got {tuple(freqs.shape)}")
     ft = ft.to(q2.device).contiguous()
     if out is None:
         q_out = torch.empty(S, dim, dtype=torch.bfloat16, device=q2.device)
@@ -126,7 +127,7 @@ def hier_prep_qk(qx, kx, freqs, num_heads, *, norm_q_weight, norm_k_weight, cam_
         raise ValueError("q and k outputs must share a row stride")
     check(_lib.lib().hier_prep_qk(
         ptr(q2), ptr(k2), q2.stride(0), ptr(cam), cam_dim, ptr(cam_q_weight), ptr(cam_k_weight),
-        ptr(nqw), ptr(nkw), ptr(ft), S, num_heads, D, float(eps), ptr(q_out), ptr(k_out),
+        ptr(nqw), ptr(nkw), ptr(ft), ft.shape[0], S, num_heads, D, float(eps), ptr(q_out), ptr(k_out),
         q_out.stride(0), ptr(out_rows), ptr(k_out_rows), stream_ptr(q2.device)))
     return q_out, k_out
 
@@ -431,7 +432,12 @@ class SelfAttention(nn.Module):
         ``build_stage2_hier_flex_block_mask`` (the Flex path), the dense bool
         mask of ``build_stage2_hier_self_attn_mask`` (the sdpa path; it
         carries its grouping and runs on the grouping's plan), any other dense
-        ``[S,S]`` mask (block plan built from its bytes), or None (unmasked)."""
+        ``[S,S]`` mask (block plan built from its bytes), or None (unmasked).
+        A batch ``x`` ``[B, L, dim]`` with ``B > 1`` is the DiT block's
+        per-frame action attention (``blocks.py:684-686``): ``mask`` is one
+        ``[L, L]`` mask shared by the batch and ``freqs`` ``[L, 1, D/2]``."""
+        if x.dim() == 3 and x.shape[0] > 1:
+            return self._forward_batch(x, freqs, mask, cam_tokens)
         mask = attention_mask_plan(mask, x.shape[1], x.device)
         sp = sequence_plan(mask, self.num_heads)
         q, k, v = self.project_qkv(x, freqs, cam_tokens,
@@ -441,6 +447,75 @@ class SelfAttention(nn.Module):
         else:
             out = attention_from_plan(q, k, v, mask, self.num_heads)
         return self.o(out.unsqueeze(0))
+
+
+    def _forward_batch(self, x, freqs, mask, cam_tokens):
+        """``B`` sequences of ``L`` tokens under one shared mask: projections,
+        the fused prologue over the ``B*L`` rows (RoPE table row ``r % L``)
+        and the shared-mask attention plan."""
+        from .action import shared_mask_attention
+
+        B, L, dim = x.shape
+        if cam_tokens is not None:
+            if self.cam_q is None or self.cam_k is None:
+                raise RuntimeError("camera_pose was provided but enable_camera_pose_qk() was not called")
+            if cam_tokens.shape[:2] != x.shape[:2]:
+                raise ValueError(f"camera tokens shape {tuple(cam_tokens.shape[:2])} must match "
+                                 f"q/k tokens {tuple(x.shape[:2])}")
+            cam_tokens = cam_tokens.reshape(B * L, -1)
+        q, k = hier_prep_qk(
+            self.q(x).reshape(B * L, dim), self.k(x).reshape(B * L, dim), freqs, self.num_heads,
+            norm_q_weight=self.norm_q.weight, norm_k_weight=self.norm_k.weight,
+            cam_tokens=cam_tokens, cam_q_weight=None if self.cam_q is None else self.cam_q.weight,
+            cam_k_weight=None if self.cam_k is None else self.cam_k.weight, eps=self.norm_q.eps)
+        out = shared_mask_attention(q.view(B, L, dim), k.view(B, L, dim), self.v(x),
+                                    self.num_heads, mask)
+        return self.o(out)
+
+
+class CrossAttention(nn.Module):
+    """The reference's ``CrossAttention`` (``attention.py:1046-1090``): same
+    constructor, parameters and ``forward(x, y, mask=None)``.  q from ``x``,
+    k and v from the context ``y`` (after 257 image tokens when
+    ``has_image_input``), RMSNorm on q and k, no RoPE; the attention runs on
+    the tcgen05 kernel with ``mask`` shared by the batch (the keyboard
+    cross-attention's repeated frame mask, ``blocks.py:692-697``) or
+    unmasked (the text cross-attention)."""
+
+    def __init__(self, dim: int, num_heads: int, eps: float = 1e-6,
+                 has_image_input: bool = False):
+        super().__init__()
+        self.dim = dim
+        self.num_heads = num_heads
+        self.head_dim = dim // num_heads
+        self.q = nn.Linear(dim, dim)
+        self.k = nn.Linear(dim, dim)
+        self.v = nn.Linear(dim, dim)
+        self.o = nn.Linear(dim, dim)
+        self.norm_q = RMSNorm(dim, eps=eps)
+        self.norm_k = RMSNorm(dim, eps=eps)
+        self.has_image_input = has_image_input
+        if has_image_input:
+            self.k_img = nn.Linear(dim, dim)
+            self.v_img = nn.Linear(dim, dim)
+            self.norm_k_img = RMSNorm(dim, eps=eps)
+
+    def forward(self, x, y, mask=None):
+        from .action import shared_mask_attention
+
+        if self.has_image_input:
+            img, ctx = y[:, :257], y[:, 257:]
+        else:
+            ctx = y
+        q = self.norm_q(self.q(x))
+        k = self.norm_k(self.k(ctx))
+        v = self.v(ctx)
+        out = shared_mask_attention(q, k, v, self.num_heads, mask)
+        if self.has_image_input:
+            k_img = self.norm_k_img(self.k_img(img))
+            v_img = self.v_img(img)
+            out = out + shared_mask_attention(q, k_img, v_img, self.num_heads, mask)
+        return self.o(out)
 
 
 _INFER_KERNELS = ("sdpa", "segmented", "tiled128", "packed_varlen", "paged_kv")

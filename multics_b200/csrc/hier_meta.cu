@@ -706,6 +706,197 @@ extern "C" int hier_dense_block_plan_build(const uint8_t* mask, int64_t S, int64
 }
 
 // ---------------------------------------------------------------------------
+// Plan of a batched attention under one mask shared by every batch entry
+// ---------------------------------------------------------------------------
+//
+// The action branch of the reference's DiT block calls
+// flash_attention(q, k, v, num_heads, mask) on B independent sequences with
+// one bool mask [Lq, Lk] broadcast over the batch (multics/models/
+// attention.py:39-54): the per-frame mouse attention (B = players x patches,
+// Lq = Lk = frames, get_temporal_block_causal_mask, hier_masks.py:1152-1166;
+// blocks.py:441-447,684-686), the keyboard cross-attention (B = players,
+// Lq = frames x patches, Lk = frames x 12, the frame mask repeated,
+// blocks.py:446-448,693-697) and their cached forms over a rolling window
+// (blocks.py:256-375).  Query row b*Lq + i sees key row b*Lk + j iff
+// mask[i, j].  Short sequences are packed: g = min(128/Lq, 128/Lk) batch
+// entries (a "unit") share one 128-row query tile and one 128-key tile, with
+// block-diagonal row masks.  Query tiles are paired two per CTA as in every
+// plan; a pair's key tiles cover the key rows its query rows see (one range
+// when both tiles are in the same unit, one range per tile otherwise).
+
+namespace hier {
+
+struct SharedMaskDims {
+  int64_t B, Lq, Lk, ld;
+  int64_t g;        // batch entries per unit
+  int64_t nqt;      // query tiles per unit
+  int64_t n_tiles;  // query tiles in all
+  int64_t n_pairs;
+  int64_t cap;      // kv_tiles entries (and mask pairs) reserved per pair
+};
+
+static int shared_mask_dims(int64_t B, int64_t Lq, int64_t Lk, SharedMaskDims* d) {
+  if (B < 1 || Lq < 1 || Lk < 1) {
+    set_error(HIER_EVALUE, "shared-mask plan: B=%lld, Lq=%lld, Lk=%lld must be positive",
+              (long long)B, (long long)Lq, (long long)Lk);
+    return HIER_EVALUE;
+  }
+  // key rows are addressed with 24 bits (stream << 24 | row); 256 rows of
+  // slack keep a tile's second half inside that range
+  if (B * Lq > (int64_t)INT32_MAX / 2 || B * Lk > (int64_t)(1 << 24) - 256) {
+    set_error(HIER_EVALUE, "shared-mask plan: %lld query rows / %lld key rows exceed the plan's "
+              "row range", (long long)(B * Lq), (long long)(B * Lk));
+    return HIER_EVALUE;
+  }
+  d->B = B, d->Lq = Lq, d->Lk = Lk, d->ld = Lk;
+  const int64_t g = (Lq <= 128 && Lk <= 128) ? (128 / Lq < 128 / Lk ? 128 / Lq : 128 / Lk) : 1;
+  d->g = g < B ? g : B;
+  const int64_t units = (B + d->g - 1) / d->g;
+  d->nqt = (d->g * Lq + 127) / 128;
+  d->n_tiles = units * d->nqt;
+  d->n_pairs = (d->n_tiles + 1) / 2;
+  d->cap = 2 * ((d->g * Lk + 127) / 128);
+  if (d->n_pairs * d->cap * 2 > (int64_t)INT32_MAX / 128) {
+    set_error(HIER_EVALUE, "shared-mask plan: %lld pairs x %lld key tiles is too large",
+              (long long)d->n_pairs, (long long)d->cap);
+    return HIER_EVALUE;
+  }
+  return HIER_OK;
+}
+
+// One 128-thread block per query pair; thread t owns row t of each tile.
+__global__ void __launch_bounds__(128) shared_mask_plan_kernel(const uint8_t* __restrict__ mask,
+                                                               SharedMaskDims d, int4* q_pairs,
+                                                               int4* kv_tiles, uint4* masks) {
+  const int64_t p = blockIdx.x;
+  const int t = threadIdx.x;
+  __shared__ int lo_s[2], hi_s[2], n_ent_s;
+  int64_t q0[2], unit[2];
+  int rows[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int64_t tile = 2 * p + h;
+    q0[h] = 0, rows[h] = 0, unit[h] = -1 - h;
+    if (tile < d.n_tiles) {
+      const int64_t u = tile / d.nqt, tt = tile % d.nqt;
+      const int64_t ur = min(d.g * d.Lq, d.B * d.Lq - u * d.g * d.Lq);  // rows of the unit
+      unit[h] = u;
+      q0[h] = u * d.g * d.Lq + tt * 128;
+      rows[h] = (int)min((int64_t)128, ur - tt * 128);
+    }
+  }
+  if (rows[1] == 0) q0[1] = q0[0];
+  if (t < 2) lo_s[t] = INT32_MAX, hi_s[t] = -1;
+  if (t == 0) n_ent_s = 0;
+  __syncthreads();
+  // key rows seen by each query row: [b*Lk + first, b*Lk + last]
+  int64_t rb[2], ri[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    rb[h] = -1, ri[h] = 0;
+    if (t < rows[h]) {
+      const int64_t r = q0[h] + t;
+      rb[h] = r / d.Lq, ri[h] = r - rb[h] * d.Lq;
+      const uint8_t* mr = mask + ri[h] * d.ld;
+      int64_t first = -1, last = -1;
+      for (int64_t j = 0; j < d.Lk; ++j)
+        if (mr[j]) {
+          if (first < 0) first = j;
+          last = j;
+        }
+      if (first >= 0) {
+        atomicMin(&lo_s[h], (int)(rb[h] * d.Lk + first));
+        atomicMax(&hi_s[h], (int)(rb[h] * d.Lk + last));
+      }
+    }
+  }
+  __syncthreads();
+  // key ranges: one shared range, or one per tile
+  int seg_lo[2] = {0, 0}, seg_hi[2] = {-1, -1}, seg_use[2] = {0, 0}, n_seg = 0;
+  const bool has0 = hi_s[0] >= 0, has1 = hi_s[1] >= 0;
+  if (has0 && has1 && unit[0] == unit[1]) {
+    seg_lo[0] = min(lo_s[0], lo_s[1]), seg_hi[0] = max(hi_s[0], hi_s[1]), seg_use[0] = 3;
+    n_seg = 1;
+  } else {
+    if (has0) seg_lo[n_seg] = lo_s[0], seg_hi[n_seg] = hi_s[0], seg_use[n_seg++] = 1;
+    if (has1) seg_lo[n_seg] = lo_s[1], seg_hi[n_seg] = hi_s[1], seg_use[n_seg++] = 2;
+  }
+  const int64_t kv_base = p * d.cap;
+  for (int sgi = 0; sgi < n_seg; ++sgi) {
+    for (int64_t ks = seg_lo[sgi]; ks <= seg_hi[sgi]; ks += 128) {
+      const int e = n_ent_s;
+      int sel[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        const bool on = (seg_use[sgi] >> h) & 1;
+        if (on && t < rows[h]) {
+          // keys of this row's batch entry inside [ks, ks + 128)
+          const int64_t kb = rb[h] * d.Lk;
+          const int64_t c_lo = max((int64_t)0, kb - ks);
+          const int64_t c_hi = min((int64_t)128, kb + d.Lk - ks);
+          const uint8_t* mr = mask + ri[h] * d.ld + (ks - kb);
+          for (int64_t c = c_lo; c < c_hi; ++c)
+            if (mr[c]) w[c >> 5] |= 1u << (c & 31);
+        }
+        const bool row_any = (w[0] | w[1] | w[2] | w[3]) != 0;
+        const bool row_full = (w[0] & w[1] & w[2] & w[3]) == 0xffffffffu;
+        const int any = __syncthreads_or(on && row_any);
+        const int full = __syncthreads_and(!on || t >= rows[h] || row_full);
+        const int64_t mi = (kv_base + e) * 2 + h;
+        if (on && any && !full) masks[mi * 128 + t] = make_uint4(w[0], w[1], w[2], w[3]);
+        sel[h] = !(on && any) ? -2 : (full ? -1 : (int)mi);
+      }
+      if (t == 0 && (sel[0] != -2 || sel[1] != -2)) {
+        kv_tiles[kv_base + e] = make_int4((int)ks, (int)ks + 64, sel[0], sel[1]);
+        n_ent_s = e + 1;
+      }
+      __syncthreads();
+    }
+  }
+  if (t == 0) {
+    q_pairs[2 * p] = make_int4((int)q0[0], rows[0], (int)q0[1], rows[1]);
+    q_pairs[2 * p + 1] = make_int4((int)kv_base, (int)(kv_base + n_ent_s), 1, 0);
+  }
+}
+
+}  // namespace hier
+
+extern "C" int hier_shared_mask_plan_size(int64_t B, int64_t Lq, int64_t Lk, int32_t* n_pairs,
+                                          int32_t* tiles_per_pair) {
+  clear_error();
+  SharedMaskDims d;
+  int rc = shared_mask_dims(B, Lq, Lk, &d);
+  if (rc) return rc;
+  *n_pairs = (int32_t)d.n_pairs;
+  *tiles_per_pair = (int32_t)d.cap;
+  return HIER_OK;
+}
+
+extern "C" int hier_shared_mask_plan_build(const uint8_t* mask, int64_t ld, int64_t B, int64_t Lq,
+                                           int64_t Lk, int32_t* q_pairs, int32_t* kv_tiles,
+                                           uint32_t* tile_masks, int32_t* order, void* stream) {
+  clear_error();
+  SharedMaskDims d;
+  int rc = shared_mask_dims(B, Lq, Lk, &d);
+  if (rc) return rc;
+  if (!mask || ld < Lk) {
+    set_error(HIER_EVALUE, "shared-mask plan: mask is NULL or its row stride %lld < Lk=%lld",
+              (long long)ld, (long long)Lk);
+    return HIER_EVALUE;
+  }
+  d.ld = ld;
+  cudaStream_t s = (cudaStream_t)stream;
+  shared_mask_plan_kernel<<<(unsigned)d.n_pairs, 128, 0, s>>>(
+      mask, d, (int4*)q_pairs, (int4*)kv_tiles, (uint4*)tile_masks);
+  if (order)
+    order_by_work_kernel<8><<<grid_for(d.n_pairs, 128), 128, 0, s>>>(q_pairs, (int)d.n_pairs,
+                                                                     order);
+  HIER_CHECK_CUDA(cudaGetLastError(), "shared-mask plan kernels launch");
+  return HIER_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Allocation-free block classification: the scratch of hier_block_mask_build
 // (unit matrix + block classes) lives in a fixed file-scope device array.
 // Host code never dereferences or passes the array's name to a kernel: its

@@ -24,6 +24,7 @@ struct PrepArgs {
   const __nv_bfloat16* nqw;
   const __nv_bfloat16* nkw;
   const float2* freqs;
+  int64_t freqs_rows;  // token r uses table row r % freqs_rows
   int64_t S;
   int dim;
   int D;
@@ -101,7 +102,8 @@ __global__ void __launch_bounds__(kPrepWarps * 32, 1) prep_qk_kernel(PrepArgs a)
     for (int i = 0; i < NCH; ++i)
       xv[i] = chunk_ok(a.dim, lane, i) ? *reinterpret_cast<const uint4*>(xr + 8 * lane + 256 * i)
                                        : make_uint4(0u, 0u, 0u, 0u);
-    const float4* fr = reinterpret_cast<const float4*>(a.freqs + r * half + pair0);
+    const int64_t rf = a.freqs_rows == a.S ? r : r % a.freqs_rows;
+    const float4* fr = reinterpret_cast<const float4*>(a.freqs + rf * half + pair0);
     const float4 f0 = fr[0], f1 = fr[1];
     if (CAM > 0) {
       const float cv = lane < CAM ? __bfloat162float(a.cam[r * CAM + lane]) : 0.f;
@@ -226,7 +228,8 @@ using namespace hier;
 
 extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, const void* cam,
                             int32_t cam_dim, const void* wcq, const void* wck, const void* nqw,
-                            const void* nkw, const float* freqs, int64_t S, int32_t H, int32_t D,
+                            const void* nkw, const float* freqs, int64_t freqs_rows, int64_t S,
+                            int32_t H, int32_t D,
                             float eps, void* q_out, void* k_out, int64_t out_stride,
                             const int32_t* out_rows, const int32_t* k_out_rows, void* stream) {
   clear_error();
@@ -242,6 +245,11 @@ extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, co
     return HIER_EVALUE;
   }
   if (S == 0) return HIER_OK;
+  if (freqs_rows <= 0 || freqs_rows > S) {
+    set_error(HIER_EVALUE, "hier_prep_qk: freqs_rows=%lld must be in [1, S=%lld]",
+              (long long)freqs_rows, (long long)S);
+    return HIER_EVALUE;
+  }
   PrepArgs p;
   p.qx = (const __nv_bfloat16*)qx;
   p.kx = (const __nv_bfloat16*)kx;
@@ -253,6 +261,7 @@ extern "C" int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, co
   p.nqw = (const __nv_bfloat16*)nqw;
   p.nkw = (const __nv_bfloat16*)nkw;
   p.freqs = (const float2*)freqs;
+  p.freqs_rows = freqs_rows;
   p.S = S;
   p.dim = dim;
   p.D = D;

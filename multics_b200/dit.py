@@ -8,11 +8,15 @@ frame, hierarchical self-attention over ``[players | hub tokens]`` with the
 camera Q/K adapters, text cross-attention, an action MLP over the mouse
 features, a per-frame (temporal) action attention, a keyboard cross-attention
 and the FFN.  This module rebuilds that block at the same shapes around
-``multics_b200.attention.SelfAttention`` so that the step time, and the
-hierarchical attention's share of it, can be measured on B200.  Weights are
-random (N(0, 0.02)), as no checkpoint is available; everything except the
-hierarchical attention runs on cuBLAS GEMMs and PyTorch's SDPA, which is the
-part of the step this library does not replace.
+``multics_b200.attention.SelfAttention`` (the hierarchical self-attention and,
+over a batch of frame sequences, the action temporal attention) and
+``multics_b200.attention.CrossAttention`` (the keyboard cross-attention), so
+that the step time, and the share of each attention in it, can be measured
+on B200.  Weights are random (N(0, 0.02)), as no checkpoint is available;
+the GEMMs, norms and the unmasked text cross-attention run on cuBLAS and
+PyTorch's SDPA, the part of the step this library does not replace.
+``DiTConfig.action_impl = "sdpa"`` runs the action branch on SDPA instead, as
+the reference's ``flash_attention(mask)`` does.
 """
 
 from __future__ import annotations
@@ -25,7 +29,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .attention import RMSNorm, SelfAttention, freqs_table
+from .attention import CrossAttention, RMSNorm, SelfAttention, freqs_table
 from .hier_masks import build_stage2_hier_flex_block_mask
 
 __all__ = ["DiTConfig", "HierDiTBlock", "HierDiT", "dit_inputs"]
@@ -58,6 +62,7 @@ class DiTConfig:
     mouse_dim: int = 2
     kb_rows: int = 12       # keyboard / mouse rows per latent frame (3 frames x 4 sub-steps)
     eps: float = 1e-6
+    action_impl: str = "b200"  # "b200" (shared-mask tcgen05 plans) or "sdpa"
 
     @property
     def tokens_per_frame(self) -> int:
@@ -148,15 +153,24 @@ class HierDiTBlock(nn.Module):
         m = cfg.mouse_dim * cfg.kb_rows
         self.action_mlp = nn.Sequential(nn.LayerNorm(d + m), nn.Linear(d + m, d + m), nn.GELU(),
                                         nn.Linear(d + m, d), nn.LayerNorm(d))
-        self.action_temporal_attn = _FrameAttention(d, cfg.heads, cfg.eps)
-        self.action_cross_attn = _CrossAttention(d, cfg.heads, cfg.eps)
+        if cfg.action_impl == "b200":
+            self.action_temporal_attn = SelfAttention(d, cfg.heads, eps=cfg.eps)
+            self.action_cross_attn = CrossAttention(d, cfg.heads, eps=cfg.eps)
+        elif cfg.action_impl == "sdpa":
+            self.action_temporal_attn = _FrameAttention(d, cfg.heads, cfg.eps)
+            self.action_cross_attn = _CrossAttention(d, cfg.heads, cfg.eps)
+        else:
+            raise ValueError(f"action_impl must be 'b200' or 'sdpa', got {cfg.action_impl!r}")
         self.ffn = nn.Sequential(nn.Linear(d, cfg.ffn), nn.GELU(approximate="tanh"),
                                  nn.Linear(cfg.ffn, d))
 
     def forward(self, x, x_hub, ctx, mouse, kb, t_mod, freqs, mask, cam, frame_mask, kb_mask,
                 rope_f, events=None):
         """x ``[P, F*L, d]`` player tokens, x_hub ``[1, F*K, d]`` hub tokens,
-        t_mod ``[P, F, 6, d]``; returns the updated ``(x, x_hub)``."""
+        t_mod ``[P, F, 6, d]``; returns the updated ``(x, x_hub)``.
+        ``events`` (six CUDA events, optional) bracket the hierarchical
+        self-attention, the action temporal attention and the keyboard
+        cross-attention."""
         cfg = self.cfg
         P, FL, d = x.shape
         Fr = cfg.frames
@@ -180,9 +194,22 @@ class HierDiTBlock(nn.Module):
         # action branches: mouse MLP, per-frame attention, keyboard cross-attention
         a = self.action_mlp(torch.cat([_modulate(self.norm2(x), sh_m, sc_m), mouse], -1))
         a = a.reshape(P, Fr, L, d).transpose(1, 2).reshape(P * L, Fr, d)
-        a = self.action_temporal_attn(a, frame_mask, *rope_f)
+        if events is not None:
+            events[2].record()
+        if isinstance(self.action_temporal_attn, SelfAttention):
+            a = self.action_temporal_attn(a, rope_f[2], frame_mask)
+        else:
+            a = self.action_temporal_attn(a, frame_mask, rope_f[0], rope_f[1])
+        if events is not None:
+            events[3].record()
         x = x + a.reshape(P, L, Fr, d).transpose(1, 2).reshape(P, FL, d)
-        x = x + self.action_cross_attn(self.norm3(x), kb, kb_mask)
+        xk = self.norm3(x)
+        if events is not None:
+            events[4].record()
+        xk = self.action_cross_attn(xk, kb, kb_mask)
+        if events is not None:
+            events[5].record()
+        x = x + xk
         # FFN
         x = x + g_m * self.ffn(_modulate(self.norm2(x), sh_m, sc_m))
         return x, x_hub
@@ -240,7 +267,8 @@ class HierDiT(nn.Module):
         hd = cfg.dim // cfg.heads
         ang = t.double()[:, None] * torch.pow(10000.0, -torch.arange(0, hd, 2, device=device,
                                                                      dtype=torch.float64) / hd)
-        rope_f = (ang.cos().float(), ang.sin().float())
+        rope_f = (ang.cos().float(), ang.sin().float(), torch.polar(torch.ones_like(ang), ang)
+                  .unsqueeze(1))
         return dict(mask=mask, freqs=freqs, cam=cam, frame_mask=frame_mask, kb_mask=kb_mask,
                     rope_f=rope_f)
 

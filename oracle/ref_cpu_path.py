@@ -254,3 +254,64 @@ def cpu_model() -> str:
     except OSError:
         pass
     return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# action branch of the DiT block (test infrastructure only)
+# ---------------------------------------------------------------------------
+
+
+def temporal_block_causal_mask(num_frames, num_frame_per_block, local_attn_size):
+    """``get_temporal_block_causal_mask`` (``hier_masks.py:1152-1166``), in
+    numpy: frame ``i`` sees frame ``j`` iff ``j // n <= i // n`` and, with a
+    window, ``i - j < local_attn_size``."""
+    t = np.arange(num_frames)
+    m = (t[None, :] // num_frame_per_block) <= (t[:, None] // num_frame_per_block)
+    if local_attn_size != -1:
+        m &= (t[:, None] - t[None, :]) < local_attn_size
+    return m
+
+
+def keyboard_mask(frame_mask, num_patches, tokens_per_kbd_frame=12):
+    """``repeat(frame_mask, "f g -> (f q) (g k)")`` (``blocks.py:446-448``)."""
+    return np.repeat(np.repeat(np.asarray(frame_mask), num_patches, 0), tokens_per_kbd_frame, 1)
+
+
+def shared_mask_sdpa(q, k, v, num_heads, mask):
+    """``flash_attention(q, k, v, num_heads, mask)`` (``attention.py:47-54``)
+    with one mask ``[Lq, Lk]`` broadcast over the batch: ``q`` ``[B, Lq,
+    n*d]``, ``k``/``v`` ``[B, Lk, n*d]``."""
+    B, Lq, nd = q.shape
+    d = nd // num_heads
+    qh, kh, vh = (t.reshape(B, t.shape[1], num_heads, d).transpose(1, 2) for t in (q, k, v))
+    o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=torch.as_tensor(mask).to(torch.bool))
+    return o.transpose(1, 2).reshape(B, Lq, nd)
+
+
+def action_temporal_forward(x, w, num_heads, mask, eps=1e-6):
+    """The per-frame action attention, a ``SelfAttention`` over ``x``
+    ``[B, F, dim]`` (``blocks.py:677-691``, ``attention.py:355-365,436-442``):
+    q/k/v linears, RMSNorm on q and k, 1-D RoPE over the frames
+    (``precompute_freqs_cis(head_dim, F)``), masked SDPA, output linear.
+    ``w`` maps ``q.weight``, ``q.bias``, ... ``norm_k.weight`` to tensors."""
+    B, F_, dim = x.shape
+    d = dim // num_heads
+    q = rms_norm(F.linear(x, w["q.weight"], w["q.bias"]), w["norm_q.weight"], eps)
+    k = rms_norm(F.linear(x, w["k.weight"], w["k.bias"]), w["norm_k.weight"], eps)
+    v = F.linear(x, w["v.weight"], w["v.bias"])
+    cs = torch.from_numpy(O.precompute_freqs(d, F_))
+    freqs = torch.complex(cs[..., 0], cs[..., 1]).unsqueeze(1)
+    q, k = rope_apply(q, freqs, num_heads), rope_apply(k, freqs, num_heads)
+    o = shared_mask_sdpa(q, k, v, num_heads, mask)
+    return F.linear(o, w["o.weight"], w["o.bias"])
+
+
+def action_cross_forward(x, ctx, w, num_heads, mask, eps=1e-6):
+    """The keyboard cross-attention, a ``CrossAttention`` without image input
+    (``attention.py:1071-1090``): q from ``x``, k/v from ``ctx``, RMSNorm on
+    q and k, masked SDPA, output linear."""
+    q = rms_norm(F.linear(x, w["q.weight"], w["q.bias"]), w["norm_q.weight"], eps)
+    k = rms_norm(F.linear(ctx, w["k.weight"], w["k.bias"]), w["norm_k.weight"], eps)
+    v = F.linear(ctx, w["v.weight"], w["v.bias"])
+    o = shared_mask_sdpa(q, k, v, num_heads, mask)
+    return F.linear(o, w["o.weight"], w["o.bias"])

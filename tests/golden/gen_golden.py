@@ -25,6 +25,11 @@ Fixtures written (all under ``tests/golden``):
 * ``causal.npz``     ``SelfAttention.causal_forward_hier_hub``
   (``multics/models/attention.py:456-1005``) over consecutive blocks with
   rolling caches: per-block inputs and outputs, final cache contents.
+* ``action.npz``     the action branch's masks (``get_temporal_block_causal_mask``,
+  ``hier_masks.py:1152-1166``, and its keyboard repeat, ``blocks.py:446-448``)
+  and fp32 outputs of the reference's ``SelfAttention`` over a batch of
+  frame sequences (the per-frame action attention, ``blocks.py:677-691``) and
+  of its ``CrossAttention`` under the keyboard mask (``blocks.py:692-697``).
 * ``numerics.npz``   fp32 outputs of the reference attention path
   (camera Q/K add ``attention.py:307-320``, RMSNorm ``:231-242``, float64
   RoPE ``rope.py:248-254``, masked SDPA ``attention.py:39-54``) on seeded
@@ -533,6 +538,74 @@ def gen_numerics(out: dict, attn_mod):
     out["num_case_names"] = np.frombuffer(json.dumps(names).encode(), dtype=np.uint8)
 
 
+def gen_action(out: dict, attn_mod):
+    import torch
+    from einops import repeat
+    from multics.models.hier_masks import get_temporal_block_causal_mask
+    from multics.models.rope import precompute_freqs_cis
+
+    mask_cases = [(42, 1, -1), (42, 7, 24), (21, 3, 21), (9, 7, 24), (5, 2, 3), (12, 4, 6)]
+    for F, n, win in mask_cases:
+        out[f"temporal/{F}_{n}_{win}"] = get_temporal_block_causal_mask(F, n, win).numpy()
+    kb_cases = [(6, 3, -1, 5), (9, 3, 4, 7)]
+    for F, n, win, L in kb_cases:
+        fm = get_temporal_block_causal_mask(F, n, win)
+        out[f"keyboard/{F}_{n}_{win}_{L}"] = repeat(fm, "f g -> (f q) (g k)", q=L, k=12).numpy()
+    out["mask_cases"] = np.array(mask_cases, dtype=np.int64)
+    out["kb_cases"] = np.array(kb_cases, dtype=np.int64)
+
+    H, D = 2, 128
+    dim = H * D
+    g = torch.Generator().manual_seed(0)
+
+    def lin_params(prefix, layer):
+        with torch.no_grad():
+            layer.weight.copy_(_bf16_round(torch.randn(layer.weight.shape, generator=g) * 0.05))
+            if layer.bias is not None:
+                layer.bias.copy_(_bf16_round(torch.randn(layer.bias.shape, generator=g) * 0.05))
+        out[f"{prefix}.weight"] = _bf16_bits(layer.weight.detach())
+        if layer.bias is not None:
+            out[f"{prefix}.bias"] = _bf16_bits(layer.bias.detach())
+
+    def norm_params(prefix, norm):
+        with torch.no_grad():
+            norm.weight.copy_(_bf16_round(1 + torch.randn(norm.weight.shape, generator=g) * 0.02))
+        out[f"{prefix}.weight"] = _bf16_bits(norm.weight.detach())
+
+    # per-frame action attention: SelfAttention over [B, F, dim] with 1-D RoPE
+    B, F, n, win = 7, 9, 3, 4
+    sa = attn_mod.SelfAttention(dim, H, eps=1e-6).float().eval()
+    for name in ("q", "k", "v", "o"):
+        lin_params(f"temporal/{name}", getattr(sa, name))
+    norm_params("temporal/norm_q", sa.norm_q)
+    norm_params("temporal/norm_k", sa.norm_k)
+    x = _bf16_round(torch.randn(B, F, dim, generator=g))
+    freqs = precompute_freqs_cis(D, end=F).unsqueeze(1)
+    mask = get_temporal_block_causal_mask(F, n, win)
+    with torch.no_grad():
+        y = sa(x, freqs, mask)
+    out["temporal/x"] = _bf16_bits(x)
+    out["temporal/out"] = y.numpy().astype(np.float32)
+    out["temporal/shape"] = np.array([B, F, n, win, H, D], dtype=np.int64)
+
+    # keyboard cross-attention: CrossAttention under the repeated frame mask
+    P, F, n, win, L, K = 2, 6, 2, -1, 5, 12
+    ca = attn_mod.CrossAttention(dim, H, eps=1e-6).float().eval()
+    for name in ("q", "k", "v", "o"):
+        lin_params(f"keyboard/{name}", getattr(ca, name))
+    norm_params("keyboard/norm_q", ca.norm_q)
+    norm_params("keyboard/norm_k", ca.norm_k)
+    xq = _bf16_round(torch.randn(P, F * L, dim, generator=g))
+    ctx = _bf16_round(torch.randn(P, F * K, dim, generator=g))
+    kmask = repeat(get_temporal_block_causal_mask(F, n, win), "f g -> (f q) (g k)", q=L, k=K)
+    with torch.no_grad():
+        y = ca(xq, ctx, kmask)
+    out["keyboard/x"] = _bf16_bits(xq)
+    out["keyboard/ctx"] = _bf16_bits(ctx)
+    out["keyboard/out"] = y.numpy().astype(np.float32)
+    out["keyboard/shape"] = np.array([P, F, n, win, L, K, H, D], dtype=np.int64)
+
+
 def _euler_zyx(ang):
     import torch
 
@@ -696,6 +769,7 @@ def main():
     for fname, fn in (("masks", lambda o: gen_masks(args.reference, o)),
                       ("segmented", gen_segmented), ("tiled", gen_tiled),
                       ("numerics", lambda o: gen_numerics(o, attn_mod)),
+                      ("action", lambda o: gen_action(o, attn_mod)),
                       ("causal", gen_causal)):
         if args.only and fname != args.only:
             continue
