@@ -516,6 +516,7 @@ def run_ours(args, rank, world, local_rank):
         del inp, q_buf, k_buf, o_buf
         torch.cuda.empty_cache()
         line["action_attention"] = run_action()
+        line["training_backward"] = run_backward(cfg)
         line["dit_step"] = run_dit()
     return line
 
@@ -677,6 +678,64 @@ def run_cached_step(steps=20, warmup=3):
             "ms_per_step": round(step_ms, 4), "host_wall_ms_per_step": round(wall, 4),
             "plan_ms": round(plan_ms, 4), "query_pairs": int(plan.n_pairs),
             "key_streams": int(plan.n_streams)}
+
+
+def run_backward(cfg, steps=10, warmup=3):
+    """Training step of the attention at the bench configuration on the block
+    plan (the plan the gradients use): the forward with its log2-sum-exp and
+    the backward (Delta, dQ over the query-major plan, dK/dV over the
+    key-major plan), inputs resident in HBM.  Useful FLOPs: the forward's 2
+    matmuls per unmasked pair and head (4*D), the backward's 4 (dV, dP, dQ,
+    dK: 8*D); the kernels also recompute S (dQ and dK/dV kernels each), which
+    is not counted."""
+    import torch
+
+    from multics_b200.attention import device_error
+    from multics_b200.hier_masks import build_stage2_hier_flex_block_mask
+    from multics_b200.synth import make_inputs
+    from multics_b200.train import block_plan_grad, hier_block_attention_grad
+
+    peak_b, _, _, peak_kind = load_peaks()
+    dev = torch.device("cuda")
+    inp = make_inputs(cfg, device=dev)
+    bm, S, _ = build_stage2_hier_flex_block_mask(cfg.P, cfg.T, cfg.L, cfg.N, cfg.KL, cfg.KG,
+                                                 cfg.n_block, cfg.local_attn, inp.labels, None,
+                                                 cfg.direct, dev)
+    block_plan_grad(bm, S)
+    g = torch.Generator(device=dev).manual_seed(9)
+    q, k, v = (torch.randn(S, cfg.dim, generator=g, device=dev).bfloat16().requires_grad_(True)
+               for _ in range(3))
+    dout = torch.randn(S, cfg.dim, generator=g, device=dev).bfloat16()
+    del inp
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for i in range(warmup + steps):
+        q.grad = k.grad = v.grad = None
+        e = ev[i - warmup] if i >= warmup else None
+        if e:
+            e[0].record()
+        out = hier_block_attention_grad(q, k, v, bm, cfg.H)
+        if e:
+            e[1].record()
+        out.backward(dout)
+        if e:
+            e[2].record()
+    torch.cuda.synchronize()
+    fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    pairs = useful_pairs(bm)
+    f_fwd = 4.0 * cfg.D * cfg.H * pairs
+    res = {"workload": f"{cfg.name}: attention forward + backward on the 128x128 block plan, "
+                       f"S={S}, {cfg.H}x{cfg.D}, random bf16 q/k/v and output gradient",
+           "forward_ms": round(fwd, 4), "backward_ms": round(bwd, 4),
+           "forward_tflops": round(f_fwd / (fwd * 1e-3) / 1e12, 1),
+           "backward_tflops": round(2 * f_fwd / (bwd * 1e-3) / 1e12, 1),
+           "backward_frac_of_peak": round(2 * f_fwd / (bwd * 1e-3) / 1e12 / peak_b, 4),
+           "peak_kind": f"{peak_kind} bf16 burst", "steps": steps,
+           "device_error": device_error(dev),
+           "note": "backward FLOPs = 2 x forward (dV, dP, dQ, dK); S recomputation not counted"}
+    del q, k, v, dout, out
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_action(steps=20, warmup=3):

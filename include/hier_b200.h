@@ -291,6 +291,66 @@ int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_t q_stride,
                           void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Attention backward (training)
+ * ------------------------------------------------------------------------- */
+
+/* Gradients of hier_attn_fwd / hier_attn_fwd_streams over a 128x128 block
+ * plan (hier_block_plan_build without a page table, or
+ * hier_dense_block_plan_build), in place of the FlexAttention backward the
+ * reference trains with (multics/models/attention.py:322-353, the Flex
+ * Jacobian of forward_hier_tiled_ste, attention.py:367-434).  With
+ * s = q.k * scale * log2(e), P = 2^(s - lse) (lse from the forward, log2
+ * units), dP = dO.v and Delta = rowsum(dO * O):
+ *   dQ = scale * (P * (dP - Delta)) K,  dK = scale * (P * (dP - Delta))^T Q,
+ *   dV = P^T dO.
+ * Tensors are bf16 [rows, H*128] (row strides in elements, multiples of 8,
+ * 16-byte aligned bases).  Every dQ, dK and dV row is written once (rows
+ * without keys or queries: 0); no atomics. */
+
+/* delta [H][rows_pad] = rowsum(dO * O) per head (fp32) and lse_t [H][rows_pad]
+ * = the forward's lse [rows][H] transposed, +inf for rows without keys and
+ * for the padding rows (rows_pad: a multiple of 128, >= rows). */
+int hier_attn_bwd_prep(const void* o, int64_t o_stride, const void* dout, int64_t do_stride,
+                       const float* lse, int64_t rows, int32_t H, int32_t D, float* delta,
+                       float* lse_t, int64_t rows_pad, void* stream);
+
+/* Key-major form of a block plan: per key block kb (keys [128 kb, 128 kb +
+ * 128)) the query blocks that see it, k_ent [capacity][4] = (q_start,
+ * q_rows, mask selector (-1 full, else an index into t_masks), q_start/128)
+ * at k_off[kb] .. k_off[kb+1] (ascending q_start), and t_masks
+ * [n_masks][128][4] = row_masks transposed (word w bit b of key row j: query
+ * row 32w + b).  capacity >= the plan's (entry, half) references (n_partial +
+ * n_full of the block classification).  workspace: int32 [2 * n_kb].
+ * *status (device) gets bit 0 if the plan is not an aligned single-stream
+ * block plan, bit 1 if capacity is too small. */
+int hier_bwd_plan_transpose(const int32_t* q_pairs, int32_t n_pairs, const int32_t* kv_tiles,
+                            const uint32_t* row_masks, int32_t n_masks, int32_t n_kb,
+                            int32_t* workspace, int32_t* k_off, int32_t* k_ent,
+                            int32_t capacity, uint32_t* t_masks, int32_t* status,
+                            void* stream);
+
+/* dQ over the forward's query-major plan (q_pairs, kv_tiles, row_masks with
+ * mask_rows 128 or 1 as in hier_attn_fwd_streams): one CTA per (query tile,
+ * head).  dout has the rows of q. */
+int hier_attn_bwd_dq(const void* q, int64_t q_rows, int64_t q_stride, const void* k,
+                     const void* v, int64_t kv_rows, int64_t kv_stride, const void* dout,
+                     int64_t do_stride, const float* lse_t, const float* delta,
+                     int64_t rows_pad, int32_t H, int32_t D, const int32_t* q_pairs,
+                     int32_t n_pairs, const int32_t* kv_tiles, const uint32_t* row_masks,
+                     int32_t mask_rows, float softmax_scale, void* dq, int64_t dq_stride,
+                     int32_t* dev_err, void* stream);
+
+/* dK and dV over the key-major plan of hier_bwd_plan_transpose: one CTA per
+ * (key block, head); n_kb * 128 >= kv_rows. */
+int hier_attn_bwd_dkv(const void* q, int64_t q_rows, int64_t q_stride, const void* k,
+                      const void* v, int64_t kv_rows, int64_t kv_stride, const void* dout,
+                      int64_t do_stride, const float* lse_t, const float* delta,
+                      int64_t rows_pad, int32_t H, int32_t D, const int32_t* k_off,
+                      const int32_t* k_ent, const uint32_t* t_masks, int32_t n_kb,
+                      float softmax_scale, void* dk, int64_t dk_stride, void* dv,
+                      int64_t dv_stride, int32_t* dev_err, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Cached (rolling key/value cache) step
  * ------------------------------------------------------------------------- */
 

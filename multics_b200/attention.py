@@ -342,6 +342,19 @@ def attention_mask_plan(mask, S: int, device) -> HierBlockMask:
     return bm
 
 
+def _rope_torch(x, freqs, num_heads):
+    """``rope_apply`` (``rope.py:248-254``) as differentiable PyTorch
+    operations: complex multiply in float64, cast back.  ``freqs`` complex
+    ``[S, 1, D/2]`` or a float ``[S, D/2, 2]`` (cos, sin) table."""
+    if not torch.is_complex(freqs):
+        f = freqs.reshape(freqs.shape[0], -1, 2).double()
+        freqs = torch.complex(f[..., 0], f[..., 1])
+    b, s, nd = x.shape
+    xc = torch.view_as_complex(x.double().reshape(b, s, num_heads, nd // num_heads // 2, 2))
+    out = torch.view_as_real(xc * freqs.reshape(s, 1, -1).to(xc.device)).flatten(3)
+    return out.reshape(b, s, nd).to(x.dtype)
+
+
 class RMSNorm(nn.Module):
     """``attention.py:231-242``: fp32 ``x*rsqrt(mean(x^2)+eps)`` then ``*weight``."""
 
@@ -435,7 +448,17 @@ class SelfAttention(nn.Module):
         ``[S,S]`` mask (block plan built from its bytes), or None (unmasked).
         A batch ``x`` ``[B, L, dim]`` with ``B > 1`` is the DiT block's
         per-frame action attention (``blocks.py:684-686``): ``mask`` is one
-        ``[L, L]`` mask shared by the batch and ``freqs`` ``[L, 1, D/2]``."""
+        ``[L, L]`` mask shared by the batch and ``freqs`` ``[L, 1, D/2]``.
+        While autograd records (training), the call runs
+        :meth:`_forward_train`: the attention on the block plan with its
+        B200 backward."""
+        if torch.is_grad_enabled() and (x.requires_grad or any(
+                p.requires_grad for p in self.parameters())):
+            if x.dim() == 3 and x.shape[0] > 1:
+                raise NotImplementedError(
+                    "the B200 attention backward covers the full-sequence (block plan) "
+                    "attention; run the batched action attention under torch.no_grad()")
+            return self._forward_train(x, freqs, mask, cam_tokens)
         if x.dim() == 3 and x.shape[0] > 1:
             return self._forward_batch(x, freqs, mask, cam_tokens)
         mask = attention_mask_plan(mask, x.shape[1], x.device)
@@ -448,6 +471,31 @@ class SelfAttention(nn.Module):
             out = attention_from_plan(q, k, v, mask, self.num_heads)
         return self.o(out.unsqueeze(0))
 
+
+    def _forward_train(self, x, freqs, mask, cam_tokens):
+        """Differentiable forward (``attention.py:355-365,436-442`` with
+        autograd): the projections, camera add, RMSNorm and float64 RoPE as
+        PyTorch operations (their backward is PyTorch's), the attention on
+        the block plan through :func:`multics_b200.train.hier_block_attention_grad`
+        (tcgen05 forward and backward kernels)."""
+        from .train import hier_block_attention_grad
+
+        if cam_tokens is not None and (self.cam_q is None or self.cam_k is None):
+            raise RuntimeError("camera_pose was provided but enable_camera_pose_qk() was not called")
+        qx, kx, v = self.q(x), self.k(x), self.v(x)
+        if cam_tokens is not None:
+            if cam_tokens.shape[:2] != x.shape[:2]:
+                raise ValueError(f"camera tokens shape {tuple(cam_tokens.shape[:2])} must match "
+                                 f"q/k tokens {tuple(x.shape[:2])}")
+            c = cam_tokens.to(qx.dtype)
+            if self.training and self.cam_dropout_p > 0:
+                c = torch.nn.functional.dropout(c, p=self.cam_dropout_p, training=True)
+            qx = qx + torch.nn.functional.linear(c, self.cam_q.weight)
+            kx = kx + torch.nn.functional.linear(c, self.cam_k.weight)
+        q = _rope_torch(self.norm_q(qx), freqs, self.num_heads)
+        k = _rope_torch(self.norm_k(kx), freqs, self.num_heads)
+        bm = attention_mask_plan(mask, x.shape[1], x.device)
+        return self.o(hier_block_attention_grad(q, k, v, bm, self.num_heads))
 
     def _forward_batch(self, x, freqs, mask, cam_tokens):
         """``B`` sequences of ``L`` tokens under one shared mask: projections,

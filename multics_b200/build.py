@@ -18,7 +18,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libhier_b200.so"
 SOURCES = ["hier_capi.cu", "hier_meta.cu", "hier_prep.cu", "hier_attn.cu", "hier_selftest.cu",
-           "hier_cached.cu", "hier_tiled.cu", "hier_shard.cu"]
+           "hier_cached.cu", "hier_tiled.cu", "hier_shard.cu", "hier_bwd.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

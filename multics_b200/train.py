@@ -1,0 +1,144 @@
+"""Training path of the hierarchical attention on B200: autograd over the
+128x128 block plan.
+
+The reference trains its hierarchical self-attention with FlexAttention
+over the grouping's BlockMask (``multics/models/attention.py:322-353``;
+``forward_hier_tiled_ste`` keeps the Flex Jacobian, ``:367-434``).  Here the
+forward is the tcgen05 attention kernel run on the block plan with its
+log2-sum-exp kept, and the backward is three kernels
+(``csrc/hier_bwd.cu``): Delta = rowsum(dO * O), dQ over the forward's
+query-major plan, dK and dV over its key-major transpose.
+
+:func:`hier_block_attention_grad` is the differentiable attention;
+:meth:`multics_b200.attention.SelfAttention.forward` uses it whenever autograd
+is recording.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr, stream_ptr
+from .attention import _dev_err, _rows
+from .hier_masks import HierBlockMask
+
+__all__ = ["BlockPlanGrad", "block_plan_grad", "hier_block_attention_grad"]
+
+
+class BlockPlanGrad:
+    """Key-major form of a block plan (``hier_bwd_plan_transpose``): per key
+    block the query blocks that see it and per-key-row masks."""
+
+    def __init__(self, bm: HierBlockMask, kv_rows: int):
+        dev = bm.q_pairs.device
+        self.n_kb = (kv_rows + 127) // 128
+        capacity = bm.n_partial + bm.n_full
+        n_masks = bm.row_masks.shape[0] if bm.n_partial > 0 else 0
+        i32 = dict(dtype=torch.int32, device=dev)
+        ws = torch.empty(2 * self.n_kb, **i32)
+        self.k_off = torch.empty(self.n_kb + 1, **i32)
+        self.k_ent = torch.empty((max(capacity, 1), 4), **i32)
+        self.t_masks = torch.empty((max(n_masks, 1), 128, 4), **i32)
+        status = torch.empty(1, **i32)
+        check(_lib.lib().hier_bwd_plan_transpose(
+            ptr(bm.q_pairs), bm.q_pairs.shape[0], ptr(bm.kv_tiles), ptr(bm.row_masks), n_masks,
+            self.n_kb, ptr(ws), ptr(self.k_off), ptr(self.k_ent), capacity, ptr(self.t_masks),
+            ptr(status), stream_ptr(dev)))
+        st = int(status.item())
+        if st & 1:
+            raise NotImplementedError(
+                "the attention backward needs a block plan without a page table")
+        if st & 2:
+            raise RuntimeError("key-major plan exceeded its capacity")
+
+
+def block_plan_grad(bm: HierBlockMask, kv_rows: int) -> BlockPlanGrad:
+    """The key-major plan of ``bm``, built once per block mask (kept on it)."""
+    gp = getattr(bm, "_grad_plan", None)
+    if gp is None or gp.n_kb != (kv_rows + 127) // 128:
+        gp = BlockPlanGrad(bm, kv_rows)
+        object.__setattr__(bm, "_grad_plan", gp)
+    return gp
+
+
+class _HierBlockAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, bm, num_heads, scale):
+        q2, k2, v2 = (_rows(t).contiguous() for t in (q, k, v))
+        for name, t in (("q", q2), ("k", k2), ("v", v2)):
+            if t.dtype != torch.bfloat16 or not t.is_cuda:
+                raise NotImplementedError(f"the B200 attention needs bf16 CUDA {name}")
+        S, dim = q2.shape
+        D = dim // num_heads
+        dev = q2.device
+        out = torch.empty_like(q2)
+        lse = torch.empty((S, num_heads), dtype=torch.float32, device=dev)
+        kp = (ctypes.c_void_p * 1)(k2.data_ptr())
+        vp = (ctypes.c_void_p * 1)(v2.data_ptr())
+        rows = (ctypes.c_int64 * 1)(k2.shape[0])
+        strides = (ctypes.c_int64 * 1)(k2.stride(0))
+        check(_lib.lib().hier_attn_fwd_streams(
+            ptr(q2), S, q2.stride(0), 1, kp, vp, rows, strides, ptr(out), out.stride(0), None,
+            num_heads, D, ptr(bm.q_pairs), bm.q_pairs.shape[0], ptr(bm.kv_tiles),
+            ptr(bm.row_masks), 128, ptr(bm.order), scale, ptr(lse), None, ptr(_dev_err(dev)),
+            stream_ptr(dev)))
+        ctx.save_for_backward(q2, k2, v2, out, lse)
+        ctx.bm, ctx.num_heads, ctx.scale = bm, num_heads, scale
+        ctx.shapes = (q.shape, k.shape, v.shape)
+        return out.view(q.shape)
+
+    @staticmethod
+    def backward(ctx, dout):
+        q2, k2, v2, out, lse = ctx.saved_tensors
+        bm, H, scale = ctx.bm, ctx.num_heads, ctx.scale
+        S, dim = q2.shape
+        D = dim // H
+        dev = q2.device
+        do2 = dout.reshape(S, dim).to(torch.bfloat16).contiguous()
+        rows_pad = (S + 127) // 128 * 128
+        delta = torch.empty((H, rows_pad), dtype=torch.float32, device=dev)
+        lse_t = torch.empty_like(delta)
+        L = _lib.lib()
+        st = stream_ptr(dev)
+        err = _dev_err(dev)
+        check(L.hier_attn_bwd_prep(ptr(out), out.stride(0), ptr(do2), do2.stride(0), ptr(lse), S,
+                                   H, D, ptr(delta), ptr(lse_t), rows_pad, st))
+        dq = torch.empty_like(q2)
+        dk = torch.empty_like(k2)
+        dv = torch.empty_like(v2)
+        kv_rows = k2.shape[0]
+        check(L.hier_attn_bwd_dq(
+            ptr(q2), S, q2.stride(0), ptr(k2), ptr(v2), kv_rows, k2.stride(0), ptr(do2),
+            do2.stride(0), ptr(lse_t), ptr(delta), rows_pad, H, D, ptr(bm.q_pairs),
+            bm.q_pairs.shape[0], ptr(bm.kv_tiles), ptr(bm.row_masks), 128, scale, ptr(dq),
+            dq.stride(0), ptr(err), st))
+        gp = block_plan_grad(bm, kv_rows)
+        check(L.hier_attn_bwd_dkv(
+            ptr(q2), S, q2.stride(0), ptr(k2), ptr(v2), kv_rows, k2.stride(0), ptr(do2),
+            do2.stride(0), ptr(lse_t), ptr(delta), rows_pad, H, D, ptr(gp.k_off), ptr(gp.k_ent),
+            ptr(gp.t_masks), gp.n_kb, scale, ptr(dk), dk.stride(0), ptr(dv), dv.stride(0),
+            ptr(err), st))
+        sq, sk, sv = ctx.shapes
+        return dq.view(sq), dk.view(sk), dv.view(sv), None, None, None
+
+
+def hier_block_attention_grad(q, k, v, mask, num_heads: int, *, softmax_scale=None):
+    """Differentiable masked attention on the B200 kernels: ``q``, ``k``,
+    ``v`` bf16 ``[S, H*128]`` (or ``[1, S, H*128]``), ``mask`` anything
+    :meth:`~multics_b200.attention.SelfAttention.forward` accepts (a
+    :class:`HierBlockMask`, a dense bool mask, or None).  Always the block
+    plan: the gradients need the aligned 128x128 tiles of its key-major
+    transpose."""
+    from .attention import attention_mask_plan
+
+    S = q.shape[-2]
+    bm = mask if isinstance(mask, HierBlockMask) else attention_mask_plan(mask, S, q.device)
+    if bm.S != S:
+        raise ValueError(f"block mask is for S={bm.S}, got {S} tokens")
+    D = q.shape[-1] // num_heads
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    return _HierBlockAttention.apply(q, k, v, bm, num_heads, scale)

@@ -30,6 +30,11 @@ Fixtures written (all under ``tests/golden``):
   and fp32 outputs of the reference's ``SelfAttention`` over a batch of
   frame sequences (the per-frame action attention, ``blocks.py:677-691``) and
   of its ``CrossAttention`` under the keyboard mask (``blocks.py:692-697``).
+* ``grads.npz``      gradients, by the reference's own autograd, of the
+  reference attention path (camera add, RMSNorm, float64 RoPE, masked SDPA;
+  ``attention.py:307-320,231-242``, ``rope.py:248-254``, ``attention.py:39-54``)
+  with respect to its inputs and the camera / norm weights, for a seeded
+  output gradient, on the config-1 head_dim-128 cases of ``numerics.npz``.
 * ``numerics.npz``   fp32 outputs of the reference attention path
   (camera Q/K add ``attention.py:307-320``, RMSNorm ``:231-242``, float64
   RoPE ``rope.py:248-254``, masked SDPA ``attention.py:39-54``) on seeded
@@ -606,6 +611,59 @@ def gen_action(out: dict, attn_mod):
     out["keyboard/shape"] = np.array([P, F, n, win, L, K, H, D], dtype=np.int64)
 
 
+def gen_grads(out: dict, attn_mod):
+    """Reads the inputs recorded in numerics.npz (run it first)."""
+    import torch
+    from multics.models.hier_masks import build_stage2_hier_self_attn_mask
+    from multics.models.rope import rope_apply
+
+    num = np.load(HERE / "numerics.npz")
+
+    def bf(a):
+        return torch.from_numpy(a.astype(np.uint16).view(np.int16)).view(torch.bfloat16).float()
+
+    names = []
+    for name in ("cfg1_d128", "cfg1_d128_n3", "cfg1_d128_mem"):
+        meta = json.loads(bytes(num[f"{name}/meta"]).decode())
+        H, S = meta["H"], meta["S"]
+        qx, kx, v = (bf(num[f"{name}/{t}"])[None].requires_grad_(True) for t in ("qx", "kx", "v"))
+        cam = bf(num[f"{name}/cam"])[None]
+        wcq, wck, nqw, nkw = (bf(num[f"{name}/{t}"]) for t in ("wcq", "wck", "nqw", "nkw"))
+        fr = torch.from_numpy(num[f"{name}/freqs"])
+        freqs = torch.complex(fr[..., 0], fr[..., 1]).unsqueeze(1)
+        P, T, L, N, KL, KG = (meta[k] for k in ("P", "T", "L", "N", "KL", "KG"))
+        labels = torch.from_numpy(num[f"{name}/labels"])
+        if meta["membership"]:
+            mask = build_stage2_hier_self_attn_mask(
+                P, T, L, N, KL, KG, meta["n"], meta["win"], labels, None, True,
+                torch.device("cpu"), membership=torch.from_numpy(num[f"{name}/membership"]),
+                global_only=torch.from_numpy(num[f"{name}/global_only"]))
+        else:
+            mask = build_stage2_hier_self_attn_mask(P, T, L, N, KL, KG, meta["n"], meta["win"],
+                                                    labels, None, True, torch.device("cpu"))
+        layer = attn_mod.SelfAttention(H * meta["D"], H, eps=1e-6).float()
+        layer.enable_camera_pose_qk(12, dropout_p=0.0)
+        with torch.no_grad():
+            layer.cam_q.weight.copy_(wcq)
+            layer.cam_k.weight.copy_(wck)
+            layer.norm_q.weight.copy_(nqw)
+            layer.norm_k.weight.copy_(nkw)
+        qc, kc = layer._apply_camera_qk(qx, kx, cam)
+        q = rope_apply(layer.norm_q(qc), freqs, H)
+        k = rope_apply(layer.norm_k(kc), freqs, H)
+        o = attn_mod.flash_attention(q, k, v, num_heads=H, mask=mask)
+        g = torch.Generator().manual_seed(7)
+        dout = _bf16_round(torch.randn(o.shape, generator=g))
+        (o * dout).sum().backward()
+        names.append(name)
+        out[f"{name}/dout"] = _bf16_bits(dout[0])
+        for t, grad in (("qx", qx.grad[0]), ("kx", kx.grad[0]), ("v", v.grad[0]),
+                        ("wcq", layer.cam_q.weight.grad), ("wck", layer.cam_k.weight.grad),
+                        ("nqw", layer.norm_q.weight.grad), ("nkw", layer.norm_k.weight.grad)):
+            out[f"{name}/d_{t}"] = grad.detach().numpy().astype(np.float32)
+    out["grad_case_names"] = np.frombuffer(json.dumps(names).encode(), dtype=np.uint8)
+
+
 def _euler_zyx(ang):
     import torch
 
@@ -770,6 +828,7 @@ def main():
                       ("segmented", gen_segmented), ("tiled", gen_tiled),
                       ("numerics", lambda o: gen_numerics(o, attn_mod)),
                       ("action", lambda o: gen_action(o, attn_mod)),
+                      ("grads", lambda o: gen_grads(o, attn_mod)),
                       ("causal", gen_causal)):
         if args.only and fname != args.only:
             continue
