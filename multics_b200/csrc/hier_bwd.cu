@@ -16,13 +16,20 @@
 //   to head-major rows (+inf for rows without keys and for padding rows, so
 //   that their P is 0).
 // * bwd_dq_kernel: one CTA per (query tile, head), the forward's query-major
-//   plan; per key tile S = Q K^T and dP = dO V^T (two SS MMAs), dS by the
-//   row threads into TMEM, dQ += dS K (TS MMA, dQ accumulated in TMEM).
+//   plan; per key tile S = Q K^T and dP = dO V^T (SS MMAs), dS by the row
+//   threads into TMEM, dQ += dS K (TS MMA, dQ accumulated in TMEM).
 // * bwd_dkv_kernel: one CTA per (key block, head) over the transposed plan
 //   (hier_bwd_plan_transpose: per key block its query blocks and per-key-row
 //   masks); per query tile S^T = K Q^T and dP^T = V dO^T, P^T and dS^T by
 //   the key-row threads, dV += P^T dO and dK += dS^T Q (TS MMAs, both
 //   accumulated in TMEM, written once).
+//
+// TMEM holds one score tile and one dP tile (128 columns each) besides the
+// accumulators, so the tile is split in two 64-wide sub-tiles, one per row
+// warpgroup (warps 4-7 and 8-11, the same 128 lanes), and one thread issues
+// the MMAs in the order S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | ...: while
+// one warpgroup turns its sub-tile into P / dS, the tensor core works on the
+// other's.
 //
 // No atomics in the gradients: every dQ, dK and dV row is written by one CTA.
 // Every mbarrier wait is bounded (device error word).
@@ -52,16 +59,66 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
+// Two row warpgroups share the 128 TMEM lanes: group g reads the fp32 columns
+// [64g, 64g + 64) of a score tile and writes their bf16 pairs to columns
+// [64g, 64g + 32), its own columns, so neither group overwrites columns the
+// other still has to read.  Element k of a packed row therefore sits at
+// column k/2 (k < 64) or 32 + k/2 (k >= 64), and the TS MMA that reads it
+// takes its K steps 4-7 from 32 columns further on.
+__device__ __forceinline__ uint32_t packed_col(int chunk) { return 16 * chunk + (chunk >= 2 ? 32 : 0); }
+
+template <int k>
+__device__ __forceinline__ void issue_pv_split_step(uint32_t o_tmem, uint32_t a_tmem, uint32_t blo,
+                                                    bool accumulate) {
+  constexpr uint32_t idesc = idesc_bf16(kBM, kHD, true);
+  constexpr uint32_t offb = (k * 2048) >> 4;
+  umma_ts_lo<k * 8 + (k >= 4 ? 32 : 0), offb>(o_tmem, a_tmem, blo, idesc,
+                                              (accumulate || k > 0) ? 1u : 0u);
+}
+
+// D (128 x 128) (+)= A (bf16 pairs in TMEM, split layout) * B (MN-major) over
+// K steps 4g .. 4g+3: the half of the reduction that sub-tile g (elements
+// 64g .. 64g+63 of A's rows) contributes.
+template <int g>
+__device__ __forceinline__ void issue_pv_sub(uint32_t o_tmem, uint32_t a_tmem, uint32_t blo,
+                                             bool accumulate) {
+  issue_pv_split_step<4 * g + 0>(o_tmem, a_tmem, blo, accumulate);
+  issue_pv_split_step<4 * g + 1>(o_tmem, a_tmem, blo, accumulate);
+  issue_pv_split_step<4 * g + 2>(o_tmem, a_tmem, blo, accumulate);
+  issue_pv_split_step<4 * g + 3>(o_tmem, a_tmem, blo, accumulate);
+}
+
+// D (128 x 64, columns 64g.. of a score tile) = A (128 x 128) * B^T with B the
+// rows 64g .. 64g+63 of a tile (both K-major): one sub-tile of S.
+template <int k, int g>
+__device__ __forceinline__ void issue_s64_step(uint32_t d_tmem, uint32_t alo, uint32_t blo) {
+  constexpr uint32_t idesc = idesc_bf16(kBM, 64, false);
+  constexpr uint32_t off = ((k >> 2) * kHalf + (k & 3) * 32) >> 4;
+  constexpr uint32_t offb = off + ((g * 64 * 128) >> 4);
+  umma_ss_lo<off, offb>(d_tmem + 64 * g, alo, blo, idesc, k > 0 ? 1u : 0u);
+}
+template <int g>
+__device__ __forceinline__ void issue_s64(uint32_t d_tmem, uint32_t alo, uint32_t blo) {
+  issue_s64_step<0, g>(d_tmem, alo, blo);
+  issue_s64_step<1, g>(d_tmem, alo, blo);
+  issue_s64_step<2, g>(d_tmem, alo, blo);
+  issue_s64_step<3, g>(d_tmem, alo, blo);
+  issue_s64_step<4, g>(d_tmem, alo, blo);
+  issue_s64_step<5, g>(d_tmem, alo, blo);
+  issue_s64_step<6, g>(d_tmem, alo, blo);
+  issue_s64_step<7, g>(d_tmem, alo, blo);
+}
+
 __device__ __forceinline__ uint32_t word_of(const uint4& m, int q) {
   return q == 0 ? m.x : (q == 1 ? m.y : (q == 2 ? m.z : m.w));
 }
 
-// A 128-wide fp32 row of TMEM (this thread's lane) times `scale`, as bf16 to
-// global memory (16-byte stores), or zeros.
+// Columns [32 q0, 32 q0 + 64) of a 128-wide fp32 row of TMEM (this thread's
+// lane) times `scale`, as bf16 to global memory (16-byte stores).
 __device__ __forceinline__ void store_row_bf16(uint32_t t_row, float scale, __nv_bfloat16* dst,
-                                               bool store) {
+                                               bool store, int q0) {
 #pragma unroll 1
-  for (int q = 0; q < 4; ++q) {
+  for (int q = q0; q < q0 + 2; ++q) {
     uint32_t r[32];
     tmem_ld32(t_row + 32 * q, r);
     tmem_wait_ld();
@@ -77,10 +134,11 @@ __device__ __forceinline__ void store_row_bf16(uint32_t t_row, float scale, __nv
   }
 }
 
-__device__ __forceinline__ void zero_row(__nv_bfloat16* dst) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
+// Columns [32 q0, 32 q0 + 64) of a row set to 0.
+__device__ __forceinline__ void zero_row(__nv_bfloat16* dst, int q0) {
+  uint4* d = reinterpret_cast<uint4*>(dst + 32 * q0);
 #pragma unroll
-  for (int k = 0; k < kHD / 8; ++k) d[k] = make_uint4(0u, 0u, 0u, 0u);
+  for (int k = 0; k < 8; ++k) d[k] = make_uint4(0u, 0u, 0u, 0u);
 }
 
 // ---------------------------------------------------------------------------
@@ -271,10 +329,10 @@ constexpr int kDqSmemDo = kTile;
 constexpr int kDqSmemK = 2 * kTile;
 constexpr int kDqSmemV = kDqSmemK + kStages * kTile;
 constexpr int kDqSmemBar = kDqSmemV + kStages * kTile;
-constexpr int kDqNumBars = 1 + 3 * kStages + 3;
+constexpr int kDqNumBars = 1 + 3 * kStages + 5;
 constexpr int kDqSmemBytes = kDqSmemBar + kDqNumBars * 8 + 16 + 1024;
 
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     bwd_dq_kernel(const __grid_constant__ DqMaps m, DqArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -284,9 +342,9 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* k_full = q_full + 1;
   uint64_t* v_full = k_full + kStages;
   uint64_t* kv_empty = v_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;
-  uint64_t* ds_full = s_full + 1;
-  uint64_t* o_final = ds_full + 1;
+  uint64_t* s_full = kv_empty + kStages;  // [sub-tile]
+  uint64_t* ds_full = s_full + 2;         // [sub-tile], its warpgroup
+  uint64_t* o_final = ds_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kDqNumBars);
 
   const int warp = warp_id(), lane = lane_id();
@@ -307,8 +365,10 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(v_full + s, 1);
       mbar_init(kv_empty + s, 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(ds_full, 128);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(s_full + g, 1);
+      mbar_init(ds_full + g, 128);
+    }
     mbar_init(o_final, 1);
     fence_mbar_init();
   }
@@ -346,35 +406,60 @@ __global__ void __launch_bounds__(256, 1)
     const uint32_t k_lo0 = sdesc_lo_kmajor(smem_u32(smem + kDqSmemK));
     const uint32_t k_mn0 = sdesc_lo_mnmajor(smem_u32(smem + kDqSmemK));
     const uint32_t v_lo0 = sdesc_lo_kmajor(smem_u32(smem + kDqSmemV));
+    // Sub-tiles g = 0, 1 (keys 64g.. of a tile) alternate as in the forward:
+    //   S0(0) S1(0) | dQ0(0) S0(1) dQ1(0) S1(1) | dQ0(1) S0(2) dQ1(1) S1(2) | ...
+    // S_g(j+1) overwrites the dS_g(j) that dQ_g(j), issued just before it, reads.
+    auto used = [&](int e) {
+      while (e < kv_end && (h ? a.kv_tiles[e].w : a.kv_tiles[e].z) == -2) ++e;
+      return e;
+    };
     bool ok = mbar_wait(q_full, 0, a.err, 32);
-    int c = 0;
-    for (int e = kv_begin; ok && e < kv_end; ++e) {
-      const int4 t = a.kv_tiles[e];
-      if ((h ? t.w : t.z) == -2) continue;
-      const int st = c % kStages;
-      const uint32_t ph = (c / kStages) & 1;
-      if (!mbar_wait(k_full + st, ph, a.err, 33) || !mbar_wait(v_full + st, ph, a.err, 34)) {
-        ok = false;
-        break;
+    int e = used(kv_begin);
+    if (ok && e < kv_end) {
+      ok = mbar_wait(k_full, 0, a.err, 33) && mbar_wait(v_full, 0, a.err, 34);
+      if (ok) {
+        tc_fence_after();
+        issue_s64<0>(tbase + kColS, q_lo, k_lo0);   // S = Q K^T
+        issue_s64<0>(tbase + kColDp, do_lo, v_lo0);  // dP = dO V^T
+        umma_commit(s_full);
+        issue_s64<1>(tbase + kColS, q_lo, k_lo0);
+        issue_s64<1>(tbase + kColDp, do_lo, v_lo0);
+        umma_commit(s_full + 1);
       }
+    }
+    for (int c = 0; ok && e < kv_end; ++c) {
+      const int st = c % kStages, stn = (c + 1) % kStages;
+      const uint32_t off = (st * kTile) >> 4, offn = (stn * kTile) >> 4;
+      const int en = used(e + 1);
+      const bool more = en < kv_end;
+      if (!mbar_wait(ds_full, c & 1, a.err, 35)) break;
       tc_fence_after();
-      const uint32_t off = (st * kTile) >> 4;
-      issue_s(tbase + kColS, q_lo, k_lo0 + off);   // S = Q K^T
-      issue_s(tbase + kColDp, do_lo, v_lo0 + off);  // dP = dO V^T
-      umma_commit(s_full);
-      if (!mbar_wait(ds_full, c & 1, a.err, 35)) {
-        ok = false;
-        break;
+      issue_pv_sub<0>(tbase + kColDq, tbase + kColS, k_mn0 + off, c > 0);  // dQ += dS K
+      if (more) {
+        const uint32_t phn = ((c + 1) / kStages) & 1;
+        if (!mbar_wait(k_full + stn, phn, a.err, 33) || !mbar_wait(v_full + stn, phn, a.err, 34))
+          break;
+        tc_fence_after();
+        issue_s64<0>(tbase + kColS, q_lo, k_lo0 + offn);
+        issue_s64<0>(tbase + kColDp, do_lo, v_lo0 + offn);
+        umma_commit(s_full);
       }
+      if (!mbar_wait(ds_full + 1, c & 1, a.err, 38)) break;
       tc_fence_after();
-      issue_pv(tbase + kColDq, tbase + kColS, k_mn0 + off, c > 0);  // dQ += dS K
+      issue_pv_sub<1>(tbase + kColDq, tbase + kColS, k_mn0 + off, true);
       umma_commit(kv_empty + st);
-      ++c;
+      if (more) {
+        issue_s64<1>(tbase + kColS, q_lo, k_lo0 + offn);
+        issue_s64<1>(tbase + kColDp, do_lo, v_lo0 + offn);
+        umma_commit(s_full + 1);
+      }
+      e = en;
     }
     umma_commit(o_final);
   } else if (warp >= 4) {
-    // -------------------------------------------------- dS of one query row
-    const int r = threadIdx.x - 128;
+    // --------------------------------- dS of one query row, half its keys
+    const int grp = warp >= 8 ? 1 : 0;
+    const int r = threadIdx.x - 128 - 128 * grp;
     const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
     const uint32_t t_s = tbase + lane_base + kColS, t_dp = tbase + lane_base + kColDp;
     const bool valid = r < q_rows;
@@ -390,13 +475,13 @@ __global__ void __launch_bounds__(256, 1)
       if (sel == -2) continue;
       uint4 mk = make_uint4(~0u, ~0u, ~0u, ~0u);
       if (sel >= 0) mk = a.masks[(int64_t)sel * mask_stride + (r & mask_row_and)];
-      if (!mbar_wait(s_full, c & 1, a.err, 36)) {
+      if (!mbar_wait(s_full + grp, c & 1, a.err, 36)) {
         ok = false;
         break;
       }
       tc_fence_after();
 #pragma unroll 1
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 2 * grp; q < 2 * grp + 2; ++q) {
         uint32_t sv[32], dv[32];
         tmem_ld32(t_s + 32 * q, sv);
         tmem_ld32(t_dp + 32 * q, dv);
@@ -416,22 +501,22 @@ __global__ void __launch_bounds__(256, 1)
           }
           pk[i] = pack_bf16x2(ds[0], ds[1]);
         }
-        // dS of keys 32q.. over S columns 16q.. (already read)
-        tmem_st16(t_s + 16 * q, pk);
+        // dS of keys 32q.. over this group's S columns (already read)
+        tmem_st16(t_s + packed_col(q), pk);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(ds_full);
+      mbar_arrive(ds_full + grp);
       ++c;
     }
     __nv_bfloat16* dst = a.dq + grow * a.dq_stride + col;
     if (ok && c > 0) {
       if (mbar_wait(o_final, 0, a.err, 37)) {
         tc_fence_after();
-        store_row_bf16(tbase + lane_base + kColDq, a.scale, dst, valid);
+        store_row_bf16(tbase + lane_base + kColDq, a.scale, dst, valid, 2 * grp);
       }
     } else if (ok && valid) {
-      zero_row(dst);
+      zero_row(dst, 2 * grp);
     }
   }
   tc_fence_before();
@@ -465,10 +550,10 @@ constexpr int kKvSmemV = kTile;
 constexpr int kKvSmemStage = 2 * kTile;  // per stage: Q, dO
 constexpr int kKvSmemVec = kKvSmemStage + kStages * 2 * kTile;  // per stage: lse[128], delta[128]
 constexpr int kKvSmemBar = kKvSmemVec + kStages * 1024;
-constexpr int kKvNumBars = 2 + 2 * kStages + 3;
+constexpr int kKvNumBars = 2 + 2 * kStages + 5;
 constexpr int kKvSmemBytes = kKvSmemBar + kKvNumBars * 8 + 16 + 1024;
 
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     bwd_dkv_kernel(const __grid_constant__ DqMaps m, DkvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -478,9 +563,9 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* v_full = bars + 1;
   uint64_t* qd_full = bars + 2;
   uint64_t* qd_empty = qd_full + kStages;
-  uint64_t* s_full = qd_empty + kStages;
-  uint64_t* p_full = s_full + 1;
-  uint64_t* o_final = p_full + 1;
+  uint64_t* s_full = qd_empty + kStages;  // [sub-tile]
+  uint64_t* p_full = s_full + 2;          // [sub-tile], its warpgroup
+  uint64_t* o_final = p_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kKvNumBars);
 
   const int warp = warp_id(), lane = lane_id();
@@ -497,8 +582,10 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(qd_full + s, 1);
       mbar_init(qd_empty + s, 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(s_full + g, 1);
+      mbar_init(p_full + g, 128);
+    }
     mbar_init(o_final, 1);
     fence_mbar_init();
   }
@@ -535,25 +622,51 @@ __global__ void __launch_bounds__(256, 1)
     const uint32_t v_lo = sdesc_lo_kmajor(smem_u32(smem + kKvSmemV));
     const uint32_t sq_lo = sdesc_lo_kmajor(smem_u32(smem + kKvSmemStage));
     const uint32_t sq_mn = sdesc_lo_mnmajor(smem_u32(smem + kKvSmemStage));
-    bool ok = mbar_wait(k_full, 0, a.err, 42) && mbar_wait(v_full, 0, a.err, 43);
-    for (int i = 0; ok && i < n_ent; ++i) {
-      const int st = i % kStages;
-      if (!mbar_wait(qd_full + st, (i / kStages) & 1, a.err, 44)) break;
+    // Sub-tiles g = 0, 1 (query rows 64g.. of a tile) alternate:
+    //   S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | ...   (PV_g: dV and dK)
+    bool ok = mbar_wait(k_full, 0, a.err, 42) && mbar_wait(v_full, 0, a.err, 43) &&
+              mbar_wait(qd_full, 0, a.err, 44);
+    if (ok) {
       tc_fence_after();
-      const uint32_t oq = (st * 2 * kTile) >> 4, od = (st * 2 * kTile + kTile) >> 4;
-      issue_s(tbase + kColS, k_lo, sq_lo + oq);   // S^T = K Q^T
-      issue_s(tbase + kColDp, v_lo, sq_lo + od);  // dP^T = V dO^T
+      issue_s64<0>(tbase + kColS, k_lo, sq_lo);            // S^T = K Q^T
+      issue_s64<0>(tbase + kColDp, v_lo, sq_lo + (kTile >> 4));  // dP^T = V dO^T
       umma_commit(s_full);
+      issue_s64<1>(tbase + kColS, k_lo, sq_lo);
+      issue_s64<1>(tbase + kColDp, v_lo, sq_lo + (kTile >> 4));
+      umma_commit(s_full + 1);
+    }
+    for (int i = 0; ok && i < n_ent; ++i) {
+      const int st = i % kStages, stn = (i + 1) % kStages;
+      const bool more = i + 1 < n_ent;
+      const uint32_t oq = (st * 2 * kTile) >> 4, od = (st * 2 * kTile + kTile) >> 4;
+      const uint32_t oqn = (stn * 2 * kTile) >> 4, odn = (stn * 2 * kTile + kTile) >> 4;
       if (!mbar_wait(p_full, i & 1, a.err, 45)) break;
       tc_fence_after();
-      issue_pv(tbase + kColDv, tbase + kColS, sq_mn + od, i > 0);   // dV += P^T dO
-      issue_pv(tbase + kColDk, tbase + kColDp, sq_mn + oq, i > 0);  // dK += dS^T Q
+      issue_pv_sub<0>(tbase + kColDv, tbase + kColS, sq_mn + od, i > 0);   // dV += P^T dO
+      issue_pv_sub<0>(tbase + kColDk, tbase + kColDp, sq_mn + oq, i > 0);  // dK += dS^T Q
+      if (more) {
+        if (!mbar_wait(qd_full + stn, ((i + 1) / kStages) & 1, a.err, 44)) break;
+        tc_fence_after();
+        issue_s64<0>(tbase + kColS, k_lo, sq_lo + oqn);
+        issue_s64<0>(tbase + kColDp, v_lo, sq_lo + odn);
+        umma_commit(s_full);
+      }
+      if (!mbar_wait(p_full + 1, i & 1, a.err, 49)) break;
+      tc_fence_after();
+      issue_pv_sub<1>(tbase + kColDv, tbase + kColS, sq_mn + od, true);
+      issue_pv_sub<1>(tbase + kColDk, tbase + kColDp, sq_mn + oq, true);
       umma_commit(qd_empty + st);
+      if (more) {
+        issue_s64<1>(tbase + kColS, k_lo, sq_lo + oqn);
+        issue_s64<1>(tbase + kColDp, v_lo, sq_lo + odn);
+        umma_commit(s_full + 1);
+      }
     }
     umma_commit(o_final);
   } else if (warp >= 4) {
-    // ------------------------------------------- P^T, dS^T of one key row
-    const int j = threadIdx.x - 128;
+    // ------------------------- P^T, dS^T of one key row, half its queries
+    const int grp = warp >= 8 ? 1 : 0;
+    const int j = threadIdx.x - 128 - 128 * grp;
     const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
     const uint32_t t_s = tbase + lane_base + kColS, t_dp = tbase + lane_base + kColDp;
     const float sl2 = a.scale_log2;
@@ -565,14 +678,14 @@ __global__ void __launch_bounds__(256, 1)
       if (e.z >= 0) mk = a.t_masks[(int64_t)e.z * 128 + j];
       // the stage's lse / Delta vectors are visible after its load barrier
       if (!mbar_wait(qd_full + st, (i / kStages) & 1, a.err, 46) ||
-          !mbar_wait(s_full, i & 1, a.err, 47)) {
+          !mbar_wait(s_full + grp, i & 1, a.err, 47)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const float* vec = reinterpret_cast<const float*>(smem + kKvSmemVec + st * 1024);
 #pragma unroll 1
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 2 * grp; q < 2 * grp + 2; ++q) {
         uint32_t sv[32], dv[32];
         tmem_ld32(t_s + 32 * q, sv);
         tmem_ld32(t_dp + 32 * q, dv);
@@ -597,12 +710,12 @@ __global__ void __launch_bounds__(256, 1)
           pp[i2] = pack_bf16x2(p2[0], p2[1]);
           pd[i2] = pack_bf16x2(d2[0], d2[1]);
         }
-        tmem_st16(t_s + 16 * q, pp);
-        tmem_st16(t_dp + 16 * q, pd);
+        tmem_st16(t_s + packed_col(q), pp);
+        tmem_st16(t_dp + packed_col(q), pd);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(p_full + grp);
     }
     const int64_t krow = (int64_t)key0 + j;
     const bool store = krow < a.kv_rows;
@@ -611,12 +724,12 @@ __global__ void __launch_bounds__(256, 1)
     if (ok && n_ent > 0) {
       if (mbar_wait(o_final, 0, a.err, 48)) {
         tc_fence_after();
-        store_row_bf16(tbase + lane_base + kColDk, a.scale, dkr, store);
-        store_row_bf16(tbase + lane_base + kColDv, 1.f, dvr, store);
+        store_row_bf16(tbase + lane_base + kColDk, a.scale, dkr, store, 2 * grp);
+        store_row_bf16(tbase + lane_base + kColDv, 1.f, dvr, store, 2 * grp);
       }
     } else if (ok && store) {
-      zero_row(dkr);
-      zero_row(dvr);
+      zero_row(dkr, 2 * grp);
+      zero_row(dvr, 2 * grp);
     }
   }
   tc_fence_before();
@@ -759,7 +872,7 @@ extern "C" int hier_attn_bwd_dq(const void* q, int64_t q_rows, int64_t q_stride,
   a.n_pairs = n_pairs;
   a.n_heads = H;
   a.err = dev_err;
-  bwd_dq_kernel<<<n_pairs * 2 * H, 256, kDqSmemBytes, (cudaStream_t)stream>>>(m, a);
+  bwd_dq_kernel<<<n_pairs * 2 * H, 384, kDqSmemBytes, (cudaStream_t)stream>>>(m, a);
   HIER_CHECK_CUDA(cudaGetLastError(), "bwd_dq_kernel launch");
   return HIER_OK;
 }
@@ -806,7 +919,7 @@ extern "C" int hier_attn_bwd_dkv(const void* q, int64_t q_rows, int64_t q_stride
   a.n_kb = n_kb;
   a.n_heads = H;
   a.err = dev_err;
-  bwd_dkv_kernel<<<n_kb * H, 256, kKvSmemBytes, (cudaStream_t)stream>>>(m, a);
+  bwd_dkv_kernel<<<n_kb * H, 384, kKvSmemBytes, (cudaStream_t)stream>>>(m, a);
   HIER_CHECK_CUDA(cudaGetLastError(), "bwd_dkv_kernel launch");
   return HIER_OK;
 }
