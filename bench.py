@@ -512,11 +512,12 @@ def run_ours(args, rank, world, local_rank):
     if world == 1:
         line["cached_step"] = run_cached_step()
         line["plans_rebuild_ms"] = plans_rebuild(cfg, dev)
-    if world == 1 and not args.no_dit:
+    if world == 1:
         del inp, q_buf, k_buf, o_buf
         torch.cuda.empty_cache()
         line["action_attention"] = run_action()
         line["training_backward"] = run_backward(cfg)
+    if world == 1 and not args.no_dit:
         line["dit_step"] = run_dit()
     return line
 
