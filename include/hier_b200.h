@@ -213,6 +213,25 @@ int hier_prep_qk(const void* qx, const void* kx, int64_t x_stride, const void* c
                  int32_t D, float eps, void* q_out, void* k_out, int64_t out_stride,
                  const int32_t* out_rows, const int32_t* k_out_rows, void* stream);
 
+/* Backward of hier_prep_qk (training): given the gradients gq, gk of the
+ * roped q and k, writes dqx, dkx (bf16, the gradients of the projections
+ * qx, kx) and the norm weights' gradients as partial rows dw_part
+ * [2][n_warps][dim] fp32 (q then k; the caller sums over n_warps, from
+ * hier_prep_qk_bwd_partials).  With y = x + cam @ Wc^T, yh = y * rstd and
+ * g_n = the gradient rotated back by the RoPE table:
+ *   dx = rstd * (g_n * w - yh * mean(g_n * w * yh)),  dw = sum_rows g_n * yh.
+ * The camera adapters' gradient is dx^T @ cam (a GEMM left to the caller);
+ * camera tokens get no gradient.  Replaces the autograd of the reference's
+ * _project_self_attn_qkv (multics/models/attention.py:355-365) for the part
+ * after the projections.  Other arguments as hier_prep_qk (no row maps). */
+int hier_prep_qk_bwd_partials(int64_t S, int32_t* n_warps);
+int hier_prep_qk_bwd(const void* qx, const void* kx, int64_t x_stride, const void* cam,
+                     int32_t cam_dim, const void* wcq, const void* wck, const void* nqw,
+                     const void* nkw, const float* freqs, int64_t freqs_rows, int64_t S,
+                     int32_t H, int32_t D, float eps, const void* gq, const void* gk,
+                     int64_t g_stride, void* dqx, void* dkx, int64_t dx_stride, float* dw_part,
+                     void* stream);
+
 /* ---------------------------------------------------------------------------
  * Attention
  * ------------------------------------------------------------------------- */

@@ -136,6 +136,10 @@ _SIGS = {
     "hier_dense_block_plan_build": (c_int, [_P, c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P, _P,
                                             _P]),
     "hier_shared_mask_plan_size": (c_int, [c_int64, c_int64, c_int64, _P, _P]),
+    "hier_prep_qk_bwd_partials": (c_int, [c_int64, _P]),
+    "hier_prep_qk_bwd": (c_int, [_P, _P, c_int64, _P, c_int32, _P, _P, _P, _P, _P, c_int64,
+                                 c_int64, c_int32, c_int32, c_float, _P, _P, c_int64, _P, _P,
+                                 c_int64, _P, _P]),
     "hier_attn_bwd_prep": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, _P,
                                    _P, c_int64, _P]),
     "hier_bwd_plan_transpose": (c_int, [_P, c_int32, _P, _P, c_int32, c_int32, _P, _P, _P,

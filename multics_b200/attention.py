@@ -474,28 +474,29 @@ class SelfAttention(nn.Module):
 
     def _forward_train(self, x, freqs, mask, cam_tokens):
         """Differentiable forward (``attention.py:355-365,436-442`` with
-        autograd): the projections, camera add, RMSNorm and float64 RoPE as
-        PyTorch operations (their backward is PyTorch's), the attention on
-        the block plan through :func:`multics_b200.train.hier_block_attention_grad`
+        autograd): the projections (cuBLAS), the camera add + RMSNorm + RoPE
+        prologue and its backward as fused kernels
+        (:func:`multics_b200.train.prologue_grad`), the attention on the block
+        plan through :func:`multics_b200.train.hier_block_attention_grad`
         (tcgen05 forward and backward kernels)."""
-        from .train import hier_block_attention_grad
+        from .train import hier_block_attention_grad, prologue_grad
 
         if cam_tokens is not None and (self.cam_q is None or self.cam_k is None):
             raise RuntimeError("camera_pose was provided but enable_camera_pose_qk() was not called")
+        if cam_tokens is not None and cam_tokens.shape[:2] != x.shape[:2]:
+            raise ValueError(f"camera tokens shape {tuple(cam_tokens.shape[:2])} must match "
+                             f"q/k tokens {tuple(x.shape[:2])}")
+        if cam_tokens is not None and self.training and self.cam_dropout_p > 0:
+            cam_tokens = torch.nn.functional.dropout(cam_tokens, p=self.cam_dropout_p, training=True)
         qx, kx, v = self.q(x), self.k(x), self.v(x)
-        if cam_tokens is not None:
-            if cam_tokens.shape[:2] != x.shape[:2]:
-                raise ValueError(f"camera tokens shape {tuple(cam_tokens.shape[:2])} must match "
-                                 f"q/k tokens {tuple(x.shape[:2])}")
-            c = cam_tokens.to(qx.dtype)
-            if self.training and self.cam_dropout_p > 0:
-                c = torch.nn.functional.dropout(c, p=self.cam_dropout_p, training=True)
-            qx = qx + torch.nn.functional.linear(c, self.cam_q.weight)
-            kx = kx + torch.nn.functional.linear(c, self.cam_k.weight)
-        q = _rope_torch(self.norm_q(qx), freqs, self.num_heads)
-        k = _rope_torch(self.norm_k(kx), freqs, self.num_heads)
+        q, k = prologue_grad(qx, kx, freqs, self.num_heads, norm_q_weight=self.norm_q.weight,
+                             norm_k_weight=self.norm_k.weight, cam_tokens=cam_tokens,
+                             cam_q_weight=None if self.cam_q is None else self.cam_q.weight,
+                             cam_k_weight=None if self.cam_k is None else self.cam_k.weight,
+                             eps=self.norm_q.eps)
         bm = attention_mask_plan(mask, x.shape[1], x.device)
-        return self.o(hier_block_attention_grad(q, k, v, bm, self.num_heads))
+        out = hier_block_attention_grad(q, k, _rows(v), bm, self.num_heads)
+        return self.o(out.view(x.shape))
 
     def _forward_batch(self, x, freqs, mask, cam_tokens):
         """``B`` sequences of ``L`` tokens under one shared mask: projections,

@@ -7,7 +7,9 @@ over the grouping's BlockMask (``multics/models/attention.py:322-353``;
 forward is the tcgen05 attention kernel run on the block plan with its
 log2-sum-exp kept, and the backward is three kernels
 (``csrc/hier_bwd.cu``): Delta = rowsum(dO * O), dQ over the forward's
-query-major plan, dK and dV over its key-major transpose.
+query-major plan, dK and dV over its key-major transpose.  The camera add,
+RMSNorm and RoPE before it run as the fused prologue kernel with its own
+backward kernel (:func:`prologue_grad`).
 
 :func:`hier_block_attention_grad` is the differentiable attention;
 :meth:`multics_b200.attention.SelfAttention.forward` uses it whenever autograd
@@ -26,7 +28,7 @@ from ._lib import check, ptr, stream_ptr
 from .attention import _dev_err, _rows
 from .hier_masks import HierBlockMask
 
-__all__ = ["BlockPlanGrad", "block_plan_grad", "hier_block_attention_grad"]
+__all__ = ["BlockPlanGrad", "block_plan_grad", "hier_block_attention_grad", "prologue_grad"]
 
 
 class BlockPlanGrad:
@@ -124,6 +126,65 @@ class _HierBlockAttention(torch.autograd.Function):
             ptr(err), st))
         sq, sk, sv = ctx.shapes
         return dq.view(sq), dk.view(sk), dv.view(sv), None, None, None
+
+
+class _PrologueFn(torch.autograd.Function):
+    """camera add + RMSNorm + RoPE of q and k with the fused kernels both ways
+    (``hier_prep_qk`` / ``hier_prep_qk_bwd``)."""
+
+    @staticmethod
+    def forward(ctx, qx, kx, nqw, nkw, wcq, wck, cam, ft, num_heads, eps):
+        from .attention import hier_prep_qk
+
+        q, k = hier_prep_qk(qx, kx, ft, num_heads, norm_q_weight=nqw, norm_k_weight=nkw,
+                            cam_tokens=cam, cam_q_weight=wcq, cam_k_weight=wck, eps=eps)
+        ctx.save_for_backward(qx, kx, nqw, nkw, wcq, wck, cam, ft)
+        ctx.num_heads, ctx.eps = num_heads, eps
+        return q, k
+
+    @staticmethod
+    def backward(ctx, gq, gk):
+        qx, kx, nqw, nkw, wcq, wck, cam, ft = ctx.saved_tensors
+        q2, k2 = _rows(qx).contiguous(), _rows(kx).contiguous()
+        S, dim = q2.shape
+        H = ctx.num_heads
+        dev = q2.device
+        gq = torch.zeros_like(q2) if gq is None else gq.reshape(S, dim).to(torch.bfloat16).contiguous()
+        gk = torch.zeros_like(k2) if gk is None else gk.reshape(S, dim).to(torch.bfloat16).contiguous()
+        n = ctypes.c_int32()
+        L = _lib.lib()
+        check(L.hier_prep_qk_bwd_partials(S, ctypes.byref(n)))
+        part = torch.empty((2, n.value, dim), dtype=torch.float32, device=dev)
+        dqx, dkx = torch.empty_like(q2), torch.empty_like(k2)
+        c2 = None if cam is None else _rows(cam).to(torch.bfloat16).contiguous()
+        bf = lambda t: None if t is None else t.to(torch.bfloat16).contiguous()
+        wq, wk, nq, nk = bf(wcq), bf(wck), bf(nqw), bf(nkw)
+        check(L.hier_prep_qk_bwd(
+            ptr(q2), ptr(k2), q2.stride(0), ptr(c2), 0 if c2 is None else c2.shape[1], ptr(wq),
+            ptr(wk), ptr(nq), ptr(nk), ptr(ft), ft.shape[0], S, H, dim // H, float(ctx.eps),
+            ptr(gq), ptr(gk), gq.stride(0), ptr(dqx), ptr(dkx), dqx.stride(0), ptr(part),
+            stream_ptr(dev)))
+        dw = part.sum(1)
+        dwcq = dwck = None
+        if c2 is not None:
+            dwcq = (dqx.t() @ c2).to(wcq.dtype)
+            dwck = (dkx.t() @ c2).to(wck.dtype)
+        return (dqx.view(qx.shape), dkx.view(kx.shape), dw[0].to(nqw.dtype), dw[1].to(nkw.dtype),
+                dwcq, dwck, None, None, None, None)
+
+
+def prologue_grad(qx, kx, freqs, num_heads, *, norm_q_weight, norm_k_weight, cam_tokens=None,
+                  cam_q_weight=None, cam_k_weight=None, eps=1e-6):
+    """Differentiable ``hier_prep_qk``: roped ``(q, k)`` ``[S, H*D]`` from the
+    projections ``qx``, ``kx``, with gradients for them, the norm weights
+    and the camera adapters (camera tokens get none)."""
+    from .attention import freqs_table
+
+    ft = freqs if (freqs.dtype == torch.float32 and freqs.dim() == 3
+                   and freqs.shape[-1] == 2) else freqs_table(freqs)
+    ft = ft.to(qx.device).contiguous()
+    return _PrologueFn.apply(qx, kx, norm_q_weight, norm_k_weight, cam_q_weight, cam_k_weight,
+                             cam_tokens, ft, num_heads, eps)
 
 
 def hier_block_attention_grad(q, k, v, mask, num_heads: int, *, softmax_scale=None):

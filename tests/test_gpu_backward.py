@@ -8,8 +8,11 @@
   no contribution) on hierarchical groupings (labels, membership with idle
   hubs, windows), a caller's dense mask with empty rows, and no mask, at
   sequence lengths that are not multiples of 128.
-* The whole attention path (camera add, RMSNorm, RoPE, attention) reproduces
-  the gradients the reference's own autograd recorded (``tests/golden/
+* The fused prologue's backward (``hier_prep_qk_bwd``) matches fp32 autograd
+  of camera add + RMSNorm + RoPE, with and without camera tokens, for one
+  RoPE row per token and for a table shared by a batch of sequences.
+* The whole attention path (fused prologue, attention) reproduces the
+  gradients the reference's own autograd recorded (``tests/golden/
   grads.npz``) for its inputs and camera / norm weights.
 * ``SelfAttention`` under autograd (projections included) matches an fp32
   copy of the module.
@@ -191,22 +194,16 @@ def _bf(a, dev):
 def test_attention_path_grads_match_reference(name):
     """camera add -> RMSNorm -> RoPE -> attention with autograd, from the
     reference's recorded inputs, against its recorded gradients."""
-    from multics_b200.attention import RMSNorm, _rope_torch
     from multics_b200.hier_masks import build_stage2_hier_flex_block_mask
-    from multics_b200.train import hier_block_attention_grad
+    from multics_b200.train import hier_block_attention_grad, prologue_grad
 
     dev = torch.device("cuda")
     meta = json.loads(bytes(NUM[f"{name}/meta"]).decode())
     H, D, S = meta["H"], meta["D"], meta["S"]
     qx, kx, v = (_bf(NUM[f"{name}/{t}"], dev)[None].requires_grad_(True) for t in ("qx", "kx", "v"))
     cam = _bf(NUM[f"{name}/cam"], dev)[None]
-    wcq, wck = (_bf(NUM[f"{name}/{t}"], dev).requires_grad_(True) for t in ("wcq", "wck"))
-    nq, nk = RMSNorm(H * D, eps=1e-6).to(dev), RMSNorm(H * D, eps=1e-6).to(dev)
-    with torch.no_grad():
-        nq.weight.copy_(_bf(NUM[f"{name}/nqw"], dev).float())
-        nk.weight.copy_(_bf(NUM[f"{name}/nkw"], dev).float())
-    nq.to(torch.bfloat16)
-    nk.to(torch.bfloat16)
+    wcq, wck, nqw, nkw = (_bf(NUM[f"{name}/{t}"], dev).requires_grad_(True)
+                          for t in ("wcq", "wck", "nqw", "nkw"))
     fr = torch.from_numpy(NUM[f"{name}/freqs"]).to(dev)
     freqs = torch.complex(fr[..., 0], fr[..., 1]).unsqueeze(1)
     P, T, L, N, KL, KG = (meta[k] for k in ("P", "T", "L", "N", "KL", "KG"))
@@ -218,15 +215,13 @@ def test_attention_path_grads_match_reference(name):
                   global_only=torch.from_numpy(NUM[f"{name}/global_only"]).to(dev))
     bm, _, _ = build_stage2_hier_flex_block_mask(P, T, L, N, KL, KG, meta["n"], meta["win"],
                                                  direct_player=True, device=dev, **kw)
-    qc = qx + torch.nn.functional.linear(cam, wcq)
-    kc = kx + torch.nn.functional.linear(cam, wck)
-    q = _rope_torch(nq(qc), freqs, H)
-    k = _rope_torch(nk(kc), freqs, H)
-    out = hier_block_attention_grad(q, k, v, bm, H)
-    out.backward(_bf(GRADS[f"{name}/dout"], dev)[None])
+    q, k = prologue_grad(qx, kx, freqs, H, norm_q_weight=nqw, norm_k_weight=nkw,
+                         cam_tokens=cam, cam_q_weight=wcq, cam_k_weight=wck)
+    out = hier_block_attention_grad(q, k, v[0], bm, H)
+    out.backward(_bf(GRADS[f"{name}/dout"], dev))
     torch.cuda.synchronize()
     for t, got in (("qx", qx.grad[0]), ("kx", kx.grad[0]), ("v", v.grad[0]), ("wcq", wcq.grad),
-                   ("wck", wck.grad), ("nqw", nq.weight.grad), ("nkw", nk.weight.grad)):
+                   ("wck", wck.grad), ("nqw", nqw.grad), ("nkw", nkw.grad)):
         _check(got, torch.from_numpy(GRADS[f"{name}/d_{t}"]).to(dev), (name, t))
 
 
@@ -281,3 +276,50 @@ def test_self_attention_training_matches_fp32_module():
     for (n1, p1), (n2, p2) in zip(layer.named_parameters(), ref.named_parameters()):
         assert n1 == n2
         _check(p1.grad, p2.grad, n1)
+
+
+@pytest.mark.parametrize("S,F,cam", [(1100, 1100, True), (517, 517, False), (42 * 9, 42, False)])
+def test_fused_prologue_grads_match_fp32(S, F, cam):
+    """hier_prep_qk / hier_prep_qk_bwd through autograd against fp32 autograd
+    of the same math (camera add, RMSNorm over the row, RoPE); F < S: one
+    table of F rows shared by S / F sequences."""
+    from multics_b200.attention import _rope_torch
+    from multics_b200.rope import precompute_freqs_cis
+    from multics_b200.train import prologue_grad
+
+    dev = torch.device("cuda")
+    H, D = 3, 128
+    dim = H * D
+    g = torch.Generator(device="cuda").manual_seed(S)
+    mk = lambda *sh, s=1.0: (torch.randn(*sh, generator=g, device=dev) * s).bfloat16()
+    qx, kx = mk(S, dim).requires_grad_(True), mk(S, dim).requires_grad_(True)
+    nqw, nkw = (1 + mk(dim, s=0.1)).requires_grad_(True), (1 + mk(dim, s=0.1)).requires_grad_(True)
+    c = wcq = wck = None
+    if cam:
+        c = mk(S, 12)
+        c[S // 2:] = 0  # hub rows without a camera
+        c[: S // 2] = c[0]  # runs of one camera row
+        c[S // 4: S // 2] = mk(12)
+        wcq, wck = mk(dim, 12, s=0.05).requires_grad_(True), mk(dim, 12, s=0.05).requires_grad_(True)
+    freqs = precompute_freqs_cis(D, end=F).unsqueeze(1).to(dev)
+    q, k = prologue_grad(qx, kx, freqs, H, norm_q_weight=nqw, norm_k_weight=nkw, cam_tokens=c,
+                         cam_q_weight=wcq, cam_k_weight=wck)
+    gq, gk = mk(S, dim), mk(S, dim)
+    (q.float() * gq.float()).sum().add_((k.float() * gk.float()).sum()).backward()
+    torch.cuda.synchronize()
+    leaves = [qx, kx, nqw, nkw] + ([wcq, wck] if cam else [])
+    ref = [t.detach().float().requires_grad_(True) for t in leaves]
+    fr = freqs.repeat(S // F, 1, 1)
+
+    def path(x, w, wc):
+        y = x if wc is None else x + c.float() @ wc.t()
+        y = y * torch.rsqrt(y.pow(2).mean(-1, keepdim=True) + 1e-6) * w
+        return _rope_torch(y[None], fr, H)[0]
+
+    qr = path(ref[0], ref[2], ref[4] if cam else None)
+    kr = path(ref[1], ref[3], ref[5] if cam else None)
+    (qr * gq.float()).sum().add_((kr * gk.float()).sum()).backward()
+    _check(q.detach(), qr.detach(), "q")
+    _check(k.detach(), kr.detach(), "k")
+    for name, got, r in zip(("dqx", "dkx", "dnqw", "dnkw", "dwcq", "dwck"), leaves, ref):
+        _check(got.grad, r.grad, name)
