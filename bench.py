@@ -736,6 +736,33 @@ def run_backward(cfg, steps=10, warmup=3):
            "note": "backward FLOPs = 2 x forward (dV, dP, dQ, dK); S recomputation not counted"}
     del q, k, v, dout, out
     torch.cuda.empty_cache()
+    # the module as the reference trains it: SelfAttention forward + backward
+    # (q/k/v/o projections, fused prologue and its backward, attention)
+    from multics_b200.attention import SelfAttention
+
+    layer = SelfAttention(cfg.dim, cfg.H).to(dev).to(torch.bfloat16)
+    layer.enable_camera_pose_qk(12, dropout_p=0.0)
+    inp = make_inputs(cfg, device=dev)
+    x = torch.randn(1, S, cfg.dim, generator=g, device=dev).bfloat16().requires_grad_(True)
+    cam = inp.cam.reshape(1, S, -1).bfloat16()
+    dy = torch.randn(1, S, cfg.dim, generator=g, device=dev).bfloat16()
+    ts = []
+    for i in range(warmup + steps):
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x.grad = None
+        layer.zero_grad(set_to_none=True)
+        a_.record()
+        layer(x, inp.freqs, bm, cam).backward(dy)
+        b_.record()
+        if i >= warmup:
+            ts.append((a_, b_))
+    torch.cuda.synchronize()
+    res["selfattention_train_step_ms"] = round(statistics.mean(a_.elapsed_time(b_) for a_, b_ in ts), 3)
+    res["selfattention_train_step_note"] = ("SelfAttention forward + backward at the bench "
+                                            "configuration: projections (cuBLAS), fused prologue "
+                                            "and its backward, attention on the block plan")
+    del layer, inp, x, cam, dy
+    torch.cuda.empty_cache()
     return res
 
 

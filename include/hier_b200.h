@@ -164,6 +164,16 @@ int hier_dense_block_plan_build(const uint8_t* mask, int64_t S, int64_t ld, void
                                 int32_t* kv_tiles, uint32_t* row_masks, int32_t* order,
                                 int32_t* n_kv_tiles, void* stream);
 
+/* Split-KV form of a query-pair plan: pair p becomes out pair p*chunks + c
+ * over part c of its key-tile list [b + len*c/chunks, b + len*(c+1)/chunks),
+ * with q_pairs[7] = 1 | c << 8 (partial rows in slot c, see
+ * hier_partial_out); order [n_pairs*chunks] (or NULL) ranks them by work.
+ * The slots are merged by hier_lse_gather_merge.  The input pairs must not
+ * be partial already.  No counterpart in the reference (a scheduling
+ * device: shorter CTAs for plans with few, long pairs). */
+int hier_plan_split_kv(const int32_t* q_pairs, int32_t n_pairs, int32_t chunks,
+                       int32_t* out_pairs, int32_t* order, void* stream);
+
 /* Batched attention under one bool mask [Lq, Lk] shared by every batch entry
  * (query row b*Lq + i sees key row b*Lk + j iff mask[i*ld + j] != 0): the
  * reference's flash_attention(q, k, v, num_heads, mask) with a mask that
@@ -288,8 +298,10 @@ int hier_attn_fwd(const void* q, int64_t q_rows_total, int64_t q_stride, const v
 /* Rows of a query-pair plan beyond the main query tensor: query rows from
  * q2_row0 on are read from q2 (row r at q2 row r - q2_row0); the outputs of
  * pairs flagged in q_pairs[7] (bit 0) are partial rows, written to o at row
- * r - row0 with their log2-sum-exp in lse ([rows][H]) for a later merge
- * (hier_lse_gather_*). */
+ * r - row0 + (q_pairs[7] >> 8) * slot_rows with their log2-sum-exp in lse
+ * ([rows][H]) for a later merge (hier_lse_gather_*): bits 8 and up select a
+ * slot, so that pairs over disjoint parts of one key list (split-KV) keep
+ * their partial rows apart. */
 typedef struct hier_partial_out {
   const void* q2;
   int64_t q2_rows, q2_stride, q2_row0;
@@ -297,6 +309,7 @@ typedef struct hier_partial_out {
   int64_t o_stride;
   float* lse;
   int64_t row0;
+  int64_t slot_rows;
 } hier_partial_out;
 
 int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_t q_stride,
@@ -437,6 +450,44 @@ int hier_cached_build(const hier_cached_grouping* g, int32_t block_m, const int3
                       int32_t* kv_index, int32_t kv_width, int32_t* q_pairs, int32_t* kv_tiles,
                       uint32_t* tile_masks, int32_t tile_capacity, int32_t* order,
                       int32_t* status, void* stream);
+
+/* Packed hub rows for the attention plan of a cached step.  A local-hub
+ * segment has K_L query rows but its members' whole cached history as keys,
+ * and a group's segments at the n query frames see almost the same keys; so
+ * the plan can pack them: pack g (g < N) = the rows of group g at every
+ * query frame (n*K_L rows, frame-major: row f*K_L + s is hub slot s of group
+ * g at query frame f), pack N = the global-hub rows (n*K_G, frame-major).  A
+ * pack's key list is the union of its frames' candidate runs; its tiles carry
+ * 128-row masks (a row sees the keys its own segment attends to).  Packing
+ * applies when n*K_L <= 128 and n*K_G <= 128 (n_packs = 0 otherwise, and
+ * without local hubs).  The packed rows are a second query block
+ * (hier_partial_out.q2, rows from q2_row0 on) written back through out_rows.
+ * The per-segment metadata (_build_metadata's contract) is unchanged. */
+typedef struct hier_cached_pack_sizes_t {
+  int32_t n_packs;       /* N + (K_G > 0), or 0 */
+  int32_t q2_rows;       /* packed query rows: n*(N*K_L + K_G) */
+  int32_t agent_pairs;   /* the plan's player pairs: q_pairs rows [0, agent_pairs) */
+  int32_t tile_capacity; /* upper bound of the packs' key tiles */
+} hier_cached_pack_sizes_t;
+
+int hier_cached_pack_sizes(const hier_cached_grouping* g, hier_cached_pack_sizes_t* out);
+
+/* 64-row key boxes of each pack (n_boxes [n_packs]). */
+int hier_cached_pack_count(const hier_cached_grouping* g, int32_t* n_boxes, int32_t* status,
+                           void* stream);
+
+/* After hier_cached_build: the packs' pairs at q_pairs rows [agent_pairs,
+ * agent_pairs + n_packs) (replacing the hub segments' pairs, so the plan
+ * has agent_pairs + n_packs pairs), their tiles at kv_tiles rows
+ * [tile_base, tile_end), their 128-row masks from index mask_base of
+ * tile_masks counted in 128-entry units (mask_base * 128 >= the per-tile
+ * masks in use), packed row i read as query row q2_row0 + i; order
+ * [agent_pairs + n_packs] ranks all pairs.  status bit 1: capacity
+ * exceeded. */
+int hier_cached_pack_build(const hier_cached_grouping* g, const int32_t* n_boxes,
+                           int32_t tile_base, int32_t tile_end, int32_t mask_base,
+                           int32_t q2_row0, int32_t* q_pairs, int32_t* kv_tiles,
+                           uint32_t* tile_masks, int32_t* order, int32_t* status, void* stream);
 
 /* Workspace bytes for hier_varlen_plan_build. */
 int hier_varlen_workspace_size(int32_t n_seg, size_t* bytes);

@@ -51,6 +51,13 @@ class HierCachedGrouping(ctypes.Structure):
     ]
 
 
+class HierCachedPackSizes(ctypes.Structure):
+    """Mirror of ``hier_cached_pack_sizes_t``."""
+
+    _fields_ = [("n_packs", ctypes.c_int32), ("q2_rows", ctypes.c_int32),
+                ("agent_pairs", ctypes.c_int32), ("tile_capacity", ctypes.c_int32)]
+
+
 class HierCachedSizes(ctypes.Structure):
     """Mirror of ``hier_cached_sizes_t``."""
 
@@ -115,6 +122,7 @@ class HierPartialOut(ctypes.Structure):
     _fields_ = [
         ("q2", c_void_p), ("q2_rows", c_int64), ("q2_stride", c_int64), ("q2_row0", c_int64),
         ("o", c_void_p), ("o_stride", c_int64), ("lse", c_void_p), ("row0", c_int64),
+        ("slot_rows", c_int64),
     ]
 
 
@@ -135,6 +143,7 @@ _SIGS = {
                                             _P]),
     "hier_dense_block_plan_build": (c_int, [_P, c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P, _P,
                                             _P]),
+    "hier_plan_split_kv": (c_int, [_P, c_int32, c_int32, _P, _P, _P]),
     "hier_shared_mask_plan_size": (c_int, [c_int64, c_int64, c_int64, _P, _P]),
     "hier_prep_qk_bwd_partials": (c_int, [c_int64, _P]),
     "hier_prep_qk_bwd": (c_int, [_P, _P, c_int64, _P, c_int32, _P, _P, _P, _P, _P, c_int64,
@@ -163,6 +172,11 @@ _SIGS = {
     "hier_cached_sizes": (c_int, [ctypes.POINTER(HierCachedGrouping), c_int32,
                                   ctypes.POINTER(HierCachedSizes)]),
     "hier_cached_count": (c_int, [ctypes.POINTER(HierCachedGrouping), _P, _P, _P, _P]),
+    "hier_cached_pack_sizes": (c_int, [ctypes.POINTER(HierCachedGrouping),
+                                       ctypes.POINTER(HierCachedPackSizes)]),
+    "hier_cached_pack_count": (c_int, [ctypes.POINTER(HierCachedGrouping), _P, _P, _P]),
+    "hier_cached_pack_build": (c_int, [ctypes.POINTER(HierCachedGrouping), _P, c_int32, c_int32,
+                                       c_int32, c_int32, _P, _P, _P, _P, _P, _P]),
     "hier_cached_build": (c_int, [ctypes.POINTER(HierCachedGrouping), c_int32, _P, _P, _P, _P, _P,
                                   c_int32, _P, _P, _P, c_int32, _P, _P, _P]),
     "hier_varlen_workspace_size": (c_int, [c_int32, ctypes.POINTER(c_size_t)]),
@@ -188,7 +202,7 @@ _SIGS = {
 _LIB = None
 
 # hier_abi_version() of the library these signatures describe
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 def lib():

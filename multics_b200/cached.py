@@ -24,6 +24,7 @@ Every path requires the CUDA library; there is no CPU fallback.
 
 from __future__ import annotations
 
+import ctypes
 import math
 import os
 from collections import OrderedDict
@@ -32,7 +33,8 @@ from typing import Optional, Sequence
 import torch
 
 from . import _lib
-from ._lib import HierCachedGrouping, HierCachedSizes, check, ptr, stream_ptr
+from ._lib import (HierCachedGrouping, HierCachedPackSizes, HierCachedSizes, HierPartialOut,
+                   check, ptr, stream_ptr)
 
 __all__ = ["build_metadata", "get_varlen_plan", "hierarchical_cached_attention",
            "clear_metadata_cache", "CachedPlan", "build_cached_plan"]
@@ -312,10 +314,29 @@ def get_varlen_plan(*, kv_index, kv_count, qbase, qlen, seg_ids, query_tokens):
 # ---------------------------------------------------------------------------
 
 
-class CachedPlan:
-    """Device attention plan of one cached step (see hier_cached_build)."""
+# Packed hub rows in the cached attention plan (hier_cached_pack_build): on
+# unless this variable is "0".
+CACHED_PACK_ENV = "MULTICS_B200_CACHED_PACK"
 
-    def __init__(self, q_pairs, kv_tiles, tile_masks, order, n_pairs, n_streams, status, grouping):
+# Split-KV of the cached step's attention: every query pair runs as this
+# many CTAs over consecutive parts of its key list, merged by log-sum-exp
+# ("1": no split).
+CACHED_SPLIT_ENV = "MULTICS_B200_CACHED_SPLIT"
+
+# (P, N, L, KL, KG, n, device) -> (packed row sources, output row map)
+_PACK_ROWS = {}
+# (q_rows, packed, chunks, device) -> (merge CSR offsets, partial rows)
+_SPLIT_CSR = {}
+
+
+class CachedPlan:
+    """Device attention plan of one cached step (see hier_cached_build and
+    hier_cached_pack_build).  With packed hub rows, ``q2_src`` lists the
+    query rows read as the second query block and ``out_rows`` maps every
+    query row (then every packed row) to its output row."""
+
+    def __init__(self, q_pairs, kv_tiles, tile_masks, order, n_pairs, n_streams, status, grouping,
+                 q2_src=None, out_rows=None):
         self.q_pairs = q_pairs
         self.kv_tiles = kv_tiles
         self.tile_masks = tile_masks
@@ -324,23 +345,86 @@ class CachedPlan:
         self.n_streams = n_streams
         self.status = status
         self.grouping = grouping
+        self.q2_src = q2_src
+        self.out_rows = out_rows
 
 
-def build_cached_plan(g: _Grouping, device) -> CachedPlan:
+def _pack_rows(g: _Grouping, q_rows: int, device):
+    """Sequence rows of the packed hub rows (group-major local hubs, then the
+    global hubs, frame-major inside a pack) and the output row map."""
+    c = g.c
+    key = (c.P, c.N, c.L, c.KL, c.KG, c.n_frames, str(device))
+    hit = _PACK_ROWS.get(key)
+    if hit is None:
+        P, N, L, KL, KG, n = c.P, c.N, c.L, c.KL, c.KG, c.n_frames
+        aq, lq = P * n * L, n * N * KL
+        src = [aq + (f * N + gi) * KL + sl for gi in range(N) for f in range(n) for sl in range(KL)]
+        src += [aq + lq + f * KG + sl for f in range(n) for sl in range(KG)]
+        src_t = torch.tensor(src, dtype=torch.int64, device=device)
+        rows = torch.cat([torch.arange(q_rows, dtype=torch.int32, device=device),
+                          src_t.to(torch.int32)])
+        hit = (src_t, rows)
+        _PACK_ROWS[key] = hit
+    return hit
+
+
+def _split_csr(q_rows: int, q2_src, chunks: int, device):
+    """Merge CSR of a split plan: output row t gathers its ``chunks`` partial
+    rows, at query index t (or, for a packed hub row, the index of its
+    packed copy) in every slot of ``q_rows + packed rows`` rows."""
+    n2 = 0 if q2_src is None else int(q2_src.numel())
+    key = (q_rows, n2, chunks, str(device), None if q2_src is None else q2_src.data_ptr())
+    hit = _SPLIT_CSR.get(key)
+    if hit is None:
+        qi = torch.arange(q_rows, dtype=torch.int64, device=device)
+        if n2:
+            qi[q2_src] = q_rows + torch.arange(n2, dtype=torch.int64, device=device)
+        slot = q_rows + n2
+        rows = (qi[:, None] + slot * torch.arange(chunks, device=device)[None]).reshape(-1)
+        off = torch.arange(q_rows + 1, dtype=torch.int32, device=device) * chunks
+        hit = (off, rows.to(torch.int32).contiguous(), slot)
+        _SPLIT_CSR[key] = hit
+    return hit
+
+
+def build_cached_plan(g: _Grouping, device, pack=None) -> CachedPlan:
+    """The step's attention plan: one query pair per player segment over its
+    key runs and, when the shape allows it (``pack`` None: unless
+    ``MULTICS_B200_CACHED_PACK=0``), the hub rows packed per group across the
+    query frames; otherwise one pair per hub segment."""
     sz = g.sizes(1)
     lib = _lib.lib()
     s = stream_ptr(device)
+    ps = HierCachedPackSizes()
+    check(lib.hier_cached_pack_sizes(g.ref(), ctypes.byref(ps)))
+    if pack is None:
+        pack = os.environ.get(CACHED_PACK_ENV, "1") != "0"
+    pack = bool(pack) and ps.n_packs > 0
     n_boxes = torch.empty(sz.n_seg, dtype=torch.int32, device=device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
     q_pairs = torch.empty((max(sz.n_pairs, 1), 8), dtype=torch.int32, device=device)
     cap = max(sz.tile_capacity, 1)
-    kv_tiles = torch.empty((cap, 4), dtype=torch.int32, device=device)
-    tile_masks = torch.empty((cap, 4), dtype=torch.int32, device=device)
+    mask_base = (cap + 127) // 128
+    n_tiles = cap + (ps.tile_capacity if pack else 0)
+    n_masks = (mask_base + ps.tile_capacity) * 128 if pack else cap
+    kv_tiles = torch.empty((n_tiles, 4), dtype=torch.int32, device=device)
+    tile_masks = torch.empty((n_masks, 4), dtype=torch.int32, device=device)
     order = torch.empty(max(sz.n_pairs, 1), dtype=torch.int32, device=device)
     check(lib.hier_cached_count(g.ref(), None, ptr(n_boxes), ptr(status), s))
     check(lib.hier_cached_build(g.ref(), 1, ptr(n_boxes), None, None, None, None, 0, ptr(q_pairs),
-                                ptr(kv_tiles), ptr(tile_masks), cap, ptr(order), ptr(status), s))
-    return CachedPlan(q_pairs, kv_tiles, tile_masks, order, sz.n_pairs, sz.n_streams, status, g)
+                                ptr(kv_tiles), ptr(tile_masks), cap,
+                                None if pack else ptr(order), ptr(status), s))
+    if not pack:
+        return CachedPlan(q_pairs, kv_tiles, tile_masks, order, sz.n_pairs, sz.n_streams,
+                          status, g)
+    nb_p = torch.empty(ps.n_packs, dtype=torch.int32, device=device)
+    check(lib.hier_cached_pack_count(g.ref(), ptr(nb_p), ptr(status), s))
+    check(lib.hier_cached_pack_build(g.ref(), ptr(nb_p), cap, n_tiles, mask_base, int(sz.q_rows),
+                                     ptr(q_pairs), ptr(kv_tiles), ptr(tile_masks), ptr(order),
+                                     ptr(status), s))
+    q2_src, out_rows = _pack_rows(g, int(sz.q_rows), device)
+    return CachedPlan(q_pairs, kv_tiles, tile_masks, order, ps.agent_pairs + ps.n_packs,
+                      sz.n_streams, status, g, q2_src, out_rows)
 
 
 def _kv_rows(t, name):
@@ -424,11 +508,48 @@ def hierarchical_cached_attention(*, roped_q, agent_frames, agent_keys, agent_va
         if v.shape != k.shape or (v.numel() and v.stride(0) != k.stride(0)):
             raise ValueError("each value cache must match its key cache's shape and layout")
     err = _dev_err(dev)
-    if plan.n_pairs > 0:
-        check(_lib.lib().hier_attn_fwd_streams(
-            ptr(q), s, q.stride(0), n, kp, vp, rows, strides, ptr(out), out.stride(0), None, heads,
-            head_dim, ptr(plan.q_pairs), plan.n_pairs, ptr(plan.kv_tiles), ptr(plan.tile_masks),
-            1, ptr(plan.order), 1.0 / math.sqrt(head_dim), None, None, ptr(err), stream_ptr(dev)))
+    lib = _lib.lib()
+    st = stream_ptr(dev)
+    part = None
+    q2 = None
+    if plan.q2_src is not None:
+        # packed hub rows: a second query block, outputs through the row map
+        q2 = q.index_select(0, plan.q2_src)
+        part = HierPartialOut()
+        part.q2, part.q2_rows, part.q2_stride, part.q2_row0 = (q2.data_ptr(), q2.shape[0],
+                                                              q2.stride(0), s)
+        part.o, part.o_stride, part.lse, part.row0 = None, 0, None, 0
+    chunks = int(os.environ.get(CACHED_SPLIT_ENV, "2"))
+    if plan.n_pairs > 0 and chunks > 1:
+        # split-KV: partial rows per chunk, then one log-sum-exp merge
+        pairs = torch.empty((plan.n_pairs * chunks, 8), dtype=torch.int32, device=dev)
+        order = torch.empty(plan.n_pairs * chunks, dtype=torch.int32, device=dev)
+        check(lib.hier_plan_split_kv(ptr(plan.q_pairs), plan.n_pairs, chunks, ptr(pairs),
+                                     ptr(order), st))
+        off, prow, slot = _split_csr(s, plan.q2_src, chunks, dev)
+        part_o = torch.empty((chunks * slot, heads * head_dim), dtype=torch.bfloat16, device=dev)
+        part_lse = torch.empty((chunks * slot, heads), dtype=torch.float32, device=dev)
+        if part is None:
+            part = HierPartialOut()
+            part.q2, part.q2_rows, part.q2_stride, part.q2_row0 = None, 0, 0, 0
+        part.o, part.o_stride, part.lse, part.row0 = (part_o.data_ptr(), part_o.stride(0),
+                                                      part_lse.data_ptr(), 0)
+        part.slot_rows = slot
+        check(lib.hier_attn_fwd_streams(
+            ptr(q), s, q.stride(0), n, kp, vp, rows, strides, ptr(out), out.stride(0), None,
+            heads, head_dim, ptr(pairs), plan.n_pairs * chunks, ptr(plan.kv_tiles),
+            ptr(plan.tile_masks), 1, ptr(order), 1.0 / math.sqrt(head_dim), None,
+            ctypes.byref(part), ptr(err), st))
+        check(lib.hier_lse_gather_merge(ptr(part_o), part_o.stride(0), ptr(part_lse), heads,
+                                        head_dim, ptr(off), ptr(prow), s, ptr(out), out.stride(0),
+                                        None, st))
+    elif plan.n_pairs > 0:
+        check(lib.hier_attn_fwd_streams(
+            ptr(q), s, q.stride(0), n, kp, vp, rows, strides, ptr(out), out.stride(0),
+            ptr(plan.out_rows), heads, head_dim, ptr(plan.q_pairs), plan.n_pairs,
+            ptr(plan.kv_tiles), ptr(plan.tile_masks), 1, ptr(plan.order),
+            1.0 / math.sqrt(head_dim), None, None if part is None else ctypes.byref(part),
+            ptr(err), st))
     if SYNC_CHECKS if sync_checks is None else sync_checks:
         st = int(plan.status.item())
         if st & 1:

@@ -83,6 +83,7 @@ struct AttnArgs {
   int64_t part_stride;
   float* part_lse;
   int part_row0;
+  int64_t part_slot_rows;  // q_pairs[7] >> 8 = partial slot: rows of one slot
   int q2_row0;  // query rows from q2_row0 on are read from the second query map
   int n_pairs;
   int mask_stride;    // entries per partial-tile mask: 128 (per row) or 1 (per key only)
@@ -238,7 +239,8 @@ __device__ __forceinline__ void rescale_o(uint32_t o_col, float alpha) {
 
 __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_begin, int n_kv,
                                              uint32_t tbase, int warp, const Bars& B, int col,
-                                             int use, bool row_masks128, bool partial_rows) {
+                                             int use, bool row_masks128, int pflags) {
+  const bool partial_rows = (pflags & 1) != 0;
   const int h = (warp >> 2) - 1;  // 0 for warps 4-7, 1 for warps 8-11
   const int row = threadIdx.x - 128 * (h + 1);
   const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
@@ -251,7 +253,7 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
   __nv_bfloat16* orow;
   float* lse_out;
   if (partial_rows) {
-    dst_row = (int64_t)(q_start + row) - a.part_row0;
+    dst_row = (int64_t)(q_start + row) - a.part_row0 + (int64_t)(pflags >> 8) * a.part_slot_rows;
     orow = a.part_out + dst_row * a.part_stride + col;
     lse_out = a.part_lse;
   } else {
@@ -439,7 +441,7 @@ __global__ void __launch_bounds__(384, 1)
   const int col = head * kHD;
   if (warp >= 4) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-    softmax_role(a, pq, kv_begin, n_kv, tbase, warp, B, col, use, pk.z == 1, (pk.w & 1) != 0);
+    softmax_role(a, pq, kv_begin, n_kv, tbase, warp, B, col, use, pk.z == 1, pk.w);
   } else {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
     control_role<kMaps>(a, pq, kv_begin, n_kv, tbase, warp, lane, smem, qm, kv, B, col, use);
@@ -502,6 +504,7 @@ int attn_launch(const QMaps& qm, int q2_row0, const KVMaps<kMaps>& kv, void* out
   args.part_stride = part ? part->o_stride : 0;
   args.part_lse = part ? part->lse : nullptr;
   args.part_row0 = part ? (int)part->row0 : 0;
+  args.part_slot_rows = part ? part->slot_rows : 0;
   args.q2_row0 = q2_row0;
   args.n_pairs = n_pairs;
   args.mask_stride = mask_rows;

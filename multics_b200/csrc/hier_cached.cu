@@ -332,6 +332,196 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Packed hub plan
+// ---------------------------------------------------------------------------
+//
+// A local-hub segment has K_L query rows (16 at the released shape) and the
+// longest key list of the step (its members' whole cached history), and
+// the segments of one group at the n query frames see almost the same keys
+// (the same members and frames; only the window edge differs).  So the
+// attention plan packs them: pack g holds the rows of group g at every query
+// frame (n*K_L rows, frame-major), pack N the global-hub rows of every
+// frame; a pack's key list is the union of its frames' candidate runs and
+// its tiles carry per-row masks (row f*K_L + s sees the keys its frame's
+// segment attends to).  The packed rows are read through the attention
+// kernel's second query tensor and written back through its output row map.
+// The per-segment metadata (_build_metadata's contract) is unchanged.
+
+int pack_count(const CDims& d) {
+  if (d.no_local || d.n * d.KL > 128 || d.n * d.KG > 128) return 0;
+  return d.N + (d.KG > 0 ? 1 : 0);
+}
+
+// Pack j: its type (1 local, 2 global), group, rows per frame.
+__device__ __forceinline__ void pack_of(const CDims& d, int j, int* type, int* gi, int* rpf) {
+  *type = j < d.N ? 1 : 2;
+  *gi = j < d.N ? j : 0;
+  *rpf = j < d.N ? d.KL : d.KG;
+}
+
+// Union of the pack's frames' candidate runs into m (w, key, pool) with the
+// frames that select each candidate in fsel (bit qrel), then runs and boxes.
+__device__ void analyse_pack(const hier_cached_grouping& g, const CDims& d, int j,
+                             const SegSmem& m, int* fsel) {
+  if (threadIdx.x == 0) m.misc[3] = 0;
+  __syncthreads();
+  int type, gi, rpf;
+  pack_of(d, j, &type, &gi, &rpf);
+  int bad = 0;
+  for (int c = threadIdx.x; c < d.C; c += kThreads) {
+    int w = 0, fs = 0, key = 0, pool = 0;
+    for (int qrel = 0; qrel < d.n; ++qrel) {
+      const Seg sg = seg_of(d, type == 1 ? d.nA + qrel * d.N + gi : d.nA + d.nLs + qrel);
+      const int wc = candidate(g, d, sg, query_frame(g, d, qrel), c, &key, &pool, &bad);
+      if (wc > 0) {
+        w = wc;
+        fs |= 1 << qrel;
+      }
+    }
+    m.w[c] = w;
+    m.key[c] = key;
+    m.pool[c] = pool;
+    fsel[c] = fs;
+  }
+  if (bad) atomicOr(&m.misc[3], 1);
+  __syncthreads();
+  segplan::analyse_runs(m, d.C);
+}
+
+__global__ void __launch_bounds__(kThreads)
+    cached_pack_count_kernel(const hier_cached_grouping g, const CDims d, int32_t* n_boxes,
+                             int32_t* status) {
+  extern __shared__ int smem_i[];
+  const SegSmem m = segplan::seg_smem(smem_i, d.C);
+  analyse_pack(g, d, blockIdx.x, m, m.dw);
+  if (threadIdx.x == 0) {
+    n_boxes[blockIdx.x] = m.misc[2];
+    if (m.misc[3] && status) atomicOr(status, kStatusBadFrame);
+  }
+}
+
+struct PackOut {
+  const int32_t* n_boxes;  // per pack
+  int32_t tile_base;       // first kv_tiles row of the packs
+  int32_t tile_end;        // capacity end
+  int32_t mask_base;       // first 128-row mask (index in 128-entry units)
+  int32_t q2_row0;         // query row of the first packed row
+  int32_t pair_base;       // first q_pairs row of the packs
+  int32_t* q_pairs;
+  int32_t* kv_tiles;
+  uint32_t* tile_masks;
+  int32_t* status;
+};
+
+__global__ void __launch_bounds__(kThreads)
+    cached_pack_build_kernel(const hier_cached_grouping g, const CDims d, const PackOut o) {
+  extern __shared__ int smem_i[];
+  const SegSmem m = segplan::seg_smem(smem_i, d.C);
+  const int j = blockIdx.x;
+  int* fsel = m.dw;
+  int* sel_c = m.doff;  // selected candidates in key order
+  analyse_pack(g, d, j, m, fsel);
+  int type, gi, rpf;
+  pack_of(d, j, &type, &gi, &rpf);
+  // selected candidates in order (their key offsets m.off ascend)
+  {
+    int* wtmp = m.misc + 8;
+    int* carry = m.misc + 16;
+    int run = 0;
+    for (int base = 0; base < d.C; base += kThreads) {
+      const int c = base + threadIdx.x;
+      const int f = (c < d.C && m.w[c] > 0) ? 1 : 0;
+      const int incl = segplan::block_scan<false>(f, wtmp) + run;
+      if (f) sel_c[incl - 1] = c;
+      if (threadIdx.x == kThreads - 1) carry[0] = incl;
+      __syncthreads();
+      run = carry[0];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) m.misc[4] = run;
+    __syncthreads();
+  }
+  const int n_sel = m.misc[4], n_runs = m.misc[1], n_box = m.misc[2];
+  const int n_tiles = (n_box + 1) >> 1;
+  int tb = 0;  // tiles of the packs before j
+  for (int i = threadIdx.x; i < j; i += kThreads) tb += (o.n_boxes[i] + 1) >> 1;
+  tb = segplan::block_scan<false>(tb, m.misc + 8);
+  __shared__ int tb_s;
+  if (threadIdx.x == kThreads - 1) tb_s = tb;
+  __syncthreads();
+  const int tile0 = o.tile_base + tb_s;
+  if (tile0 + n_tiles > o.tile_end) {
+    if (threadIdx.x == 0 && o.status) atomicOr(o.status, kStatusTileOverflow);
+    return;
+  }
+  const int mask0 = o.mask_base + tb_s;  // this pack's first 128-row mask
+  const int rows = d.n * rpf;
+  // key rows of the boxes and the tile selectors
+  for (int b = threadIdx.x; b < 2 * n_tiles; b += kThreads) {
+    const int t = b >> 1, slot = b & 1;
+    const int bb = b < n_box ? b : b - 1;  // odd count: the last tile repeats its first box
+    const int r = segplan::run_of_box(m, n_runs, bb);
+    o.kv_tiles[(int64_t)(tile0 + t) * 4 + slot] = m.rk[r] + kBoxRows * (bb - m.rb[r]);
+    if (slot == 0) {
+      o.kv_tiles[(int64_t)(tile0 + t) * 4 + 2] = mask0 + t;
+      o.kv_tiles[(int64_t)(tile0 + t) * 4 + 3] = -2;
+    }
+  }
+  // per-row masks: one item per (tile, box, frame) computes the frame's two
+  // words and writes them to the frame's rows
+  uint4* masks = reinterpret_cast<uint4*>(o.tile_masks);
+  for (int it = threadIdx.x; it < n_tiles * 2 * d.n; it += kThreads) {
+    const int t = it / (2 * d.n), rem = it % (2 * d.n), slot = rem / d.n, f = rem % d.n;
+    const int b = 2 * t + slot;
+    uint32_t w0 = 0u, w1 = 0u;
+    if (b < n_box) {
+      const int r = segplan::run_of_box(m, n_runs, b);
+      const int kofs0 = m.rf[r] + kBoxRows * (b - m.rb[r]);
+      const int valid = min(kBoxRows, m.rf[r + 1] - kofs0);
+      int lo = 0, hi = n_sel - 1;  // last selected candidate starting at or before kofs0
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (m.off[sel_c[mid]] <= kofs0) lo = mid;
+        else hi = mid - 1;
+      }
+      for (int jj = lo; jj < n_sel; ++jj) {
+        const int c = sel_c[jj];
+        const int a0 = m.off[c];
+        if (a0 >= kofs0 + valid) break;
+        if (!((fsel[c] >> f) & 1)) continue;
+        const int s0 = max(a0, kofs0) - kofs0, s1 = min(a0 + m.w[c], kofs0 + valid) - kofs0;
+        for (int k = s0; k < s1; ++k) {
+          if (k < 32) w0 |= 1u << k;
+          else w1 |= 1u << (k - 32);
+        }
+      }
+    }
+    for (int rr = f * rpf; rr < (f + 1) * rpf; ++rr) {
+      uint32_t* dst = reinterpret_cast<uint32_t*>(masks + (int64_t)(mask0 + t) * 128 + rr);
+      dst[2 * slot] = w0;
+      dst[2 * slot + 1] = w1;
+    }
+  }
+  for (int it = threadIdx.x; it < n_tiles * (128 - rows); it += kThreads) {
+    const int t = it / (128 - rows), rr = rows + it % (128 - rows);
+    masks[(int64_t)(mask0 + t) * 128 + rr] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  if (threadIdx.x == 0) {
+    int row0 = 0;
+    for (int i = 0; i < j; ++i) row0 += d.n * (i < d.N ? d.KL : d.KG);
+    int32_t* q = o.q_pairs + (int64_t)(o.pair_base + j) * 8;
+    q[0] = o.q2_row0 + row0;
+    q[1] = rows;
+    q[2] = o.q2_row0 + row0;
+    q[3] = 0;
+    q[4] = tile0;
+    q[5] = tile0 + n_tiles;
+    q[6] = 1;  // 128-row masks
+    q[7] = 0;
+  }
+}
+
 int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
 int make_dims(const hier_cached_grouping* g, int32_t block_m, CDims* d) {
@@ -660,5 +850,89 @@ extern "C" int hier_varlen_plan_build(const int32_t* prog_qbase, const int32_t* 
   }
   varlen_finish_kernel<<<1, 1, 0, s>>>(minmax, scalars);
   HIER_CHECK_CUDA(cudaGetLastError(), "varlen_finish_kernel launch");
+  return HIER_OK;
+}
+
+extern "C" int hier_cached_pack_sizes(const hier_cached_grouping* g,
+                                      hier_cached_pack_sizes_t* out) {
+  clear_error();
+  CDims d;
+  int rc = make_dims(g, 1, &d);
+  if (rc) return rc;
+  if (!out) {
+    set_error(HIER_EVALUE, "pack sizes output is NULL");
+    return HIER_EVALUE;
+  }
+  out->n_packs = pack_count(d);
+  out->q2_rows = out->n_packs ? d.n * (d.N * d.KL + d.KG) : 0;
+  out->agent_pairs = d.nA * d.npA;
+  const int64_t boxes = (int64_t)d.cA * ceil_div(d.L, kBoxRows) +
+                        (int64_t)d.cL * (d.KL > 0 ? ceil_div(d.KL, kBoxRows) : 0) +
+                        (int64_t)d.cG * (d.KG > 0 ? ceil_div(d.KG, kBoxRows) : 0);
+  const int64_t cap = (int64_t)out->n_packs * ((boxes + 1) / 2);
+  if (cap > INT32_MAX / 512) {
+    set_error(HIER_EVALUE, "packed hub plan too large");
+    return HIER_EVALUE;
+  }
+  out->tile_capacity = (int32_t)cap;
+  return HIER_OK;
+}
+
+extern "C" int hier_cached_pack_count(const hier_cached_grouping* g, int32_t* n_boxes,
+                                      int32_t* status, void* stream) {
+  clear_error();
+  CDims d;
+  int rc = make_dims(g, 1, &d);
+  if (rc) return rc;
+  const int np = pack_count(d);
+  if (np == 0) return HIER_OK;
+  const size_t sm = seg_smem_bytes(d.C);
+  HIER_CHECK_CUDA(cudaFuncSetAttribute(cached_pack_count_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                  "cudaFuncSetAttribute(cached_pack_count_kernel)");
+  cached_pack_count_kernel<<<np, kThreads, sm, (cudaStream_t)stream>>>(*g, d, n_boxes, status);
+  HIER_CHECK_CUDA(cudaGetLastError(), "cached_pack_count_kernel launch");
+  return HIER_OK;
+}
+
+extern "C" int hier_cached_pack_build(const hier_cached_grouping* g, const int32_t* n_boxes,
+                                      int32_t tile_base, int32_t tile_end, int32_t mask_base,
+                                      int32_t q2_row0, int32_t* q_pairs, int32_t* kv_tiles,
+                                      uint32_t* tile_masks, int32_t* order, int32_t* status,
+                                      void* stream) {
+  clear_error();
+  CDims d;
+  int rc = make_dims(g, 1, &d);
+  if (rc) return rc;
+  const int np = pack_count(d);
+  if (np == 0) return HIER_OK;
+  if (!n_boxes || !q_pairs || !kv_tiles || !tile_masks || tile_base < 0 || tile_end < tile_base ||
+      mask_base < 0 || q2_row0 < 0) {
+    set_error(HIER_EVALUE, "hier_cached_pack_build: invalid outputs or offsets");
+    return HIER_EVALUE;
+  }
+  PackOut o;
+  o.n_boxes = n_boxes;
+  o.tile_base = tile_base;
+  o.tile_end = tile_end;
+  o.mask_base = mask_base;
+  o.q2_row0 = q2_row0;
+  o.pair_base = d.nA * d.npA;
+  o.q_pairs = q_pairs;
+  o.kv_tiles = kv_tiles;
+  o.tile_masks = tile_masks;
+  o.status = status;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t sm = seg_smem_bytes(d.C);
+  HIER_CHECK_CUDA(cudaFuncSetAttribute(cached_pack_build_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm),
+                  "cudaFuncSetAttribute(cached_pack_build_kernel)");
+  cached_pack_build_kernel<<<np, kThreads, sm, s>>>(*g, d, o);
+  HIER_CHECK_CUDA(cudaGetLastError(), "cached_pack_build_kernel launch");
+  const int total = o.pair_base + np;
+  if (order) {
+    order_by_work_kernel<8><<<(total + 127) / 128, 128, 0, s>>>(q_pairs, total, order);
+    HIER_CHECK_CUDA(cudaGetLastError(), "order_by_work_kernel launch");
+  }
   return HIER_OK;
 }

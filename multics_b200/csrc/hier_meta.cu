@@ -706,6 +706,51 @@ extern "C" int hier_dense_block_plan_build(const uint8_t* mask, int64_t S, int64
 }
 
 // ---------------------------------------------------------------------------
+// Split-KV form of a query-pair plan
+// ---------------------------------------------------------------------------
+//
+// Pair p becomes `chunks` pairs over consecutive parts of its key-tile list,
+// flagged as partial rows in slot c (q_pairs[7] = 1 | c << 8): a plan whose
+// pairs are few and long (one cached step: 21 pairs x heads, about 2.4
+// waves of CTAs on 148 SMs) runs as shorter CTAs that balance across the
+// SMs, and the slots are merged by log-sum-exp afterwards
+// (hier_lse_gather_merge).
+
+namespace hier {
+
+__global__ void split_kv_kernel(const int4* in, int np, int chunks, int4* out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < np * chunks;
+       i += gridDim.x * blockDim.x) {
+    const int p = i / chunks, c = i % chunks;
+    const int4 q = in[2 * p], k = in[2 * p + 1];
+    const int len = k.y - k.x;
+    const int b = k.x + (int)((int64_t)len * c / chunks);
+    const int e = k.x + (int)((int64_t)len * (c + 1) / chunks);
+    out[2 * i] = q;
+    out[2 * i + 1] = make_int4(b, e, k.z, 1 | (c << 8));
+  }
+}
+
+}  // namespace hier
+
+extern "C" int hier_plan_split_kv(const int32_t* q_pairs, int32_t n_pairs, int32_t chunks,
+                                  int32_t* out_pairs, int32_t* order, void* stream) {
+  clear_error();
+  if (n_pairs < 0 || chunks < 1 || chunks > 255 || (int64_t)n_pairs * chunks > INT32_MAX / 8) {
+    set_error(HIER_EVALUE, "hier_plan_split_kv: %d pairs x %d chunks", n_pairs, chunks);
+    return HIER_EVALUE;
+  }
+  if (n_pairs == 0) return HIER_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int n = n_pairs * chunks;
+  split_kv_kernel<<<grid_for(n, 128), 128, 0, s>>>((const int4*)q_pairs, n_pairs, chunks,
+                                                    (int4*)out_pairs);
+  if (order) order_by_work_kernel<8><<<grid_for(n, 128), 128, 0, s>>>(out_pairs, n, order);
+  HIER_CHECK_CUDA(cudaGetLastError(), "split_kv_kernel launch");
+  return HIER_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Plan of a batched attention under one mask shared by every batch entry
 // ---------------------------------------------------------------------------
 //

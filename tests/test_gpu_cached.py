@@ -147,8 +147,18 @@ def _check(out, ref, segs):
             assert not o[q0:q0 + ql].any()
 
 
+@pytest.fixture(params=["packed", "per-segment"])
+def pack_mode(request, monkeypatch):
+    """Run a cached test with the hub rows packed per group (the default) and
+    with one query pair per hub segment."""
+    from multics_b200 import cached as C
+
+    monkeypatch.setenv(C.CACHED_PACK_ENV, "1" if request.param == "packed" else "0")
+    return request.param
+
+
 @pytest.mark.parametrize("name", [n for n in case_names("seg") if n.endswith("/tile")])
-def test_cached_attention_matches_oracle(name):
+def test_cached_attention_matches_oracle(name, pack_mode):
     from multics_b200 import cached as C
 
     meta, _ = seg_case(name)
@@ -171,7 +181,7 @@ def _released_meta(KL=16, inactive_q=False):
 
 
 @pytest.mark.parametrize("variant", ["released", "inactive_hub", "token_activity", "pool_views"])
-def test_cached_attention_released_shape(variant):
+def test_cached_attention_released_shape(variant, pack_mode):
     """P=4, L=220 (11x20 patches), 24 retained frames, window 21, n=3."""
     from multics_b200 import cached as C
 
@@ -184,7 +194,7 @@ def test_cached_attention_released_shape(variant):
     _check(out, ref, segs)
 
 
-def test_cached_attention_membership_released_shape():
+def test_cached_attention_membership_released_shape(pack_mode):
     from multics_b200 import cached as C
 
     T = 24
@@ -222,3 +232,40 @@ def test_cached_membership_frame_out_of_range_raises():
     kw = _plugin_inputs(meta, 1, seed=5, dev="cuda")
     with pytest.raises(IndexError):
         C.hierarchical_cached_attention(sync_checks=True, **kw)
+
+
+def test_packed_plan_structure():
+    """Released shape: 12 player pairs + one pack per group (48 rows) + the
+    global pack (18 rows), 128-row masks, rows read from the second query
+    block and mapped back to the hub rows."""
+    from multics_b200 import cached as C
+
+    meta = _released_meta()
+    kw = _plugin_inputs(meta, 2, seed=3, dev="cuda")
+    agent = [f.reshape(-1) for f in kw["agent_frames"]]
+    local = [f.reshape(-1) for f in kw["local_frames"]]
+    g = C._Grouping(P=4, N=2, L=220, KL=16, KG=6, n_frames=3, n_block=3, local_attn=21,
+                    direct=True, no_local=False, agent_frames=agent, local_frames=local,
+                    local_active=[t.view(torch.uint8) for t in kw["local_active_tokens"]],
+                    global_frames=kw["global_frames"].reshape(-1), labels=kw["labels"],
+                    q_active=kw["active"].view(torch.uint8), membership=None, global_only=None)
+    plan = C.build_cached_plan(g, torch.device("cuda"), pack=True)
+    flat = C.build_cached_plan(g, torch.device("cuda"), pack=False)
+    qp = plan.q_pairs[:plan.n_pairs].cpu().numpy()
+    assert plan.n_pairs == 15 and flat.n_pairs == 21
+    S = 4 * 3 * 220 + 3 * (2 * 16 + 6)
+    assert [tuple(r[:4]) for r in qp[12:]] == [(S, 48, S, 0), (S + 48, 48, S + 48, 0),
+                                               (S + 96, 18, S + 96, 0)]
+    assert (qp[12:, 6] == 1).all()
+    rows = plan.out_rows.cpu().numpy()
+    assert (rows[:S] == np.arange(S)).all()
+    aq = 4 * 3 * 220
+    assert rows[S:S + 3].tolist() == [aq, aq + 1, aq + 2]            # group 0, frame 0
+    assert rows[S + 16] == aq + 2 * 16                               # group 0, frame 1
+    assert rows[S + 48] == aq + 16                                   # group 1, frame 0
+    assert rows[S + 96] == aq + 3 * 2 * 16                           # global, frame 0
+    # a pack of one group has about the tiles of one of its segments
+    fq = flat.q_pairs.cpu().numpy()
+    seg_tiles = fq[12:18, 5] - fq[12:18, 4]
+    pack_tiles = qp[12:14, 5] - qp[12:14, 4]
+    assert pack_tiles.max() <= seg_tiles.max() + 2
