@@ -443,7 +443,9 @@ int hier_cached_count(const hier_cached_grouping* g, int32_t* kv_count, int32_t*
  *       kv_width = ceil64(max kv_count), as _build_metadata);
  *   q_pairs [n_pairs][8], kv_tiles [tile_capacity][4], tile_masks
  *       [tile_capacity][4] (mask_rows = 1), order [n_pairs]: the attention
- *       plan for hier_attn_fwd_streams, needs n_boxes from hier_cached_count.
+ *       plan for hier_attn_fwd_streams; with n_boxes from hier_cached_count
+ *       the segments' tiles are packed, with n_boxes NULL each segment gets
+ *       tile_capacity / n_seg tiles (no count launch needed).
  * status bit 1 is set if the plan exceeds tile_capacity.  No host sync. */
 int hier_cached_build(const hier_cached_grouping* g, int32_t block_m, const int32_t* n_boxes,
                       int32_t* prog_qbase, int32_t* prog_nq, int32_t* prog_seg,
@@ -476,7 +478,8 @@ int hier_cached_pack_sizes(const hier_cached_grouping* g, hier_cached_pack_sizes
 int hier_cached_pack_count(const hier_cached_grouping* g, int32_t* n_boxes, int32_t* status,
                            void* stream);
 
-/* After hier_cached_build: the packs' pairs at q_pairs rows [agent_pairs,
+/* After hier_cached_build (n_boxes from hier_cached_pack_count, or NULL:
+ * each pack gets (tile_end - tile_base) / n_packs tiles): the packs' pairs at q_pairs rows [agent_pairs,
  * agent_pairs + n_packs) (replacing the hub segments' pairs, so the plan
  * has agent_pairs + n_packs pairs), their tiles at kv_tiles rows
  * [tile_base, tile_end), their 128-row masks from index mask_base of

@@ -400,7 +400,6 @@ def build_cached_plan(g: _Grouping, device, pack=None) -> CachedPlan:
     if pack is None:
         pack = os.environ.get(CACHED_PACK_ENV, "1") != "0"
     pack = bool(pack) and ps.n_packs > 0
-    n_boxes = torch.empty(sz.n_seg, dtype=torch.int32, device=device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
     q_pairs = torch.empty((max(sz.n_pairs, 1), 8), dtype=torch.int32, device=device)
     cap = max(sz.tile_capacity, 1)
@@ -410,16 +409,14 @@ def build_cached_plan(g: _Grouping, device, pack=None) -> CachedPlan:
     kv_tiles = torch.empty((n_tiles, 4), dtype=torch.int32, device=device)
     tile_masks = torch.empty((n_masks, 4), dtype=torch.int32, device=device)
     order = torch.empty(max(sz.n_pairs, 1), dtype=torch.int32, device=device)
-    check(lib.hier_cached_count(g.ref(), None, ptr(n_boxes), ptr(status), s))
-    check(lib.hier_cached_build(g.ref(), 1, ptr(n_boxes), None, None, None, None, 0, ptr(q_pairs),
+    # no count launch: each segment's tiles sit at a fixed stride of the capacity
+    check(lib.hier_cached_build(g.ref(), 1, None, None, None, None, None, 0, ptr(q_pairs),
                                 ptr(kv_tiles), ptr(tile_masks), cap,
                                 None if pack else ptr(order), ptr(status), s))
     if not pack:
         return CachedPlan(q_pairs, kv_tiles, tile_masks, order, sz.n_pairs, sz.n_streams,
                           status, g)
-    nb_p = torch.empty(ps.n_packs, dtype=torch.int32, device=device)
-    check(lib.hier_cached_pack_count(g.ref(), ptr(nb_p), ptr(status), s))
-    check(lib.hier_cached_pack_build(g.ref(), ptr(nb_p), cap, n_tiles, mask_base, int(sz.q_rows),
+    check(lib.hier_cached_pack_build(g.ref(), None, cap, n_tiles, mask_base, int(sz.q_rows),
                                      ptr(q_pairs), ptr(kv_tiles), ptr(tile_masks), ptr(order),
                                      ptr(status), s))
     q2_src, out_rows = _pack_rows(g, int(sz.q_rows), device)

@@ -317,7 +317,10 @@ __global__ void __launch_bounds__(kThreads)
     for (int i = total + threadIdx.x; i < o.kv_width; i += kThreads) row[i] = 0;
   }
   if (!o.q_pairs) return;
-  const int tile_base = segplan::tile_base_of(o.n_boxes, s, m.misc + 8);
+  // tiles at the exclusive scan of the counted boxes, or at a fixed stride
+  // per segment (the capacity bound of one segment) without a count
+  const int tile_base = o.n_boxes ? segplan::tile_base_of(o.n_boxes, s, m.misc + 8)
+                                  : s * (o.tile_capacity / d.n_seg);
   const int n_tiles = (n_box + 1) >> 1;
   if (tile_base + n_tiles > o.tile_capacity) {
     if (threadIdx.x == 0 && o.status) atomicOr(o.status, kStatusTileOverflow);
@@ -348,7 +351,7 @@ __global__ void __launch_bounds__(kThreads)
 // kernel's second query tensor and written back through its output row map.
 // The per-segment metadata (_build_metadata's contract) is unchanged.
 
-int pack_count(const CDims& d) {
+__host__ __device__ inline int pack_count(const CDims& d) {
   if (d.no_local || d.n * d.KL > 128 || d.n * d.KG > 128) return 0;
   return d.N + (d.KG > 0 ? 1 : 0);
 }
@@ -444,11 +447,13 @@ __global__ void __launch_bounds__(kThreads)
   }
   const int n_sel = m.misc[4], n_runs = m.misc[1], n_box = m.misc[2];
   const int n_tiles = (n_box + 1) >> 1;
-  int tb = 0;  // tiles of the packs before j
-  for (int i = threadIdx.x; i < j; i += kThreads) tb += (o.n_boxes[i] + 1) >> 1;
+  int tb = 0;  // tiles of the packs before j (a fixed stride without counts)
+  if (o.n_boxes)
+    for (int i = threadIdx.x; i < j; i += kThreads) tb += (o.n_boxes[i] + 1) >> 1;
   tb = segplan::block_scan<false>(tb, m.misc + 8);
   __shared__ int tb_s;
-  if (threadIdx.x == kThreads - 1) tb_s = tb;
+  if (threadIdx.x == kThreads - 1)
+    tb_s = o.n_boxes ? tb : j * ((o.tile_end - o.tile_base) / pack_count(d));
   __syncthreads();
   const int tile0 = o.tile_base + tb_s;
   if (tile0 + n_tiles > o.tile_end) {
@@ -778,8 +783,8 @@ extern "C" int hier_cached_build(const hier_cached_grouping* g, int32_t block_m,
     set_error(HIER_EVALUE, "program outputs must be given together");
     return HIER_EVALUE;
   }
-  if (q_pairs && (!kv_tiles || !tile_masks || !n_boxes)) {
-    set_error(HIER_EVALUE, "attention plan outputs need kv_tiles, tile_masks and n_boxes");
+  if (q_pairs && (!kv_tiles || !tile_masks)) {
+    set_error(HIER_EVALUE, "attention plan outputs need kv_tiles and tile_masks");
     return HIER_EVALUE;
   }
   if (kv_index && kv_width <= 0) {
@@ -906,7 +911,7 @@ extern "C" int hier_cached_pack_build(const hier_cached_grouping* g, const int32
   if (rc) return rc;
   const int np = pack_count(d);
   if (np == 0) return HIER_OK;
-  if (!n_boxes || !q_pairs || !kv_tiles || !tile_masks || tile_base < 0 || tile_end < tile_base ||
+  if (!q_pairs || !kv_tiles || !tile_masks || tile_base < 0 || tile_end < tile_base ||
       mask_base < 0 || q2_row0 < 0) {
     set_error(HIER_EVALUE, "hier_cached_pack_build: invalid outputs or offsets");
     return HIER_EVALUE;
