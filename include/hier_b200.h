@@ -630,7 +630,14 @@ typedef struct hier_shard_desc {
    * in place.  Paging needs a single shard holding every player. */
   const int32_t* page_table;
   int32_t n_pages;
-  int32_t reserved_paged;
+  /* With hub_keys set: the hub-key pairs this rank computes (one group's
+   * T*K_L local-hub rows or the T*K_G global-hub rows per 256-row strip, in
+   * the order local group 0 .. N-1, then global): [hub_key_first,
+   * hub_key_first + hub_key_count), or all of them for hub_key_count = 0.
+   * Spread over the ranks, each hub-token partial row is computed on one
+   * rank; hier_lse_gather_merge_peers reads it there (local_owner). */
+  int32_t hub_key_first;
+  int32_t hub_key_count;
 } hier_shard_desc;
 
 typedef struct hier_shard_sizes_t {
@@ -679,8 +686,9 @@ int hier_lse_gather_merge(const void* o, int64_t o_stride, const float* lse, int
  * rank that computed them: o_bases / lse_bases are device arrays of n_ranks
  * pointers (this rank's own buffers and the other ranks' buffers mapped into
  * this GPU's address space, e.g. symmetric memory); partial row pr < local_rows
- * is read from rank self, a higher row from rank (pr - local_rows) / slot_rows,
- * at the same row of that rank's buffer.  The caller orders the reads after
+ * is read from rank local_owner[pr] (rank self when local_owner is NULL), a
+ * higher row from rank (pr - local_rows) / slot_rows, at the same row of that
+ * rank's buffer.  The caller orders the reads after
  * every rank's writes (a collective on the stream after the attention).
  * (Having the attention kernels write each partial row into every rank's
  * buffer instead was measured slower at 8 GPUs: the NVLink stores slow the
@@ -690,7 +698,7 @@ int hier_lse_gather_merge_peers(const void* const* o_bases, const float* const* 
                                 int64_t slot_rows, int64_t o_stride, int32_t H, int32_t D,
                                 const int32_t* off, const int32_t* rows, int64_t n_targets,
                                 void* out, int64_t out_stride, const int32_t* out_rows,
-                                void* stream);
+                                const int32_t* local_owner, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Self-test of the tensor-core operand encodings (no reference counterpart):

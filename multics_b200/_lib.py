@@ -102,7 +102,8 @@ class HierShardDesc(ctypes.Structure):
         ("labels", c_void_p), ("active", c_void_p), ("remote_key", c_void_p),
         ("local_player", c_int32 * SHARD_MAX_LOCAL), ("strip_begin", c_int32 * SHARD_MAX_LOCAL),
         ("strip_end", c_int32 * SHARD_MAX_LOCAL), ("hub_partials", c_int32 * SHARD_MAX_LOCAL),
-        ("page_table", c_void_p), ("n_pages", c_int32), ("reserved_paged", c_int32),
+        ("page_table", c_void_p), ("n_pages", c_int32), ("hub_key_first", c_int32),
+        ("hub_key_count", c_int32),
     ]
 
 
@@ -194,7 +195,7 @@ _SIGS = {
                                       c_int64, _P, _P]),
     "hier_lse_gather_merge_peers": (c_int, [_P, _P, c_int32, c_int32, c_int64, c_int64, c_int64,
                                             c_int32, c_int32, _P, _P, c_int64, _P, c_int64, _P,
-                                            _P]),
+                                            _P, _P]),
     "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "hier_selftest_wait_timeout": (c_int, [c_int64, _P, _P, _P]),
 }

@@ -659,6 +659,7 @@ struct PartialSrc {
   const float* lse;
   const __nv_bfloat16* const* o_bases;  // per rank (kPeers)
   const float* const* lse_bases;
+  const int32_t* local_owner;  // rank of each partial row below local_rows (NULL: self)
   int self;
   int64_t local_rows, slot_rows;
 };
@@ -671,7 +672,8 @@ __device__ __forceinline__ void partial_at(const PartialSrc& p, int64_t pr,
     *lse = p.lse;
     return;
   }
-  const int owner = pr < p.local_rows ? p.self : (int)((pr - p.local_rows) / p.slot_rows);
+  const int owner = pr < p.local_rows ? (p.local_owner ? p.local_owner[pr] : p.self)
+                                      : (int)((pr - p.local_rows) / p.slot_rows);
   *o = p.o_bases[owner];
   *lse = p.lse_bases[owner];
 }
@@ -758,7 +760,8 @@ extern "C" int hier_lse_gather_merge_peers(const void* const* o_bases, const flo
                                            int64_t slot_rows, int64_t o_stride, int32_t H,
                                            int32_t D, const int32_t* off, const int32_t* rows,
                                            int64_t n_targets, void* out, int64_t out_stride,
-                                           const int32_t* out_rows, void* stream) {
+                                           const int32_t* out_rows, const int32_t* local_owner,
+                                           void* stream) {
   clear_error();
   int rc = merge_check(n_targets, H, D, o_stride);
   if (!rc) rc = merge_check(n_targets, H, D, out_stride);
@@ -773,6 +776,7 @@ extern "C" int hier_lse_gather_merge_peers(const void* const* o_bases, const flo
   src.o_bases = reinterpret_cast<const __nv_bfloat16* const*>(o_bases);
   src.lse_bases = lse_bases;
   src.self = self;
+  src.local_owner = local_owner;
   src.local_rows = local_rows;
   src.slot_rows = slot_rows;
   lse_gather_kernel<true><<<merge_grid(n_targets * H * (D / 8)), 256, 0, (cudaStream_t)stream>>>(

@@ -89,7 +89,8 @@ struct SDims {
   int nps;             // 256-row strips of one player's rows
   int nph;             // hub-partial strips per hub-partial player
   int npl, npg;        // hub-key pairs per group, global hub-key pairs (hub_keys rank)
-  int n_hh;            // hub-key pairs
+  int n_hh;            // hub-key pairs of this shard
+  int hh0;             // its first hub-key pair (in the order of all hub-key pairs)
   int n_pairs;         // all pairs: player strips, hub-partial strips, hub-key pairs
   int nf_mate;         // mate frames enumerated per player strip
   int c_player, c_hub; // candidates per player strip / hub-key pair
@@ -147,7 +148,7 @@ __device__ Pair pair_of(const SDims& d, int i) {
     rows = d.T * d.KL;
     r.unit = d.KL;
     r.q0 = d.own_rows + d.hub_rows + d.hp_row0 + k * rows + r.j0;
-  } else if ((i -= n_hp) < d.N * d.npl) {
+  } else if ((i = i - n_hp + d.hh0) < d.N * d.npl) {
     const int h = i;
     r.kind = kPairLocal;
     r.id = h / d.npl;
@@ -697,7 +698,13 @@ int make_sdims(const hier_shard_desc* g, SDims* d) {
   d->nph = d->KL > 0 ? cdiv((int64_t)d->T * d->KL, kStripRows) : 0;
   d->npl = d->KL > 0 ? cdiv((int64_t)d->T * d->KL, kStripRows) : 0;
   d->npg = d->KG > 0 ? cdiv((int64_t)d->T * d->KG, kStripRows) : 0;
-  d->n_hh = d->hub_keys ? d->N * d->npl + d->npg : 0;
+  {
+    const int all = d->N * d->npl + d->npg;
+    const int first = g->hub_key_count > 0 ? std::min(std::max(g->hub_key_first, 0), all) : 0;
+    const int cnt = g->hub_key_count > 0 ? std::min(g->hub_key_count, all - first) : all;
+    d->hh0 = d->hub_keys ? first : 0;
+    d->n_hh = d->hub_keys ? cnt : 0;
+  }
   d->n_pairs = d->n_strips + d->n_hp_players * d->nph + d->n_hh;
   if ((int64_t)own_rows + hub_rows + d->hp_row0 + (int64_t)d->n_hp_players * d->T * d->KL >
       INT_MAX / 2) {

@@ -220,6 +220,28 @@ class ShardTopology:
         g = self.labels[t_i, p_i]
         return ((g * T + t_i) * KL + s_i).reshape(-1).astype(np.int64)
 
+    def hub_key_split(self):
+        """This rank's share of the hub-key pairs (one group's ``T*K_L``
+        local-hub rows or the ``T*K_G`` global rows per 256-row strip, local
+        groups first) as ``(first, count)``, and the rank that computes the
+        hub-token partial of every hub row (group-major order), ``int32
+        [hub_rows]``."""
+        T, N, KL, KG, W = self.T, self.N, self.KL, self.KG, self.world
+        npl = -(-T * KL // 256) if KL > 0 else 0
+        npg = -(-T * KG // 256) if KG > 0 else 0
+        n = N * npl + npg
+        bounds = [r * n // W for r in range(W + 1)]
+        rank_of = np.zeros(max(n, 1), np.int32)
+        for r in range(W):
+            rank_of[bounds[r]:bounds[r + 1]] = r
+        h = np.arange(self.hub_rows)
+        loc = T * N * KL
+        pair = np.where(h < loc, (h // max(T * KL, 1)) * npl + (h % max(T * KL, 1)) // 256,
+                        N * npl + (h - loc) // 256)
+        owner = rank_of[np.minimum(pair, max(n, 1) - 1)].astype(np.int32)
+        first = bounds[self.rank]
+        return first, bounds[self.rank + 1] - first, owner
+
     @property
     def hub_partial_slot(self) -> int:
         """Rows of one rank's player-partial block in the shared partial-row
@@ -291,10 +313,16 @@ class ShardedHierAttention:
     ``"peer"`` keeps every rank's K/V in symmetric memory and the attention
     kernel reads the other ranks' rows in place over NVLink (plain TMA loads
     of peer memory, no copy).  In peer mode K and V must be written into
-    :meth:`k_buffer` / :meth:`v_buffer` (other tensors are copied there)."""
+    :meth:`k_buffer` / :meth:`v_buffer` (other tensors are copied there).
+
+    ``spread_hub_keys`` (default: with the peer transport) gives each rank a
+    share of the hub-token partial pairs instead of all of them; the peer
+    merge then reads each hub row's hub-token partial from the rank that
+    computed it (:attr:`hub_key_owner`)."""
 
     def __init__(self, topo: ShardTopology, num_heads: int, device, group=None,
-                 transport: str = "exchange", active=None, page_table=None):
+                 transport: str = "exchange", active=None, page_table=None,
+                 spread_hub_keys=None):
         if transport not in ("exchange", "peer"):
             raise ValueError(f"unknown transport {transport!r}")
         self.topo = topo
@@ -322,9 +350,18 @@ class ShardedHierAttention:
         d = HierShardDesc()
         d.P, d.N, d.L, d.KL, d.KG, d.T = t.P, t.N, t.L, t.KL, t.KG, t.T
         d.n_block, d.local_attn, d.direct = t.n_block, t.local_attn, int(t.direct)
-        # every rank computes the hub-token partials (a few key tiles per hub
-        # row), so only the per-player hub partials cross GPUs
+        # hub-token partials: with the peer transport the hub-key pairs are
+        # spread over the ranks and the merge reads each partial from its
+        # rank (hub_key_owner); otherwise every rank computes all of them, so
+        # that only the per-player hub partials cross GPUs
         d.n_local, d.hub_keys = t.n_local, 1
+        self.hub_key_owner = None
+        spread = (self.transport == "peer") if spread_hub_keys is None else bool(spread_hub_keys)
+        if spread and t.world > 1:
+            first, count, owner = t.hub_key_split()
+            d.hub_keys = int(count > 0)
+            d.hub_key_first, d.hub_key_count = first, count
+            self.hub_key_owner = torch.from_numpy(owner).to(dev)
         d.hub_partial_row0 = t.rank * t.hub_partial_slot
         for i, p in enumerate(t.local_players):
             b, e = next(((b_, e_) for p_, b_, e_ in t.segments[t.rank] if p_ == p), (0, 0))
@@ -545,6 +582,8 @@ class ShardedHierAttention:
         t = self.topo
         if t.hub_rows == 0:
             return out_hub
+        if self.hub_key_owner is not None and self.transport != "peer":
+            raise RuntimeError("hub-token partials spread over the ranks need the peer merge")
         if t.world > 1 and self.transport == "peer":
             import torch.distributed as dist
 
@@ -553,7 +592,8 @@ class ShardedHierAttention:
                 ptr(self._part_o_bases), ptr(self._part_lse_bases), t.world, t.rank, t.hub_rows,
                 max(t.hub_partial_slot, 1), self.part_o.stride(0), self.H, self.D,
                 ptr(self.csr_off), ptr(self.csr_rows), t.hub_rows, ptr(out_hub),
-                out_hub.stride(0), ptr(out_rows), stream_ptr(self.device)))
+                out_hub.stride(0), ptr(out_rows), ptr(self.hub_key_owner),
+                stream_ptr(self.device)))
             return out_hub
         self.gather_partials()
         return self.merge_partials(out_hub, out_rows)

@@ -30,10 +30,17 @@ def _case(P, T, L, N, KL, KG, labels, H, seed, n_block=1, win=-1):
     return q, k, v, ref
 
 
-def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v, n_block=1, win=-1):
+def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v, n_block=1, win=-1,
+                 spread=False):
     """Every rank's plan and attention launch in one process; the ranks'
     player-partial slots are copied together as the all-gather would, then
-    merged."""
+    merged.  With ``spread`` the ranks share the hub-token partial pairs and
+    the merge reads every partial from its rank's buffer, as the peer
+    transport's merge does (all buffers are on this GPU)."""
+    import ctypes
+
+    from multics_b200 import _lib
+    from multics_b200._lib import check, ptr, stream_ptr
     from multics_b200.sharded import ShardedHierAttention, ShardTopology
 
     S = q.shape[0]
@@ -43,7 +50,7 @@ def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v, n_block=1, win=-
     for rank in range(world):
         t = ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=n_block, local_attn=win,
                           direct=True, labels=labels, world=world, rank=rank)
-        sh = ShardedHierAttention(t, H, "cuda")
+        sh = ShardedHierAttention(t, H, "cuda", spread_hub_keys=spread)
         loc = torch.from_numpy(t.local_rows()).cuda()
         ql, kl, vl = qc[loc].contiguous(), kc[loc].contiguous(), vc[loc].contiguous()
         sh.fill_remote_from(kc, vc)
@@ -53,9 +60,21 @@ def _run_sharded(P, T, L, N, KL, KG, labels, H, world, q, k, v, n_block=1, win=-
         mine = torch.from_numpy(t.computed_rows()).cuda()
         out[loc[mine]] = o[mine].float()
         shards.append(sh)
-    # the all-gather: every rank's player-partial slot into rank 0's buffer
     s0 = shards[0]
     h0, slot = s0.topo.hub_rows, s0.topo.hub_partial_slot
+    if spread and world > 1:
+        dev = torch.device("cuda")
+        ob = torch.tensor([sh.part_o.data_ptr() for sh in shards], dtype=torch.int64, device=dev)
+        lb = torch.tensor([sh.part_lse.data_ptr() for sh in shards], dtype=torch.int64,
+                          device=dev)
+        merged = torch.empty((h0, H * 128), dtype=torch.bfloat16, device=dev)
+        check(_lib.lib().hier_lse_gather_merge_peers(
+            ptr(ob), ptr(lb), world, 0, h0, max(slot, 1), s0.part_o.stride(0), H, 128,
+            ptr(s0.csr_off), ptr(s0.csr_rows), h0, ptr(merged), merged.stride(0), None,
+            ptr(s0.hub_key_owner), stream_ptr(dev)))
+        out[torch.from_numpy(s0.topo.hub_rows_order()).cuda()] = merged.float()
+        return out.cpu().numpy()
+    # the all-gather: every rank's player-partial slot into rank 0's buffer
     for r, sh in enumerate(shards[1:], start=1):
         rows = slice(h0 + r * slot, h0 + (r + 1) * slot)
         s0.part_o[rows] = sh.part_o[rows]
@@ -123,3 +142,20 @@ def test_sharded_strip_split_dynamic_groups_match_oracle(world):
     lab = _regrouped_labels(P, T, 3, seed=9)
     q, k, v, ref = _case(P, T, L, N, KL, KG, lab, H, seed=9)
     _check(_run_sharded(P, T, L, N, KL, KG, lab, H, world, q, k, v), ref)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_spread_hub_keys_match_oracle(world):
+    """The hub-token partial pairs shared out among the ranks (the peer
+    transport's default) and each hub row merged from the partials on their
+    ranks: dynamic groups, and enough hub frames for several hub-key pairs per
+    group."""
+    P, T, L, N, KL, KG, H = 8, 6, 40, 4, 4, 3, 2
+    lab = _regrouped_labels(P, T, 3, seed=3)
+    q, k, v, ref = _case(P, T, L, N, KL, KG, lab, H, seed=1)
+    _check(_run_sharded(P, T, L, N, KL, KG, lab, H, world, q, k, v, spread=True), ref)
+    P, T, L, N, KL, KG = 4, 20, 24, 2, 16, 6
+    lab = _regrouped_labels(P, T, 4, seed=6)
+    q, k, v, ref = _case(P, T, L, N, KL, KG, lab, H, seed=6, n_block=2, win=5)
+    _check(_run_sharded(P, T, L, N, KL, KG, lab, H, min(world, 4), q, k, v, n_block=2, win=5,
+                        spread=True), ref)

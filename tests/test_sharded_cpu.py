@@ -242,3 +242,33 @@ def test_random_strip_splits_cover_needs_and_partials(seed):
             rk, i = divmod(int(x) - tops[0].hub_rows, slot)
             players.append(tops[rk].hp_players[rk][i // (T * KL)])
         assert sorted(players) == [p for p in range(P) if lab[f, p] == g]
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_hub_key_split_partitions_the_pairs(world):
+    """The ranks' hub-key pair ranges partition every pair once, and the
+    owner of each hub row is the rank whose range holds its pair."""
+    from multics_b200.sharded import ShardTopology
+
+    P, T, L, N, KL, KG = 8, 20, 40, 4, 16, 6
+    lab = _regrouped_labels(P, T, 3, seed=2)
+    tops = [ShardTopology(P=P, T=T, L=L, N=N, KL=KL, KG=KG, n_block=1, local_attn=-1,
+                          direct=True, labels=lab, world=world, rank=r) for r in range(world)]
+    splits = [t.hub_key_split() for t in tops]
+    npl, npg = -(-T * KL // 256), -(-T * KG // 256)
+    covered = []
+    for first, count, _ in splits:
+        covered += list(range(first, first + count))
+    assert covered == list(range(N * npl + npg))
+    owner = splits[0][2]
+    assert all(np.array_equal(owner, s[2]) for s in splits)
+    h = np.arange(tops[0].hub_rows)
+    for r, (first, count, _) in enumerate(splits):
+        for pair in range(first, first + count):
+            if pair < N * npl:
+                g, j = divmod(pair, npl)
+                rows = h[g * T * KL + 256 * j: min(g * T * KL + 256 * (j + 1), (g + 1) * T * KL)]
+            else:
+                j = pair - N * npl
+                rows = T * N * KL + np.arange(256 * j, min(256 * (j + 1), T * KG))
+            assert (owner[rows] == r).all()
