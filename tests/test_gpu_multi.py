@@ -1,4 +1,5 @@
-"""Player-sharded layer over NCCL: one process per GPU (2 GPUs), group-mate
+"""Player-sharded layer over NCCL: one process per GPU (every GPU of the
+box, 2 to 8), group-mate
 frames by all_to_all or read in place from the peer's memory, hub rows merged
 by log-sum-exp over the ranks' partial rows (all-gathered, or read in place
 from the peers), checked against the oracle.  Skipped on boxes with fewer
@@ -13,7 +14,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-WORLD = 2
+WORLD = max(2, min(torch.cuda.device_count() if torch.cuda.is_available() else 0, 8))
 
 
 def _rank_main(rank, world, port, q, transport):
