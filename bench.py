@@ -775,7 +775,10 @@ def run_action(steps=20, warmup=3):
     (``shared_mask_attention``, plan built once) and as the reference calls it
     (``flash_attention(q, k, v, num_heads, mask)`` = rearrange + SDPA with the
     bool mask + rearrange, bf16, ``attention.py:47-54``) on the same GPU.
-    Bound: HBM; algorithmic bytes = q, k, v read once and o written once."""
+    Bound: HBM; algorithmic bytes = q, k, v read once and o written once.
+    The training form (forward + backward of the attention under autograd:
+    the aligned plan with the tcgen05 backward kernels, against SDPA's
+    autograd) is timed beside it."""
     import torch
     import torch.nn.functional as F
 
@@ -805,8 +808,24 @@ def run_action(steps=20, warmup=3):
             o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=m)
             return o.transpose(1, 2).reshape(B, Lq, H * 128)
 
+        qg, kg, vg = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+        dout = torch.randn(B, Lq, H * 128, generator=g, device=dev).bfloat16()
+
+        def ours_train():
+            for t in (qg, kg, vg):
+                t.grad = None
+            shared_mask_attention(qg, kg, vg, H, m).backward(dout)
+
+        def reference_train():
+            for t in (qg, kg, vg):
+                t.grad = None
+            qh, kh, vh = (t.view(B, t.shape[1], H, 128).transpose(1, 2) for t in (qg, kg, vg))
+            o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=m)
+            o.transpose(1, 2).reshape(B, Lq, H * 128).backward(dout)
+
         times = {}
-        for arm, fn in (("ours", ours), ("sdpa", reference)):
+        for arm, fn in (("ours", ours), ("sdpa", reference), ("ours_train", ours_train),
+                        ("sdpa_train", reference_train)):
             for _ in range(warmup):
                 fn()
             torch.cuda.synchronize()
@@ -824,14 +843,19 @@ def run_action(steps=20, warmup=3):
                      "reference_sdpa_ms": round(times["sdpa"], 4),
                      "speedup_vs_sdpa": round(times["sdpa"] / times["ours"], 2),
                      "algorithmic_mb": round(byts / 1e6, 1), "achieved_gbs": round(gbs, 1),
-                     "hbm_frac": round(gbs / hbm, 4), "n_pairs": plan.n_pairs}
-        del q, k, v, out
+                     "hbm_frac": round(gbs / hbm, 4), "n_pairs": plan.n_pairs,
+                     "train_fwd_bwd_ms": round(times["ours_train"], 4),
+                     "reference_sdpa_train_ms": round(times["sdpa_train"], 4),
+                     "train_speedup_vs_sdpa": round(times["sdpa_train"] / times["ours_train"], 2)}
+        del q, k, v, out, qg, kg, vg, dout
         torch.cuda.empty_cache()
     res["hbm_peak_gbs"] = hbm
     res["peak_kind"] = f"{peak_kind} copy bandwidth"
     res["device_error"] = device_error(dev)
     res["note"] = ("kernel: hier_attn_kernel over the shared-mask plan (one launch per call); "
-                   "reference: torch SDPA with the bool mask on the same GPU")
+                   "training: forward with lse over the aligned plan, then Delta, dQ and dK/dV "
+                   "kernels; reference: torch SDPA with the bool mask (and its autograd) on the "
+                   "same GPU")
     return res
 
 

@@ -187,15 +187,21 @@ int hier_plan_split_kv(const int32_t* q_pairs, int32_t n_pairs, int32_t chunks,
  * q_pairs [n_pairs][8], kv_tiles [n_pairs * tiles_per_pair][4], tile_masks
  * [n_pairs * tiles_per_pair * 2][128][4] uint32 and order [n_pairs] (or
  * passes NULL for the identity order).  Sequences of at most 64 rows are
- * packed several to a 128-row tile with block-diagonal masks.  The plan runs
- * on hier_attn_fwd (keys and values [B*Lk, H*D]).  Errors: HIER_EVALUE for
- * non-positive sizes, more than 2^24 - 256 key rows, or a NULL mask /
- * ld < Lk. */
-int hier_shared_mask_plan_size(int64_t B, int64_t Lq, int64_t Lk, int32_t* n_pairs,
-                               int32_t* tiles_per_pair);
+ * packed several to a 128-row tile with block-diagonal masks.  With aligned
+ * != 0 the plan is instead cut on the 128-row grid of the flat rows: query
+ * tiles are rows [128 i, 128 i + 128) of the B*Lq rows and key tiles start at
+ * multiples of 128 of the B*Lk rows, per-row masks carrying the batch
+ * diagonal; that is the form the backward (hier_bwd_plan_transpose,
+ * hier_attn_bwd_dq, hier_attn_bwd_dkv) takes, at the price of partial tiles
+ * for short sequences.  The plan runs on hier_attn_fwd (keys and values
+ * [B*Lk, H*D]).  Errors: HIER_EVALUE for non-positive sizes, more than
+ * 2^24 - 256 key rows, or a NULL mask / ld < Lk. */
+int hier_shared_mask_plan_size(int64_t B, int64_t Lq, int64_t Lk, int32_t aligned,
+                               int32_t* n_pairs, int32_t* tiles_per_pair);
 int hier_shared_mask_plan_build(const uint8_t* mask, int64_t ld, int64_t B, int64_t Lq,
-                                int64_t Lk, int32_t* q_pairs, int32_t* kv_tiles,
-                                uint32_t* tile_masks, int32_t* order, void* stream);
+                                int64_t Lk, int32_t aligned, int32_t* q_pairs,
+                                int32_t* kv_tiles, uint32_t* tile_masks, int32_t* order,
+                                void* stream);
 
 /* ---------------------------------------------------------------------------
  * Fused Q/K prologue

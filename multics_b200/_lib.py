@@ -145,7 +145,7 @@ _SIGS = {
     "hier_dense_block_plan_build": (c_int, [_P, c_int64, c_int64, _P, _P, _P, _P, _P, _P, _P, _P,
                                             _P]),
     "hier_plan_split_kv": (c_int, [_P, c_int32, c_int32, _P, _P, _P]),
-    "hier_shared_mask_plan_size": (c_int, [c_int64, c_int64, c_int64, _P, _P]),
+    "hier_shared_mask_plan_size": (c_int, [c_int64, c_int64, c_int64, c_int32, _P, _P]),
     "hier_prep_qk_bwd_partials": (c_int, [c_int64, _P]),
     "hier_prep_qk_bwd": (c_int, [_P, _P, c_int64, _P, c_int32, _P, _P, _P, _P, _P, c_int64,
                                  c_int64, c_int32, c_int32, c_float, _P, _P, c_int64, _P, _P,
@@ -160,8 +160,8 @@ _SIGS = {
     "hier_attn_bwd_dkv": (c_int, [_P, c_int64, c_int64, _P, _P, c_int64, c_int64, _P, c_int64, _P,
                                   _P, c_int64, c_int32, c_int32, _P, _P, _P, c_int32, c_float, _P,
                                   c_int64, _P, c_int64, _P, _P]),
-    "hier_shared_mask_plan_build": (c_int, [_P, c_int64, c_int64, c_int64, c_int64, _P, _P, _P,
-                                            _P, _P]),
+    "hier_shared_mask_plan_build": (c_int, [_P, c_int64, c_int64, c_int64, c_int64, c_int32, _P,
+                                            _P, _P, _P, _P]),
     "hier_prep_qk": (c_int, [_P, _P, c_int64, _P, c_int32, _P, _P, _P, _P, _P, c_int64, c_int64,
                              c_int32,
                              c_int32, c_float, _P, _P, c_int64, _P, _P, _P]),
@@ -203,7 +203,7 @@ _SIGS = {
 _LIB = None
 
 # hier_abi_version() of the library these signatures describe
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 
 def lib():

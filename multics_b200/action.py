@@ -78,9 +78,11 @@ class SharedMaskPlan(AttentionPlan):
     """Work plan of ``B`` independent attentions under one ``[Lq, Lk]`` mask:
     query row ``b*Lq + i`` sees key row ``b*Lk + j`` iff ``mask[i, j]``.
     Built on the GPU by ``hier_shared_mask_plan_build``; the fields are those
-    of :class:`~multics_b200.attention.AttentionPlan` (per-row masks)."""
+    of :class:`~multics_b200.attention.AttentionPlan` (per-row masks).
+    ``aligned`` cuts the tiles on the 128-row grid of the flat rows, the form
+    the backward kernels take (:func:`multics_b200.train.plan_attention_grad`)."""
 
-    def __init__(self, mask: torch.Tensor, B: int):
+    def __init__(self, mask: torch.Tensor, B: int, aligned: bool = False):
         if mask.dim() != 2:
             raise ValueError(f"shared mask must be [Lq, Lk], got {tuple(mask.shape)}")
         dev = mask.device
@@ -90,8 +92,9 @@ class SharedMaskPlan(AttentionPlan):
         Lq, Lk = m.shape
         lib = _lib.lib()
         n_pairs, cap = ctypes.c_int32(), ctypes.c_int32()
-        check(lib.hier_shared_mask_plan_size(B, Lq, Lk, ctypes.byref(n_pairs), ctypes.byref(cap)))
-        self.B, self.Lq, self.Lk = int(B), int(Lq), int(Lk)
+        check(lib.hier_shared_mask_plan_size(B, Lq, Lk, int(aligned), ctypes.byref(n_pairs),
+                                             ctypes.byref(cap)))
+        self.B, self.Lq, self.Lk, self.aligned = int(B), int(Lq), int(Lk), bool(aligned)
         self.n_pairs, self.tiles_per_pair = int(n_pairs.value), int(cap.value)
         n_ent = self.n_pairs * self.tiles_per_pair
         q_pairs = torch.empty((self.n_pairs, 8), dtype=torch.int32, device=dev)
@@ -102,14 +105,14 @@ class SharedMaskPlan(AttentionPlan):
         order = (torch.empty(self.n_pairs, dtype=torch.int32, device=dev)
                  if self.n_pairs <= 4096 else None)
         check(lib.hier_shared_mask_plan_build(
-            ptr(m), m.stride(0), B, Lq, Lk, ptr(q_pairs), ptr(kv_tiles), ptr(row_masks),
-            ptr(order), stream_ptr(dev)))
+            ptr(m), m.stride(0), B, Lq, Lk, int(aligned), ptr(q_pairs), ptr(kv_tiles),
+            ptr(row_masks), ptr(order), stream_ptr(dev)))
         super().__init__(q_pairs, kv_tiles, row_masks, order)
         self._mask_bytes = m  # read by the builder on the stream
 
 
 # (weakref to the caller's mask or None, its _version, B, Lq, Lk, device,
-# plan): the most recent plans, as the reference's bounded mask caches
+# aligned, plan): the most recent plans, as the reference's bounded mask caches
 _PLANS = []
 _PLAN_LIMIT = 8
 
@@ -137,12 +140,13 @@ def _shared_mask(mask, Lq: int, Lk: int, device) -> Optional[torch.Tensor]:
     return m.to(device=device, dtype=torch.bool)
 
 
-def shared_mask_plan(mask, B: int, Lq: int, Lk: int, device) -> SharedMaskPlan:
+def shared_mask_plan(mask, B: int, Lq: int, Lk: int, device,
+                     aligned: bool = False) -> SharedMaskPlan:
     """The plan for ``mask`` (any form :func:`shared_mask_attention` takes),
     reused while the same mask tensor is passed unmodified."""
     dev = torch.device(device)
-    for ref, ver, b_, q_, k_, d_, plan in _PLANS:
-        if (b_, q_, k_, d_) != (B, Lq, Lk, dev):
+    for ref, ver, b_, q_, k_, d_, a_, plan in _PLANS:
+        if (b_, q_, k_, d_, a_) != (B, Lq, Lk, dev, bool(aligned)):
             continue
         if mask is None and ref is None:
             return plan
@@ -151,9 +155,10 @@ def shared_mask_plan(mask, B: int, Lq: int, Lk: int, device) -> SharedMaskPlan:
     m = _shared_mask(mask, Lq, Lk, dev)
     if m is None:
         m = torch.ones((Lq, Lk), dtype=torch.bool, device=dev)
-    plan = SharedMaskPlan(m, B)
+    plan = SharedMaskPlan(m, B, aligned)
     _PLANS.insert(0, (None if mask is None else weakref.ref(mask),
-                      None if mask is None else mask._version, B, Lq, Lk, dev, plan))
+                      None if mask is None else mask._version, B, Lq, Lk, dev, bool(aligned),
+                      plan))
     del _PLANS[_PLAN_LIMIT:]
     return plan
 
@@ -167,7 +172,10 @@ def shared_mask_attention(q, k, v, num_heads: int, mask=None, *, out=None,
     ``mask`` bool (or any dtype, read as ``mask.to(bool)``) ``[Lq, Lk]``, with
     optional leading size-1 dimensions or SDPA broadcasting, or None.
     Returns ``[B, Lq, H*128]`` bf16.  A query row that sees no key is 0 (SDPA
-    gives NaN there)."""
+    gives NaN there).  While autograd records and ``q``, ``k`` or ``v``
+    requires grad, the call is differentiable: the attention runs on the
+    aligned form of the plan with the B200 backward kernels
+    (:func:`multics_b200.train.plan_attention_grad`)."""
     if q.dim() != 3 or k.dim() != 3 or v.shape != k.shape:
         raise ValueError(f"expected q [B,Lq,dim] and k, v [B,Lk,dim]; got {tuple(q.shape)}, "
                          f"{tuple(k.shape)}, {tuple(v.shape)}")
@@ -178,10 +186,21 @@ def shared_mask_attention(q, k, v, num_heads: int, mask=None, *, out=None,
     if dim % num_heads or dim // num_heads != 128:
         raise NotImplementedError(
             f"the B200 attention kernel needs head_dim 128; got dim {dim} over {num_heads} heads")
+    grad = torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad)
+    if plan is not None and (plan.B, plan.Lq, plan.Lk) != (B, Lq, Lk):
+        raise ValueError(f"plan is for B={plan.B}, Lq={plan.Lq}, Lk={plan.Lk}")
+    if grad:
+        from .train import plan_attention_grad
+
+        if out is not None:
+            raise ValueError("out= is not supported while autograd records")
+        if plan is None or not plan.aligned:
+            plan = shared_mask_plan(mask, B, Lq, Lk, q.device, aligned=True)
+        res = plan_attention_grad(q.reshape(B * Lq, dim), k.reshape(B * Lk, dim),
+                                  v.reshape(B * Lk, dim), plan, num_heads)
+        return res.view(B, Lq, dim)
     if plan is None:
         plan = shared_mask_plan(mask, B, Lq, Lk, q.device)
-    elif (plan.B, plan.Lq, plan.Lk) != (B, Lq, Lk):
-        raise ValueError(f"plan is for B={plan.B}, Lq={plan.Lq}, Lk={plan.Lk}")
     o = None if out is None else out.view(B * Lq, dim)
     res = attention_from_plan(q.reshape(B * Lq, dim), k.reshape(B * Lk, dim),
                               v.reshape(B * Lk, dim), plan, num_heads, out=o)

@@ -450,17 +450,15 @@ class SelfAttention(nn.Module):
         per-frame action attention (``blocks.py:684-686``): ``mask`` is one
         ``[L, L]`` mask shared by the batch and ``freqs`` ``[L, 1, D/2]``.
         While autograd records (training), the call runs
-        :meth:`_forward_train`: the attention on the block plan with its
-        B200 backward."""
-        if torch.is_grad_enabled() and (x.requires_grad or any(
-                p.requires_grad for p in self.parameters())):
-            if x.dim() == 3 and x.shape[0] > 1:
-                raise NotImplementedError(
-                    "the B200 attention backward covers the full-sequence (block plan) "
-                    "attention; run the batched action attention under torch.no_grad()")
-            return self._forward_train(x, freqs, mask, cam_tokens)
+        :meth:`_forward_train` (or :meth:`_forward_batch` with the fused
+        prologue's backward): the attention on an aligned plan with its B200
+        backward."""
+        train = torch.is_grad_enabled() and (x.requires_grad or any(
+            p.requires_grad for p in self.parameters()))
         if x.dim() == 3 and x.shape[0] > 1:
-            return self._forward_batch(x, freqs, mask, cam_tokens)
+            return self._forward_batch(x, freqs, mask, cam_tokens, train=train)
+        if train:
+            return self._forward_train(x, freqs, mask, cam_tokens)
         mask = attention_mask_plan(mask, x.shape[1], x.device)
         sp = sequence_plan(mask, self.num_heads)
         q, k, v = self.project_qkv(x, freqs, cam_tokens,
@@ -498,10 +496,12 @@ class SelfAttention(nn.Module):
         out = hier_block_attention_grad(q, k, _rows(v), bm, self.num_heads)
         return self.o(out.view(x.shape))
 
-    def _forward_batch(self, x, freqs, mask, cam_tokens):
+    def _forward_batch(self, x, freqs, mask, cam_tokens, train=False):
         """``B`` sequences of ``L`` tokens under one shared mask: projections,
         the fused prologue over the ``B*L`` rows (RoPE table row ``r % L``)
-        and the shared-mask attention plan."""
+        and the shared-mask attention plan.  ``train``: the prologue and the
+        attention with their backward kernels (:func:`multics_b200.train.prologue_grad`,
+        the aligned shared-mask plan)."""
         from .action import shared_mask_attention
 
         B, L, dim = x.shape
@@ -512,7 +512,15 @@ class SelfAttention(nn.Module):
                 raise ValueError(f"camera tokens shape {tuple(cam_tokens.shape[:2])} must match "
                                  f"q/k tokens {tuple(x.shape[:2])}")
             cam_tokens = cam_tokens.reshape(B * L, -1)
-        q, k = hier_prep_qk(
+            if self.training and self.cam_dropout_p > 0:
+                cam_tokens = torch.nn.functional.dropout(cam_tokens, p=self.cam_dropout_p,
+                                                         training=True)
+        if train:
+            from .train import prologue_grad
+            prep = prologue_grad
+        else:
+            prep = hier_prep_qk
+        q, k = prep(
             self.q(x).reshape(B * L, dim), self.k(x).reshape(B * L, dim), freqs, self.num_heads,
             norm_q_weight=self.norm_q.weight, norm_k_weight=self.norm_k.weight,
             cam_tokens=cam_tokens, cam_q_weight=None if self.cam_q is None else self.cam_q.weight,

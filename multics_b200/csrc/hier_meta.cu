@@ -778,9 +778,10 @@ struct SharedMaskDims {
   int64_t n_tiles;  // query tiles in all
   int64_t n_pairs;
   int64_t cap;      // kv_tiles entries (and mask pairs) reserved per pair
+  int aligned;      // 128-row query tiles of the flat rows, key tiles on the 128-row grid
 };
 
-static int shared_mask_dims(int64_t B, int64_t Lq, int64_t Lk, SharedMaskDims* d) {
+static int shared_mask_dims(int64_t B, int64_t Lq, int64_t Lk, int aligned, SharedMaskDims* d) {
   if (B < 1 || Lq < 1 || Lk < 1) {
     set_error(HIER_EVALUE, "shared-mask plan: B=%lld, Lq=%lld, Lk=%lld must be positive",
               (long long)B, (long long)Lq, (long long)Lk);
@@ -801,6 +802,18 @@ static int shared_mask_dims(int64_t B, int64_t Lq, int64_t Lk, SharedMaskDims* d
   d->n_tiles = units * d->nqt;
   d->n_pairs = (d->n_tiles + 1) / 2;
   d->cap = 2 * ((d->g * Lk + 127) / 128);
+  d->aligned = aligned != 0;
+  if (d->aligned) {
+    // one unit of every row: query tiles are the 128-row blocks of the flat
+    // rows; a pair's 256 rows touch at most ceil(256/Lq) + 1 batch entries
+    d->g = B;
+    d->nqt = (B * Lq + 127) / 128;
+    d->n_tiles = d->nqt;
+    d->n_pairs = (d->n_tiles + 1) / 2;
+    const int64_t span = ((256 + Lq - 1) / Lq + 1) * Lk;
+    const int64_t all = (B * Lk + 127) / 128;
+    d->cap = std::min(all, span / 128 + 2);
+  }
   if (d->n_pairs * d->cap * 2 > (int64_t)INT32_MAX / 128) {
     set_error(HIER_EVALUE, "shared-mask plan: %lld pairs x %lld key tiles is too large",
               (long long)d->n_pairs, (long long)d->cap);
@@ -862,11 +875,17 @@ __global__ void __launch_bounds__(128) shared_mask_plan_kernel(const uint8_t* __
   if (has0 && has1 && unit[0] == unit[1]) {
     seg_lo[0] = min(lo_s[0], lo_s[1]), seg_hi[0] = max(hi_s[0], hi_s[1]), seg_use[0] = 3;
     n_seg = 1;
+  } else if (d.aligned && (has0 || has1)) {
+    seg_lo[0] = has0 ? (has1 ? min(lo_s[0], lo_s[1]) : lo_s[0]) : lo_s[1];
+    seg_hi[0] = has0 ? (has1 ? max(hi_s[0], hi_s[1]) : hi_s[0]) : hi_s[1];
+    seg_use[0] = (has0 ? 1 : 0) | (has1 ? 2 : 0);
+    n_seg = 1;
   } else {
     if (has0) seg_lo[n_seg] = lo_s[0], seg_hi[n_seg] = hi_s[0], seg_use[n_seg++] = 1;
     if (has1) seg_lo[n_seg] = lo_s[1], seg_hi[n_seg] = hi_s[1], seg_use[n_seg++] = 2;
   }
   const int64_t kv_base = p * d.cap;
+  if (d.aligned && n_seg) seg_lo[0] = seg_lo[0] / 128 * 128;  // key tiles on the 128-row grid
   for (int sgi = 0; sgi < n_seg; ++sgi) {
     for (int64_t ks = seg_lo[sgi]; ks <= seg_hi[sgi]; ks += 128) {
       const int e = n_ent_s;
@@ -907,11 +926,11 @@ __global__ void __launch_bounds__(128) shared_mask_plan_kernel(const uint8_t* __
 
 }  // namespace hier
 
-extern "C" int hier_shared_mask_plan_size(int64_t B, int64_t Lq, int64_t Lk, int32_t* n_pairs,
-                                          int32_t* tiles_per_pair) {
+extern "C" int hier_shared_mask_plan_size(int64_t B, int64_t Lq, int64_t Lk, int32_t aligned,
+                                          int32_t* n_pairs, int32_t* tiles_per_pair) {
   clear_error();
   SharedMaskDims d;
-  int rc = shared_mask_dims(B, Lq, Lk, &d);
+  int rc = shared_mask_dims(B, Lq, Lk, aligned, &d);
   if (rc) return rc;
   *n_pairs = (int32_t)d.n_pairs;
   *tiles_per_pair = (int32_t)d.cap;
@@ -919,11 +938,12 @@ extern "C" int hier_shared_mask_plan_size(int64_t B, int64_t Lq, int64_t Lk, int
 }
 
 extern "C" int hier_shared_mask_plan_build(const uint8_t* mask, int64_t ld, int64_t B, int64_t Lq,
-                                           int64_t Lk, int32_t* q_pairs, int32_t* kv_tiles,
-                                           uint32_t* tile_masks, int32_t* order, void* stream) {
+                                           int64_t Lk, int32_t aligned, int32_t* q_pairs,
+                                           int32_t* kv_tiles, uint32_t* tile_masks,
+                                           int32_t* order, void* stream) {
   clear_error();
   SharedMaskDims d;
-  int rc = shared_mask_dims(B, Lq, Lk, &d);
+  int rc = shared_mask_dims(B, Lq, Lk, aligned, &d);
   if (rc) return rc;
   if (!mask || ld < Lk) {
     set_error(HIER_EVALUE, "shared-mask plan: mask is NULL or its row stride %lld < Lk=%lld",

@@ -28,18 +28,28 @@ from ._lib import check, ptr, stream_ptr
 from .attention import _dev_err, _rows
 from .hier_masks import HierBlockMask
 
-__all__ = ["BlockPlanGrad", "block_plan_grad", "hier_block_attention_grad", "prologue_grad"]
+__all__ = ["BlockPlanGrad", "block_plan_grad", "hier_block_attention_grad", "plan_attention_grad",
+           "prologue_grad"]
+
+
+def _plan_extent(plan):
+    """(references of key blocks by query tiles at most, row masks) of a plan."""
+    if isinstance(plan, HierBlockMask):
+        return plan.n_partial + plan.n_full, (plan.row_masks.shape[0] if plan.n_partial > 0 else 0)
+    return 2 * plan.kv_tiles.shape[0], plan.row_masks.shape[0]
 
 
 class BlockPlanGrad:
-    """Key-major form of a block plan (``hier_bwd_plan_transpose``): per key
-    block the query blocks that see it and per-key-row masks."""
+    """Key-major form of a 128-aligned plan (``hier_bwd_plan_transpose``): per
+    key block the query tiles that see it and per-key-row masks.  ``plan`` is
+    a :class:`HierBlockMask` or any plan whose query tiles start on multiples
+    of 128 rows and whose key tiles are 128-row blocks (an aligned
+    :class:`~multics_b200.action.SharedMaskPlan`)."""
 
-    def __init__(self, bm: HierBlockMask, kv_rows: int):
-        dev = bm.q_pairs.device
+    def __init__(self, plan, kv_rows: int):
+        dev = plan.q_pairs.device
         self.n_kb = (kv_rows + 127) // 128
-        capacity = bm.n_partial + bm.n_full
-        n_masks = bm.row_masks.shape[0] if bm.n_partial > 0 else 0
+        capacity, n_masks = _plan_extent(plan)
         i32 = dict(dtype=torch.int32, device=dev)
         ws = torch.empty(2 * self.n_kb, **i32)
         self.k_off = torch.empty(self.n_kb + 1, **i32)
@@ -47,33 +57,40 @@ class BlockPlanGrad:
         self.t_masks = torch.empty((max(n_masks, 1), 128, 4), **i32)
         status = torch.empty(1, **i32)
         check(_lib.lib().hier_bwd_plan_transpose(
-            ptr(bm.q_pairs), bm.q_pairs.shape[0], ptr(bm.kv_tiles), ptr(bm.row_masks), n_masks,
-            self.n_kb, ptr(ws), ptr(self.k_off), ptr(self.k_ent), capacity, ptr(self.t_masks),
-            ptr(status), stream_ptr(dev)))
+            ptr(plan.q_pairs), plan.q_pairs.shape[0], ptr(plan.kv_tiles), ptr(plan.row_masks),
+            n_masks, self.n_kb, ptr(ws), ptr(self.k_off), ptr(self.k_ent), capacity,
+            ptr(self.t_masks), ptr(status), stream_ptr(dev)))
         st = int(status.item())
         if st & 1:
             raise NotImplementedError(
-                "the attention backward needs a block plan without a page table")
+                "the attention backward needs a plan of 128-aligned query and key tiles over "
+                "one key stream (a block plan, or an aligned shared-mask plan)")
         if st & 2:
             raise RuntimeError("key-major plan exceeded its capacity")
 
 
-def block_plan_grad(bm: HierBlockMask, kv_rows: int) -> BlockPlanGrad:
-    """The key-major plan of ``bm``, built once per block mask (kept on it)."""
-    gp = getattr(bm, "_grad_plan", None)
+def block_plan_grad(plan, kv_rows: int) -> BlockPlanGrad:
+    """The key-major plan of ``plan``, built once per plan (kept on it)."""
+    gp = getattr(plan, "_grad_plan", None)
     if gp is None or gp.n_kb != (kv_rows + 127) // 128:
-        gp = BlockPlanGrad(bm, kv_rows)
-        object.__setattr__(bm, "_grad_plan", gp)
+        gp = BlockPlanGrad(plan, kv_rows)
+        object.__setattr__(plan, "_grad_plan", gp)
     return gp
 
 
-class _HierBlockAttention(torch.autograd.Function):
+class _PlanAttention(torch.autograd.Function):
+    """Attention of query rows ``[Sq, H*D]`` over key/value rows ``[Sk, H*D]``
+    under an aligned plan; forward keeps the log2-sum-exp for the backward."""
+
     @staticmethod
-    def forward(ctx, q, k, v, bm, num_heads, scale):
+    def forward(ctx, q, k, v, plan, num_heads, scale):
         q2, k2, v2 = (_rows(t).contiguous() for t in (q, k, v))
         for name, t in (("q", q2), ("k", k2), ("v", v2)):
             if t.dtype != torch.bfloat16 or not t.is_cuda:
                 raise NotImplementedError(f"the B200 attention needs bf16 CUDA {name}")
+        if k2.shape != v2.shape or k2.shape[1] != q2.shape[1]:
+            raise ValueError(f"q {tuple(q2.shape)}, k {tuple(k2.shape)}, v {tuple(v2.shape)} "
+                             f"disagree")
         S, dim = q2.shape
         D = dim // num_heads
         dev = q2.device
@@ -85,18 +102,18 @@ class _HierBlockAttention(torch.autograd.Function):
         strides = (ctypes.c_int64 * 1)(k2.stride(0))
         check(_lib.lib().hier_attn_fwd_streams(
             ptr(q2), S, q2.stride(0), 1, kp, vp, rows, strides, ptr(out), out.stride(0), None,
-            num_heads, D, ptr(bm.q_pairs), bm.q_pairs.shape[0], ptr(bm.kv_tiles),
-            ptr(bm.row_masks), 128, ptr(bm.order), scale, ptr(lse), None, ptr(_dev_err(dev)),
+            num_heads, D, ptr(plan.q_pairs), plan.q_pairs.shape[0], ptr(plan.kv_tiles),
+            ptr(plan.row_masks), 128, ptr(plan.order), scale, ptr(lse), None, ptr(_dev_err(dev)),
             stream_ptr(dev)))
         ctx.save_for_backward(q2, k2, v2, out, lse)
-        ctx.bm, ctx.num_heads, ctx.scale = bm, num_heads, scale
+        ctx.plan, ctx.num_heads, ctx.scale = plan, num_heads, scale
         ctx.shapes = (q.shape, k.shape, v.shape)
         return out.view(q.shape)
 
     @staticmethod
     def backward(ctx, dout):
         q2, k2, v2, out, lse = ctx.saved_tensors
-        bm, H, scale = ctx.bm, ctx.num_heads, ctx.scale
+        plan, H, scale = ctx.plan, ctx.num_heads, ctx.scale
         S, dim = q2.shape
         D = dim // H
         dev = q2.device
@@ -115,10 +132,10 @@ class _HierBlockAttention(torch.autograd.Function):
         kv_rows = k2.shape[0]
         check(L.hier_attn_bwd_dq(
             ptr(q2), S, q2.stride(0), ptr(k2), ptr(v2), kv_rows, k2.stride(0), ptr(do2),
-            do2.stride(0), ptr(lse_t), ptr(delta), rows_pad, H, D, ptr(bm.q_pairs),
-            bm.q_pairs.shape[0], ptr(bm.kv_tiles), ptr(bm.row_masks), 128, scale, ptr(dq),
+            do2.stride(0), ptr(lse_t), ptr(delta), rows_pad, H, D, ptr(plan.q_pairs),
+            plan.q_pairs.shape[0], ptr(plan.kv_tiles), ptr(plan.row_masks), 128, scale, ptr(dq),
             dq.stride(0), ptr(err), st))
-        gp = block_plan_grad(bm, kv_rows)
+        gp = block_plan_grad(plan, kv_rows)
         check(L.hier_attn_bwd_dkv(
             ptr(q2), S, q2.stride(0), ptr(k2), ptr(v2), kv_rows, k2.stride(0), ptr(do2),
             do2.stride(0), ptr(lse_t), ptr(delta), rows_pad, H, D, ptr(gp.k_off), ptr(gp.k_ent),
@@ -202,4 +219,15 @@ def hier_block_attention_grad(q, k, v, mask, num_heads: int, *, softmax_scale=No
         raise ValueError(f"block mask is for S={bm.S}, got {S} tokens")
     D = q.shape[-1] // num_heads
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
-    return _HierBlockAttention.apply(q, k, v, bm, num_heads, scale)
+    return _PlanAttention.apply(q, k, v, bm, num_heads, scale)
+
+
+def plan_attention_grad(q, k, v, plan, num_heads: int, *, softmax_scale=None):
+    """Differentiable attention of query rows ``q`` ``[Sq, H*128]`` over
+    key/value rows ``k``, ``v`` ``[Sk, H*128]`` (bf16) under a 128-aligned
+    ``plan`` (a :class:`HierBlockMask` or an aligned
+    :class:`~multics_b200.action.SharedMaskPlan`, as the batched action
+    attentions use it)."""
+    D = q.shape[-1] // num_heads
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    return _PlanAttention.apply(q, k, v, plan, num_heads, scale)

@@ -83,11 +83,12 @@ def test_oracle_keyboard_attention_matches_reference():
     assert float((got - ref).abs().max()) < 1e-5
 
 
-def _plan_size(B, Lq, Lk):
+def _plan_size(B, Lq, Lk, aligned=0):
     from multics_b200 import _lib
 
     n, cap = ctypes.c_int32(), ctypes.c_int32()
-    rc = _lib.lib().hier_shared_mask_plan_size(B, Lq, Lk, ctypes.byref(n), ctypes.byref(cap))
+    rc = _lib.lib().hier_shared_mask_plan_size(B, Lq, Lk, aligned, ctypes.byref(n),
+                                               ctypes.byref(cap))
     return rc, n.value, cap.value
 
 
@@ -101,6 +102,17 @@ def _plan_size(B, Lq, Lk):
 ])
 def test_shared_mask_plan_size(B, Lq, Lk, pairs, cap):
     rc, n, c = _plan_size(B, Lq, Lk)
+    assert rc == 0 and (n, c) == (pairs, cap)
+
+
+@pytest.mark.parametrize("B,Lq,Lk,pairs,cap", [
+    (880, 42, 42, 145, 4),      # per-frame attention on the 128-row grid: 289 query tiles
+    (4, 9240, 504, 145, 9),     # keyboard cross-attention: a pair spans 2 players' keys
+    (1, 1, 1, 1, 1),
+    (3, 128, 300, 2, 8),        # every key tile of the 900 rows
+])
+def test_aligned_shared_mask_plan_size(B, Lq, Lk, pairs, cap):
+    rc, n, c = _plan_size(B, Lq, Lk, aligned=1)
     assert rc == 0 and (n, c) == (pairs, cap)
 
 

@@ -1,8 +1,9 @@
 """Action-branch attention on the GPU (the DiT block's per-frame mouse
 attention and keyboard cross-attention, ``multics/models/blocks.py:677-697``).
 
-* The shared-mask plan re-expands to exactly the batch's block-diagonal mask:
-  every (query row, key row) pair is covered once, with the mask's bit.
+* The shared-mask plan, packed and aligned, re-expands to exactly the
+  batch's block-diagonal mask: every (query row, key row) pair is covered
+  once, with the mask's bit; the aligned plan's tiles sit on the 128-row grid.
 * ``shared_mask_attention`` matches an fp32 torch SDPA restatement
   (``oracle.ref_cpu_path.shared_mask_sdpa``) on random inputs, including
   rows without keys (0 here; SDPA gives NaN).
@@ -90,13 +91,20 @@ def _mask(kind, arg, Lq, Lk, seed=0):
     return m
 
 
+@pytest.mark.parametrize("aligned", [False, True], ids=["packed", "aligned"])
 @pytest.mark.parametrize("B,Lq,Lk,kind,arg", PLAN_CASES)
-def test_shared_mask_plan_expands_to_block_diagonal(B, Lq, Lk, kind, arg):
+def test_shared_mask_plan_expands_to_block_diagonal(B, Lq, Lk, kind, arg, aligned):
     from multics_b200.action import SharedMaskPlan
 
     m = _mask(kind, arg, Lq, Lk)
-    plan = SharedMaskPlan(torch.from_numpy(m).cuda(), B)
+    plan = SharedMaskPlan(torch.from_numpy(m).cuda(), B, aligned=aligned)
     torch.cuda.synchronize()
+    if aligned:  # the form the backward's transpose takes
+        qp, kv = plan.q_pairs.cpu(), plan.kv_tiles.cpu()
+        assert bool((qp[:, [0, 2]] % 128 == 0).all())
+        for p in range(qp.shape[0]):
+            ks = kv[int(qp[p, 4]):int(qp[p, 5]), 0]
+            assert bool((ks % 128 == 0).all()) and bool((ks[1:] > ks[:-1]).all())
     cover, seen = _expand(plan, B, Lq, Lk)
     want = np.kron(np.eye(B, dtype=bool), m)
     assert np.array_equal(seen, want)
