@@ -38,6 +38,55 @@ struct PrepArgs {
 
 constexpr int kMaxCam = 16;
 
+// Camera weights W [dim][CAM] (bf16, row-major) into shared memory
+// transposed, wt[c * dim + d]: one thread per channel d reads its CAM
+// contiguous weights (8-byte loads when aligned) and writes them to CAM rows,
+// consecutive threads to consecutive channels (no bank conflicts); the loop is
+// unrolled so that a thread's loads are in flight together.
+template <int CAM>
+__device__ __forceinline__ void load_cam_weights_t(__nv_bfloat16* wt, const __nv_bfloat16* wc,
+                                                   int dim) {
+  if (CAM == 0) return;
+  const bool vec = CAM % 4 == 0 && (reinterpret_cast<uintptr_t>(wc) & 7) == 0;
+#pragma unroll 2
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    __nv_bfloat16 w[CAM > 0 ? CAM : 1];
+    if (vec) {
+      const uint2* src = reinterpret_cast<const uint2*>(wc + (int64_t)d * CAM);
+#pragma unroll
+      for (int j = 0; j < CAM / 4; ++j) {
+        const uint2 v = src[j];
+        memcpy(&w[4 * j], &v, sizeof(v));
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < CAM; ++c) w[c] = wc[(int64_t)d * CAM + c];
+    }
+#pragma unroll
+    for (int c = 0; c < CAM; ++c) wt[c * dim + d] = w[c];
+  }
+}
+
+// x rounded to the nearest bf16 (the value the forward keeps for y = x + proj)
+__device__ __forceinline__ float round_bf16(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// two bf16 channels (low half first) as an fp32x2 pair
+__device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t v) {
+  return f2_pack(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+
+// eight bf16 channels added pairwise, each sum rounded to bf16 once
+__device__ __forceinline__ uint4 bf16x8_add(uint4 a, uint4 b) {
+  uint4 r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r.x) : "r"(a.x), "r"(b.x));
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r.y) : "r"(a.y), "r"(b.y));
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r.z) : "r"(a.z), "r"(b.z));
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r.w) : "r"(a.w), "r"(b.w));
+  return r;
+}
+
 __device__ __forceinline__ void bf16x8_to_f32(uint4 v, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
@@ -54,11 +103,16 @@ __device__ __forceinline__ void bf16x8_to_f32(uint4 v, float (&f)[8]) {
 // warp reduction (no block barrier), and the RoPE pairs of a lane are the
 // same for all its chunks (channel offsets 256i are whole heads apart), so
 // a lane reads 4 (cos, sin) pairs per row.  A warp walks a contiguous run of
-// rows; the camera projection W cam_r of its channels (camera weights
-// transposed into shared memory, fp32 sums, kept as bf16 in the warp's slice
-// of shared memory) is recomputed only when the camera row changes: the rows
-// of a player frame share one camera row and hub rows have none.
-constexpr int kPrepWarps = 12;
+// rows with the next row's channels loaded while it computes the current one
+// (8 warps per CTA leave the registers for both rows); the camera projection
+// W cam_r of its channels (camera weights transposed into shared memory, fp32
+// sums, kept as bf16 in the warp's slice of shared memory) is recomputed only
+// when the camera row changes: the rows of a player frame share one camera
+// row and hub rows have none.  Per channel pair: one bf16x2 add of the
+// projection (y, rounded to bf16 as the reference's add), one fp32x2 FMA for
+// the sum of squares, one fp32x2 multiply by the norm weight, and the rotation
+// with rstd folded into the row's (cos, sin) pairs.
+constexpr int kPrepWarps = 8;
 constexpr int kPrepMaxChunks = 12;  // dim <= 256 * 12 = 3072
 
 // chunk i of a lane exists (a row of dim = 256k + 128 leaves the upper half of
@@ -78,10 +132,7 @@ __global__ void __launch_bounds__(kPrepWarps * 32, 1) prep_qk_kernel(PrepArgs a)
   const __nv_bfloat16* wc = is_k ? a.wck : a.wcq;
   const __nv_bfloat16* nw = is_k ? a.nkw : a.nqw;
   __nv_bfloat16* out = is_k ? a.k_out : a.q_out;
-  for (int e = threadIdx.x; e < CAM * a.dim; e += blockDim.x) {
-    const int d = e / (CAM > 0 ? CAM : 1), c = e % (CAM > 0 ? CAM : 1);  // coalesced reads of W[d][c]
-    wt[c * a.dim + d] = wc[e];
-  }
+  load_cam_weights_t<CAM>(wt, wc, a.dim);
   for (int e = threadIdx.x; e < a.dim / 8; e += blockDim.x)
     reinterpret_cast<uint4*>(nws)[e] = reinterpret_cast<const uint4*>(nw)[e];
   __syncthreads();
@@ -95,18 +146,45 @@ __global__ void __launch_bounds__(kPrepWarps * 32, 1) prep_qk_kernel(PrepArgs a)
   float cam_prev = 0.f;  // lane c < CAM: camera value c of the projected row
   bool have_proj = false;
   const float inv_dim = 1.f / (float)a.dim;
-  for (int64_t r = r_begin; r < r_end; ++r) {
-    const __nv_bfloat16* xr = x + r * a.x_stride;
-    uint4 xv[NCH];
+  // the camera value and the output row of a token are loaded one row ahead:
+  // the camera value decides whether the projection is recomputed and the
+  // output row addresses the stores, so neither load waits on its own row
+  const int32_t* rows_map = (is_k && a.k_out_rows) ? a.k_out_rows : a.out_rows;
+  float cv_next = 0.f;
+  int64_t dst_next = r_begin;
+  if (r_begin < r_end) {
+    if (CAM > 0 && lane < CAM) cv_next = __bfloat162float(a.cam[r_begin * CAM + lane]);
+    if (rows_map) dst_next = rows_map[r_begin];
+  }
+  uint4 xn[NCH];
+  if (r_begin < r_end) {
+    const __nv_bfloat16* xr = x + r_begin * a.x_stride;
 #pragma unroll
     for (int i = 0; i < NCH; ++i)
-      xv[i] = chunk_ok(a.dim, lane, i) ? *reinterpret_cast<const uint4*>(xr + 8 * lane + 256 * i)
+      xn[i] = chunk_ok(a.dim, lane, i) ? *reinterpret_cast<const uint4*>(xr + 8 * lane + 256 * i)
                                        : make_uint4(0u, 0u, 0u, 0u);
+  }
+  for (int64_t r = r_begin; r < r_end; ++r) {
+    uint4 xv[NCH];
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) xv[i] = xn[i];
+    if (r + 1 < r_end) {
+      const __nv_bfloat16* xr = x + (r + 1) * a.x_stride;
+#pragma unroll
+      for (int i = 0; i < NCH; ++i)
+        xn[i] = chunk_ok(a.dim, lane, i) ? *reinterpret_cast<const uint4*>(xr + 8 * lane + 256 * i)
+                                         : make_uint4(0u, 0u, 0u, 0u);
+    }
     const int64_t rf = a.freqs_rows == a.S ? r : r % a.freqs_rows;
     const float4* fr = reinterpret_cast<const float4*>(a.freqs + rf * half + pair0);
     const float4 f0 = fr[0], f1 = fr[1];
+    const float cv = cv_next;
+    const int64_t dst = dst_next;
+    if (r + 1 < r_end) {
+      if (CAM > 0 && lane < CAM) cv_next = __bfloat162float(a.cam[(r + 1) * CAM + lane]);
+      dst_next = rows_map ? (int64_t)rows_map[r + 1] : r + 1;
+    }
     if (CAM > 0) {
-      const float cv = lane < CAM ? __bfloat162float(a.cam[r * CAM + lane]) : 0.f;
       const bool same = __all_sync(0xffffffffu, cv == cam_prev);
       if (!(same && have_proj)) {
         const bool zero = __all_sync(0xffffffffu, cv == 0.f);
@@ -134,48 +212,46 @@ __global__ void __launch_bounds__(kPrepWarps * 32, 1) prep_qk_kernel(PrepArgs a)
         have_proj = true;
       }
     }
-    // pass 1: sum of squares of (x + proj) over the row
-    float ss = 0.f;
+    // pass 1: y = x + proj rounded to bf16 (the reference adds the camera
+    // projection in bf16, attention.py:320) kept in place of x, and the row's
+    // sum of squares of y, two channels per fp32x2 FMA
+    uint64_t ss2 = f2_pack(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
-      float xf[8], pf[8];
-      bf16x8_to_f32(xv[i], xf);
-      if (CAM > 0) {
-        bf16x8_to_f32(proj[i * 32 + lane], pf);
+      if (CAM > 0) xv[i] = bf16x8_add(xv[i], proj[i * 32 + lane]);
+      const uint32_t* yw = reinterpret_cast<const uint32_t*>(&xv[i]);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) xf[q] += pf[q];
+      for (int q = 0; q < 4; ++q) {
+        const uint64_t v = bf16x2_to_f2(yw[q]);
+        ss2 = f2_fma(v, v, ss2);
       }
-#pragma unroll
-      for (int q = 0; q < 8; ++q) ss = fmaf(xf[q], xf[q], ss);
     }
+    float ss_lo, ss_hi;
+    f2_unpack(ss2, ss_lo, ss_hi);
+    float ss = ss_lo + ss_hi;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float rs = rsqrtf(ss * inv_dim + a.eps);
-    // pass 2: normalise, rotate, store
-    const int32_t* rows_map = (is_k && a.k_out_rows) ? a.k_out_rows : a.out_rows;
-    const int64_t dst = rows_map ? (int64_t)rows_map[r] : r;
+    // pass 2: (y * w) rotated, with rstd folded into the row's (cos, sin)
+    // pairs (RoPE is linear), one bf16 rounding
+    float rc[4], rsn[4];
+    rc[0] = f0.x * rs, rsn[0] = f0.y * rs, rc[1] = f0.z * rs, rsn[1] = f0.w * rs;
+    rc[2] = f1.x * rs, rsn[2] = f1.y * rs, rc[3] = f1.z * rs, rsn[3] = f1.w * rs;
     __nv_bfloat16* orow = out + dst * a.out_stride;
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
-      float xf[8], pf[8], wf[8];
-      bf16x8_to_f32(xv[i], xf);
-      if (CAM > 0) {
-        bf16x8_to_f32(proj[i * 32 + lane], pf);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) xf[q] += pf[q];
-      }
-      bf16x8_to_f32(chunk_ok(a.dim, lane, i)
-                        ? *reinterpret_cast<const uint4*>(nws + 8 * lane + 256 * i)
-                        : make_uint4(0u, 0u, 0u, 0u), wf);
+      const uint4 wv = chunk_ok(a.dim, lane, i)
+                           ? *reinterpret_cast<const uint4*>(nws + 8 * lane + 256 * i)
+                           : make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t* yw = reinterpret_cast<const uint32_t*>(&xv[i]);
+      const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
       uint4 o;
       uint32_t* po = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const float4 f = q < 2 ? f0 : f1;
-        const float c = (q & 1) ? f.z : f.x;
-        const float s = (q & 1) ? f.w : f.y;
-        const float a0 = xf[2 * q] * rs * wf[2 * q], a1 = xf[2 * q + 1] * rs * wf[2 * q + 1];
-        po[q] = pack_bf16x2(a0 * c - a1 * s, a0 * s + a1 * c);
+        float a0, a1;
+        f2_unpack(f2_mul(bf16x2_to_f2(yw[q]), bf16x2_to_f2(ww[q])), a0, a1);
+        po[q] = pack_bf16x2(fmaf(a0, rc[q], -a1 * rsn[q]), fmaf(a0, rsn[q], a1 * rc[q]));
       }
       if (chunk_ok(a.dim, lane, i)) *reinterpret_cast<uint4*>(orow + 8 * lane + 256 * i) = o;
     }
@@ -260,10 +336,7 @@ __global__ void __launch_bounds__(kPrepBwdWarps * 32, 1) prep_qk_bwd_kernel(Prep
   const __nv_bfloat16* nw = is_k ? a.nkw : a.nqw;
   const __nv_bfloat16* g = is_k ? b.gk : b.gq;
   __nv_bfloat16* dx = is_k ? b.dkx : b.dqx;
-  for (int e = threadIdx.x; e < CAM * a.dim; e += blockDim.x) {
-    const int d = e / (CAM > 0 ? CAM : 1), c = e % (CAM > 0 ? CAM : 1);
-    wt[c * a.dim + d] = wc[e];
-  }
+  load_cam_weights_t<CAM>(wt, wc, a.dim);
   for (int e = threadIdx.x; e < a.dim / 8; e += blockDim.x)
     reinterpret_cast<uint4*>(nws)[e] = reinterpret_cast<const uint4*>(nw)[e];
   __syncthreads();
@@ -323,7 +396,7 @@ __global__ void __launch_bounds__(kPrepBwdWarps * 32, 1) prep_qk_bwd_kernel(Prep
         have_proj = true;
       }
     }
-    // y = x + projection; its sum of squares
+    // y = x + projection, rounded to bf16 as in the forward; its sum of squares
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
@@ -332,7 +405,7 @@ __global__ void __launch_bounds__(kPrepBwdWarps * 32, 1) prep_qk_bwd_kernel(Prep
       if (CAM > 0) {
         bf16x8_to_f32(proj[i * 32 + lane], pf);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) xf[q] += pf[q];
+        for (int q = 0; q < 8; ++q) xf[q] = round_bf16(xf[q] + pf[q]);
       }
 #pragma unroll
       for (int q = 0; q < 8; ++q) ss = fmaf(xf[q], xf[q], ss);
@@ -349,7 +422,7 @@ __global__ void __launch_bounds__(kPrepBwdWarps * 32, 1) prep_qk_bwd_kernel(Prep
       if (CAM > 0) {
         bf16x8_to_f32(proj[i * 32 + lane], pf);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) xf[q] += pf[q];
+        for (int q = 0; q < 8; ++q) xf[q] = round_bf16(xf[q] + pf[q]);
       }
       ld(gr, i, gf);
       ld(nws, i, wf);
@@ -378,7 +451,7 @@ __global__ void __launch_bounds__(kPrepBwdWarps * 32, 1) prep_qk_bwd_kernel(Prep
       if (CAM > 0) {
         bf16x8_to_f32(proj[i * 32 + lane], pf);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) xf[q] += pf[q];
+        for (int q = 0; q < 8; ++q) xf[q] = round_bf16(xf[q] + pf[q]);
       }
       ld(gr, i, gf);
       ld(nws, i, wf);
