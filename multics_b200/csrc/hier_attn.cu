@@ -28,7 +28,10 @@
 // P (bf16, two per 32-bit column) is written over the first 64 columns of the
 // S buffer it came from and read by the TS-form MMA; S_h(j+1) is issued after
 // PV_h(j) by the same thread, and tcgen05 MMAs of one thread execute in issue
-// order, so it never overwrites P_h(j) before PV_h(j) has read it.
+// order, so it never overwrites P_h(j) before PV_h(j) has read it.  The
+// softmax signals P's first 64 keys before it computes the other 64, and
+// PV_h(j) is issued in those two halves: the tensor core multiplies the first
+// half while the exponentials of the second are still being computed.
 //
 // Shared memory: Q0, Q1 (32 KiB each), K ring 3 x 32 KiB, V ring 2 x 32 KiB;
 // each tile is two 64-column halves in the 128-byte swizzled layout, loaded
@@ -57,7 +60,7 @@ constexpr int kSmemQ = 0;               // Q0, Q1
 constexpr int kSmemK = 2 * kTile;
 constexpr int kSmemV = kSmemK + kKStages * kTile;
 constexpr int kSmemBar = kSmemV + kVStages * kTile;
-constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 2 + 2 + 2;
+constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 2 + 2 + 2 + 2;
 constexpr int kSmemBytes = kSmemBar + 256 + 1024;  // + slack for 1024-byte alignment
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;
@@ -120,6 +123,7 @@ struct Bars {
   uint64_t* v_empty;
   uint64_t* s_full;   // [half]
   uint64_t* p_full;   // [half], 128 softmax threads
+  uint64_t* p_lo;     // [half], 128 softmax threads: P of keys 0-63 written
   uint64_t* o_final;  // [half], one phase after the last PV
 };
 
@@ -186,10 +190,14 @@ __device__ __forceinline__ void control_role(const AttnArgs& a, int4 pq, int kv_
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         if (half_sel(e_cur, h, use) != kSkip) {
+          const uint32_t o_t = tbase + kColO + h * kBN, p_t = tbase + h * kBN;
+          const uint32_t v_lo = v_lo0 + ((stv * kTile) >> 4);
+          if (!mbar_wait(B.p_lo + h, cp[h] & 1, a.err, 6 + h)) return;
+          tc_fence_after();
+          issue_pv_half<0>(o_t, p_t, v_lo, cp[h] > 0);
           if (!mbar_wait(B.p_full + h, cp[h] & 1, a.err, 6 + h)) return;
           tc_fence_after();
-          issue_pv(tbase + kColO + h * kBN, tbase + h * kBN, v_lo0 + ((stv * kTile) >> 4),
-                   cp[h] > 0);
+          issue_pv_half<1>(o_t, p_t, v_lo, true);
           ++cp[h];
         }
         if (!more) continue;
@@ -333,6 +341,11 @@ __device__ __forceinline__ void softmax_role(const AttnArgs& a, int4 pq, int kv_
         pk[i] = pack_bf16x2(p0, p1);
       }
       tmem_st32(s_col + 32 * half, pk);
+      if (half == 0) {  // keys 0-63 of P: the first half of PV can start
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(B.p_lo + h);
+      }
     }
     {
       const uint64_t s2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
@@ -401,7 +414,8 @@ __global__ void __launch_bounds__(384, 1)
   B.v_empty = B.v_full + kVStages;
   B.s_full = B.v_empty + kVStages;
   B.p_full = B.s_full + 2;
-  B.o_final = B.p_full + 2;
+  B.p_lo = B.p_full + 2;
+  B.o_final = B.p_lo + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
 
   const int warp = warp_id();
@@ -428,6 +442,7 @@ __global__ void __launch_bounds__(384, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(B.s_full + i, 1);
       mbar_init(B.p_full + i, 128);
+      mbar_init(B.p_lo + i, 128);
       mbar_init(B.o_final + i, 1);
     }
     fence_mbar_init();

@@ -98,18 +98,17 @@ __device__ __forceinline__ void issue_s(uint32_t d_tmem, uint32_t qlo, uint32_t 
   issue_s_step<7>(d_tmem, qlo, klo);
 }
 
-// O (128 x 128) += P (128 x 128 keys, bf16 in TMEM) * V (128 keys x 128)
-__device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t vlo,
-                                         bool accumulate) {
-  static_assert(kBN / 16 == 8, "eight K steps");
-  issue_pv_step<0>(o_tmem, p_tmem, vlo, accumulate);
-  issue_pv_step<1>(o_tmem, p_tmem, vlo, accumulate);
-  issue_pv_step<2>(o_tmem, p_tmem, vlo, accumulate);
-  issue_pv_step<3>(o_tmem, p_tmem, vlo, accumulate);
-  issue_pv_step<4>(o_tmem, p_tmem, vlo, accumulate);
-  issue_pv_step<5>(o_tmem, p_tmem, vlo, accumulate);
-  issue_pv_step<6>(o_tmem, p_tmem, vlo, accumulate);
-  issue_pv_step<7>(o_tmem, p_tmem, vlo, accumulate);
+// O (128 x 128) += P (128 x 128 keys, bf16 in TMEM) * V (128 keys x 128), the
+// half over keys 64*H .. 64*H + 63 (K steps 4H .. 4H+3): the first half can
+// run while the second half of P is computed.
+template <int H>
+__device__ __forceinline__ void issue_pv_half(uint32_t o_tmem, uint32_t p_tmem, uint32_t vlo,
+                                              bool accumulate) {
+  static_assert(kBN / 16 == 8 && (H == 0 || H == 1), "two halves of four K steps");
+  issue_pv_step<4 * H + 0>(o_tmem, p_tmem, vlo, accumulate);
+  issue_pv_step<4 * H + 1>(o_tmem, p_tmem, vlo, accumulate);
+  issue_pv_step<4 * H + 2>(o_tmem, p_tmem, vlo, accumulate);
+  issue_pv_step<4 * H + 3>(o_tmem, p_tmem, vlo, accumulate);
 }
 
 template <int kMaps>
