@@ -7,6 +7,8 @@ block's per-frame mouse attention and keyboard cross-attention,
   key-major transpose, tcgen05 backward kernels) match fp32 autograd of the
   batch's block-diagonal masked attention, on temporal, keyboard and random
   masks with rows without keys and keys no query sees.
+* At configuration 3's sizes (880 x 42 frames; 4 x 9 240 rows over 504
+  keys; 24 heads) on sampled batch entries.
 * ``SelfAttention`` over a batch (projections, fused prologue with a RoPE
   table shared by the batch, attention) and ``CrossAttention`` train against
   the fp32 autograd of the reference's module math
@@ -237,3 +239,38 @@ def test_keyboard_cross_attention_training_matches_fp32(P, F, n, win, L):
     _check(ctx.grad, cr.grad, "dctx", b_dc)
     for name, p in ca.named_parameters():
         _check(p.grad, w[name].grad, name, b_w[name])
+
+
+def test_config3_action_backward_full_size():
+    """Gradients at configuration 3's sizes, 24 heads: the per-frame attention
+    (880 sequences of 42 frames, 1-frame block-causal mask) and the keyboard
+    cross-attention (4 players x 9 240 rows over 504 keyboard keys).  A batch
+    entry's gradients depend on its own rows only, so sampled entries are
+    checked against fp32 autograd."""
+    from multics_b200.action import (get_temporal_block_causal_mask, keyboard_frame_mask,
+                                     shared_mask_attention)
+    from multics_b200.attention import device_error
+
+    dev = torch.device("cuda")
+    H = 24
+    dim = H * 128
+    fm = get_temporal_block_causal_mask(42, 1, -1, device=dev)
+    cases = (("temporal", 880, 42, 42, fm, (0, 437, 879)),
+             ("keyboard", 4, 42 * 220, 42 * 12, keyboard_frame_mask(fm, 220, 12), (0, 3)))
+    for name, B, Lq, Lk, m, sample in cases:
+        g = torch.Generator(device="cuda").manual_seed(B)
+        q, k, v = (torch.randn(B, L, dim, generator=g, device=dev).mul(0.7).bfloat16()
+                   .requires_grad_(True) for L in (Lq, Lk, Lk))
+        dout = torch.randn(B, Lq, dim, generator=g, device=dev).bfloat16()
+        shared_mask_attention(q, k, v, H, m).backward(dout)
+        torch.cuda.synchronize()
+        assert device_error(dev) == 0, name
+        for b in sample:
+            qf, kf, vf = (t[b].detach().float().requires_grad_(True) for t in (q, k, v))
+            _fp32_attention(qf, kf, vf, m, H).backward(dout[b].float())
+            _check(q.grad[b], qf.grad, (name, b, "dq"))
+            _check(k.grad[b], kf.grad, (name, b, "dk"))
+            _check(v.grad[b], vf.grad, (name, b, "dv"))
+            del qf, kf, vf
+        del q, k, v, dout
+        torch.cuda.empty_cache()
