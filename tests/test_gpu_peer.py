@@ -107,8 +107,7 @@ def test_peer_rows_on_second_gpu_match_local_copy(monkeypatch):
     # key/value boxes the plan reads from stream 2 and up (the peer's rows)
     qp = sh.q_pairs[:sh.n_pairs].cpu().numpy()
     kv = sh.kv_tiles.cpu().numpy()
-    boxes = sum(int((kv[qp[p, 4]:qp[p, 5], :2] >> 24) >= 2).sum() for p in range(sh.n_pairs)) \
-        if sh.n_pairs else 0
+    boxes = sum(int(((kv[qp[p, 4]:qp[p, 5], :2] >> 24) >= 2).sum()) for p in range(sh.n_pairs))
     assert boxes > 0, "the plan reads no peer rows"
 
     outs, parts = [], []
