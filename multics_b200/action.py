@@ -109,6 +109,17 @@ class SharedMaskPlan(AttentionPlan):
             ptr(row_masks), ptr(order), stream_ptr(dev)))
         super().__init__(q_pairs, kv_tiles, row_masks, order)
         self._mask_bytes = m  # read by the builder on the stream
+        self._aligned_form = None
+
+    def aligned_form(self) -> "SharedMaskPlan":
+        """This plan's mask and batch as an aligned plan (itself when it is
+        one), built once."""
+        if self.aligned:
+            return self
+        if self._aligned_form is None:
+            self._aligned_form = SharedMaskPlan(self._mask_bytes.view(torch.bool), self.B,
+                                                aligned=True)
+        return self._aligned_form
 
 
 # (weakref to the caller's mask or None, its _version, B, Lq, Lk, device,
@@ -194,8 +205,9 @@ def shared_mask_attention(q, k, v, num_heads: int, mask=None, *, out=None,
 
         if out is not None:
             raise ValueError("out= is not supported while autograd records")
-        if plan is None or not plan.aligned:
-            plan = shared_mask_plan(mask, B, Lq, Lk, q.device, aligned=True)
+        # a caller's plan carries its own mask: its aligned form, not `mask`
+        plan = (shared_mask_plan(mask, B, Lq, Lk, q.device, aligned=True) if plan is None
+                else plan.aligned_form())
         res = plan_attention_grad(q.reshape(B * Lq, dim), k.reshape(B * Lk, dim),
                                   v.reshape(B * Lk, dim), plan, num_heads)
         return res.view(B, Lq, dim)

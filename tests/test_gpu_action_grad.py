@@ -274,3 +274,33 @@ def test_config3_action_backward_full_size():
             del qf, kf, vf
         del q, k, v, dout
         torch.cuda.empty_cache()
+
+
+def test_grads_follow_a_callers_packed_plan():
+    """A packed plan passed with ``mask=None`` while autograd records: the
+    attention and its gradients follow the plan's own mask (its aligned
+    form), not an unmasked plan."""
+    from multics_b200.action import shared_mask_attention, shared_mask_plan
+
+    dev = torch.device("cuda")
+    B, Lq, Lk, H = 5, 42, 42, 2
+    dim = H * 128
+    m = torch.from_numpy(_mask("temporal", (7, 24), Lq, Lk)).to(dev)
+    plan = shared_mask_plan(m, B, Lq, Lk, dev)
+    assert not plan.aligned
+    g = torch.Generator(device="cuda").manual_seed(21)
+    q, k, v = (torch.randn(B, L, dim, generator=g, device=dev).mul(0.7).bfloat16()
+               .requires_grad_(True) for L in (Lq, Lk, Lk))
+    dout = torch.randn(B, Lq, dim, generator=g, device=dev).bfloat16()
+    out = shared_mask_attention(q, k, v, H, None, plan=plan)
+    out.backward(dout)
+    torch.cuda.synchronize()
+    assert plan.aligned_form().aligned and plan.aligned_form() is plan.aligned_form()
+    dense = torch.block_diag(*([m] * B))
+    qf, kf, vf = (t.detach().float().reshape(-1, dim).requires_grad_(True) for t in (q, k, v))
+    ref = _fp32_attention(qf, kf, vf, dense, H)
+    ref.backward(dout.float().reshape(-1, dim))
+    _check(out.detach().reshape(-1, dim), ref.detach(), "out")
+    _check(q.grad.reshape(-1, dim), qf.grad, "dq")
+    _check(k.grad.reshape(-1, dim), kf.grad, "dk")
+    _check(v.grad.reshape(-1, dim), vf.grad, "dv")
