@@ -646,7 +646,8 @@ extern "C" int hier_attn_fwd_streams(const void* q, int64_t q_rows_total, int64_
 namespace hier {
 namespace {
 
-__device__ __forceinline__ void bf16x8_unpack(const uint4& raw, float (&f)[8]) {
+__device__ __forceinline__ void bf16x8_load(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
   const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -654,10 +655,6 @@ __device__ __forceinline__ void bf16x8_unpack(const uint4& raw, float (&f)[8]) {
     f[2 * i] = v.x;
     f[2 * i + 1] = v.y;
   }
-}
-
-__device__ __forceinline__ void bf16x8_load(const __nv_bfloat16* p, float (&f)[8]) {
-  bf16x8_unpack(*reinterpret_cast<const uint4*>(p), f);
 }
 
 __device__ __forceinline__ void bf16x8_store(__nv_bfloat16* p, const float (&f)[8], float s) {
@@ -697,18 +694,11 @@ __device__ __forceinline__ void partial_at(const PartialSrc& p, int64_t pr,
 }
 
 // Per (target, head, 8 channels): the normalised weighted sum of the partials.
-// For the peer merge (partials in other GPUs' memory) the first kCached
-// partials of a target are requested together (their log-sum-exps and their
-// 8 channels), so that a thread waits for one NVLink round trip rather than
-// one per dependent load; more partials take a second loop.  With one local
-// buffer the loads hit L2 and the lighter loop (more threads resident) is
-// faster.  The sums run in partial order either way.
 template <bool kPeers>
 __global__ void lse_gather_kernel(PartialSrc src, int64_t o_stride, int H, int D,
                                   const int32_t* off, const int32_t* rows, int64_t n_targets,
                                   __nv_bfloat16* out, int64_t out_stride,
                                   const int32_t* out_rows) {
-  constexpr int kCached = kPeers ? 8 : 0;
   const int per = D / 8;
   const int64_t n = n_targets * H * per;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n;
@@ -718,26 +708,8 @@ __global__ void lse_gather_kernel(PartialSrc src, int64_t o_stride, int H, int D
     const int64_t r = rh / H;
     const int h = (int)(rh % H);
     const int b = off[r], e = off[r + 1];
-    const int nc = min(e - b, kCached);
-    float lv[kCached > 0 ? kCached : 1];
-    uint4 ov[kCached > 0 ? kCached : 1];
-#pragma unroll
-    for (int i = 0; i < kCached; ++i) {
-      lv[i] = -INFINITY;
-      ov[i] = make_uint4(0u, 0u, 0u, 0u);
-      if (i < nc) {
-        const int64_t pr = rows[b + i];
-        const __nv_bfloat16* o;
-        const float* lse;
-        partial_at<kPeers>(src, pr, &o, &lse);
-        lv[i] = lse[pr * H + h];
-        ov[i] = *reinterpret_cast<const uint4*>(o + pr * o_stride + h * D + part * 8);
-      }
-    }
     float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < kCached; ++i) m = fmaxf(m, lv[i]);
-    for (int i = b + kCached; i < e; ++i) {
+    for (int i = b; i < e; ++i) {
       const __nv_bfloat16* o;
       const float* lse;
       partial_at<kPeers>(src, rows[i], &o, &lse);
@@ -745,17 +717,7 @@ __global__ void lse_gather_kernel(PartialSrc src, int64_t o_stride, int H, int D
     }
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     float ws = 0.f;
-#pragma unroll
-    for (int i = 0; i < kCached; ++i) {
-      if (i >= nc || lv[i] == -INFINITY || m == -INFINITY) continue;
-      const float wt = exp2f(lv[i] - m);
-      float f[8];
-      bf16x8_unpack(ov[i], f);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] = fmaf(wt, f[q], acc[q]);
-      ws += wt;
-    }
-    for (int i = b + kCached; i < e; ++i) {
+    for (int i = b; i < e; ++i) {
       const int64_t pr = rows[i];
       const __nv_bfloat16* o;
       const float* lse;
