@@ -513,6 +513,9 @@ def run_ours(args, rank, world, local_rank):
     if world == 1:
         line["cached_step"] = run_cached_step()
         line["plans_rebuild_ms"] = plans_rebuild(cfg, dev)
+        line["plans_once_note"] = ("breakdown_ms.plans_once is the first plan build of the "
+                                   "process, which also loads the CUDA library and its "
+                                   "kernels; plans_rebuild_ms is the cost per regrouping")
     if world == 1:
         del inp, q_buf, k_buf, o_buf
         torch.cuda.empty_cache()
