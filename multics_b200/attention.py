@@ -257,14 +257,19 @@ class HierSequencePlan:
                 and spec.T % spec.n_block == 0
                 and (spec.local_attn == -1 or spec.local_attn >= spec.n_block))
 
-    def attend(self, q_plan, k_plan, v, out=None):
+    def attend(self, q_plan, k_plan, v, out=None, events=None):
         """Attention of roped ``q_plan`` / ``k_plan`` (plan row order) and
         ``v`` (sequence order), all ``[S, H*D]`` bf16; returns ``out`` in
-        sequence order."""
+        sequence order.  ``events`` (two CUDA events) are recorded on the
+        current stream around the attention kernel's launch alone."""
         if out is None:
             out = torch.empty_like(v)
         v_hub = v[self.A:].index_select(0, self.hub_src)
+        if events is not None:
+            events[0].record()
         self.core.attend(q_plan, k_plan, v, out, v_hub=v_hub, out_rows=self.plan_to_seq)
+        if events is not None:
+            events[1].record()
         self.core.merge(out, out_rows=self.hub_dst)
         return out
 
