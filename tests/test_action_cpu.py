@@ -123,3 +123,16 @@ def test_shared_mask_plan_rejects_bad_sizes():
         rc, _, _ = _plan_size(B, Lq, Lk)
         assert rc == 1, (B, Lq, Lk)
         assert b"shared-mask plan" in _lib.lib().hier_last_error()
+
+
+def test_out_refused_while_autograd_records():
+    """The differentiable form allocates its own output: ``out=`` is refused
+    (before any device work) when q, k or v requires grad."""
+    import torch
+
+    from multics_b200.action import shared_mask_attention
+
+    q = torch.zeros(2, 4, 256, dtype=torch.bfloat16, requires_grad=True)
+    k = torch.zeros(2, 6, 256, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="out="):
+        shared_mask_attention(q, k, k, 2, None, out=torch.empty_like(q))
