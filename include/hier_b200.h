@@ -678,6 +678,26 @@ int hier_shard_build(const hier_shard_desc* g, const int32_t* counts, int32_t* q
                      int32_t* kv_tiles, int32_t tile_capacity, uint32_t* tile_masks,
                      int64_t mask_capacity, int32_t* order, int32_t* status, void* stream);
 
+/* Bounds check of an attention work plan (q_pairs [n_pairs][8], kv_tiles
+ * [n_tiles][4], order [n_pairs] or NULL) before a launch, for plans that a
+ * caller built, stored or received: every pair's key-tile range inside
+ * [0, n_tiles), its query rows inside [0, q_rows_total) (count a second query
+ * block's rows in) and at most 128 per tile, every selector -1, -2 or a
+ * row-mask index below n_masks, every 64-row key box in an existing stream
+ * (stream index row >> 24 below n_streams) starting before the stream's end
+ * plus 64 rows (row & 0xFFFFFF below stream_rows[stream] + 64: the second
+ * box of a block plan's last tile may start past the end; rows past the end
+ * read as zero), every order entry below n_pairs.  The check reads a table entry
+ * only after checking its index.  status (device int32, cleared first): bit
+ * 0 key-tile range, bit 1 query rows, bit 2 selector, bit 3 key rows or
+ * stream, bit 4 order.  stream_rows is a host array of n_streams (1..32)
+ * entries.  Partial-row destinations are not checked.  No host sync.  This
+ * is the metadata-corruption check the reference's plugin performs on the
+ * host (kernels/hier_packed_attention.py:224-225), on the device. */
+int hier_plan_check(const int32_t* q_pairs, int32_t n_pairs, const int32_t* kv_tiles,
+                    int64_t n_tiles, int64_t n_masks, const int32_t* order, int64_t q_rows_total,
+                    const int64_t* stream_rows, int32_t n_streams, int32_t* status, void* stream);
+
 /* Merge of partial rows over disjoint key sets.  Target t has the partial
  * rows rows[off[t] .. off[t+1]) of o (bf16 [.., H*D], row stride o_stride)
  * with log2-sum-exp lse ([..][H]); out[out_rows ? out_rows[t] : t] =

@@ -196,6 +196,8 @@ _SIGS = {
     "hier_lse_gather_merge_peers": (c_int, [_P, _P, c_int32, c_int32, c_int64, c_int64, c_int64,
                                             c_int32, c_int32, _P, _P, c_int64, _P, c_int64, _P,
                                             _P, _P]),
+    "hier_plan_check": (c_int, [_P, c_int32, _P, c_int64, c_int64, _P, c_int64, _P, c_int32, _P,
+                                _P]),
     "hier_selftest_umma": (c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "hier_selftest_wait_timeout": (c_int, [c_int64, _P, _P, _P]),
 }
@@ -203,7 +205,7 @@ _SIGS = {
 _LIB = None
 
 # hier_abi_version() of the library these signatures describe
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 
 def lib():

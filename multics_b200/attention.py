@@ -16,6 +16,7 @@ Drop-in counterparts of the reference's ``multics/models/attention.py``:
 
 from __future__ import annotations
 
+import ctypes
 import math
 import os
 from typing import Optional
@@ -147,9 +148,42 @@ class AttentionPlan:
         self.order = order
 
 
+PLAN_CHECK_ENV = "MULTICS_B200_CHECK_PLANS"
+
+_PLAN_CHECK_BITS = ((1, "a pair's key-tile range leaves the tile table"),
+                    (2, "query rows leave the query tensor"),
+                    (4, "a mask selector leaves the row-mask table"),
+                    (8, "a key box starts outside its key/value stream"),
+                    (16, "an order entry leaves the pairs"))
+
+
+def check_plan(plan, q_rows: int, kv_rows, *, n_masks: Optional[int] = None,
+               n_tiles: Optional[int] = None):
+    """Raise ValueError when an attention plan's indices leave its tables or
+    the tensors it will read (``hier_plan_check`` on the device, then one host
+    read): the check to run before launching a plan that was built, stored or
+    received elsewhere.  ``kv_rows``: rows of the key/value stream, or a list
+    of them (one per stream)."""
+    qp, kv = plan.q_pairs, plan.kv_tiles
+    dev = qp.device
+    rows = [int(kv_rows)] if isinstance(kv_rows, (int, np.integer)) else [int(r) for r in kv_rows]
+    arr = (ctypes.c_int64 * len(rows))(*rows)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(_lib.lib().hier_plan_check(
+        ptr(qp), qp.shape[0], ptr(kv), kv.shape[0] if n_tiles is None else int(n_tiles),
+        plan.row_masks.shape[0] if n_masks is None else int(n_masks), ptr(plan.order),
+        int(q_rows), arr, len(rows), ptr(status), stream_ptr(dev)))
+    bits = int(status.item())
+    if bits:
+        raise ValueError("attention plan rejected before launch: " +
+                         "; ".join(msg for bit, msg in _PLAN_CHECK_BITS if bits & bit))
+
+
 def attention_from_plan(q, k, v, plan, num_heads, *, out=None, softmax_scale=None,
                         q_rows_total=None):
-    """Run the tcgen05 attention kernel for ``plan`` on ``[S,H*D]`` bf16 rows."""
+    """Run the tcgen05 attention kernel for ``plan`` on ``[S,H*D]`` bf16 rows.
+    With ``MULTICS_B200_CHECK_PLANS=1`` the plan is bounds-checked first
+    (:func:`check_plan`)."""
     q2, k2, v2 = _rows(q), _rows(k), _rows(v)
     for name, t in (("q", q2), ("k", k2), ("v", v2)):
         if t.dtype != torch.bfloat16:
@@ -164,6 +198,8 @@ def attention_from_plan(q, k, v, plan, num_heads, *, out=None, softmax_scale=Non
         out = torch.empty(S, dim, dtype=torch.bfloat16, device=q2.device)
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
     n_pairs = plan.q_pairs.shape[0]
+    if os.environ.get(PLAN_CHECK_ENV, "0") == "1":
+        check_plan(plan, S if q_rows_total is None else q_rows_total, k2.shape[0])
     check(_lib.lib().hier_attn_fwd(
         ptr(q2), S if q_rows_total is None else q_rows_total, q2.stride(0), ptr(k2), ptr(v2),
         k2.shape[0], k2.stride(0), ptr(out), out.stride(0), num_heads, D, ptr(plan.q_pairs),

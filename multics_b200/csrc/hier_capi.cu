@@ -75,4 +75,4 @@ int make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t r
 
 extern "C" const char* hier_last_error(void) { return hier::g_msg; }
 extern "C" int hier_last_error_code(void) { return hier::g_code; }
-extern "C" int hier_abi_version(void) { return 4; }
+extern "C" int hier_abi_version(void) { return 5; }

@@ -1031,3 +1031,89 @@ extern "C" int hier_block_mask_build_static(const hier_grouping* g, int32_t* kv_
   HIER_CHECK_CUDA(cudaGetLastError(), "static block mask kernels launch");
   return HIER_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Bounds check of an attention work plan before a launch.  Reads a table
+// entry only after checking its index, so a corrupted plan cannot make the
+// check itself read out of range.
+// ---------------------------------------------------------------------------
+namespace hier {
+
+constexpr int kCheckMaxStreams = 32;
+
+struct PlanCheckArgs {
+  const int4* pairs;  // [n_pairs][2] int4
+  int32_t n_pairs;
+  const int4* kv_tiles;
+  int64_t n_tiles, n_masks, q_rows_total;
+  const int32_t* order;
+  int32_t n_streams;
+  int64_t stream_rows[kCheckMaxStreams];
+};
+
+// A 64-row key box: its stream exists (the kernel indexes its tensor maps by
+// it) and it starts before the stream's end plus 64 rows (the second box of a
+// block plan's last tile may start past the end; TMA reads such rows as 0).
+__device__ __forceinline__ bool key_box_ok(const PlanCheckArgs& a, int32_t r) {
+  if (r < 0) return false;
+  const int s = r >> 24;
+  return s < a.n_streams && (int64_t)(r & ((1 << 24) - 1)) < a.stream_rows[s] + 64;
+}
+
+__global__ void plan_check_kernel(PlanCheckArgs a, int32_t* status) {
+  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < a.n_pairs;
+       p += (int64_t)gridDim.x * blockDim.x) {
+    const int4 pq = a.pairs[2 * p], pk = a.pairs[2 * p + 1];
+    int bits = 0;
+    const int qs[2] = {pq.x, pq.z}, qr[2] = {pq.y, pq.w};
+    for (int h = 0; h < 2; ++h)
+      if (qr[h] < 0 || qr[h] > 128 ||
+          (qr[h] > 0 && (qs[h] < 0 || (int64_t)qs[h] + qr[h] > a.q_rows_total)))
+        bits |= 2;
+    if (pk.x < 0 || pk.y < pk.x || (int64_t)pk.y > a.n_tiles) {
+      bits |= 1;
+    } else {
+      for (int e = pk.x; e < pk.y; ++e) {
+        const int4 t = a.kv_tiles[e];
+        const int sel[2] = {t.z, t.w};
+        for (int h = 0; h < 2; ++h)
+          if (sel[h] < -2 || (sel[h] >= 0 && (int64_t)sel[h] >= a.n_masks)) bits |= 4;
+        if (!key_box_ok(a, t.x) || !key_box_ok(a, t.y)) bits |= 8;
+      }
+    }
+    if (a.order && (a.order[p] < 0 || a.order[p] >= a.n_pairs)) bits |= 16;
+    if (bits) atomicOr(status, bits);
+  }
+}
+
+}  // namespace hier
+
+extern "C" int hier_plan_check(const int32_t* q_pairs, int32_t n_pairs, const int32_t* kv_tiles,
+                               int64_t n_tiles, int64_t n_masks, const int32_t* order,
+                               int64_t q_rows_total, const int64_t* stream_rows,
+                               int32_t n_streams, int32_t* status, void* stream) {
+  clear_error();
+  if (n_pairs < 0 || n_tiles < 0 || n_masks < 0 || q_rows_total < 0 || n_streams < 1 ||
+      n_streams > kCheckMaxStreams || !stream_rows || !status ||
+      (n_pairs > 0 && !q_pairs) || (n_tiles > 0 && !kv_tiles)) {
+    set_error(HIER_EVALUE, "hier_plan_check: invalid arguments (pairs %d, tiles %lld, "
+              "streams %d)", n_pairs, (long long)n_tiles, n_streams);
+    return HIER_EVALUE;
+  }
+  PlanCheckArgs a{};
+  a.pairs = (const int4*)q_pairs;
+  a.n_pairs = n_pairs;
+  a.kv_tiles = (const int4*)kv_tiles;
+  a.n_tiles = n_tiles;
+  a.n_masks = n_masks;
+  a.q_rows_total = q_rows_total;
+  a.order = order;
+  a.n_streams = n_streams;
+  for (int s = 0; s < n_streams; ++s) a.stream_rows[s] = stream_rows[s];
+  cudaStream_t s = (cudaStream_t)stream;
+  HIER_CHECK_CUDA(cudaMemsetAsync(status, 0, sizeof(int32_t), s), "plan check status clear");
+  if (n_pairs > 0)
+    plan_check_kernel<<<grid_for(n_pairs, 128), 128, 0, s>>>(a, status);
+  HIER_CHECK_CUDA(cudaGetLastError(), "plan_check_kernel launch");
+  return HIER_OK;
+}
