@@ -118,3 +118,24 @@ def test_sequence_plan_selection_rules(monkeypatch):
     monkeypatch.setenv(FULL_SEQUENCE_PLAN_ENV, "tiles")
     with pytest.raises(ValueError, match="segments"):
         sequence_plan(SimpleNamespace(spec=ok), 2)
+
+
+def test_plan_check_rejects_bad_arguments_on_the_host():
+    """hier_plan_check refuses invalid sizes (no streams, more than 32, a
+    negative count, missing tables) before any device work."""
+    import ctypes
+
+    from multics_b200 import _lib
+
+    h = _lib.lib()
+    rows1 = (ctypes.c_int64 * 1)(100)
+    rows33 = (ctypes.c_int64 * 33)(*([100] * 33))
+    st = ctypes.c_void_p(16)  # never written: the host check fails first
+    for args in [(None, 0, None, 0, 0, None, 100, rows1, 0, st, None),
+                 (None, 0, None, 0, 0, None, 100, rows33, 33, st, None),
+                 (None, -1, None, 0, 0, None, 100, rows1, 1, st, None),
+                 (None, 4, None, 0, 0, None, 100, rows1, 1, st, None),
+                 (None, 0, None, 0, 0, None, 100, None, 1, st, None),
+                 (None, 0, None, 0, 0, None, 100, rows1, 1, None, None)]:
+        assert h.hier_plan_check(*args) == 1, args
+        assert b"hier_plan_check" in h.hier_last_error()
