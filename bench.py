@@ -697,10 +697,10 @@ def run_cached_step(steps=20, warmup=3):
 
 
 def run_backward(cfg, steps=10, warmup=3):
-    """Training step of the attention at the bench configuration on the block
-    plan (the plan the gradients use): the forward with its log2-sum-exp and
-    the backward (Delta, dQ over the query-major plan, dK/dV over the
-    key-major plan), inputs resident in HBM.  Useful FLOPs: the forward's 2
+    """Training step of the attention at the bench configuration: the forward
+    with its log2-sum-exp (on the grouping's sequence plan when it has one)
+    and the backward on the block plan (Delta, dQ over the query-major plan,
+    dK/dV over the key-major plan), inputs resident in HBM.  Useful FLOPs: the forward's 2
     matmuls per unmasked pair and head (4*D), the backward's 4 (dV, dP, dQ,
     dK: 8*D); the kernels also recompute S (dQ and dK/dV kernels each), which
     is not counted."""
@@ -740,7 +740,7 @@ def run_backward(cfg, steps=10, warmup=3):
     bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
     pairs = useful_pairs(bm)
     f_fwd = 4.0 * cfg.D * cfg.H * pairs
-    res = {"workload": f"{cfg.name}: attention forward + backward on the 128x128 block plan, "
+    res = {"workload": f"{cfg.name}: attention forward (sequence plan) + backward (128x128 block plan), "
                        f"S={S}, {cfg.H}x{cfg.D}, random bf16 q/k/v and output gradient",
            "forward_ms": round(fwd, 4), "backward_ms": round(bwd, 4),
            "forward_tflops": round(f_fwd / (fwd * 1e-3) / 1e12, 1),

@@ -293,21 +293,47 @@ class HierSequencePlan:
                 and spec.T % spec.n_block == 0
                 and (spec.local_attn == -1 or spec.local_attn >= spec.n_block))
 
-    def attend(self, q_plan, k_plan, v, out=None, events=None):
+    def attend(self, q_plan, k_plan, v, out=None, events=None, lse=None):
         """Attention of roped ``q_plan`` / ``k_plan`` (plan row order) and
         ``v`` (sequence order), all ``[S, H*D]`` bf16; returns ``out`` in
         sequence order.  ``events`` (two CUDA events) are recorded on the
-        current stream around the attention kernel's launch alone."""
+        current stream around the attention kernel's launch alone.  ``lse``
+        (float32 ``[S, H]``, optional) receives every row's log2-sum-exp in
+        sequence order (:meth:`hub_lse` for the hub rows)."""
         if out is None:
             out = torch.empty_like(v)
         v_hub = v[self.A:].index_select(0, self.hub_src)
         if events is not None:
             events[0].record()
-        self.core.attend(q_plan, k_plan, v, out, v_hub=v_hub, out_rows=self.plan_to_seq)
+        self.core.attend(q_plan, k_plan, v, out, v_hub=v_hub, out_rows=self.plan_to_seq, lse=lse)
         if events is not None:
             events[1].record()
         self.core.merge(out, out_rows=self.hub_dst)
+        if lse is not None:
+            self.hub_lse(lse)
         return out
+
+    def hub_lse(self, lse):
+        """The hub rows' log2-sum-exp over all their keys, log2 of the sum of
+        2^lse over their partial rows (the merge's lists), into ``lse`` at
+        their sequence rows."""
+        c = self.core
+        if not self.hub_dst.numel():
+            return lse
+        if getattr(self, "_lse_gather", None) is None:
+            off = c.csr_off.long()
+            counts = off[1:] - off[:-1]
+            kmax = max(int(counts.max().item()), 1)
+            idx = off[:-1, None] + torch.arange(kmax, device=off.device)[None]
+            valid = idx < off[1:, None]
+            rows = c.csr_rows.long()[torch.where(valid, idx, torch.zeros_like(idx))]
+            self._lse_gather = (rows, valid)
+        rows, valid = self._lse_gather
+        vals = c.part_lse[rows]  # [hub rows, partials, H]
+        vals = torch.where(valid[..., None], vals, torch.full_like(vals, float("-inf")))
+        ln2 = math.log(2.0)
+        lse[self.hub_dst.long()] = torch.logsumexp(vals * ln2, dim=1) / ln2
+        return lse
 
 
 def sequence_plan(block_mask: HierBlockMask, num_heads: int) -> Optional[HierSequencePlan]:

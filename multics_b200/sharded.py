@@ -514,11 +514,14 @@ class ShardedHierAttention:
             self.remote[i * t.L:(i + 1) * t.L, :self.dim] = k_all[src:src + t.L]
             self.remote[i * t.L:(i + 1) * t.L, self.dim:] = v_all[src:src + t.L]
 
-    def attend(self, q, k, v, out, *, v_hub=None, out_rows=None):
+    def attend(self, q, k, v, out, *, v_hub=None, out_rows=None, lse=None):
         """One attention launch over this rank's query rows: player rows into
         ``out`` (row ``out_rows[r]`` when given), hub rows as partial rows
         (merged by :meth:`merge`).  ``v_hub`` replaces ``v``'s hub rows (a
-        group-major copy when ``v`` keeps the sequence order)."""
+        group-major copy when ``v`` keeps the sequence order).  ``lse``
+        (float32 ``[rows, H]``, optional) receives the player rows'
+        log2-sum-exp at the same rows as ``out``; the hub rows' partials keep
+        theirs in :attr:`part_lse`."""
         t = self.topo
         own, hub = t.own_rows, t.hub_rows
         if self.transport == "peer":
@@ -545,7 +548,7 @@ class ShardedHierAttention:
         check(_lib.lib().hier_attn_fwd_streams(
             ptr(q), q.shape[0], q.stride(0), n, kp, vp, rows, strides, ptr(out), out.stride(0),
             ptr(out_rows), self.H, self.D, ptr(self.q_pairs), self.n_pairs, ptr(self.kv_tiles),
-            ptr(self.tile_masks), 128, ptr(self.order), 1.0 / math.sqrt(self.D), None,
+            ptr(self.tile_masks), 128, ptr(self.order), 1.0 / math.sqrt(self.D), ptr(lse),
             ctypes.byref(part), ptr(self.err), stream_ptr(q.device)))
 
     # ---- hub merge: partial rows -> hub rows ---------------------------------

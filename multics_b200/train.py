@@ -78,9 +78,24 @@ def block_plan_grad(plan, kv_rows: int) -> BlockPlanGrad:
     return gp
 
 
+def _sequence_plan_for(plan, num_heads, scale, D, q_rows, kv_rows):
+    """The sequence plan of a block mask's grouping when the forward can run
+    on it (self-attention at the default softmax scale), else None."""
+    if not isinstance(plan, HierBlockMask) or q_rows != kv_rows or q_rows != plan.S:
+        return None
+    if abs(scale - 1.0 / math.sqrt(D)) > 1e-9 * scale:
+        return None
+    from .attention import sequence_plan
+
+    return sequence_plan(plan, num_heads)
+
+
 class _PlanAttention(torch.autograd.Function):
     """Attention of query rows ``[Sq, H*D]`` over key/value rows ``[Sk, H*D]``
-    under an aligned plan; forward keeps the log2-sum-exp for the backward."""
+    under an aligned plan; forward keeps the log2-sum-exp for the backward.
+    For a block mask whose grouping has a sequence plan the forward runs on
+    that plan (the backward only needs O and the log2-sum-exp, whichever
+    plan produced them)."""
 
     @staticmethod
     def forward(ctx, q, k, v, plan, num_heads, scale):
@@ -96,6 +111,19 @@ class _PlanAttention(torch.autograd.Function):
         dev = q2.device
         out = torch.empty_like(q2)
         lse = torch.empty((S, num_heads), dtype=torch.float32, device=dev)
+        sp = _sequence_plan_for(plan, num_heads, scale, D, S, k2.shape[0])
+        if sp is not None:
+            # the forward on the grouping's sequence plan (denser tiles than
+            # the block plan the backward needs): q and k with the hub rows
+            # in the plan's group-major order, out and lse in sequence order
+            A = sp.A
+            q_plan = torch.cat([q2[:A], q2[A:].index_select(0, sp.hub_src)])
+            k_plan = torch.cat([k2[:A], k2[A:].index_select(0, sp.hub_src)])
+            sp.attend(q_plan, k_plan, v2, out=out, lse=lse)
+            ctx.save_for_backward(q2, k2, v2, out, lse)
+            ctx.plan, ctx.num_heads, ctx.scale = plan, num_heads, scale
+            ctx.shapes = (q.shape, k.shape, v.shape)
+            return out.view(q.shape)
         kp = (ctypes.c_void_p * 1)(k2.data_ptr())
         vp = (ctypes.c_void_p * 1)(v2.data_ptr())
         rows = (ctypes.c_int64 * 1)(k2.shape[0])

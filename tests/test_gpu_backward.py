@@ -323,3 +323,30 @@ def test_fused_prologue_grads_match_fp32(S, F, cam):
     _check(k.detach(), kr.detach(), "k")
     for name, got, r in zip(("dqx", "dkx", "dnqw", "dnkw", "dwcq", "dwck"), leaves, ref):
         _check(got.grad, r.grad, name)
+
+
+@pytest.mark.parametrize("case", HIER_CASES[:2] + HIER_CASES[3:], ids=str)
+def test_sequence_plan_forward_matches_block_plan_forward(case, monkeypatch):
+    """For labels groupings the training forward runs on the sequence plan
+    (hub rows' log2-sum-exp from their partials); forcing the block plan
+    gives the same output and gradients within rounding."""
+    from multics_b200.attention import FULL_SEQUENCE_PLAN_ENV, sequence_plan
+    from multics_b200.train import hier_block_attention_grad
+
+    dev = torch.device("cuda")
+    bm, _ = _hier_case(case, dev)
+    assert sequence_plan(bm, 2) is not None
+    S, H = bm.S, 2
+    g = torch.Generator(device="cuda").manual_seed(17)
+    base = [torch.randn(S, H * 128, generator=g, device=dev).mul(0.7).bfloat16() for _ in range(3)]
+    dout = torch.randn(S, H * 128, generator=g, device=dev).bfloat16()
+    res = []
+    for mode in ("segments", "blocks"):
+        monkeypatch.setenv(FULL_SEQUENCE_PLAN_ENV, mode)
+        q, k, v = (t.clone().requires_grad_(True) for t in base)
+        out = hier_block_attention_grad(q, k, v, bm, H)
+        out.backward(dout)
+        torch.cuda.synchronize()
+        res.append((out.detach(), q.grad, k.grad, v.grad))
+    for name, a, b in zip(("out", "dq", "dk", "dv"), res[0], res[1]):
+        _check(a, b, name)
