@@ -139,3 +139,35 @@ def test_plan_check_rejects_bad_arguments_on_the_host():
                  (None, 0, None, 0, 0, None, 100, rows1, 1, None, None)]:
         assert h.hier_plan_check(*args) == 1, args
         assert b"hier_plan_check" in h.hier_last_error()
+
+
+def test_hub_lse_merges_partials_on_cpu():
+    """HierSequencePlan.hub_lse: a hub row's log2-sum-exp is log2 of the sum
+    of 2^lse over its partial rows (ragged lists, -inf partials, a row
+    without keys), written at the row's sequence position."""
+    from types import SimpleNamespace
+
+    import numpy as np
+
+    from multics_b200.attention import HierSequencePlan
+
+    H = 3
+    rng = np.random.default_rng(0)
+    part = rng.normal(0, 4, (9, H)).astype(np.float32)
+    part[2, 1] = -np.inf
+    off = np.array([0, 3, 4, 7, 9], np.int32)
+    rows = np.array([8, 7, 6, 5, 4, 3, 2, 1, 0], np.int32)
+    part[[1, 0]] = -np.inf                    # target 3's partials: no keys at all
+    dst = np.array([10, 12, 11, 13], np.int32)
+    core = SimpleNamespace(csr_off=torch.from_numpy(off), csr_rows=torch.from_numpy(rows),
+                           part_lse=torch.from_numpy(part))
+    sp = SimpleNamespace(core=core, hub_dst=torch.from_numpy(dst))
+    lse = torch.full((14, H), 7.0)
+    HierSequencePlan.hub_lse(sp, lse)
+    for t in range(4):
+        vals = part[rows[off[t]:off[t + 1]]].astype(np.float64)
+        with np.errstate(divide="ignore"):
+            want = np.log2(np.exp2(vals).sum(0))
+        np.testing.assert_allclose(lse[dst[t]].numpy(), want, rtol=1e-5, atol=1e-5)
+    assert bool((lse[:10] == 7.0).all())      # other rows untouched
+    assert bool(torch.isinf(lse[13]).all())
